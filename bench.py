@@ -1,0 +1,459 @@
+"""Decode throughput benchmark for the B200 DeepSeek-V2-Lite engine.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3|4|5] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N   (expert parallel)
+
+Workload (synthetic seeded inputs stand in for real prompts):
+  config 2: 27-layer DeepSeek-V2-Lite, bf16 N(0, 0.02) weights seed 1, B=1, 512-token prompt, small family
+  config 3: same weights, B=32, 512-token prompts (seed 2), batch family
+  config 4: same weights, B=256, prompt lengths U[128, 1024] (seed 3), ragged latent cache, batch family
+            (default: the north-star roofline target and the largest single-GPU config)
+  config 5: same weights, B=64, 8192-token prompts (seed 4), Zipf(1.1)-skewed router
+One step = one CUDA-graph replay of the q_len=1 decode step for every row (all 27
+layers, lm_head and greedy argmax).  `value` = decoded tokens / s over all ranks, timed
+with CUDA events over K replays (max over ranks); the per-step working set (~31 GB of
+weights) is far larger than L2, so no flush is needed between steps.  `e2e` repeats the
+decode through the public engine API with the token ids crossing host<->device every
+step (pinned buffers, copies inside the timed region).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "flash-deepseek-v2-lite_b200"))
+sys.path.insert(0, str(REPO))
+
+METRIC = "decode tok/s at bsz 1/32/256, ctx 512; ms/step vs HBM roofline; 1/2/4/8 GPU"
+
+CONFIGS = {
+    2: dict(batch=1, prompt=("fixed", 512), seed=1, family="small", skew=False),
+    3: dict(batch=32, prompt=("fixed", 512), seed=2, family="batch", skew=False),
+    4: dict(batch=256, prompt=("uniform", 128, 1024), seed=3, family="batch", skew=False),
+    5: dict(batch=64, prompt=("fixed", 8192), seed=4, family="batch", skew=True),
+}
+WEIGHT_SEED = 1
+
+# algorithmic bytes (bf16 weights + latent KV), SURVEY section 8(d)
+ATTN_BYTES = 2 * 13_767_168
+DENSE_BYTES = 2 * 67_239_936
+SHARED_BYTES = 2 * 17_301_504
+GATE_BYTES = 2 * 131_072
+LMHEAD_BYTES = 2 * 209_715_200
+EXPERT_BYTES = 2 * 8_650_752
+KV_ROW_BYTES = 576 * 2
+
+
+def prompt_lengths(cfg: dict, batch: int) -> list[int]:
+    kind = cfg["prompt"][0]
+    if kind == "fixed":
+        return [cfg["prompt"][1]] * batch
+    g = torch.Generator().manual_seed(cfg["seed"])
+    lo, hi = cfg["prompt"][1], cfg["prompt"][2]
+    return torch.randint(lo, hi + 1, (batch,), generator=g).tolist()
+
+
+def make_prompts(cfg: dict, batch: int, vocab: int) -> list[torch.Tensor]:
+    lens = prompt_lengths(cfg, batch)
+    g = torch.Generator().manual_seed(cfg["seed"] + 1000)
+    return [torch.randint(0, vocab, (n,), generator=g) for n in lens]
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons with NVML every 200 ms (read-only)."""
+
+    def __init__(self, index: int):
+        self.samples: list[tuple[float, float, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                reasons = int(nv.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+                util = float(nv.nvmlDeviceGetUtilizationRates(self._h).gpu)
+                self.samples.append((sm, util, reasons))
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t is not None:
+            self._t.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        nv = self._nv
+        names = {
+            "sw_power_cap": getattr(nv, "nvmlClocksEventReasonSwPowerCap", 0x4),
+            "hw_slowdown": getattr(nv, "nvmlClocksEventReasonHwSlowdown", 0x8),
+            "sw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+            "hw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+            "hw_power_brake_slowdown": getattr(nv, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
+        }
+        load = [s for s in self.samples if s[1] > 0] or self.samples
+        mhz = sorted(s[0] for s in load)
+        seen = 0
+        for s in load:
+            seen |= s[2]
+        return {"sm_mhz": mhz[len(mhz) // 2], "sm_max_mhz": self.max_mhz,
+                "reasons": [k for k, bit in names.items() if seen & bit], "samples": len(load)}
+
+
+def measured_peak() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def init_dist(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+        return rank, world, local, dist.group.WORLD
+    if torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return 0, 1, 0, None
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def count_launches(fn) -> int:
+    """Number of libdsv2 kernels one call of fn launches (C-ABI calls, mla_decode = 2)."""
+    from dsv2 import _lib
+    orig = _lib.call
+    n = [0]
+
+    def counting(name, *a):
+        n[0] += 2 if name == "dsv2_mla_decode" else 1
+        return orig(name, *a)
+    _lib.call = counting
+    try:
+        fn()
+    finally:
+        _lib.call = orig
+    return n[0]
+
+
+def step_bytes(eng, lens_now: list[int], distinct: list[int]) -> float:
+    """Algorithmic HBM bytes of one decode step on this rank (weights read once + latent KV)."""
+    n_moe = len(distinct)
+    n_dense = eng.L - n_moe
+    b = eng.L * ATTN_BYTES + n_dense * DENSE_BYTES + n_moe * (SHARED_BYTES + GATE_BYTES) + LMHEAD_BYTES
+    b += sum(distinct) * EXPERT_BYTES
+    b += sum(lens_now) * eng.L * KV_ROW_BYTES
+    return float(b)
+
+
+def distinct_experts(eng) -> list[int]:
+    go = eng.group_offsets_hist.cpu()
+    counts = go[:, 1:eng.n_groups - 1] - go[:, :eng.n_groups - 2]
+    return [int((c > 0).sum()) for c in counts]
+
+
+def run_ours(args, cfg_id: int):
+    from dsv2.engine import DecodeEngine
+    from oracle.hf_model import add_router_bias, build_model, dsv2_lite_config, router_bias_zipf
+
+    rank, world, local, group = init_dist(args)
+    dev = torch.device("cuda", local)
+    cfg = CONFIGS[cfg_id]
+    B_all = args.batch or cfg["batch"]
+    if B_all % world:
+        raise SystemExit(f"batch {B_all} not divisible by {world} ranks")
+    B = B_all // world
+    family = args.family or cfg["family"]
+    t0 = time.time()
+    mcfg = dsv2_lite_config(num_layers=args.layers)
+    model = build_model(mcfg, seed=WEIGHT_SEED, device=dev, dtype=torch.bfloat16)
+    bias = router_bias_zipf(mcfg.n_routed_experts, 1.1, seed=4).to(dev) if cfg["skew"] else None
+    if bias is not None:
+        add_router_bias(model, bias)
+    prompts_all = make_prompts(cfg, B_all, mcfg.vocab_size)
+    prompts = prompts_all[rank * B:(rank + 1) * B]
+    total_steps = args.warmup + args.steps + args.e2e_steps + 8
+    max_len = max(len(p) for p in prompts_all) + total_steps + 8
+    eng = DecodeEngine(model, B, max_len, family, rank=rank, world=world, group=group, gate_bias=bias)
+    t_build = time.time() - t0
+    t0 = time.time()
+    eng.prefill(prompts, max_tokens_per_chunk=args.prefill_chunk)
+    torch.cuda.synchronize()
+    t_prefill = time.time() - t0
+    launches_per_step = count_launches(lambda: (eng.step(), eng.restore()))
+    eng.capture()
+    barrier(world)
+    for _ in range(args.warmup):
+        eng.replay()
+    lens_before = [int(x) for x in eng.positions.cpu()]
+    barrier(world)
+    stream = torch.cuda.current_stream()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            eng.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = start.elapsed_time(end)
+    ms = max_over_ranks(ms, world)
+    ms_step = ms / args.steps
+    tokens = B_all * args.steps
+    value = tokens / (ms / 1000.0)
+    distinct = distinct_experts(eng)
+    lens_mid = [l + args.steps // 2 for l in lens_before]
+    bytes_rank = step_bytes(eng, lens_mid, distinct)
+    bytes_rank = max_over_ranks(bytes_rank, world)
+    peak, peak_kind = measured_peak()
+    step_gbs = bytes_rank / (ms_step / 1000.0) / 1e9
+
+    # dominant kernel: grouped MoE GEMMs (gate_up+SwiGLU and down) of all MoE layers,
+    # replayed alone from a graph with the last routing in place
+    moe_ms, moe_bytes, moe_launches = eng.time_moe_gemms(iters=max(3, min(args.steps, 20)))
+    moe_ms = max_over_ranks(moe_ms, world)
+    dk_gbs = moe_bytes / (moe_ms / 1000.0) / 1e9 if moe_ms > 0 else None
+
+    # end to end through the public API: token ids cross host<->device every step
+    pin_in = torch.zeros(B, dtype=torch.int64, pin_memory=True)
+    pin_out = torch.zeros(B, dtype=torch.int64, pin_memory=True)
+    pin_in.copy_(eng.input_ids.cpu())
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_e2e = time.perf_counter()
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        eng.input_ids.copy_(pin_in, non_blocking=True)
+        eng.replay()
+        pin_out.copy_(eng.next_ids, non_blocking=True)
+        stream.synchronize()
+        pin_in.copy_(pin_out)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t_e2e = time.perf_counter() - t_e2e
+    e2e_s = max_over_ranks(max(t_e2e, e0.elapsed_time(e1) / 1000.0), world)
+    e2e_val = B_all * args.e2e_steps / e2e_s
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(model, prompts_all, cfg, args)
+    eng.release()
+    barrier(world)
+    out = None
+    if rank == 0:
+        out = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "tok/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic: seeded random-init N(0,0.02) bf16 weights, seeded uniform random prompt ids",
+            "config": {
+                "workload": f"config {cfg_id}: DeepSeek-V2-Lite {args.layers} layers, batch {B_all}, "
+                            f"prompts {cfg['prompt']}, {family} kernel family, CUDA-graph q_len=1 decode",
+                "global_batch": B_all,
+                "seq_len": int(sum(lens_before) / len(lens_before)),
+                "parallelism": f"ep{world}+dp{world}" if world > 1 else "single",
+                "kernel_family": family,
+                "l2": "inputs larger than L2 (31 GB of weights streamed per step)",
+                "split_len": eng.split_len,
+            },
+            "roofline": {
+                "bound": "hbm",
+                "kernel": "linear_tc_kernel/gemv_mma_kernel grouped MoE gate_up+down (all MoE layers)",
+                "achieved": round(dk_gbs, 1) if dk_gbs else None,
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": round(dk_gbs / peak, 4) if dk_gbs else None,
+                "peak_kind": peak_kind,
+                "traffic": None,
+                "algorithmic_bytes_per_launch": round(moe_bytes / max(moe_launches, 1)),
+                "launch_ms": round(moe_ms / max(moe_launches, 1), 5),
+            },
+            "step_roofline": {
+                "algorithmic_bytes_per_step": bytes_rank,
+                "achieved": round(step_gbs, 1),
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": round(step_gbs / peak, 4),
+                "distinct_experts_mean": round(sum(distinct) / max(len(distinct), 1), 2),
+            },
+            "e2e": {"value": round(e2e_val, 2), "unit": "tok/s", "h2d_bytes_per_step": 8 * B_all,
+                    "d2h_bytes_per_step": 8 * B_all, "steps": args.e2e_steps},
+            "gpu_launches": launches_per_step * args.steps,
+            "launches_per_step": launches_per_step,
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+            "setup_s": {"build": round(t_build, 1), "prefill": round(t_prefill, 1)},
+        }
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return out
+
+
+def cpu_baseline(model, prompts_all, cfg, args, rows: int = 4, steps: int = 3) -> dict:
+    """HF eager decode (the reference's CPU path) on the host cores for a bounded sample:
+    a 2-layer slice (dense layer 0 + MoE layer 1) of the same weights, `rows` rows of the
+    workload's prompts, `steps` greedy decode steps; per-layer times are extrapolated to
+    the full depth and the tok/s figure is rows / (extrapolated step time)."""
+    from oracle.hf_model import build_model, dsv2_lite_config
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg2 = dsv2_lite_config(num_layers=2)
+    cpu_model = build_model(cfg2, seed=0, device="cpu", dtype=torch.bfloat16, std=0.0)
+    sd = {k: v for k, v in model.state_dict().items()
+          if not k.startswith("model.layers.") or k.split(".")[2] in ("0", "1")}
+    cpu_model.load_state_dict({k: v.cpu() for k, v in sd.items()}, strict=False)
+    from transformers import DynamicCache
+    rows = min(rows, len(prompts_all))
+    times = []
+    with torch.no_grad():
+        for r in range(rows):
+            p = prompts_all[r].view(1, -1)
+            cache = DynamicCache(config=cfg2)
+            out = cpu_model(input_ids=p, past_key_values=cache, use_cache=True)
+            tok = out.logits[:, -1:].argmax(-1)
+            for _ in range(steps):
+                t = time.perf_counter()
+                out = cpu_model(input_ids=tok, past_key_values=cache, use_cache=True)
+                times.append(time.perf_counter() - t)
+                tok = out.logits[:, -1:].argmax(-1)
+    per_row_step_2l = sorted(times)[len(times) // 2]
+    # 2-layer step = embed + dense layer + MoE layer + lm_head; the other 25 layers are MoE
+    # layers at least as costly as layer 1: estimate the MoE layer as half the sampled step.
+    moe_layer = per_row_step_2l / 2
+    step_full = per_row_step_2l + (args.layers - 2) * moe_layer
+    return {"value": round(1.0 / step_full, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"HF eager bf16 (transformers 5.5) 2-layer slice, {rows} rows x {steps} decode steps "
+                      f"at the workload's prompt lengths, batch 1 per call, extrapolated to "
+                      f"{args.layers} layers ({per_row_step_2l * 1000:.1f} ms per 2-layer row-step)"}
+
+
+def run_reference(args, cfg_id: int):
+    """Reference arm: the reference's CPU path (HF eager torch) on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    from oracle.hf_model import build_model, dsv2_lite_config
+    cfg = CONFIGS[cfg_id]
+    B_all = args.batch or cfg["batch"]
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    mcfg = dsv2_lite_config(num_layers=2)
+    model = build_model(mcfg, seed=WEIGHT_SEED, device="cpu", dtype=torch.bfloat16)
+    prompts = make_prompts(cfg, B_all, mcfg.vocab_size)
+    rows = min(4, B_all)
+    from transformers import DynamicCache
+    per_step = []
+    with torch.no_grad():
+        for _ in range(max(args.warmup, 0) and 1):
+            pass
+        for r in range(rows):
+            cache = DynamicCache(config=mcfg)
+            out = model(input_ids=prompts[r].view(1, -1), past_key_values=cache, use_cache=True)
+            tok = out.logits[:, -1:].argmax(-1)
+            for s in range(args.steps):
+                t = time.perf_counter()
+                out = model(input_ids=tok, past_key_values=cache, use_cache=True)
+                per_step.append(time.perf_counter() - t)
+                tok = out.logits[:, -1:].argmax(-1)
+    t2 = sorted(per_step)[len(per_step) // 2]
+    step_full = t2 + (args.layers - 2) * (t2 / 2)
+    value = 1.0 / step_full
+    sample = (f"HF eager bf16 (transformers 5.5) 2-layer slice, {rows} rows x {args.steps} decode steps, "
+              f"batch 1 per call, extrapolated to {args.layers} layers")
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "tok/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(step_full * 1000, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"config {cfg_id}: DeepSeek-V2-Lite, batch {B_all}, prompts {cfg['prompt']}",
+                   "global_batch": B_all, "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=4, choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=None, help="override the config's global batch")
+    ap.add_argument("--family", default=None, choices=["small", "batch"])
+    ap.add_argument("--layers", type=int, default=27)
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--prefill-chunk", type=int, default=16384)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        out = run_reference(args, args.config)
+    else:
+        out = run_ours(args, args.config)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,495 @@
+// extern "C" entry points of libdsv2.so (declared in include/dsv2.h).
+//
+// Argument validation, per-device one-time setup, TMA tensor-map construction (cached
+// by shape and address), and dispatch to the kernel launchers.  No entry point
+// allocates device memory or synchronises the stream.
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+
+#include "../../include/dsv2.h"
+#include "params.cuh"
+
+
+using namespace dsv2;
+
+namespace {
+
+thread_local std::string g_last_error;
+std::mutex g_mu;
+bool g_dev_init[128];
+int g_dev_sms[128];
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int check_launch(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) return fail(DSV2_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
+  return DSV2_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int ensure_init(int* sms_out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(DSV2_ERR_LAUNCH, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 128) return fail(DSV2_ERR_INVALID, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_dev_init[dev]) {
+    int major = 0, minor = 0, sms = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (major != 10)
+      return fail(DSV2_ERR_UNSUPPORTED, "libdsv2 is built for sm_100a; device %d is sm_%d%d", dev,
+                  major, minor);
+    if ((e = mla_decode_init()) != cudaSuccess)
+      return fail(DSV2_ERR_LAUNCH, "mla_decode_init: %s", cudaGetErrorString(e));
+    if ((e = linear_tc_init()) != cudaSuccess)
+      return fail(DSV2_ERR_LAUNCH, "linear_tc_init: %s", cudaGetErrorString(e));
+    g_dev_sms[dev] = sms;
+    g_dev_init[dev] = true;
+  }
+  if (sms_out) *sms_out = g_dev_sms[dev];
+  return DSV2_OK;
+}
+
+// ---- TMA tensor maps ---------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int get_encode() {
+  if (g_encode) return DSV2_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+    return fail(DSV2_ERR_LAUNCH, "cuTensorMapEncodeTiled unavailable");
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return DSV2_OK;
+}
+
+typedef std::tuple<int, uintptr_t, uint64_t, uint64_t, uint64_t, uint64_t, uint64_t, uint32_t,
+                   uint32_t>
+    MapKey;
+std::map<MapKey, CUtensorMap> g_maps;
+
+// 3-D bf16 tensor map {inner, rows, groups} with a {64, box_rows, 1} box, 128-byte swizzle.
+int tensor_map_3d(const void* base, uint64_t inner, uint64_t rows, uint64_t groups,
+                  uint64_t row_stride_b, uint64_t group_stride_b, uint32_t box_rows,
+                  CUtensorMap* out) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const MapKey key(dev, reinterpret_cast<uintptr_t>(base), inner, rows, groups, row_stride_b,
+                   group_stride_b, box_rows, 0);
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+      *out = it->second;
+      return DSV2_OK;
+    }
+  }
+  int rc = get_encode();
+  if (rc) return rc;
+  if (!aligned16(base) || (row_stride_b & 15) || (group_stride_b & 15))
+    return fail(DSV2_ERR_INVALID, "TMA operand not 16-byte aligned (base %p, strides %llu/%llu)",
+                base, (unsigned long long)row_stride_b, (unsigned long long)group_stride_b);
+  cuuint64_t dims[3] = {inner, rows, groups};
+  cuuint64_t strides[2] = {row_stride_b, group_stride_b};
+  cuuint32_t box[3] = {64, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUtensorMap m;
+  CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(DSV2_ERR_INVALID,
+                "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu x %llu strides %llu %llu",
+                static_cast<int>(r), (unsigned long long)inner, (unsigned long long)rows,
+                (unsigned long long)groups, (unsigned long long)row_stride_b,
+                (unsigned long long)group_stride_b);
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_maps.size() > 4096) g_maps.clear();
+  g_maps[key] = m;
+  *out = m;
+  return DSV2_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int dsv2_version(void) { return 100; }
+
+const char* dsv2_last_error(void) { return g_last_error.c_str(); }
+
+int dsv2_init(void) { return ensure_init(nullptr); }
+
+int dsv2_get_device_error(int* code, int clear) {
+  if (!code) return fail(DSV2_ERR_INVALID, "code is NULL");
+  cudaError_t e = cudaMemcpyFromSymbol(code, g_device_error, sizeof(int));
+  if (e != cudaSuccess) return check_launch(e, "read device error");
+  if (clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+    if (e != cudaSuccess) return check_launch(e, "clear device error");
+  }
+  return DSV2_OK;
+}
+
+int dsv2_rmsnorm(const void* x, int64_t x_row_stride, const void* w, int w_dtype, void* y,
+                 int64_t y_row_stride, int rows, int cols, float eps, void* stream) {
+  if (!x || !w || !y) return fail(DSV2_ERR_INVALID, "rmsnorm: null pointer");
+  if (cols <= 0 || cols % 8 || cols > 4096)
+    return fail(DSV2_ERR_UNSUPPORTED, "rmsnorm: cols=%d (need multiple of 8, <= 4096)", cols);
+  if (w_dtype != DSV2_BF16 && w_dtype != DSV2_F32)
+    return fail(DSV2_ERR_UNSUPPORTED, "rmsnorm: weight dtype %d", w_dtype);
+  if (!aligned16(x) || !aligned16(y) || (x_row_stride % 8) || (y_row_stride % 8))
+    return fail(DSV2_ERR_INVALID, "rmsnorm: rows must be 16-byte aligned");
+  if (rows <= 0) return DSV2_OK;
+  return check_launch(launch_rmsnorm(x, x_row_stride, w, w_dtype, y, y_row_stride, rows, cols, eps,
+                                     static_cast<cudaStream_t>(stream)),
+                      "rmsnorm");
+}
+
+int dsv2_add_rmsnorm(void* h, void* h_out, const void* delta, int delta_dtype, int n_delta,
+                     int64_t delta_part_stride, int64_t delta_row_stride, const void* w,
+                     int w_dtype, void* y, int rows, int cols, float eps, void* stream) {
+  if (!h || (n_delta > 0 && !delta) || (y && !w))
+    return fail(DSV2_ERR_INVALID, "add_rmsnorm: null pointer");
+  if (cols <= 0 || cols % 8 || cols > 4096)
+    return fail(DSV2_ERR_UNSUPPORTED, "add_rmsnorm: cols=%d", cols);
+  if (delta_dtype != DSV2_BF16 && delta_dtype != DSV2_F32)
+    return fail(DSV2_ERR_UNSUPPORTED, "add_rmsnorm: delta dtype %d", delta_dtype);
+  if (!aligned16(h) || (h_out && !aligned16(h_out)) || (y && !aligned16(y)) ||
+      (n_delta > 0 && (!aligned16(delta) || delta_part_stride % 8 || delta_row_stride % 8)))
+    return fail(DSV2_ERR_INVALID, "add_rmsnorm: operands must be 16-byte aligned");
+  if (rows <= 0) return DSV2_OK;
+  return check_launch(launch_add_rmsnorm(h, h_out, delta, delta_dtype, n_delta, delta_part_stride,
+                                         delta_row_stride, w, w_dtype, y, rows, cols, eps,
+                                         static_cast<cudaStream_t>(stream)),
+                      "add_rmsnorm");
+}
+
+int dsv2_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, const void* w,
+                       int w_dtype, void* h, void* y, int rows, int cols, float eps,
+                       void* stream) {
+  if (!ids || !table || !w || !h || !y) return fail(DSV2_ERR_INVALID, "embed_rmsnorm: null pointer");
+  if (cols <= 0 || cols % 8 || cols > 4096)
+    return fail(DSV2_ERR_UNSUPPORTED, "embed_rmsnorm: cols=%d", cols);
+  if (!aligned16(table) || !aligned16(h) || !aligned16(y))
+    return fail(DSV2_ERR_INVALID, "embed_rmsnorm: operands must be 16-byte aligned");
+  if (rows <= 0) return DSV2_OK;
+  return check_launch(
+      launch_embed_rmsnorm(reinterpret_cast<const long long*>(ids), table, vocab, w, w_dtype, h, y,
+                           rows, cols, eps, static_cast<cudaStream_t>(stream)),
+      "embed_rmsnorm");
+}
+
+int dsv2_residual_add(const void* a, const void* b, void* out, int64_t n, void* stream) {
+  if (!a || !b || !out) return fail(DSV2_ERR_INVALID, "residual_add: null pointer");
+  if (n % 8) return fail(DSV2_ERR_UNSUPPORTED, "residual_add: n=%lld not a multiple of 8", (long long)n);
+  if (!aligned16(a) || !aligned16(b) || !aligned16(out))
+    return fail(DSV2_ERR_INVALID, "residual_add: operands must be 16-byte aligned");
+  if (n <= 0) return DSV2_OK;
+  return check_launch(launch_residual_add(a, b, out, n, static_cast<cudaStream_t>(stream)),
+                      "residual_add");
+}
+
+int dsv2_silu_mul(const void* gate, const void* up, void* out, int64_t n, void* stream) {
+  if (!gate || !up || !out) return fail(DSV2_ERR_INVALID, "silu_mul: null pointer");
+  if (n % 8) return fail(DSV2_ERR_UNSUPPORTED, "silu_mul: n=%lld not a multiple of 8", (long long)n);
+  if (!aligned16(gate) || !aligned16(up) || !aligned16(out))
+    return fail(DSV2_ERR_INVALID, "silu_mul: operands must be 16-byte aligned");
+  if (n <= 0) return DSV2_OK;
+  return check_launch(launch_silu_mul(gate, up, out, n, static_cast<cudaStream_t>(stream)),
+                      "silu_mul");
+}
+
+int dsv2_prepare_decode_inputs(const int64_t* cache_position, int pos_numel,
+                               int64_t* attention_mask, int64_t mask_stride_b,
+                               int64_t* position_ids, int64_t position_ids_stride_b,
+                               const int64_t* attention_mask_index, int batch, int max_len,
+                               void* stream) {
+  if (!cache_position || (attention_mask && !attention_mask_index))
+    return fail(DSV2_ERR_INVALID, "prepare_decode_inputs: null pointer");
+  if (pos_numel != 1 && pos_numel != batch)
+    return fail(DSV2_ERR_INVALID, "prepare_decode_inputs: cache_position has %d elements for batch %d",
+                pos_numel, batch);
+  if (batch <= 0 || max_len <= 0) return DSV2_OK;
+  return check_launch(
+      launch_prepare_decode_inputs(reinterpret_cast<const long long*>(cache_position), pos_numel,
+                                   reinterpret_cast<long long*>(attention_mask), mask_stride_b,
+                                   reinterpret_cast<long long*>(position_ids), position_ids_stride_b,
+                                   reinterpret_cast<const long long*>(attention_mask_index), batch,
+                                   max_len, static_cast<cudaStream_t>(stream)),
+      "prepare_decode_inputs");
+}
+
+int dsv2_copy_token_to_cache(const void* src, const int64_t* src_strides, void* dst,
+                             const int64_t* dst_strides, const int64_t* cache_position,
+                             int pos_numel, int batch, int heads, int dim, int elem_size,
+                             int max_len, void* stream) {
+  if (!src || !dst || !src_strides || !dst_strides || !cache_position)
+    return fail(DSV2_ERR_INVALID, "copy_token_to_cache: null pointer");
+  if (elem_size != 2 && elem_size != 4)
+    return fail(DSV2_ERR_UNSUPPORTED, "copy_token_to_cache: element size %d", elem_size);
+  if (pos_numel != 1 && pos_numel != batch)
+    return fail(DSV2_ERR_INVALID, "copy_token_to_cache: cache_position numel %d", pos_numel);
+  if (batch <= 0 || heads <= 0 || dim <= 0) return DSV2_OK;
+  long long ss[3] = {src_strides[0], src_strides[1], src_strides[2]};
+  long long ds[4] = {dst_strides[0], dst_strides[1], dst_strides[2], dst_strides[3]};
+  return check_launch(launch_copy_token_to_cache(src, ss, dst, ds,
+                                                 reinterpret_cast<const long long*>(cache_position),
+                                                 pos_numel, batch, heads, dim, elem_size, max_len,
+                                                 static_cast<cudaStream_t>(stream)),
+                      "copy_token_to_cache");
+}
+
+int dsv2_advance_positions(int64_t* pos, int n, void* stream) {
+  if (!pos) return fail(DSV2_ERR_INVALID, "advance_positions: null pointer");
+  if (n <= 0) return DSV2_OK;
+  return check_launch(launch_advance_positions(reinterpret_cast<long long*>(pos), n,
+                                               static_cast<cudaStream_t>(stream)),
+                      "advance_positions");
+}
+
+int dsv2_linear(const dsv2_linear_args* a, int family, void* stream) {
+  if (!a || !a->w || !a->x || !a->y) return fail(DSV2_ERR_INVALID, "linear: null pointer");
+  if (a->n_rows <= 0 || a->k <= 0 || a->n_groups <= 0)
+    return fail(DSV2_ERR_INVALID, "linear: n_rows=%d k=%d n_groups=%d", a->n_rows, a->k, a->n_groups);
+  if (a->epilogue < DSV2_EPI_STORE_BF16 || a->epilogue > DSV2_EPI_SCALE_F32)
+    return fail(DSV2_ERR_INVALID, "linear: epilogue %d", a->epilogue);
+  if (a->epilogue == DSV2_EPI_SCALE_F32 && !a->route_scale)
+    return fail(DSV2_ERR_INVALID, "linear: SCALE epilogue needs route_scale");
+  if (a->epilogue == DSV2_EPI_SCALE_F32 && !a->group_offsets)
+    return fail(DSV2_ERR_INVALID, "linear: SCALE epilogue needs grouped mode");
+  if (!aligned16(a->w) || !aligned16(a->x) || a->w_row_stride % 8 || a->x_row_stride % 8 ||
+      a->w_group_stride % 8 || a->x_group_stride % 8 || a->up_offset % 8)
+    return fail(DSV2_ERR_INVALID, "linear: W/X rows must be 16-byte aligned");
+  const int n_tok = a->group_offsets ? a->max_routes_per_group : a->n_tokens;
+  if (n_tok <= 0) return DSV2_OK;
+  LinearParams p;
+  p.w = reinterpret_cast<const bf16*>(a->w);
+  p.w_row_stride = a->w_row_stride;
+  p.w_group_stride = a->w_group_stride;
+  p.up_offset = a->up_offset;
+  p.n_rows = a->n_rows;
+  p.k = a->k;
+  p.x = reinterpret_cast<const bf16*>(a->x);
+  p.x_row_stride = a->x_row_stride;
+  p.x_group_stride = a->x_group_stride;
+  p.y = a->y;
+  p.y_row_stride = a->y_row_stride;
+  p.y_group_stride = a->y_group_stride;
+  p.epilogue = a->epilogue;
+  p.n_groups = a->n_groups;
+  p.n_tokens = a->n_tokens;
+  p.group_offsets = a->group_offsets;
+  p.route_x_row = a->route_x_row;
+  p.route_y_row = a->route_y_row;
+  p.route_scale = a->route_scale;
+  p.max_routes_per_group = a->max_routes_per_group;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (family == DSV2_FAMILY_SMALL) {
+    if (a->k % 32) return fail(DSV2_ERR_UNSUPPORTED, "linear(small): k=%d not a multiple of 32", a->k);
+    return check_launch(launch_linear_gemv(p, st), "linear(small)");
+  }
+  if (family != DSV2_FAMILY_BATCH) return fail(DSV2_ERR_INVALID, "linear: family %d", family);
+  if (a->k % 64) return fail(DSV2_ERR_UNSUPPORTED, "linear(batch): k=%d not a multiple of 64", a->k);
+  if (a->route_x_row)
+    return fail(DSV2_ERR_UNSUPPORTED, "linear(batch): gathered X rows are not supported (gather first)");
+  if (a->w_group_rows <= 0 || a->x_group_rows <= 0)
+    return fail(DSV2_ERR_INVALID, "linear(batch): w_group_rows / x_group_rows required");
+  if (a->n_groups > 1 && a->w_group_stride == 0)
+    return fail(DSV2_ERR_INVALID, "linear(batch): groups need a weight group stride");
+  int up_rows = 0;
+  if (a->epilogue == DSV2_EPI_SWIGLU) {
+    if (a->up_offset % a->w_row_stride)
+      return fail(DSV2_ERR_INVALID, "linear(batch): up_offset must be whole rows");
+    up_rows = static_cast<int>(a->up_offset / a->w_row_stride);
+  }
+  int sms = 0;
+  int rc = ensure_init(&sms);
+  if (rc) return rc;
+  CUtensorMap mw, mx;
+  const uint64_t wrs = static_cast<uint64_t>(a->w_row_stride) * 2;
+  const uint64_t wgs = a->n_groups > 1 ? static_cast<uint64_t>(a->w_group_stride) * 2
+                                       : wrs * static_cast<uint64_t>(a->w_group_rows);
+  rc = tensor_map_3d(a->w, a->k, a->w_group_rows, a->n_groups, wrs, wgs, 128, &mw);
+  if (rc) return rc;
+  const bool xg = a->x_group_stride != 0 && a->n_groups > 1;
+  const uint64_t xrs = static_cast<uint64_t>(a->x_row_stride) * 2;
+  const uint64_t xgs = xg ? static_cast<uint64_t>(a->x_group_stride) * 2
+                          : xrs * static_cast<uint64_t>(a->x_group_rows);
+  rc = tensor_map_3d(a->x, a->k, a->x_group_rows, xg ? a->n_groups : 1, xrs, xgs, 16, &mx);
+  if (rc) return rc;
+  return check_launch(launch_linear_tc_impl(p, mw, mx, up_rows, xg ? 1 : 0, sms, st),
+                      "linear(batch)");
+}
+
+int dsv2_router(const dsv2_router_args* a, void* stream) {
+  if (!a || !a->x || !a->w || !a->logits || !a->topk_ids32 || !a->topk_weights)
+    return fail(DSV2_ERR_INVALID, "router: null pointer");
+  if (a->n_experts <= 0 || a->n_experts > 64)
+    return fail(DSV2_ERR_UNSUPPORTED, "router: n_experts=%d (max 64)", a->n_experts);
+  if (a->hidden % 8 || !aligned16(a->x) || a->x_row_stride % 8)
+    return fail(DSV2_ERR_INVALID, "router: activations must be 16-byte aligned rows");
+  if (a->w_dtype != DSV2_BF16 && a->w_dtype != DSV2_F32)
+    return fail(DSV2_ERR_UNSUPPORTED, "router: gate dtype %d", a->w_dtype);
+  if (a->rows <= 0) return DSV2_OK;
+  const int experts_per_cta = a->rows <= 16 ? 8 : a->n_experts;
+  const bool need_ticket = experts_per_cta < a->n_experts || a->group_offsets;
+  if (need_ticket && !a->ticket) return fail(DSV2_ERR_INVALID, "router: ticket buffer required");
+  if (a->group_offsets) {
+    if (!a->route_token || !a->route_slot || !a->route_weight)
+      return fail(DSV2_ERR_INVALID, "router: bucketing outputs missing");
+    if (a->expert_lo < 0 || a->n_local < 0 || a->expert_lo + a->n_local > a->n_experts ||
+        a->shared_lo < 0 || a->shared_hi < a->shared_lo || a->shared_hi > a->rows)
+      return fail(DSV2_ERR_INVALID, "router: bad expert/shared ranges");
+  }
+  RouterParams p;
+  p.x = reinterpret_cast<const bf16*>(a->x);
+  p.x_row_stride = a->x_row_stride;
+  p.w = a->w;
+  p.w_dtype = a->w_dtype;
+  p.bias = a->bias;
+  p.rows = a->rows;
+  p.hidden = a->hidden;
+  p.n_experts = a->n_experts;
+  p.scaling = a->scaling;
+  p.logits = a->logits;
+  p.topk_ids = reinterpret_cast<long long*>(a->topk_ids64);
+  p.topk_ids32 = a->topk_ids32;
+  p.topk_w = a->topk_weights;
+  p.ticket = a->ticket;
+  p.experts_per_cta = experts_per_cta;
+  p.expert_lo = a->expert_lo;
+  p.n_local = a->n_local;
+  p.shared_lo = a->shared_lo;
+  p.shared_hi = a->shared_hi;
+  p.group_offsets = a->group_offsets;
+  p.route_token = a->route_token;
+  p.route_slot = a->route_slot;
+  p.route_weight = a->route_weight;
+  return check_launch(launch_router(p, static_cast<cudaStream_t>(stream)), "router");
+}
+
+int dsv2_softmax_topk(const float* logits, int rows, int n_experts, float scaling,
+                      int64_t* topk_ids64, int32_t* topk_ids32, float* topk_weights,
+                      void* stream) {
+  if (!logits || !topk_ids32 || !topk_weights) return fail(DSV2_ERR_INVALID, "softmax_topk: null pointer");
+  if (n_experts < 6 || n_experts > 64)
+    return fail(DSV2_ERR_UNSUPPORTED, "softmax_topk: n_experts=%d", n_experts);
+  if (rows <= 0) return DSV2_OK;
+  return check_launch(launch_softmax_topk(logits, rows, n_experts, scaling,
+                                          reinterpret_cast<long long*>(topk_ids64), topk_ids32,
+                                          topk_weights, static_cast<cudaStream_t>(stream)),
+                      "softmax_topk");
+}
+
+int dsv2_moe_bucket(const int32_t* topk_ids32, const float* topk_weights, int rows,
+                    int expert_lo, int n_local, int shared_lo, int shared_hi,
+                    int32_t* group_offsets, int32_t* route_token, int32_t* route_slot,
+                    float* route_weight, void* stream) {
+  if (!topk_ids32 || !topk_weights || !group_offsets || !route_token || !route_slot || !route_weight)
+    return fail(DSV2_ERR_INVALID, "moe_bucket: null pointer");
+  if (n_local < 0 || n_local > 64 || shared_lo < 0 || shared_hi < shared_lo || shared_hi > rows)
+    return fail(DSV2_ERR_INVALID, "moe_bucket: bad ranges");
+  return check_launch(launch_bucket(topk_ids32, topk_weights, rows, expert_lo, n_local, shared_lo,
+                                    shared_hi, group_offsets, route_token, route_slot,
+                                    route_weight, static_cast<cudaStream_t>(stream)),
+                      "moe_bucket");
+}
+
+int dsv2_gather_rows(const void* x, int64_t x_row_stride, const int32_t* route_token,
+                     const int32_t* group_offsets, int n_groups, void* out, int cols,
+                     int max_routes, void* stream) {
+  if (!x || !route_token || !group_offsets || !out) return fail(DSV2_ERR_INVALID, "gather_rows: null pointer");
+  if (cols % 8 || !aligned16(x) || !aligned16(out) || x_row_stride % 8)
+    return fail(DSV2_ERR_INVALID, "gather_rows: rows must be 16-byte aligned");
+  return check_launch(launch_gather_rows(x, x_row_stride, route_token, group_offsets, n_groups,
+                                         out, cols, max_routes, static_cast<cudaStream_t>(stream)),
+                      "gather_rows");
+}
+
+int dsv2_mla_prep(const dsv2_mla_prep_args* a, void* stream) {
+  if (!a || !a->qkva || !a->kv_norm_w || !a->cos_tab || !a->sin_tab || !a->positions || !a->cache ||
+      !a->q_pe_out)
+    return fail(DSV2_ERR_INVALID, "mla_prep: null pointer");
+  if (a->pos_numel != 1 && a->pos_numel != a->batch)
+    return fail(DSV2_ERR_INVALID, "mla_prep: positions numel %d for batch %d", a->pos_numel, a->batch);
+  if (!aligned16(a->qkva) || a->qkva_row_stride % 8 || !aligned16(a->cache) || a->cache_b_stride % 8)
+    return fail(DSV2_ERR_INVALID, "mla_prep: operands must be 16-byte aligned");
+  if (a->rope_stride < 32) return fail(DSV2_ERR_INVALID, "mla_prep: rope table stride %lld < 32", (long long)a->rope_stride);
+  if (a->batch <= 0) return DSV2_OK;
+  MlaPrepParams p;
+  p.qkva = reinterpret_cast<const bf16*>(a->qkva);
+  p.qkva_row_stride = a->qkva_row_stride;
+  p.kv_norm_w = reinterpret_cast<const bf16*>(a->kv_norm_w);
+  p.eps = a->eps;
+  p.cos_tab = a->cos_tab;
+  p.sin_tab = a->sin_tab;
+  p.rope_stride = a->rope_stride;
+  p.rope_rows = a->rope_rows;
+  p.positions = reinterpret_cast<const long long*>(a->positions);
+  p.pos_numel = a->pos_numel;
+  p.cache = reinterpret_cast<bf16*>(a->cache);
+  p.cache_b_stride = a->cache_b_stride;
+  p.max_len = a->max_len;
+  p.q_pe_out = reinterpret_cast<bf16*>(a->q_pe_out);
+  return check_launch(launch_mla_prep(p, a->batch, static_cast<cudaStream_t>(stream)), "mla_prep");
+}
+
+int dsv2_mla_decode(const dsv2_mla_decode_args* a, void* stream) {
+  if (!a || !a->q_abs || !a->q_pe || !a->cache || !a->positions || !a->o_part || !a->ml_part || !a->o_lat)
+    return fail(DSV2_ERR_INVALID, "mla_decode: null pointer");
+  if (a->split_len <= 0 || a->split_len % 64)
+    return fail(DSV2_ERR_INVALID, "mla_decode: split_len %d must be a positive multiple of 64", a->split_len);
+  if (static_cast<long long>(a->n_splits) * a->split_len < a->max_len)
+    return fail(DSV2_ERR_INVALID, "mla_decode: n_splits * split_len < max_len");
+  if (a->pos_numel != 1 && a->pos_numel != a->batch)
+    return fail(DSV2_ERR_INVALID, "mla_decode: positions numel %d for batch %d", a->pos_numel, a->batch);
+  if (!aligned16(a->q_abs) || !aligned16(a->q_pe) || !aligned16(a->cache) || a->cache_b_stride % 8 ||
+      !aligned16(a->o_part))
+    return fail(DSV2_ERR_INVALID, "mla_decode: operands must be 16-byte aligned");
+  if (a->batch <= 0) return DSV2_OK;
+  int rc = ensure_init(nullptr);
+  if (rc) return rc;
+  MlaDecodeParams p;
+  p.q_abs = reinterpret_cast<const bf16*>(a->q_abs);
+  p.q_pe = reinterpret_cast<const bf16*>(a->q_pe);
+  p.cache = reinterpret_cast<const bf16*>(a->cache);
+  p.cache_b_stride = a->cache_b_stride;
+  p.max_len = a->max_len;
+  p.positions = reinterpret_cast<const long long*>(a->positions);
+  p.pos_numel = a->pos_numel;
+  p.scale_log2 = a->softmax_scale * 1.4426950408889634f;
+  p.split_len = a->split_len;
+  p.n_splits = a->n_splits;
+  p.o_part = a->o_part;
+  p.ml_part = a->ml_part;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = check_launch(launch_mla_decode(p, a->batch, st), "mla_decode");
+  if (rc) return rc;
+  return check_launch(launch_mla_combine(a->o_part, a->ml_part, a->n_splits, a->o_lat, a->batch, st),
+                      "mla_combine");
+}
+
+}  // extern "C"

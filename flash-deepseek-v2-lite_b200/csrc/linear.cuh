@@ -1,0 +1,66 @@
+// Parameters shared by the two linear kernels (CUDA-core/mma.sync "small" family and
+// the tcgen05 "batch" family).  Mirrors dsv2_linear_args of the public header.
+#pragma once
+#include "common.cuh"
+
+namespace dsv2 {
+
+enum Epilogue : int {
+  kEpiStoreBf16 = 0,   // y = bf16(acc)
+  kEpiStoreF32 = 1,    // y = acc
+  kEpiSwiglu = 2,      // y = bf16(silu(bf16(acc_gate)) * bf16(acc_up)) computed in fp32
+  kEpiScaleF32 = 3,    // y = bf16(acc) * route_scale[route]   (fp32 store)
+};
+
+struct LinearParams {
+  const bf16* w;
+  long long w_row_stride;
+  long long w_group_stride;
+  long long up_offset;
+  int n_rows;
+  int k;
+  const bf16* x;
+  long long x_row_stride;
+  long long x_group_stride;
+  void* y;
+  long long y_row_stride;
+  long long y_group_stride;
+  int epilogue;
+  int n_groups;
+  int n_tokens;
+  const int* group_offsets;
+  const int* route_x_row;
+  const int* route_y_row;
+  const float* route_scale;
+  int max_routes_per_group;
+};
+
+__device__ __forceinline__ float silu_ref(float g) { return g / (1.f + expf(-g)); }
+
+// Epilogue for one output element (row n, route r, accumulators acc/acc_up).
+__device__ __forceinline__ void linear_store(const LinearParams& p, int g, int r, int n, float acc,
+                                             float acc_up) {
+  const int yrow = p.route_y_row ? p.route_y_row[r] : r;
+  const long long off = g * p.y_group_stride + static_cast<long long>(yrow) * p.y_row_stride + n;
+  switch (p.epilogue) {
+    case kEpiStoreBf16:
+      reinterpret_cast<bf16*>(p.y)[off] = __float2bfloat16_rn(acc);
+      break;
+    case kEpiStoreF32:
+      reinterpret_cast<float*>(p.y)[off] = acc;
+      break;
+    case kEpiSwiglu: {
+      const float gt = bf16_round(acc), up = bf16_round(acc_up);
+      reinterpret_cast<bf16*>(p.y)[off] = __float2bfloat16_rn(silu_ref(gt) * up);
+      break;
+    }
+    default: {
+      reinterpret_cast<float*>(p.y)[off] = bf16_round(acc) * p.route_scale[r];
+      break;
+    }
+  }
+}
+
+cudaError_t launch_linear_gemv(const LinearParams& p, cudaStream_t st);
+
+}  // namespace dsv2

@@ -1,0 +1,137 @@
+// "Small" kernel family: weight-streaming GEMV for up to 8 tokens per pass.
+//
+// Replaces the reference's GEMV-style Triton kernels:
+//   attention_decode_small.py:54-137   _gemv_contig_kernel / _gemv_2048x2048_o_kernel (B = 1)
+//   attention_decode_small.py:857-901  _small_batch_gemv_kernel (B >= 2, one row per program)
+//   moe_small_gemv.py:52-158, 194-307  per-route gate/up + SwiGLU and down GEMVs
+// Design: each CTA owns 16 weight rows (plus the 16 matching "up" rows for SwiGLU)
+// and one chunk of <= 8 tokens.  Its 8 warps split K; every lane streams 16-byte
+// weight chunks straight from HBM (no L1 allocation) and feeds them to
+// mma.sync.m16n8k16 with the tokens as the 8-wide N dimension.  The k order inside
+// each 32-wide block is permuted identically for weights and activations, so a
+// 16-byte load maps directly onto the A/B fragments without shuffles.  Partial
+// sums of the 8 warps are reduced through shared memory and the epilogue (bf16 /
+// fp32 store, SwiGLU, route-weight scaling) is fused.
+//
+// Routed (MoE) mode: group g owns routes [group_offsets[g], group_offsets[g+1]),
+// read on the device, so the launch grid is fixed by host-side upper bounds and the
+// kernel is CUDA-graph safe.  Unlike the reference's route-GEMV, tokens routed to
+// the same expert share one pass over the expert's weights (up to 8 at a time).
+#include "linear.cuh"
+
+namespace dsv2 {
+
+constexpr int kGemvWarps = 8;
+constexpr int kGemvRows = 16;
+constexpr int kGemvTok = 8;
+
+template <bool SWIGLU, int U>
+__global__ __launch_bounds__(kGemvWarps * 32) void gemv_mma_kernel(const LinearParams p,
+                                                                    int rb_count, int tc_count) {
+  __shared__ float red[kGemvWarps][32][SWIGLU ? 8 : 4];
+  int item = blockIdx.x;
+  const int tc = item % tc_count;
+  item /= tc_count;
+  const int rb = item % rb_count;
+  const int g = item / rb_count;
+
+  int r0, cnt;
+  if (p.group_offsets) {
+    r0 = p.group_offsets[g];
+    cnt = p.group_offsets[g + 1] - r0;
+  } else {
+    r0 = 0;
+    cnt = p.n_tokens;
+  }
+  const int tbeg = tc * kGemvTok;
+  if (tbeg >= cnt) return;
+  const int tn = min(kGemvTok, cnt - tbeg);
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int n0 = rb * kGemvRows;
+  const int rowA = n0 + gq, rowB = n0 + gq + 8;
+  const bool okA = rowA < p.n_rows, okB = rowB < p.n_rows;
+  const bf16* wg = p.w + g * p.w_group_stride;
+  const bf16* wA = wg + static_cast<long long>(okA ? rowA : 0) * p.w_row_stride + tq * 8;
+  const bf16* wB = wg + static_cast<long long>(okB ? rowB : 0) * p.w_row_stride + tq * 8;
+
+  // activation row for token gq of this chunk (B operand column gq)
+  const bool okT = gq < tn;
+  const int rtok = r0 + tbeg + (okT ? gq : 0);
+  const int xrow = p.route_x_row ? p.route_x_row[rtok] : rtok;
+  const bf16* xp = p.x + g * p.x_group_stride + static_cast<long long>(xrow) * p.x_row_stride + tq * 8;
+
+  float c[4] = {0.f, 0.f, 0.f, 0.f};
+  float cu[4] = {0.f, 0.f, 0.f, 0.f};
+  const int nkb = p.k / 32;
+  for (int kb0 = warp; kb0 < nkb; kb0 += kGemvWarps * U) {
+    uint4 wa[U], wb[U], ua[U], ub[U], xv[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int kb = kb0 + u * kGemvWarps;
+      const uint4 z = make_uint4(0, 0, 0, 0);
+      wa[u] = z; wb[u] = z; ua[u] = z; ub[u] = z; xv[u] = z;
+      if (kb < nkb) {
+        if (okA) wa[u] = ld_stream_v4(wA + kb * 32);
+        if (okB) wb[u] = ld_stream_v4(wB + kb * 32);
+        if (SWIGLU) {
+          if (okA) ua[u] = ld_stream_v4(wA + p.up_offset + kb * 32);
+          if (okB) ub[u] = ld_stream_v4(wB + p.up_offset + kb * 32);
+        }
+        if (okT) xv[u] = *reinterpret_cast<const uint4*>(xp + kb * 32);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      {
+        const uint32_t a0[4] = {wa[u].x, wb[u].x, wa[u].y, wb[u].y};
+        mma_bf16_16816(c, a0, xv[u].x, xv[u].y);
+        const uint32_t a1[4] = {wa[u].z, wb[u].z, wa[u].w, wb[u].w};
+        mma_bf16_16816(c, a1, xv[u].z, xv[u].w);
+      }
+      if (SWIGLU) {
+        const uint32_t a0[4] = {ua[u].x, ub[u].x, ua[u].y, ub[u].y};
+        mma_bf16_16816(cu, a0, xv[u].x, xv[u].y);
+        const uint32_t a1[4] = {ua[u].z, ub[u].z, ua[u].w, ub[u].w};
+        mma_bf16_16816(cu, a1, xv[u].z, xv[u].w);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    red[warp][lane][i] = c[i];
+    if (SWIGLU) red[warp][lane][4 + i] = cu[i];
+  }
+  __syncthreads();
+  // 128 output elements (16 rows x 8 tokens): thread i -> lane i/4, fragment slot i%4
+  if (threadIdx.x < 128) {
+    const int l = threadIdx.x >> 2, s = threadIdx.x & 3;
+    float acc = 0.f, accu = 0.f;
+#pragma unroll
+    for (int w = 0; w < kGemvWarps; ++w) {
+      acc += red[w][l][s];
+      if (SWIGLU) accu += red[w][l][4 + s];
+    }
+    const int n = n0 + (l >> 2) + ((s & 2) ? 8 : 0);
+    const int j = 2 * (l & 3) + (s & 1);
+    if (j < tn && n < p.n_rows) linear_store(p, g, r0 + tbeg + j, n, acc, accu);
+  }
+}
+
+cudaError_t launch_linear_gemv(const LinearParams& p, cudaStream_t st) {
+  const int rb_count = (p.n_rows + kGemvRows - 1) / kGemvRows;
+  const int max_tok = p.group_offsets ? p.max_routes_per_group : p.n_tokens;
+  const int tc_count = max(1, (max_tok + kGemvTok - 1) / kGemvTok);
+  const long long items = static_cast<long long>(p.n_groups) * rb_count * tc_count;
+  if (items <= 0) return cudaSuccess;
+  if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
+  const dim3 grid(static_cast<unsigned>(items));
+  if (p.epilogue == kEpiSwiglu)
+    gemv_mma_kernel<true, 4><<<grid, kGemvWarps * 32, 0, st>>>(p, rb_count, tc_count);
+  else
+    gemv_mma_kernel<false, 8><<<grid, kGemvWarps * 32, 0, st>>>(p, rb_count, tc_count);
+  return cudaGetLastError();
+}
+
+}  // namespace dsv2

@@ -1,0 +1,368 @@
+// Multi-head latent attention (MLA) decode over the 576-wide latent KV cache.
+//
+// Replaces the reference's expanded-cache attention pipeline (Flash-DeepSeeek-V2-Lite):
+//   attention_decode_small.py:140-264 / :1073-1216  q/k/v build + RoPE (half-split layout)
+//   attention_decode_small.py:267-339               write of expanded K (192) / V (128) per head
+//   attention_decode_small.py:342-423, attention_decode_batch.py:240-342
+//                                                    one-CTA-per-(b,h) online-softmax attention
+// Absorbed formulation: the cache row of every position is
+//   [ RMSNorm(c_kv) (512) | RoPE(k_pe) (64) ]  (bf16, shared by all 16 heads)
+// and the per-head query is [ q_nope @ W_UK[h] (512) | RoPE(q_pe) (64) ], so
+//   score[h, s] = scale * <q[h], row[s]>,   o_lat[h] = sum_s p[h, s] * row[s][:512],
+// and the per-head value projection W_UV[h] is applied after attention.
+// RoPE rotates interleaved pairs (2j, 2j+1) exactly like the HF model's
+// apply_rotary_emb; q and k use the same pairing, so q.k matches the reference's
+// half-split layout.
+//
+// mla_decode_kernel: split-KV flash-decode.  One CTA = (split, sequence), 4 warps.
+// 64-position tiles of the latent cache are staged through a 2-deep cp.async ring in
+// a 128-byte-swizzled layout (conflict-free ldmatrix).  Scores use mma.sync with
+// the 16 heads as M: each warp owns a 144-wide slice of the 576 dims and keeps its
+// query fragments in registers for the whole kernel; slices are summed through
+// shared memory.  P @ V (the latent part) uses mma.sync with each warp owning 128
+// latent dims.  Partial (o, m, l) per split are merged by mla_combine_kernel.
+#include "params.cuh"
+
+namespace dsv2 {
+
+constexpr int kHeads = 16;
+constexpr int kLatent = 512;
+constexpr int kRope = 64;
+constexpr int kRow = kLatent + kRope;           // 576
+constexpr int kRowBytes = kRow * 2;             // 1152
+constexpr int kChunks = kRow / 64;              // 9 swizzle chunks of 64 dims
+constexpr int kTile = 64;                       // positions per tile
+constexpr int kStages = 2;
+constexpr int kTileBytes = kTile * kRowBytes;   // 73728
+constexpr int kQBytes = kHeads * kRowBytes;     // 18432
+constexpr int kSRedStride = kTile + 4;          // fp32 row stride of the score-reduction buffer
+constexpr int kPStride = kTile + 8;             // bf16 row stride of P
+constexpr int kMlaThreads = 128;
+
+// ----------------------------------------------------------------------------
+// mla_prep: latent RMSNorm + RoPE + cache write for the new token, RoPE of q_pe
+// ----------------------------------------------------------------------------
+
+__global__ __launch_bounds__(256) void mla_prep_kernel(const MlaPrepParams p) {
+  __shared__ float red[8];
+  const int b = blockIdx.x;
+  const bf16* row = p.qkva + b * p.qkva_row_stride;
+  long long pos = p.positions[p.pos_numel == 1 ? 0 : b];
+  const bool pos_ok = (pos >= 0 && pos < p.max_len && pos < p.rope_rows);
+  if (!pos_ok) {
+    if (threadIdx.x == 0) set_device_error(kErrIndex);
+    return;
+  }
+  bf16* crow = p.cache + b * p.cache_b_stride + pos * kRow;
+  const float* cs = p.cos_tab + pos * p.rope_stride;
+  const float* sn = p.sin_tab + pos * p.rope_stride;
+  // latent RMSNorm: threads 0..63 own 8 elements each
+  const int t = threadIdx.x;
+  float v[8];
+  float ss = 0.f;
+  if (t < 64) {
+    const uint4 u = *reinterpret_cast<const uint4*>(row + kHeads * 192 + t * 8);
+    const uint32_t* up = reinterpret_cast<const uint32_t*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[2 * j] = bf16lo(up[j]);
+      v[2 * j + 1] = bf16hi(up[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+  }
+  ss = warp_sum(ss);
+  if ((t & 31) == 0) red[t >> 5] = ss;
+  __syncthreads();
+  if (t < 64) {
+    const float inv = rsqrtf((red[0] + red[1]) / static_cast<float>(kLatent) + p.eps);
+    uint4 o;
+    uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float w0 = __bfloat162float(p.kv_norm_w[t * 8 + 2 * j]);
+      const float w1 = __bfloat162float(p.kv_norm_w[t * 8 + 2 * j + 1]);
+      op[j] = pack_bf16x2(v[2 * j] * inv * w0, v[2 * j + 1] * inv * w1);
+    }
+    *reinterpret_cast<uint4*>(crow + t * 8) = o;
+  }
+  // RoPE pairs: 16 heads x 32 pairs of q_pe, plus 32 pairs of k_pe
+  for (int i = t; i < (kHeads + 1) * 32; i += 256) {
+    const int h = i >> 5, j = i & 31;
+    const bf16* src = (h < kHeads) ? (row + h * 192 + 128 + 2 * j) : (row + kHeads * 192 + kLatent + 2 * j);
+    const float e = __bfloat162float(src[0]), o = __bfloat162float(src[1]);
+    const float c = cs[j], s = sn[j];
+    const float re = e * c - o * s, im = o * c + e * s;
+    const uint32_t packed = pack_bf16x2(re, im);
+    if (h < kHeads)
+      *reinterpret_cast<uint32_t*>(p.q_pe_out + (static_cast<long long>(b) * kHeads + h) * kRope + 2 * j) = packed;
+    else
+      *reinterpret_cast<uint32_t*>(crow + kLatent + 2 * j) = packed;
+  }
+}
+
+// ----------------------------------------------------------------------------
+// split-KV decode
+// ----------------------------------------------------------------------------
+
+// byte offset of (row r, 16-byte column c16) inside one 64-dim swizzle chunk of R rows
+__device__ __forceinline__ uint32_t swz(int r, int c16) {
+  return static_cast<uint32_t>(r * 128 + ((c16 ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, bool valid) {
+  const int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n));
+}
+
+__global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDecodeParams p) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  unsigned char* s_q = smem;                                     // 9 chunks x 16 rows x 128 B
+  unsigned char* s_kv = smem + kQBytes;                          // stages x 9 chunks x 64 rows x 128 B
+  float* s_red = reinterpret_cast<float*>(s_kv + kStages * kTileBytes);  // [4][16][kSRedStride]
+  bf16* s_p = reinterpret_cast<bf16*>(s_red + 4 * kHeads * kSRedStride); // [16][kPStride]
+  float* s_alpha = reinterpret_cast<float*>(s_p + kHeads * kPStride);    // [16]
+
+  const int split = blockIdx.x, b = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gq = lane >> 2, tq = lane & 3;
+  const long long pos = p.positions[p.pos_numel == 1 ? 0 : b];
+  const int len = static_cast<int>(min(static_cast<long long>(p.max_len), pos + 1));
+  const int s_beg = split * p.split_len;
+  const int s_end = min(len, s_beg + p.split_len);
+  float* mlp = p.ml_part + ((static_cast<long long>(b) * p.n_splits + split) * kHeads) * 2;
+  if (s_beg >= s_end) {
+    if (tid < kHeads) {
+      mlp[tid * 2] = -INFINITY;
+      mlp[tid * 2 + 1] = 0.f;
+    }
+    return;
+  }
+  const bf16* cache_b = p.cache + b * p.cache_b_stride;
+
+  // --- stage Q = [q_abs | q_pe] (16 x 576) into swizzled smem
+  for (int i = tid; i < kHeads * kChunks * 8; i += kMlaThreads) {
+    const int h = i / (kChunks * 8), rem = i % (kChunks * 8);
+    const int ch = rem / 8, c16 = rem % 8;
+    const int d = ch * 64 + c16 * 8;
+    const bf16* src = (d < kLatent)
+                          ? p.q_abs + (static_cast<long long>(b) * kHeads + h) * kLatent + d
+                          : p.q_pe + (static_cast<long long>(b) * kHeads + h) * kRope + (d - kLatent);
+    *reinterpret_cast<uint4*>(s_q + ch * (kHeads * 128) + swz(h, c16)) = *reinterpret_cast<const uint4*>(src);
+  }
+
+  const int n_tiles = (s_end - s_beg + kTile - 1) / kTile;
+  auto load_tile = [&](int ti, int stage) {
+    const int t0 = s_beg + ti * kTile;
+    const uint32_t base = smem_u32(s_kv + stage * kTileBytes);
+    for (int i = tid; i < kTile * kChunks * 8; i += kMlaThreads) {
+      const int r = i / (kChunks * 8), rem = i % (kChunks * 8);
+      const int ch = rem / 8, c16 = rem % 8;
+      const int sp = t0 + r;
+      const bool valid = sp < s_end;
+      const bf16* src = cache_b + static_cast<long long>(valid ? sp : s_beg) * kRow + ch * 64 + c16 * 8;
+      cp_async16_zfill(base + ch * (kTile * 128) + swz(r, c16), src, valid);
+    }
+  };
+
+  load_tile(0, 0);
+  cp_async_commit();
+  __syncthreads();  // Q visible
+
+  // --- query fragments for this warp's 9 k-steps (dims [144*warp, 144*warp + 144))
+  uint32_t qa[9][4];
+#pragma unroll
+  for (int ks = 0; ks < 9; ++ks) {
+    const int d0 = warp * 144 + ks * 16;
+    const int mi = lane >> 3, ri = lane & 7;
+    const int row = (mi & 1) * 8 + ri;
+    const int d = d0 + (mi >> 1) * 8;
+    const uint32_t addr = smem_u32(s_q + (d / 64) * (kHeads * 128) + swz(row, (d % 64) / 8));
+    ldmatrix_x4(addr, qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+  }
+
+  // softmax state: thread tid owns head hs = tid / 8 and positions [8*(tid%8), +8) of a tile
+  const int hs = tid >> 3, js = tid & 7;
+  float m_run = -INFINITY, l_run = 0.f;
+  float o_acc[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o_acc[j][0] = o_acc[j][1] = o_acc[j][2] = o_acc[j][3] = 0.f;
+
+  for (int ti = 0; ti < n_tiles; ++ti) {
+    const int stage = ti % kStages;
+    // tile ti has landed and every warp has finished with the buffer refilled below
+    cp_async_wait<0>();
+    __syncthreads();
+    if (ti + 1 < n_tiles) load_tile(ti + 1, (ti + 1) % kStages);
+    cp_async_commit();
+    const unsigned char* kv = s_kv + stage * kTileBytes;
+
+    // --- partial scores over this warp's 144 dims for all 64 positions
+    float sc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 9; ++ks) {
+      const int d0 = warp * 144 + ks * 16;
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {  // pairs of n8 tiles (16 positions)
+        const int mi = lane >> 3, ri = lane & 7;
+        const int r = np * 16 + (mi >> 1) * 8 + ri;
+        const int d = d0 + (mi & 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4(smem_u32(kv + (d / 64) * (kTile * 128) + swz(r, (d % 64) / 8)), b0, b1, b2, b3);
+        mma_bf16_16816(sc[2 * np], qa[ks], b0, b1);
+        mma_bf16_16816(sc[2 * np + 1], qa[ks], b2, b3);
+      }
+    }
+    float* red_w = s_red + warp * kHeads * kSRedStride;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = j * 8 + 2 * tq;
+      red_w[gq * kSRedStride + c] = sc[j][0];
+      red_w[gq * kSRedStride + c + 1] = sc[j][1];
+      red_w[(gq + 8) * kSRedStride + c] = sc[j][2];
+      red_w[(gq + 8) * kSRedStride + c + 1] = sc[j][3];
+    }
+    __syncthreads();
+
+    // --- online softmax (log2 domain) for head hs, positions [8*js, 8*js+8)
+    {
+      const int t0 = s_beg + ti * kTile;
+      float s[8];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = js * 8 + i;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) v += s_red[(w * kHeads + hs) * kSRedStride + c];
+        v = (t0 + c < s_end) ? v * p.scale_log2 : -INFINITY;
+        s[i] = v;
+        mx = fmaxf(mx, v);
+      }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float m_new = fmaxf(m_run, mx);
+      const float alpha = exp2f(m_run - m_new);
+      float sum = 0.f;
+      uint32_t pk[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float p0 = exp2f(s[2 * i] - m_new), p1 = exp2f(s[2 * i + 1] - m_new);
+        pk[i] = pack_bf16x2(p0, p1);
+        sum += p0 + p1;
+      }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      l_run = l_run * alpha + sum;
+      m_run = m_new;
+      *reinterpret_cast<uint4*>(s_p + hs * kPStride + js * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      if (js == 0) s_alpha[hs] = alpha;
+    }
+    __syncthreads();
+
+    // --- O[:, 128*warp .. +128] = alpha * O + P @ V
+    {
+      const float a0 = s_alpha[gq], a1 = s_alpha[gq + 8];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        o_acc[j][0] *= a0; o_acc[j][1] *= a0;
+        o_acc[j][2] *= a1; o_acc[j][3] *= a1;
+      }
+#pragma unroll
+      for (int kk = 0; kk < kTile / 16; ++kk) {
+        uint32_t pa[4];
+        {
+          const int mi = lane >> 3, ri = lane & 7;
+          const int row = (mi & 1) * 8 + ri;
+          const int col = kk * 16 + (mi >> 1) * 8;
+          ldmatrix_x4(smem_u32(s_p + row * kPStride + col), pa[0], pa[1], pa[2], pa[3]);
+        }
+#pragma unroll
+        for (int np = 0; np < 8; ++np) {
+          const int mi = lane >> 3, ri = lane & 7;
+          const int r = kk * 16 + (mi & 1) * 8 + ri;
+          const int d = warp * 128 + np * 16 + (mi >> 1) * 8;
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4_trans(smem_u32(kv + (d / 64) * (kTile * 128) + swz(r, (d % 64) / 8)), b0, b1, b2, b3);
+          mma_bf16_16816(o_acc[2 * np], pa, b0, b1);
+          mma_bf16_16816(o_acc[2 * np + 1], pa, b2, b3);
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+
+  // --- write partial results
+  float* op = p.o_part + ((static_cast<long long>(b) * p.n_splits + split) * kHeads) * kLatent;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int d = warp * 128 + j * 8 + 2 * tq;
+    *reinterpret_cast<float2*>(op + gq * kLatent + d) = make_float2(o_acc[j][0], o_acc[j][1]);
+    *reinterpret_cast<float2*>(op + (gq + 8) * kLatent + d) = make_float2(o_acc[j][2], o_acc[j][3]);
+  }
+  if (js == 0) {
+    mlp[hs * 2] = m_run;
+    mlp[hs * 2 + 1] = l_run;
+  }
+}
+
+// o_lat[b, h, :] = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s   (bf16 out)
+__global__ __launch_bounds__(128) void mla_combine_kernel(const float* __restrict__ o_part,
+                                                          const float* __restrict__ ml_part,
+                                                          int n_splits, bf16* __restrict__ o_lat) {
+  const int b = blockIdx.x, h = blockIdx.y;
+  const float* ml = ml_part + (static_cast<long long>(b) * n_splits) * kHeads * 2;
+  float M = -INFINITY;
+  for (int s = 0; s < n_splits; ++s) {
+    const float l = ml[(s * kHeads + h) * 2 + 1];
+    if (l > 0.f) M = fmaxf(M, ml[(s * kHeads + h) * 2]);
+  }
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float den = 0.f;
+  const int d = threadIdx.x * 4;
+  for (int s = 0; s < n_splits; ++s) {
+    const float l = ml[(s * kHeads + h) * 2 + 1];
+    if (!(l > 0.f)) continue;
+    const float w = exp2f(ml[(s * kHeads + h) * 2] - M);
+    den += w * l;
+    const float4 v = *reinterpret_cast<const float4*>(
+        o_part + ((static_cast<long long>(b) * n_splits + s) * kHeads + h) * kLatent + d);
+    acc[0] += w * v.x; acc[1] += w * v.y; acc[2] += w * v.z; acc[3] += w * v.w;
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  uint2 o;
+  o.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+  o.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
+  *reinterpret_cast<uint2*>(o_lat + (static_cast<long long>(b) * kHeads + h) * kLatent + d) = o;
+}
+
+constexpr size_t mla_decode_smem_bytes() {
+  return kQBytes + kStages * kTileBytes + 4 * kHeads * kSRedStride * sizeof(float) +
+         kHeads * kPStride * sizeof(bf16) + kHeads * sizeof(float);
+}
+
+cudaError_t launch_mla_prep(const MlaPrepParams& p, int batch, cudaStream_t st) {
+  mla_prep_kernel<<<batch, 256, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t mla_decode_init() {
+  return cudaFuncSetAttribute(mla_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(mla_decode_smem_bytes()));
+}
+
+cudaError_t launch_mla_decode(const MlaDecodeParams& p, int batch, cudaStream_t st) {
+  mla_decode_kernel<<<dim3(p.n_splits, batch), kMlaThreads, mla_decode_smem_bytes(), st>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_mla_combine(const float* o_part, const float* ml_part, int n_splits, void* o_lat,
+                               int batch, cudaStream_t st) {
+  mla_combine_kernel<<<dim3(batch, kHeads), 128, 0, st>>>(o_part, ml_part, n_splits,
+                                                           reinterpret_cast<bf16*>(o_lat));
+  return cudaGetLastError();
+}
+
+}  // namespace dsv2

@@ -1,0 +1,357 @@
+// RMSNorm family, residual add, SwiGLU elementwise, decode-input preparation and
+// single-token cache copies.
+//
+// Reference kernels these replace (Flash-DeepSeeek-V2-Lite, triton_kernels/):
+//   rmsnorm.py:8-57            two-pass fp32 RMSNorm, output rounded once to the input dtype
+//   attention_prepost.py:85-110 residual add in fp32 -> bf16
+//   mlp_elementwise.py:8-21     silu(gate) * up in fp32 -> bf16
+//   attention_prepost.py:8-36   attention_mask[b, s] = (s <= pos), position_ids[b] = pos
+//   attention_prepost.py:39-82  cache[b, h, pos, :] = src[b, h, 0, :]
+// The fused add_rmsnorm / embed_rmsnorm kernels merge the residual add that
+// src/run.py:459-493 performs around every sublayer with the RMSNorm that follows it.
+#include "params.cuh"
+
+namespace dsv2 {
+
+// y = bf16(x * rsqrt(mean(x^2) + eps) * w); one CTA per row, cols % 8 == 0.
+// w_dtype: 0 bf16, 2 fp32.
+template <int THREADS>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < THREADS / 32; ++i) s += red[i];
+  __syncthreads();
+  return s;
+}
+
+__device__ __forceinline__ float load_w(const void* w, int w_dtype, int i) {
+  if (w_dtype == 2) return reinterpret_cast<const float*>(w)[i];
+  return __bfloat162float(reinterpret_cast<const bf16*>(w)[i]);
+}
+
+// Normalise the 8-element chunks held in v[] (fp32) and store them as bf16.
+template <int MAXCH>
+__device__ __forceinline__ void norm_store(const float (&v)[MAXCH][8], int nch_mine, int chunk0,
+                                           int chunk_step, float inv, const void* w, int w_dtype,
+                                           bf16* y) {
+#pragma unroll
+  for (int i = 0; i < MAXCH; ++i) {
+    if (i >= nch_mine) break;
+    const int c = chunk0 + i * chunk_step;
+    uint4 o;
+    uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float a = v[i][2 * j] * inv * load_w(w, w_dtype, c * 8 + 2 * j);
+      const float b = v[i][2 * j + 1] * inv * load_w(w, w_dtype, c * 8 + 2 * j + 1);
+      op[j] = pack_bf16x2(a, b);
+    }
+    *reinterpret_cast<uint4*>(y + c * 8) = o;
+  }
+}
+
+constexpr int kNormThreads = 256;
+constexpr int kNormMaxCh = 2;  // up to 256 * 2 * 8 = 4096 columns
+
+__global__ __launch_bounds__(kNormThreads) void rmsnorm_kernel(const bf16* __restrict__ x,
+                                                               long long x_stride,
+                                                               const void* __restrict__ w,
+                                                               int w_dtype, bf16* __restrict__ y,
+                                                               long long y_stride, int cols,
+                                                               float eps) {
+  __shared__ float red[kNormThreads / 32];
+  const int row = blockIdx.x;
+  const bf16* xr = x + row * x_stride;
+  const int nch = cols / 8;
+  float v[kNormMaxCh][8];
+  float ss = 0.f;
+  int mine = 0;
+#pragma unroll
+  for (int i = 0; i < kNormMaxCh; ++i) {
+    const int c = threadIdx.x + i * kNormThreads;
+    if (c < nch) {
+      const uint4 u = *reinterpret_cast<const uint4*>(xr + c * 8);
+      const uint32_t* up = reinterpret_cast<const uint32_t*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[i][2 * j] = bf16lo(up[j]);
+        v[i][2 * j + 1] = bf16hi(up[j]);
+        ss += v[i][2 * j] * v[i][2 * j] + v[i][2 * j + 1] * v[i][2 * j + 1];
+      }
+      mine = i + 1;
+    }
+  }
+  ss = block_sum<kNormThreads>(ss, red);
+  const float inv = rsqrtf(ss / static_cast<float>(cols) + eps);
+  norm_store<kNormMaxCh>(v, mine, threadIdx.x, kNormThreads, inv, w, w_dtype, y + row * y_stride);
+}
+
+// h[row] = bf16(h[row] + sum_p delta[row, p]); y[row] = rmsnorm(h[row]) * w.
+// delta_dtype: 0 bf16 (row stride delta_row_stride), 2 fp32 partials laid out
+// [rows][n_delta][cols] (part stride delta_part_stride).  n_delta == 0 means no add.
+// When h_out != nullptr the sum is written there instead of in place.
+__global__ __launch_bounds__(kNormThreads) void add_rmsnorm_kernel(
+    bf16* __restrict__ h, bf16* __restrict__ h_out, const void* __restrict__ delta, int delta_dtype,
+    int n_delta, long long delta_part_stride, long long delta_row_stride,
+    const void* __restrict__ w, int w_dtype, bf16* __restrict__ y, int cols, float eps) {
+  __shared__ float red[kNormThreads / 32];
+  const int row = blockIdx.x;
+  bf16* hr = h + static_cast<long long>(row) * cols;
+  bf16* ho = (h_out ? h_out : h) + static_cast<long long>(row) * cols;
+  const int nch = cols / 8;
+  float v[kNormMaxCh][8];
+  float ss = 0.f;
+  int mine = 0;
+#pragma unroll
+  for (int i = 0; i < kNormMaxCh; ++i) {
+    const int c = threadIdx.x + i * kNormThreads;
+    if (c < nch) {
+      const uint4 u = *reinterpret_cast<const uint4*>(hr + c * 8);
+      const uint32_t* up = reinterpret_cast<const uint32_t*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[i][2 * j] = bf16lo(up[j]);
+        v[i][2 * j + 1] = bf16hi(up[j]);
+      }
+      if (n_delta > 0) {
+        float d[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) d[j] = 0.f;
+        if (delta_dtype == 2) {
+          const float* dp = reinterpret_cast<const float*>(delta) + row * delta_row_stride + c * 8;
+          for (int p = 0; p < n_delta; ++p) {
+            const float4 a = *reinterpret_cast<const float4*>(dp + p * delta_part_stride);
+            const float4 b = *reinterpret_cast<const float4*>(dp + p * delta_part_stride + 4);
+            d[0] += a.x; d[1] += a.y; d[2] += a.z; d[3] += a.w;
+            d[4] += b.x; d[5] += b.y; d[6] += b.z; d[7] += b.w;
+          }
+        } else {
+          const bf16* dp = reinterpret_cast<const bf16*>(delta) + row * delta_row_stride + c * 8;
+          for (int p = 0; p < n_delta; ++p) {
+            const uint4 a = *reinterpret_cast<const uint4*>(dp + p * delta_part_stride);
+            const uint32_t* ap = reinterpret_cast<const uint32_t*>(&a);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              d[2 * j] += bf16lo(ap[j]);
+              d[2 * j + 1] += bf16hi(ap[j]);
+            }
+          }
+        }
+        uint4 o;
+        uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          op[j] = pack_bf16x2(v[i][2 * j] + d[2 * j], v[i][2 * j + 1] + d[2 * j + 1]);
+          v[i][2 * j] = bf16lo(op[j]);
+          v[i][2 * j + 1] = bf16hi(op[j]);
+        }
+        *reinterpret_cast<uint4*>(ho + c * 8) = o;
+      } else if (h_out) {
+        *reinterpret_cast<uint4*>(ho + c * 8) = u;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+      mine = i + 1;
+    }
+  }
+  ss = block_sum<kNormThreads>(ss, red);
+  const float inv = rsqrtf(ss / static_cast<float>(cols) + eps);
+  if (y) norm_store<kNormMaxCh>(v, mine, threadIdx.x, kNormThreads, inv, w, w_dtype,
+                                y + static_cast<long long>(row) * cols);
+}
+
+// h[row] = table[ids[row]]; y[row] = rmsnorm(h[row]) * w   (embedding + first input norm)
+__global__ __launch_bounds__(kNormThreads) void embed_rmsnorm_kernel(
+    const long long* __restrict__ ids, const bf16* __restrict__ table, long long vocab,
+    const void* __restrict__ w, int w_dtype, bf16* __restrict__ h, bf16* __restrict__ y, int cols,
+    float eps) {
+  __shared__ float red[kNormThreads / 32];
+  const int row = blockIdx.x;
+  long long id = ids[row];
+  if (id < 0 || id >= vocab) {
+    set_device_error(kErrIndex);
+    id = 0;
+  }
+  const bf16* src = table + id * cols;
+  bf16* hr = h + static_cast<long long>(row) * cols;
+  const int nch = cols / 8;
+  float v[kNormMaxCh][8];
+  float ss = 0.f;
+  int mine = 0;
+#pragma unroll
+  for (int i = 0; i < kNormMaxCh; ++i) {
+    const int c = threadIdx.x + i * kNormThreads;
+    if (c < nch) {
+      const uint4 u = *reinterpret_cast<const uint4*>(src + c * 8);
+      *reinterpret_cast<uint4*>(hr + c * 8) = u;
+      const uint32_t* up = reinterpret_cast<const uint32_t*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[i][2 * j] = bf16lo(up[j]);
+        v[i][2 * j + 1] = bf16hi(up[j]);
+        ss += v[i][2 * j] * v[i][2 * j] + v[i][2 * j + 1] * v[i][2 * j + 1];
+      }
+      mine = i + 1;
+    }
+  }
+  ss = block_sum<kNormThreads>(ss, red);
+  const float inv = rsqrtf(ss / static_cast<float>(cols) + eps);
+  norm_store<kNormMaxCh>(v, mine, threadIdx.x, kNormThreads, inv, w, w_dtype,
+                         y + static_cast<long long>(row) * cols);
+}
+
+// out = bf16(a + b), 8 elements per thread
+__global__ void residual_add_kernel(const bf16* __restrict__ a, const bf16* __restrict__ b,
+                                    bf16* __restrict__ out, long long n8) {
+  const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (i >= n8) return;
+  const uint4 x = reinterpret_cast<const uint4*>(a)[i];
+  const uint4 z = reinterpret_cast<const uint4*>(b)[i];
+  const uint32_t* xp = reinterpret_cast<const uint32_t*>(&x);
+  const uint32_t* zp = reinterpret_cast<const uint32_t*>(&z);
+  uint4 o;
+  uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    op[j] = pack_bf16x2(bf16lo(xp[j]) + bf16lo(zp[j]), bf16hi(xp[j]) + bf16hi(zp[j]));
+  reinterpret_cast<uint4*>(out)[i] = o;
+}
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.f + expf(-g)); }
+
+// out = bf16(silu(gate) * up)
+__global__ void silu_mul_kernel(const bf16* __restrict__ gate, const bf16* __restrict__ up,
+                                bf16* __restrict__ out, long long n8) {
+  const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (i >= n8) return;
+  const uint4 x = reinterpret_cast<const uint4*>(gate)[i];
+  const uint4 z = reinterpret_cast<const uint4*>(up)[i];
+  const uint32_t* xp = reinterpret_cast<const uint32_t*>(&x);
+  const uint32_t* zp = reinterpret_cast<const uint32_t*>(&z);
+  uint4 o;
+  uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    op[j] = pack_bf16x2(silu_f(bf16lo(xp[j])) * bf16lo(zp[j]), silu_f(bf16hi(xp[j])) * bf16hi(zp[j]));
+  reinterpret_cast<uint4*>(out)[i] = o;
+}
+
+// attention_mask[b, s] = (index[s] <= pos_b); position_ids[b] = pos_b.
+// pos_numel == 1: one shared position (reference semantics); == batch: per-row.
+__global__ void prepare_decode_inputs_kernel(const long long* __restrict__ cache_position,
+                                             int pos_numel, long long* __restrict__ mask,
+                                             long long mask_stride_b, long long* __restrict__ pos_ids,
+                                             long long pos_ids_stride_b,
+                                             const long long* __restrict__ mask_index, int max_len) {
+  const int b = blockIdx.y;
+  const long long pos = cache_position[pos_numel == 1 ? 0 : b];
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (mask && s < max_len) mask[b * mask_stride_b + s] = (mask_index[s] <= pos) ? 1 : 0;
+  if (s == 0 && pos_ids) pos_ids[b * pos_ids_stride_b] = pos;
+}
+
+// dst[b, h, pos_b, :] = src[b, h, 0, :]   (element size 2 or 4 bytes)
+__global__ void copy_token_to_cache_kernel(const char* __restrict__ src, long long sb, long long sh,
+                                           long long sd, char* __restrict__ dst, long long db,
+                                           long long dh, long long ds, long long dd,
+                                           const long long* __restrict__ cache_position,
+                                           int pos_numel, int heads, int dim, int esize,
+                                           int max_len) {
+  const int b = blockIdx.x, h = blockIdx.y;
+  long long pos = cache_position[pos_numel == 1 ? 0 : b];
+  if (pos < 0 || pos >= max_len) {
+    set_device_error(kErrIndex);
+    return;
+  }
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+    const char* s = src + (b * sb + h * sh + d * sd) * esize;
+    char* t = dst + (b * db + h * dh + pos * ds + d * dd) * esize;
+    if (esize == 2)
+      *reinterpret_cast<uint16_t*>(t) = *reinterpret_cast<const uint16_t*>(s);
+    else
+      *reinterpret_cast<uint32_t*>(t) = *reinterpret_cast<const uint32_t*>(s);
+  }
+}
+
+// Advance per-row decode state after a step: pos[b] += 1 (int64 positions).
+__global__ void advance_positions_kernel(long long* __restrict__ pos, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) pos[i] += 1;
+}
+
+// ---------------------------------------------------------------------------
+// host launchers (called from api.cu)
+// ---------------------------------------------------------------------------
+cudaError_t launch_rmsnorm(const void* x, long long xs, const void* w, int wd, void* y,
+                           long long ys, int rows, int cols, float eps, cudaStream_t st) {
+  rmsnorm_kernel<<<rows, kNormThreads, 0, st>>>(reinterpret_cast<const bf16*>(x), xs, w, wd,
+                                                reinterpret_cast<bf16*>(y), ys, cols, eps);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_add_rmsnorm(void* h, void* h_out, const void* delta, int dd, int nd,
+                               long long dps, long long drs, const void* w, int wd, void* y,
+                               int rows, int cols, float eps, cudaStream_t st) {
+  add_rmsnorm_kernel<<<rows, kNormThreads, 0, st>>>(
+      reinterpret_cast<bf16*>(h), reinterpret_cast<bf16*>(h_out), delta, dd, nd, dps, drs, w, wd,
+      reinterpret_cast<bf16*>(y), cols, eps);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_embed_rmsnorm(const long long* ids, const void* table, long long vocab,
+                                 const void* w, int wd, void* h, void* y, int rows, int cols,
+                                 float eps, cudaStream_t st) {
+  embed_rmsnorm_kernel<<<rows, kNormThreads, 0, st>>>(ids, reinterpret_cast<const bf16*>(table),
+                                                      vocab, w, wd, reinterpret_cast<bf16*>(h),
+                                                      reinterpret_cast<bf16*>(y), cols, eps);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_residual_add(const void* a, const void* b, void* out, long long n,
+                                cudaStream_t st) {
+  const long long n8 = n / 8;
+  const int thr = 256;
+  residual_add_kernel<<<static_cast<unsigned>((n8 + thr - 1) / thr), thr, 0, st>>>(
+      reinterpret_cast<const bf16*>(a), reinterpret_cast<const bf16*>(b),
+      reinterpret_cast<bf16*>(out), n8);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_silu_mul(const void* g, const void* u, void* out, long long n, cudaStream_t st) {
+  const long long n8 = n / 8;
+  const int thr = 256;
+  silu_mul_kernel<<<static_cast<unsigned>((n8 + thr - 1) / thr), thr, 0, st>>>(
+      reinterpret_cast<const bf16*>(g), reinterpret_cast<const bf16*>(u),
+      reinterpret_cast<bf16*>(out), n8);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prepare_decode_inputs(const long long* cp, int pn, long long* mask, long long msb,
+                                         long long* pid, long long psb, const long long* mi,
+                                         int batch, int max_len, cudaStream_t st) {
+  dim3 grid((max_len + 255) / 256, batch);
+  prepare_decode_inputs_kernel<<<grid, 256, 0, st>>>(cp, pn, mask, msb, pid, psb, mi, max_len);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_copy_token_to_cache(const void* src, const long long* ss, void* dst,
+                                       const long long* ds, const long long* cp, int pn, int batch,
+                                       int heads, int dim, int esize, int max_len,
+                                       cudaStream_t st) {
+  dim3 grid(batch, heads);
+  copy_token_to_cache_kernel<<<grid, 128, 0, st>>>(
+      reinterpret_cast<const char*>(src), ss[0], ss[1], ss[2], reinterpret_cast<char*>(dst), ds[0],
+      ds[1], ds[2], ds[3], cp, pn, heads, dim, esize, max_len);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_advance_positions(long long* pos, int n, cudaStream_t st) {
+  advance_positions_kernel<<<(n + 255) / 256, 256, 0, st>>>(pos, n);
+  return cudaGetLastError();
+}
+
+}  // namespace dsv2

@@ -1,0 +1,99 @@
+// Kernel parameter blocks and launcher declarations shared between the kernel
+// translation units and the C-ABI layer (api.cu).
+#pragma once
+#include "linear.cuh"
+
+namespace dsv2 {
+
+struct RouterParams {
+  const bf16* x;           // [rows, hidden] normalised activations
+  long long x_row_stride;
+  const void* w;           // [n_experts, hidden] gate weight, bf16 or fp32
+  int w_dtype;             // 0 bf16, 2 fp32
+  const float* bias;       // optional per-expert logit offset (nullptr = none)
+  int rows;
+  int hidden;
+  int n_experts;
+  float scaling;
+  float* logits;           // [rows, n_experts] workspace (fp32)
+  long long* topk_ids;     // [rows, 6] int64 (may be nullptr)
+  int* topk_ids32;         // [rows, 6] int32 (bucketing input)
+  float* topk_w;           // [rows, 6]
+  unsigned int* ticket;    // one zero-initialised counter, reset by the last CTA
+  int experts_per_cta;     // 8 (small batches, softmax in the last CTA) or n_experts
+  // bucketing (skipped when group_offsets == nullptr)
+  int expert_lo;           // first local expert
+  int n_local;             // local routed experts
+  int shared_lo, shared_hi;  // rows whose shared-expert routes are local
+  int* group_offsets;      // [n_local + 3]
+  int* route_token;        // [rows*6 + 2*(shared_hi-shared_lo)]
+  int* route_slot;
+  float* route_weight;
+};
+
+struct MlaPrepParams {
+  const bf16* qkva;            // [B, 3072 + 576]: q (16 x 192) | c_kv (512) | k_pe (64)
+  long long qkva_row_stride;
+  const bf16* kv_norm_w;       // [512]
+  float eps;
+  const float* cos_tab;        // [positions, rope_stride] (first 32 entries used)
+  const float* sin_tab;
+  long long rope_stride;
+  int rope_rows;
+  const long long* positions;  // [1] or [B]: write position of the new token
+  int pos_numel;
+  bf16* cache;                 // [B, max_len, 576] (this layer)
+  long long cache_b_stride;    // elements
+  int max_len;
+  bf16* q_pe_out;              // [B, 16, 64]
+};
+
+struct MlaDecodeParams {
+  const bf16* q_abs;           // [B, 16, 512]
+  const bf16* q_pe;            // [B, 16, 64]
+  const bf16* cache;           // [B, max_len, 576]
+  long long cache_b_stride;
+  int max_len;
+  const long long* positions;  // [1] or [B]; attended length = position + 1
+  int pos_numel;
+  float scale_log2;            // softmax_scale * log2(e)
+  int split_len;               // positions per split, multiple of the tile
+  int n_splits;
+  float* o_part;               // [B, n_splits, 16, 512]
+  float* ml_part;              // [B, n_splits, 16, 2]  (m in log2 domain, l)
+};
+
+// norm.cu
+cudaError_t launch_rmsnorm(const void*, long long, const void*, int, void*, long long, int, int,
+                           float, cudaStream_t);
+cudaError_t launch_add_rmsnorm(void*, void*, const void*, int, int, long long, long long,
+                               const void*, int, void*, int, int, float, cudaStream_t);
+cudaError_t launch_embed_rmsnorm(const long long*, const void*, long long, const void*, int, void*,
+                                 void*, int, int, float, cudaStream_t);
+cudaError_t launch_residual_add(const void*, const void*, void*, long long, cudaStream_t);
+cudaError_t launch_silu_mul(const void*, const void*, void*, long long, cudaStream_t);
+cudaError_t launch_prepare_decode_inputs(const long long*, int, long long*, long long, long long*,
+                                         long long, const long long*, int, int, cudaStream_t);
+cudaError_t launch_copy_token_to_cache(const void*, const long long*, void*, const long long*,
+                                       const long long*, int, int, int, int, int, int,
+                                       cudaStream_t);
+cudaError_t launch_advance_positions(long long*, int, cudaStream_t);
+// router.cu
+cudaError_t launch_router(const RouterParams&, cudaStream_t);
+cudaError_t launch_bucket(const int*, const float*, int, int, int, int, int, int*, int*, int*,
+                          float*, cudaStream_t);
+cudaError_t launch_softmax_topk(const float*, int, int, float, long long*, int*, float*,
+                                cudaStream_t);
+cudaError_t launch_gather_rows(const void*, long long, const int*, const int*, int, void*, int,
+                               int, cudaStream_t);
+// mla.cu
+cudaError_t launch_mla_prep(const MlaPrepParams&, int, cudaStream_t);
+cudaError_t mla_decode_init();
+cudaError_t launch_mla_decode(const MlaDecodeParams&, int, cudaStream_t);
+cudaError_t launch_mla_combine(const float*, const float*, int, void*, int, cudaStream_t);
+// linear_tc.cu
+cudaError_t linear_tc_init();
+cudaError_t launch_linear_tc_impl(const LinearParams&, const CUtensorMap&, const CUtensorMap&, int,
+                                  int, int, cudaStream_t);
+
+}  // namespace dsv2

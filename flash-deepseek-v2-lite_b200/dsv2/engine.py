@@ -1,0 +1,396 @@
+"""Decode engine: HF DeepSeek-V2 model + latent KV cache + CUDA-graph q_len=1 decode.
+
+Mirrors the reference runner (src/run.py):
+  * the HF model object stays the source of weights and runs the eager prefill
+    (src/run.py:526-544);
+  * one q_len = 1 decode step over all layers is captured in a torch.cuda.CUDAGraph
+    and replayed (src/run.py:591-688), after warm-up steps whose effects are rolled
+    back (src/run.py:641-656);
+  * --kernel-family small | batch selects the GEMV or the tcgen05 linear kernels
+    (src/run.py:53-64).
+Differences by design: the cache is the 576-wide latent cache [L, B, S, 576] with
+per-row positions (ragged batches), the residual add is fused into the following
+RMSNorm, and the two shared experts run inside the grouped MoE launch.  With
+world > 1 the routed experts are sharded across ranks (expert parallel) and the
+batch rows across ranks (attention data parallel); the MoE activations are
+all-gathered and the expert outputs reduce-scattered with NCCL inside the graph.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+from .model import (HIDDEN, KV_LORA, LATENT_ROW, N_HEADS, QK_NOPE, QKVA_ROWS, Q_DIM, SLOTS, TOPK,
+                    V_DIM, LayerPack, check_config, pack_layer, rope_tables)
+
+FAMILIES = {"small": ops.FAMILY_SMALL, "batch": ops.FAMILY_BATCH}
+
+
+def choose_split_len(batch: int, max_len: int, num_sms: int) -> int:
+    """Positions per split-KV CTA: about two CTAs per SM over the whole batch."""
+    target = max(1, 2 * num_sms)
+    s = math.ceil(batch * max_len / target)
+    s = (s + 63) // 64 * 64
+    return int(min(max(s, 64), 4096))
+
+
+@dataclass
+class DecodeState:
+    positions: torch.Tensor   # [B] int64: write position of the next token
+    input_ids: torch.Tensor   # [B] int64: token fed to the next step
+
+
+class DecodeEngine:
+    def __init__(self, model, batch: int, max_len: int, family: str = "batch", *,
+                 rank: int = 0, world: int = 1, group=None, gate_bias: torch.Tensor | None = None,
+                 alias_hf: bool = True):
+        cfg = model.config
+        check_config(cfg)
+        if family not in FAMILIES:
+            raise ValueError(f"Unknown kernel family: {family}")
+        if world > 1 and cfg.n_routed_experts % world:
+            raise ValueError("expert count must divide the world size")
+        self.model = model
+        self.cfg = cfg
+        self.family_name = family
+        self.family = FAMILIES[family]
+        self.dev = model.lm_head.weight.device
+        self.B = int(batch)                  # rows owned by this rank
+        self.max_len = int(max_len)
+        self.rank, self.world, self.group = rank, world, group
+        self.B_all = self.B * world
+        n_exp = int(cfg.n_routed_experts)
+        self.n_local = n_exp // world
+        self.expert_lo = rank * self.n_local
+        self.layers: list[LayerPack] = [
+            pack_layer(l, self.expert_lo, self.n_local, alias_hf=alias_hf and world == 1, gate_bias=gate_bias)
+            for l in model.model.layers
+        ]
+        self.L = len(self.layers)
+        self.embed = model.model.embed_tokens.weight
+        self.final_norm_w = model.model.norm.weight
+        self.final_eps = float(model.model.norm.variance_epsilon)
+        self.lm_head = model.lm_head.weight
+        self.vocab = int(self.lm_head.shape[0])
+        self.scale = float(model.model.layers[0].self_attn.scaling)
+        self.cos, self.sin = rope_tables(model, self.max_len, self.dev)
+        props = torch.cuda.get_device_properties(self.dev)
+        self.num_sms = props.multi_processor_count
+        self.split_len = choose_split_len(self.B, self.max_len, self.num_sms)
+        self.n_splits = math.ceil(self.max_len / self.split_len)
+        self._alloc()
+        self.graph = None
+        self._saved = None
+
+    # ------------------------------------------------------------------ buffers
+    def _alloc(self):
+        B, dev, bf = self.B, self.dev, torch.bfloat16
+        f32, i32, i64 = torch.float32, torch.int32, torch.int64
+        self.cache = torch.zeros((self.L, B, self.max_len, LATENT_ROW), device=dev, dtype=bf)
+        self.positions = torch.zeros(B, device=dev, dtype=i64)
+        self.input_ids = torch.zeros(B, device=dev, dtype=i64)
+        self.next_ids = torch.zeros(B, device=dev, dtype=i64)
+        self.h = torch.zeros((B, HIDDEN), device=dev, dtype=bf)
+        self.x = torch.zeros((B, HIDDEN), device=dev, dtype=bf)
+        self.qkva = torch.zeros((B, QKVA_ROWS), device=dev, dtype=bf)
+        self.q_pe = torch.zeros((B, N_HEADS, 64), device=dev, dtype=bf)
+        self.q_abs = torch.zeros((B, N_HEADS, KV_LORA), device=dev, dtype=bf)
+        self.o_lat = torch.zeros((B, N_HEADS, KV_LORA), device=dev, dtype=bf)
+        self.attn_o = torch.zeros((B, N_HEADS * V_DIM), device=dev, dtype=bf)
+        self.attn_out = torch.zeros((B, HIDDEN), device=dev, dtype=bf)
+        self.o_part = torch.zeros((B, self.n_splits, N_HEADS, KV_LORA), device=dev, dtype=f32)
+        self.ml_part = torch.zeros((B, self.n_splits, N_HEADS, 2), device=dev, dtype=f32)
+        dense = [lp.dense for lp in self.layers if lp.dense is not None]
+        inter_d = max([d.inter for d in dense], default=8)
+        self.mlp_h = torch.zeros((B, inter_d), device=dev, dtype=bf)
+        self.mlp_out = torch.zeros((B, HIDDEN), device=dev, dtype=bf)
+        moe = [lp.moe for lp in self.layers if lp.moe is not None]
+        Ball = self.B_all
+        if moe:
+            m0 = moe[0]
+            self.r_max = TOPK * Ball + 2 * B
+            self.n_groups = m0.n_local + 2
+            self.logits_r = torch.zeros((B, m0.n_experts), device=dev, dtype=f32)
+            self.topk_ids64 = torch.zeros((B, TOPK), device=dev, dtype=i64)
+            self.topk_ids32 = torch.zeros((Ball, TOPK), device=dev, dtype=i32)
+            self.topk_w = torch.zeros((Ball, TOPK), device=dev, dtype=f32)
+            self.ids_local = torch.zeros((B, TOPK), device=dev, dtype=i32)
+            self.w_local = torch.zeros((B, TOPK), device=dev, dtype=f32)
+            self.ticket = torch.zeros(4, device=dev, dtype=i32)
+            # per-MoE-layer group offsets (kept per layer so the routing of the last step
+            # can be inspected: distinct experts per layer for the roofline)
+            self.moe_index = {li: i for i, li in enumerate(l for l, lp in enumerate(self.layers)
+                                                           if lp.moe is not None)}
+            self.group_offsets_hist = torch.zeros((len(moe), self.n_groups + 1), device=dev, dtype=i32)
+            self.route_token = torch.zeros(self.r_max, device=dev, dtype=i32)
+            self.route_slot = torch.zeros(self.r_max, device=dev, dtype=i32)
+            self.route_weight = torch.zeros(self.r_max, device=dev, dtype=f32)
+            self.x_sorted = torch.zeros((self.r_max, HIDDEN), device=dev, dtype=bf)
+            self.h_moe = torch.zeros((self.r_max, m0.inter), device=dev, dtype=bf)
+            self.partial = torch.zeros((Ball, SLOTS, HIDDEN), device=dev, dtype=f32)
+            if self.world > 1:
+                self.x_all = torch.zeros((Ball, HIDDEN), device=dev, dtype=bf)
+                self.moe_sum = torch.zeros((Ball, HIDDEN), device=dev, dtype=f32)
+                self.moe_local = torch.zeros((B, 1, HIDDEN), device=dev, dtype=f32)
+        self.logits = torch.zeros((B, self.vocab), device=dev, dtype=bf)
+
+    # ------------------------------------------------------------------ layers
+    def _linear(self, **kw):
+        ops.linear(family=self.family, **kw)
+
+    def _attention(self, li: int, lp: LayerPack) -> None:
+        a, B = lp.attn, self.B
+        self._linear(w=a.qkva, n_rows=QKVA_ROWS, k=HIDDEN, x=self.x, y=self.qkva, n_tokens=B,
+                     x_group_rows=B)
+        ops.mla_prep(qkva=self.qkva, kv_norm_w=a.kv_norm_w, eps=a.kv_norm_eps, cos=self.cos, sin=self.sin,
+                     positions=self.positions, cache=self.cache[li], q_pe_out=self.q_pe)
+        # q_abs[b, h] = q_nope[b, h] @ W_UK[h]
+        self._linear(w=a.w_uk_t, n_rows=KV_LORA, k=QK_NOPE, w_row_stride=QK_NOPE,
+                     w_group_stride=KV_LORA * QK_NOPE, x=self.qkva, x_row_stride=QKVA_ROWS,
+                     x_group_stride=Q_DIM, y=self.q_abs, y_row_stride=N_HEADS * KV_LORA,
+                     y_group_stride=KV_LORA, n_groups=N_HEADS, n_tokens=B, w_group_rows=KV_LORA,
+                     x_group_rows=B)
+        ops.mla_decode(q_abs=self.q_abs, q_pe=self.q_pe, cache=self.cache[li], positions=self.positions,
+                       softmax_scale=self.scale, split_len=self.split_len, o_part=self.o_part,
+                       ml_part=self.ml_part, o_lat=self.o_lat)
+        # o[b, h] = o_lat[b, h] @ W_UV[h]^T,  W_UV[h] = kv_b[h*256 + 128 : h*256 + 256]
+        self._linear(w=a.kv_b[QK_NOPE:], n_rows=V_DIM, k=KV_LORA, w_row_stride=KV_LORA,
+                     w_group_stride=(QK_NOPE + V_DIM) * KV_LORA, x=self.o_lat, x_row_stride=N_HEADS * KV_LORA,
+                     x_group_stride=KV_LORA, y=self.attn_o, y_row_stride=N_HEADS * V_DIM,
+                     y_group_stride=V_DIM, n_groups=N_HEADS, n_tokens=B, w_group_rows=V_DIM,
+                     x_group_rows=B)
+        self._linear(w=a.o, n_rows=HIDDEN, k=N_HEADS * V_DIM, x=self.attn_o, y=self.attn_out, n_tokens=B,
+                     x_group_rows=B)
+
+    def _dense_mlp(self, lp: LayerPack) -> torch.Tensor:
+        d, B = lp.dense, self.B
+        h = self.mlp_h[:, :d.inter]
+        self._linear(w=d.gate_up, n_rows=d.inter, k=HIDDEN, up_offset=d.inter * HIDDEN, x=self.x, y=h,
+                     epilogue=ops.EPI_SWIGLU, n_tokens=B, w_group_rows=2 * d.inter, x_group_rows=B)
+        self._linear(w=d.down, n_rows=HIDDEN, k=d.inter, x=h, y=self.mlp_out, n_tokens=B, x_group_rows=B)
+        return self.mlp_out
+
+    def _moe(self, li: int, lp: LayerPack) -> torch.Tensor:
+        m, B = lp.moe, self.B
+        go = self.group_offsets_hist[self.moe_index[li]]
+        if self.world == 1:
+            ops.router(x=self.x, w=m.gate_w, scaling=m.scaling, bias=m.gate_bias, logits=self.logits_r,
+                       topk_ids32=self.topk_ids32, topk_weights=self.topk_w, topk_ids64=self.topk_ids64,
+                       ticket=self.ticket, expert_lo=m.expert_lo, n_local=m.n_local, shared_lo=0,
+                       shared_hi=B, group_offsets=go, route_token=self.route_token,
+                       route_slot=self.route_slot, route_weight=self.route_weight)
+            x_src = self.x
+        else:
+            import torch.distributed as dist
+            r0 = self.rank * B
+            ops.router(x=self.x, w=m.gate_w, scaling=m.scaling, bias=m.gate_bias, logits=self.logits_r,
+                       topk_ids32=self.ids_local, topk_weights=self.w_local, topk_ids64=self.topk_ids64,
+                       ticket=self.ticket)
+            dist.all_gather_into_tensor(self.x_all, self.x, group=self.group)
+            dist.all_gather_into_tensor(self.topk_ids32, self.ids_local, group=self.group)
+            dist.all_gather_into_tensor(self.topk_w, self.w_local, group=self.group)
+            ops.moe_bucket(self.topk_ids32, self.topk_w, m.expert_lo, m.n_local, r0, r0 + B,
+                           go, self.route_token, self.route_slot, self.route_weight)
+            self.partial.zero_()
+            x_src = self.x_all
+        if self.family == ops.FAMILY_BATCH:
+            ops.gather_rows(x_src, self.route_token, go, self.n_groups, self.x_sorted, self.r_max)
+        self._moe_gemms(m, go, x_src)
+        if self.world == 1:
+            return self.partial
+        import torch.distributed as dist
+        torch.sum(self.partial, dim=1, out=self.moe_sum)
+        dist.reduce_scatter_tensor(self.moe_local.view(B, HIDDEN), self.moe_sum, group=self.group)
+        return self.moe_local
+
+    def _moe_gemms(self, m, go: torch.Tensor, x_src: torch.Tensor) -> None:
+        """gate_up + SwiGLU and down + route-weight scaling over local experts + shared halves."""
+        if self.family == ops.FAMILY_BATCH:
+            gx, rx = self.x_sorted, None
+        else:
+            gx, rx = x_src, self.route_token
+        G = self.n_groups
+        self._linear(w=m.gate_up, n_rows=m.inter, k=HIDDEN, up_offset=m.inter * HIDDEN,
+                     w_group_stride=2 * m.inter * HIDDEN, x=gx, y=self.h_moe, epilogue=ops.EPI_SWIGLU,
+                     n_groups=G, group_offsets=go, max_routes_per_group=self.B_all,
+                     route_x_row=rx, w_group_rows=2 * m.inter, x_group_rows=self.r_max)
+        self._linear(w=m.down, n_rows=HIDDEN, k=m.inter, w_group_stride=HIDDEN * m.inter, x=self.h_moe,
+                     y=self.partial.view(-1, HIDDEN), epilogue=ops.EPI_SCALE_F32, n_groups=G,
+                     group_offsets=go, max_routes_per_group=self.B_all,
+                     route_y_row=self.route_slot, route_scale=self.route_weight, w_group_rows=HIDDEN,
+                     x_group_rows=self.r_max)
+
+    def time_moe_gemms(self, iters: int = 10) -> tuple[float, float, int]:
+        """Replay only the grouped MoE GEMMs of every MoE layer (routing of the last step's
+        last MoE layer) from a CUDA graph; returns (ms per replay, algorithmic bytes per
+        replay, launches per replay).  Bytes: weights of the distinct routed experts hit plus
+        the two shared-expert halves, once per layer."""
+        moe_layers = [lp for lp in self.layers if lp.moe is not None]
+        if not moe_layers:
+            return 0.0, 0.0, 0
+        go = self.group_offsets_hist[len(moe_layers) - 1]
+        x_src = self.x if self.world == 1 else self.x_all
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            for lp in moe_layers:
+                self._moe_gemms(lp.moe, go, x_src)
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        with torch.cuda.graph(g):
+            for lp in moe_layers:
+                self._moe_gemms(lp.moe, go, x_src)
+        g.replay()
+        torch.cuda.synchronize(self.dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(iters):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize(self.dev)
+        ms = a.elapsed_time(b) / iters
+        off = go.cpu()
+        counts = off[1:] - off[:-1]
+        m0 = moe_layers[0].moe
+        per_expert = (2 * m0.inter * HIDDEN + HIDDEN * m0.inter) * 2
+        nbytes = len(moe_layers) * int((counts > 0).sum()) * per_expert
+        del g
+        return ms, float(nbytes), 2 * len(moe_layers)
+
+    # ------------------------------------------------------------------ step
+    def step(self, trace: dict | None = None) -> None:
+        """One q_len = 1 decode step for every row (kernel launches only; graph-capturable).
+
+        trace (eager debugging/tests only): collects the residual stream after every layer
+        ("hidden", fp32 [B, 2048] each, HF output_hidden_states order starting with the
+        embeddings) and the router's top-6 ids of every MoE layer ("routes")."""
+        lp0 = self.layers[0]
+        ops.embed_rmsnorm(self.input_ids, self.embed, lp0.in_norm_w, lp0.eps, self.h, self.x)
+        if trace is not None:
+            trace.setdefault("hidden", []).append(self.h.float().clone())
+            trace.setdefault("routes", [])
+        delta = None
+        for li, lp in enumerate(self.layers):
+            if li > 0:
+                ops.add_rmsnorm(self.h, delta, lp.in_norm_w, lp.eps, self.x)
+            self._attention(li, lp)
+            ops.add_rmsnorm(self.h, self.attn_out, lp.post_norm_w, lp.eps, self.x)
+            delta = self._dense_mlp(lp) if lp.dense is not None else self._moe(li, lp)
+            if trace is not None:
+                d = delta.float().sum(1) if delta.dim() == 3 else delta.float()
+                trace["hidden"].append(self.h.float() + d)
+                if lp.moe is not None:
+                    trace["routes"].append(self.topk_ids64.clone())
+        ops.add_rmsnorm(self.h, delta, self.final_norm_w, self.final_eps, self.x)
+        torch.mm(self.x, self.lm_head.t(), out=self.logits)
+        torch.argmax(self.logits, dim=-1, out=self.next_ids)
+        self.input_ids.copy_(self.next_ids)
+        ops.advance_positions(self.positions)
+
+    # ------------------------------------------------------------------ state
+    def set_state(self, positions: torch.Tensor, input_ids: torch.Tensor) -> None:
+        self.positions.copy_(positions.to(self.positions))
+        self.input_ids.copy_(input_ids.to(self.input_ids).view(-1))
+        self._saved = (self.positions.clone(), self.input_ids.clone())
+
+    def restore(self) -> None:
+        """Roll back positions / next tokens to the post-prefill state.  Cache rows at or
+        beyond a row's position are never read before being rewritten, so the latent cache
+        needs no snapshot (unlike the expanded cache of src/run.py:161-217)."""
+        pos, ids = self._saved
+        self.positions.copy_(pos)
+        self.input_ids.copy_(ids)
+
+    def capture(self, warmup: int = 3) -> None:
+        """Warm up eagerly (rolled back), then capture one decode step in a CUDA graph."""
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                self.step()
+                self.restore()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        torch.cuda.synchronize(self.dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.step()
+        torch.cuda.synchronize(self.dev)
+        self.restore()
+        self.graph = g
+
+    def replay(self) -> None:
+        self.graph.replay()
+
+    def release(self) -> None:
+        self.graph = None
+
+    # ------------------------------------------------------------------ prefill
+    @torch.no_grad()
+    def prefill(self, prompts: list[torch.Tensor], max_tokens_per_chunk: int = 16384) -> torch.Tensor:
+        """Eager HF prefill of this rank's rows (ragged prompts, right-padded in chunks).
+
+        The latent cache rows are rebuilt from the kv_a_proj_with_mqa outputs that the HF
+        forward produces: [rmsnorm(c_kv) * w | rope(k_pe)] with the same formulas as the
+        decode kernel.  Returns the first generated token of every row (greedy).
+        """
+        if len(prompts) != self.B:
+            raise ValueError(f"expected {self.B} prompts, got {len(prompts)}")
+        model = self.model
+        lens = [int(p.numel()) for p in prompts]
+        if max(lens) >= self.max_len:
+            raise ValueError("prompt longer than the cache")
+        captured: dict[int, torch.Tensor] = {}
+        hooks = []
+        for li, layer in enumerate(model.model.layers):
+            hooks.append(layer.self_attn.kv_a_proj_with_mqa.register_forward_hook(
+                lambda mod, inp, out, li=li: captured.__setitem__(li, out)))
+        first = torch.zeros(self.B, dtype=torch.int64, device=self.dev)
+        try:
+            r0 = 0
+            while r0 < self.B:
+                T = lens[r0]
+                r1 = r0 + 1
+                while r1 < self.B and (r1 - r0 + 1) * max(T, lens[r1]) <= max_tokens_per_chunk:
+                    T = max(T, lens[r1])
+                    r1 += 1
+                nr = r1 - r0
+                ids = torch.zeros((nr, T), dtype=torch.int64, device=self.dev)
+                mask = torch.zeros((nr, T), dtype=torch.int64, device=self.dev)
+                for i in range(nr):
+                    n = lens[r0 + i]
+                    ids[i, :n] = prompts[r0 + i].to(self.dev)
+                    mask[i, :n] = 1
+                out = model.model(input_ids=ids, attention_mask=mask, use_cache=False)
+                hid = out.last_hidden_state
+                idx = torch.tensor([lens[r0 + i] - 1 for i in range(nr)], device=self.dev)
+                last = hid[torch.arange(nr, device=self.dev), idx]
+                first[r0:r1] = torch.argmax(model.lm_head(last), dim=-1)
+                for li, lp in enumerate(self.layers):
+                    self.cache[li, r0:r1, :T] = latent_rows(captured[li], lp.attn.kv_norm_w,
+                                                            lp.attn.kv_norm_eps, self.cos[:T], self.sin[:T])
+                captured.clear()
+                r0 = r1
+        finally:
+            for h in hooks:
+                h.remove()
+        pos = torch.tensor(lens, dtype=torch.int64, device=self.dev)
+        self.set_state(pos, first)
+        return first
+
+
+def latent_rows(kva: torch.Tensor, norm_w: torch.Tensor, eps: float, cos: torch.Tensor,
+                sin: torch.Tensor) -> torch.Tensor:
+    """[.., T, 576] kv_a_proj_with_mqa output -> latent cache rows [.., T, 576] (bf16):
+    bf16(c * rsqrt(mean(c^2) + eps) * w) | interleaved-pair RoPE of k_pe (fp32 math)."""
+    c = kva[..., :KV_LORA].float()
+    inv = torch.rsqrt(c.pow(2).mean(-1, keepdim=True) + eps)
+    lat = (c * inv * norm_w.float()).to(torch.bfloat16)
+    kpe = kva[..., KV_LORA:].float()
+    e, o = kpe[..., 0::2], kpe[..., 1::2]
+    re = e * cos - o * sin
+    im = o * cos + e * sin
+    rope = torch.stack([re, im], dim=-1).flatten(-2).to(torch.bfloat16)
+    return torch.cat([lat, rope], dim=-1)

@@ -1,0 +1,257 @@
+"""Tensor-level wrappers over the libdsv2 C ABI.
+
+Every function enqueues on the current torch CUDA stream, writes into caller-owned
+output tensors and never synchronises, so the whole decode step can be captured in
+a CUDA graph.  Validation mirrors the reference wrappers' checks (device, dtype,
+contiguity) and raises the same exception classes.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import (
+    DSV2_BF16, DSV2_F32, EPI_STORE_BF16, EPI_STORE_F32, EPI_SWIGLU, EPI_SCALE_F32,
+    FAMILY_SMALL, FAMILY_BATCH, LinearArgs, MlaDecodeArgs, MlaPrepArgs, RouterArgs,
+)
+
+__all__ = [
+    "stream", "rmsnorm", "add_rmsnorm", "embed_rmsnorm", "residual_add", "silu_mul",
+    "prepare_decode_inputs", "copy_token_to_cache", "advance_positions", "linear",
+    "router", "softmax_topk", "moe_bucket", "gather_rows", "mla_prep", "mla_decode",
+    "EPI_STORE_BF16", "EPI_STORE_F32", "EPI_SWIGLU", "EPI_SCALE_F32", "FAMILY_SMALL", "FAMILY_BATCH",
+]
+
+
+def stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _cuda(t: torch.Tensor, name: str) -> None:
+    if t.device.type != "cuda":
+        raise NotImplementedError(f"{name} must be a CUDA tensor")
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _wdtype(w: torch.Tensor) -> int:
+    if w.dtype == torch.bfloat16:
+        return DSV2_BF16
+    if w.dtype == torch.float32:
+        return DSV2_F32
+    raise NotImplementedError(f"unsupported weight dtype {w.dtype}")
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor) -> torch.Tensor:
+    """out[r] = bf16(x[r] * rsqrt(mean(x[r]^2) + eps) * w) for 2-D x (rows, cols)."""
+    _cuda(x, "x")
+    if x.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
+        raise NotImplementedError("rmsnorm supports bf16 activations")
+    if x.stride(-1) != 1 or out.stride(-1) != 1 or not w.is_contiguous():
+        raise NotImplementedError("rmsnorm requires a contiguous last dimension and weight")
+    rows, cols = x.shape
+    _lib.call("dsv2_rmsnorm", x.data_ptr(), x.stride(0), w.data_ptr(), _wdtype(w), out.data_ptr(),
+              out.stride(0), rows, cols, float(eps), stream())
+    return out
+
+
+def add_rmsnorm(h: torch.Tensor, delta: torch.Tensor | None, w: torch.Tensor | None, eps: float,
+                y: torch.Tensor | None, h_out: torch.Tensor | None = None) -> None:
+    """h(_out) = bf16(h + sum of delta parts); y = rmsnorm(h(_out)) * w.
+
+    delta: None, bf16 [rows, cols], or fp32 [rows, parts, cols] (summed over parts).
+    """
+    _cuda(h, "h")
+    rows, cols = h.shape
+    if delta is None:
+        dptr, ddt, nd, dps, drs = None, DSV2_BF16, 0, 0, 0
+    elif delta.dim() == 2:
+        if delta.dtype != torch.bfloat16:
+            raise NotImplementedError("2-D delta must be bf16")
+        dptr, ddt, nd, dps, drs = delta.data_ptr(), DSV2_BF16, 1, 0, delta.stride(0)
+    else:
+        if delta.dtype != torch.float32:
+            raise NotImplementedError("3-D delta (per-slot partials) must be fp32")
+        dptr, ddt, nd, dps, drs = delta.data_ptr(), DSV2_F32, delta.shape[1], delta.stride(1), delta.stride(0)
+    _lib.call("dsv2_add_rmsnorm", h.data_ptr(), _ptr(h_out), dptr, ddt, nd, dps, drs,
+              _ptr(w), _wdtype(w) if w is not None else DSV2_BF16, _ptr(y), rows, cols, float(eps), stream())
+
+
+def embed_rmsnorm(ids: torch.Tensor, table: torch.Tensor, w: torch.Tensor, eps: float,
+                  h: torch.Tensor, y: torch.Tensor) -> None:
+    if ids.dtype != torch.int64:
+        raise ValueError("ids must be int64")
+    rows, cols = h.shape
+    _lib.call("dsv2_embed_rmsnorm", ids.data_ptr(), table.data_ptr(), table.shape[0], w.data_ptr(),
+              _wdtype(w), h.data_ptr(), y.data_ptr(), rows, cols, float(eps), stream())
+
+
+def residual_add(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    _lib.call("dsv2_residual_add", a.data_ptr(), b.data_ptr(), out.data_ptr(), a.numel(), stream())
+    return out
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    _lib.call("dsv2_silu_mul", gate.data_ptr(), up.data_ptr(), out.data_ptr(), gate.numel(), stream())
+    return out
+
+
+def prepare_decode_inputs(cache_position: torch.Tensor, attention_mask: torch.Tensor | None,
+                          position_ids: torch.Tensor | None, attention_mask_index: torch.Tensor | None,
+                          batch: int, max_len: int) -> None:
+    _lib.call("dsv2_prepare_decode_inputs", cache_position.data_ptr(), cache_position.numel(),
+              _ptr(attention_mask), attention_mask.stride(0) if attention_mask is not None else 0,
+              _ptr(position_ids), position_ids.stride(0) if position_ids is not None else 0,
+              _ptr(attention_mask_index), batch, max_len, stream())
+
+
+def copy_token_to_cache(src: torch.Tensor, dst: torch.Tensor, cache_position: torch.Tensor) -> None:
+    """dst[b, h, pos_b, :] = src[b, h, 0, :]  (src [B, H, 1, D], dst [B, H, S, D])."""
+    ss = (ctypes.c_int64 * 3)(src.stride(0), src.stride(1), src.stride(3))
+    ds = (ctypes.c_int64 * 4)(*dst.stride())
+    _lib.call("dsv2_copy_token_to_cache", src.data_ptr(), ss, dst.data_ptr(), ds, cache_position.data_ptr(),
+              cache_position.numel(), src.shape[0], src.shape[1], src.shape[3], src.element_size(),
+              dst.shape[2], stream())
+
+
+def advance_positions(pos: torch.Tensor) -> None:
+    _lib.call("dsv2_advance_positions", pos.data_ptr(), pos.numel(), stream())
+
+
+def linear(*, w: torch.Tensor, n_rows: int, k: int, x: torch.Tensor, y: torch.Tensor,
+           family: int, epilogue: int = EPI_STORE_BF16,
+           w_row_stride: int | None = None, w_group_stride: int = 0, up_offset: int = 0,
+           x_row_stride: int | None = None, x_group_stride: int = 0,
+           y_row_stride: int | None = None, y_group_stride: int = 0,
+           n_groups: int = 1, n_tokens: int = 0,
+           group_offsets: torch.Tensor | None = None, max_routes_per_group: int = 0,
+           route_x_row: torch.Tensor | None = None, route_y_row: torch.Tensor | None = None,
+           route_scale: torch.Tensor | None = None,
+           w_group_rows: int | None = None, x_group_rows: int | None = None,
+           x_base: int | None = None) -> None:
+    """Generic linear (see dsv2_linear_args in include/dsv2.h).
+
+    Strides are in elements; defaults take them from the 2-D views of w / x / y.
+    x_base overrides x's data pointer (strided column views such as q_nope).
+    """
+    a = LinearArgs()
+    a.w = w.data_ptr()
+    a.w_row_stride = w.stride(-2) if w_row_stride is None else w_row_stride
+    a.w_group_stride = w_group_stride
+    a.up_offset = up_offset
+    a.n_rows = n_rows
+    a.k = k
+    a.x = x.data_ptr() if x_base is None else x_base
+    a.x_row_stride = x.stride(-2) if x_row_stride is None else x_row_stride
+    a.x_group_stride = x_group_stride
+    a.y = y.data_ptr()
+    a.y_row_stride = y.stride(-2) if y_row_stride is None else y_row_stride
+    a.y_group_stride = y_group_stride
+    a.epilogue = epilogue
+    a.n_groups = n_groups
+    a.n_tokens = n_tokens
+    a.max_routes_per_group = max_routes_per_group
+    a.group_offsets = _ptr(group_offsets)
+    a.route_x_row = _ptr(route_x_row)
+    a.route_y_row = _ptr(route_y_row)
+    a.route_scale = _ptr(route_scale)
+    a.w_group_rows = n_rows if w_group_rows is None else w_group_rows
+    a.x_group_rows = (n_tokens if x_group_rows is None else x_group_rows)
+    _lib.call("dsv2_linear", ctypes.byref(a), family, stream())
+
+
+def router(*, x: torch.Tensor, w: torch.Tensor, scaling: float, logits: torch.Tensor,
+           topk_ids32: torch.Tensor, topk_weights: torch.Tensor, topk_ids64: torch.Tensor | None = None,
+           bias: torch.Tensor | None = None, ticket: torch.Tensor | None = None,
+           expert_lo: int = 0, n_local: int = 0, shared_lo: int = 0, shared_hi: int = 0,
+           group_offsets: torch.Tensor | None = None, route_token: torch.Tensor | None = None,
+           route_slot: torch.Tensor | None = None, route_weight: torch.Tensor | None = None) -> None:
+    a = RouterArgs()
+    a.x = x.data_ptr()
+    a.x_row_stride = x.stride(0)
+    a.w = w.data_ptr()
+    a.w_dtype = _wdtype(w)
+    a.rows = x.shape[0]
+    a.hidden = x.shape[1]
+    a.n_experts = w.shape[0]
+    a.bias = _ptr(bias)
+    a.scaling = float(scaling)
+    a.logits = logits.data_ptr()
+    a.topk_ids64 = _ptr(topk_ids64)
+    a.topk_ids32 = topk_ids32.data_ptr()
+    a.topk_weights = topk_weights.data_ptr()
+    a.ticket = _ptr(ticket)
+    a.expert_lo, a.n_local, a.shared_lo, a.shared_hi = expert_lo, n_local, shared_lo, shared_hi
+    a.group_offsets = _ptr(group_offsets)
+    a.route_token = _ptr(route_token)
+    a.route_slot = _ptr(route_slot)
+    a.route_weight = _ptr(route_weight)
+    _lib.call("dsv2_router", ctypes.byref(a), stream())
+
+
+def softmax_topk(logits: torch.Tensor, scaling: float, topk_ids64: torch.Tensor | None,
+                 topk_ids32: torch.Tensor, topk_weights: torch.Tensor) -> None:
+    _lib.call("dsv2_softmax_topk", logits.data_ptr(), logits.shape[0], logits.shape[1], float(scaling),
+              _ptr(topk_ids64), topk_ids32.data_ptr(), topk_weights.data_ptr(), stream())
+
+
+def moe_bucket(topk_ids32: torch.Tensor, topk_weights: torch.Tensor, expert_lo: int, n_local: int,
+               shared_lo: int, shared_hi: int, group_offsets: torch.Tensor, route_token: torch.Tensor,
+               route_slot: torch.Tensor, route_weight: torch.Tensor) -> None:
+    _lib.call("dsv2_moe_bucket", topk_ids32.data_ptr(), topk_weights.data_ptr(), topk_ids32.shape[0],
+              expert_lo, n_local, shared_lo, shared_hi, group_offsets.data_ptr(), route_token.data_ptr(),
+              route_slot.data_ptr(), route_weight.data_ptr(), stream())
+
+
+def gather_rows(x: torch.Tensor, route_token: torch.Tensor, group_offsets: torch.Tensor,
+                n_groups: int, out: torch.Tensor, max_routes: int) -> None:
+    _lib.call("dsv2_gather_rows", x.data_ptr(), x.stride(0), route_token.data_ptr(),
+              group_offsets.data_ptr(), n_groups, out.data_ptr(), x.shape[1], max_routes, stream())
+
+
+def mla_prep(*, qkva: torch.Tensor, kv_norm_w: torch.Tensor, eps: float, cos: torch.Tensor,
+             sin: torch.Tensor, positions: torch.Tensor, cache: torch.Tensor,
+             q_pe_out: torch.Tensor) -> None:
+    """cache: [B, max_len, 576] (one layer, any batch stride); positions int64 [1] or [B]."""
+    a = MlaPrepArgs()
+    a.qkva = qkva.data_ptr()
+    a.qkva_row_stride = qkva.stride(0)
+    a.kv_norm_w = kv_norm_w.data_ptr()
+    a.eps = float(eps)
+    a.cos_tab = cos.data_ptr()
+    a.sin_tab = sin.data_ptr()
+    a.rope_stride = cos.stride(0)
+    a.rope_rows = cos.shape[0]
+    a.positions = positions.data_ptr()
+    a.pos_numel = positions.numel()
+    a.cache = cache.data_ptr()
+    a.cache_b_stride = cache.stride(0)
+    a.max_len = cache.shape[1]
+    a.q_pe_out = q_pe_out.data_ptr()
+    a.batch = qkva.shape[0]
+    _lib.call("dsv2_mla_prep", ctypes.byref(a), stream())
+
+
+def mla_decode(*, q_abs: torch.Tensor, q_pe: torch.Tensor, cache: torch.Tensor, positions: torch.Tensor,
+               softmax_scale: float, split_len: int, o_part: torch.Tensor, ml_part: torch.Tensor,
+               o_lat: torch.Tensor) -> None:
+    a = MlaDecodeArgs()
+    a.q_abs = q_abs.data_ptr()
+    a.q_pe = q_pe.data_ptr()
+    a.cache = cache.data_ptr()
+    a.cache_b_stride = cache.stride(0)
+    a.max_len = cache.shape[1]
+    a.positions = positions.data_ptr()
+    a.pos_numel = positions.numel()
+    a.softmax_scale = float(softmax_scale)
+    a.split_len = split_len
+    a.n_splits = o_part.shape[1]
+    a.o_part = o_part.data_ptr()
+    a.ml_part = ml_part.data_ptr()
+    a.o_lat = o_lat.data_ptr()
+    a.batch = q_abs.shape[0]
+    _lib.call("dsv2_mla_decode", ctypes.byref(a), stream())

@@ -1,0 +1,284 @@
+/*
+ * dsv2.h - C ABI of the B200 (sm_100a) DeepSeek-V2-Lite decode kernels (libdsv2.so).
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t passed as
+ * void*, enqueues its kernels on that stream and returns a status code.  Nothing
+ * here allocates device memory, synchronises the stream or reads device values on
+ * the host, so every call can be captured in a CUDA graph.  Work buffers are owned
+ * by the caller.  Integers are element counts/strides unless the name says bytes.
+ *
+ * Each function cites the reference (heiheiha798/Flash-DeepSeeek-V2-Lite) Python
+ * function whose behaviour it provides; the Python package re-exports those names
+ * on top of this ABI.
+ */
+#ifndef DSV2_H
+#define DSV2_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DSV2_API __attribute__((visibility("default")))
+#else
+#define DSV2_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes --------------------------------------------------------- */
+#define DSV2_OK 0
+#define DSV2_ERR_INVALID 1     /* bad argument (shape, alignment, null pointer)     */
+#define DSV2_ERR_LAUNCH 2      /* CUDA launch/driver error                          */
+#define DSV2_ERR_DEVICE 3      /* device error word set (bounded wait gave up, index) */
+#define DSV2_ERR_UNSUPPORTED 4 /* shape or dtype class the kernels do not cover      */
+
+/* ---- dtype codes ---------------------------------------------------------- */
+#define DSV2_BF16 0
+#define DSV2_F32 2
+
+/* ---- linear epilogues ----------------------------------------------------- */
+#define DSV2_EPI_STORE_BF16 0 /* y = bf16(acc)                                       */
+#define DSV2_EPI_STORE_F32 1  /* y = acc                                             */
+#define DSV2_EPI_SWIGLU 2     /* y = bf16(silu(bf16(gate)) * bf16(up)), fp32 math    */
+#define DSV2_EPI_SCALE_F32 3  /* y = bf16(acc) * route_scale[route] (fp32 store)     */
+
+/* ---- linear families ------------------------------------------------------ */
+#define DSV2_FAMILY_SMALL 0 /* mma.sync weight-streaming GEMV (<= 8 tokens per pass)  */
+#define DSV2_FAMILY_BATCH 1 /* tcgen05/TMEM tensor-core GEMM (up to 256 tokens/tile)  */
+
+/* Library version (major*100 + minor). */
+DSV2_API int dsv2_version(void);
+
+/* Text of the last host-side error of this thread (static storage). */
+DSV2_API const char* dsv2_last_error(void);
+
+/* One-time per-device setup: kernel attributes (large shared memory) and the SM
+ * count of the current device.  Must run outside stream capture; the other entry
+ * points call it lazily. */
+DSV2_API int dsv2_init(void);
+
+/* Reads (and optionally clears) the device error word of the current device.
+ * Synchronous (cudaMemcpyFromSymbol); call outside the hot loop. */
+DSV2_API int dsv2_get_device_error(int* code, int clear);
+
+/* RMSNorm: y[r] = bf16(x[r] * rsqrt(mean(x[r]^2) + eps) * w), fp32 math, one
+ * rounding.  cols % 8 == 0, cols <= 4096.  w_dtype DSV2_BF16 or DSV2_F32.
+ * Reference: rmsnorm_triton, triton_kernels/rmsnorm.py:60-95 (kernel :8-57). */
+DSV2_API int dsv2_rmsnorm(const void* x, int64_t x_row_stride, const void* w, int w_dtype, void* y,
+                 int64_t y_row_stride, int rows, int cols, float eps, void* stream);
+
+/* Fused residual add + RMSNorm (two outputs):
+ *   h_out[r] = bf16(h[r] + sum_p delta[r, p]),  y[r] = rmsnorm(h_out[r]) * w.
+ * delta_dtype DSV2_BF16: delta rows at delta_row_stride, parts at delta_part_stride;
+ * DSV2_F32: same, fp32 (MoE per-slot partials).  n_delta == 0 skips the add.
+ * h_out == NULL updates h in place; y == NULL skips the norm.  h rows are contiguous.
+ * Reference: residual_add_triton (attention_prepost.py:191-223) followed by
+ * rmsnorm_triton, as applied per decoder layer in src/run.py:459-493. */
+DSV2_API int dsv2_add_rmsnorm(void* h, void* h_out, const void* delta, int delta_dtype, int n_delta,
+                     int64_t delta_part_stride, int64_t delta_row_stride, const void* w,
+                     int w_dtype, void* y, int rows, int cols, float eps, void* stream);
+
+/* Embedding gather + first input RMSNorm: h[r] = table[ids[r]]; y[r] = rmsnorm(h[r]) * w.
+ * ids are int64; an id outside [0, vocab) sets the device error word and reads row 0.
+ * Reference: the HF embedding + input_layernorm at the top of the decode step
+ * (src/run.py:574-581 through model.forward). */
+DSV2_API int dsv2_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, const void* w,
+                       int w_dtype, void* h, void* y, int rows, int cols, float eps,
+                       void* stream);
+
+/* out = bf16(a + b) over n contiguous bf16 elements (n % 8 == 0).
+ * Reference: residual_add_triton, triton_kernels/attention_prepost.py:191-223. */
+DSV2_API int dsv2_residual_add(const void* a, const void* b, void* out, int64_t n, void* stream);
+
+/* out = bf16(silu(gate) * up) over n contiguous bf16 elements (n % 8 == 0).
+ * Reference: silu_mul_triton, triton_kernels/mlp_elementwise.py:24-45. */
+DSV2_API int dsv2_silu_mul(const void* gate, const void* up, void* out, int64_t n, void* stream);
+
+/* attention_mask[b, s] = (attention_mask_index[s] <= pos_b), position_ids[b] = pos_b,
+ * pos_b = cache_position[pos_numel == 1 ? 0 : b] (int64 everywhere).  Either output
+ * may be NULL.  Reference: prepare_decode_inputs_triton, attention_prepost.py:152-188. */
+DSV2_API int dsv2_prepare_decode_inputs(const int64_t* cache_position, int pos_numel,
+                               int64_t* attention_mask, int64_t mask_stride_b,
+                               int64_t* position_ids, int64_t position_ids_stride_b,
+                               const int64_t* attention_mask_index, int batch, int max_len,
+                               void* stream);
+
+/* dst[b, h, pos_b, :] = src[b, h, 0, :] with element strides src_strides = {b, h, d},
+ * dst_strides = {b, h, s, d}; elem_size 2 or 4.  A position outside [0, max_len)
+ * sets the device error word and skips the row.
+ * Reference: copy_single_token_to_cache, attention_prepost.py:113-149. */
+DSV2_API int dsv2_copy_token_to_cache(const void* src, const int64_t* src_strides, void* dst,
+                             const int64_t* dst_strides, const int64_t* cache_position,
+                             int pos_numel, int batch, int heads, int dim, int elem_size,
+                             int max_len, void* stream);
+
+/* pos[i] += 1 for i < n (int64): the cache_position.add_(1) that closes each captured
+ * decode step (src/run.py:588). */
+DSV2_API int dsv2_advance_positions(int64_t* pos, int n, void* stream);
+
+/* ---- linear layers --------------------------------------------------------- */
+/* Y[row_y(t), n] = epilogue( sum_k W_g[n, k] * X_g[row_x(t), k] ) for every group g,
+ * output feature n < n_rows and token t of the group.
+ *   W_g = w + g * w_group_stride, rows at w_row_stride (bf16, 16-byte aligned rows)
+ *   X_g = x + g * x_group_stride, rows at x_row_stride
+ *   Y_g = y + g * y_group_stride, rows at y_row_stride
+ * Dense mode (group_offsets == NULL): every group has n_tokens tokens, row_x = row_y = t.
+ * Grouped mode: group g owns routes [group_offsets[g], group_offsets[g+1]) (device
+ * memory, read by the kernel); row_x(r) = route_x_row ? route_x_row[r] : r,
+ * row_y(r) = route_y_row ? route_y_row[r] : r, and max_routes_per_group bounds every
+ * group's route count.  SwiGLU: the up row of feature n is W_g row n + up_offset/w_row_stride.
+ * k % 32 == 0 (small family) / k % 64 == 0 (batch family).  The batch family also needs
+ * w_group_rows / x_group_rows (rows spanned by one group of W / X, for the TMA bounds)
+ * and route_x_row == NULL.
+ * Reference: _gemv_contig_kernel / _small_batch_gemv_kernel (attention_decode_small.py:54-137,
+ * :857-901), _batched_linear_kernel (attention_decode_batch.py:420-468), the grouped MoE
+ * GEMMs (moe_batch.py:151-307, moe_small_gemv.py:52-158). */
+typedef struct dsv2_linear_args {
+  const void* w;
+  int64_t w_row_stride;
+  int64_t w_group_stride;
+  int64_t up_offset;
+  int32_t n_rows;
+  int32_t k;
+  const void* x;
+  int64_t x_row_stride;
+  int64_t x_group_stride;
+  void* y;
+  int64_t y_row_stride;
+  int64_t y_group_stride;
+  int32_t epilogue;
+  int32_t n_groups;
+  int32_t n_tokens;
+  int32_t max_routes_per_group;
+  const int32_t* group_offsets;
+  const int32_t* route_x_row;
+  const int32_t* route_y_row;
+  const float* route_scale;
+  int64_t w_group_rows;
+  int64_t x_group_rows;
+} dsv2_linear_args;
+
+DSV2_API int dsv2_linear(const dsv2_linear_args* args, int family, void* stream);
+
+/* ---- MoE routing ------------------------------------------------------------ */
+/* Fused gate GEMV (fp32 over bf16 activations) + softmax + top-6 + bucketing, one launch.
+ *   logits[r, e] = sum_k x[r, k] * w[e, k] (+ bias[e]);  p = softmax(logits[r]);
+ *   topk_ids / topk_weights = 6 largest p (descending, lowest index first on ties),
+ *   weights multiplied by `scaling` (routed_scaling_factor).
+ * When group_offsets != NULL the routes of experts [expert_lo, expert_lo + n_local) are
+ * bucketed (stable, ascending (token, k) order) into n_local groups followed by two
+ * shared-expert groups holding rows [shared_lo, shared_hi) with weight 1:
+ *   group_offsets[n_local + 3], route_token / route_slot / route_weight[6*rows + 2*shared rows],
+ *   route_slot = token * 8 + k (k = 0..5 routed, 6..7 the two shared-expert halves).
+ * ticket: one int32 in device memory, zero before the first call; the kernel leaves it zero.
+ * logits: [rows, n_experts] fp32 work buffer.  topk_ids64 may be NULL.
+ * Reference: router_softmax_topk6_triton (moe_router.py:63-86) with the fp32 gate linear of
+ * src/run.py:257-275, and the bucketing of packed_routed_moe (moe_batch.py:101-148, 425-470). */
+typedef struct dsv2_router_args {
+  const void* x;
+  int64_t x_row_stride;
+  const void* w;
+  int32_t w_dtype;
+  int32_t rows;
+  int32_t hidden;
+  int32_t n_experts;
+  const float* bias;
+  float scaling;
+  float* logits;
+  int64_t* topk_ids64;
+  int32_t* topk_ids32;
+  float* topk_weights;
+  uint32_t* ticket;
+  int32_t expert_lo;
+  int32_t n_local;
+  int32_t shared_lo;
+  int32_t shared_hi;
+  int32_t* group_offsets;
+  int32_t* route_token;
+  int32_t* route_slot;
+  float* route_weight;
+} dsv2_router_args;
+
+DSV2_API int dsv2_router(const dsv2_router_args* args, void* stream);
+
+/* Softmax + top-6 over precomputed fp32 logits [rows, n_experts] (n_experts <= 64).
+ * Reference: router_softmax_topk6_triton, triton_kernels/moe_router.py:63-86. */
+DSV2_API int dsv2_softmax_topk(const float* logits, int rows, int n_experts, float scaling,
+                      int64_t* topk_ids64, int32_t* topk_ids32, float* topk_weights,
+                      void* stream);
+
+/* Bucketing alone (expert parallel: after the all-gather of the top-k results); same
+ * outputs as dsv2_router.  Reference: moe_batch.py:101-148. */
+DSV2_API int dsv2_moe_bucket(const int32_t* topk_ids32, const float* topk_weights, int rows,
+                    int expert_lo, int n_local, int shared_lo, int shared_hi,
+                    int32_t* group_offsets, int32_t* route_token, int32_t* route_slot,
+                    float* route_weight, void* stream);
+
+/* out[r] = x[route_token[r]] for r < group_offsets[n_groups] (r < max_routes): gathers
+ * activations into expert-contiguous rows for the batch family.  cols % 8 == 0. */
+DSV2_API int dsv2_gather_rows(const void* x, int64_t x_row_stride, const int32_t* route_token,
+                     const int32_t* group_offsets, int n_groups, void* out, int cols,
+                     int max_routes, void* stream);
+
+/* ---- multi-head latent attention ----------------------------------------------- */
+/* New-token preparation for one layer: from qkva[b] = [q (16 x 192) | c_kv (512) | k_pe (64)]
+ *   cache[b, pos_b, 0:512]   = bf16(rmsnorm(c_kv) * kv_norm_w)
+ *   cache[b, pos_b, 512:576] = rope(k_pe, pos_b)          (interleaved pairs 2j, 2j+1)
+ *   q_pe_out[b, h, :]        = rope(q[b, h, 128:192], pos_b)
+ * cos/sin: [rope_rows, rope_stride] fp32, entries 0..31 used (attention scaling folded in).
+ * Reference: _build_qkv_rope_kernel + _cache_write_q1_dual_kernel
+ * (attention_decode_small.py:140-339) and the kv-a RMSNorm (:581). */
+typedef struct dsv2_mla_prep_args {
+  const void* qkva;
+  int64_t qkva_row_stride;
+  const void* kv_norm_w;
+  float eps;
+  const float* cos_tab;
+  const float* sin_tab;
+  int64_t rope_stride;
+  int32_t rope_rows;
+  const int64_t* positions;
+  int32_t pos_numel;
+  void* cache;
+  int64_t cache_b_stride;
+  int32_t max_len;
+  void* q_pe_out;
+  int32_t batch;
+} dsv2_mla_prep_args;
+
+DSV2_API int dsv2_mla_prep(const dsv2_mla_prep_args* args, void* stream);
+
+/* Split-KV latent attention for q_len = 1:
+ *   score[h, s] = softmax_scale * (q_abs[b, h] . cache[b, s, :512] + q_pe[b, h] . cache[b, s, 512:])
+ *   o_lat[b, h] = sum_{s <= pos_b} softmax(score)[h, s] * cache[b, s, :512]   (bf16 out)
+ * for 16 heads.  split_len (multiple of 64) positions per CTA; o_part [batch, n_splits,
+ * 16, 512] and ml_part [batch, n_splits, 16, 2] fp32 are caller work buffers with
+ * n_splits >= ceil(max_len / split_len).  Runs the split kernel and the merge kernel.
+ * Reference: _decode_attention_q1_kernel / _batched_decode_attention_q1_kernel
+ * (attention_decode_small.py:342-423, attention_decode_batch.py:240-342) over the
+ * expanded cache; here over the latent cache. */
+typedef struct dsv2_mla_decode_args {
+  const void* q_abs;
+  const void* q_pe;
+  const void* cache;
+  int64_t cache_b_stride;
+  int32_t max_len;
+  const int64_t* positions;
+  int32_t pos_numel;
+  float softmax_scale;
+  int32_t split_len;
+  int32_t n_splits;
+  float* o_part;
+  float* ml_part;
+  void* o_lat;
+  int32_t batch;
+} dsv2_mla_decode_args;
+
+DSV2_API int dsv2_mla_decode(const dsv2_mla_decode_args* args, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSV2_H */

@@ -1,0 +1,209 @@
+"""CPU tests: the C-ABI library loads and exports the declared symbols, and the oracle
+restatement (oracle/ops.py) reproduces the reference's own kernel outputs and the HF
+model's decode trace (golden fixtures under tests/golden/)."""
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from oracle import ops as O
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+def header_symbols():
+    text = (REPO / "include" / "dsv2.h").read_text()
+    return sorted(set(re.findall(r"DSV2_API\s+[\w\s\*]+?\b(dsv2_\w+)\s*\(", text)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    from dsv2 import _lib
+    lib = _lib.load()
+    syms = header_symbols()
+    assert len(syms) >= 19
+    for s in syms:
+        assert hasattr(lib, s), s
+    assert set(syms) == set(_lib.EXPORTED)
+    assert lib.dsv2_version() >= 100
+
+
+def test_ops_fail_loudly_without_valid_args():
+    from dsv2 import _lib
+    with pytest.raises(ValueError):
+        _lib.call("dsv2_rmsnorm", None, 0, None, 0, None, 0, 1, 2048, 1e-6, None)
+    with pytest.raises(NotImplementedError):
+        _lib.call("dsv2_rmsnorm", 16, 2048, 16, 0, 16, 2048, 1, 4100, 1e-6, None)
+
+
+def trunc_bf16(x: torch.Tensor) -> torch.Tensor:
+    """fp32 -> bf16 rounding toward zero: the Triton CPU interpreter's conversion, so the
+    golden bf16 outputs of the reference kernels are truncations (on a GPU Triton rounds
+    to nearest even, like the oracle and libdsv2)."""
+    return (x.float().contiguous().view(torch.int32) & ~0xFFFF).view(torch.float32).to(torch.bfloat16)
+
+
+def test_oracle_rmsnorm_residual_silu_vs_reference_golden(golden_ref):
+    for key in ("rmsnorm_2048", "rmsnorm_512"):
+        g = golden_ref[key]
+        y = O.rmsnorm(g["x"], g["w"], g["eps"])
+        # round-to-nearest oracle vs truncated golden: one bf16 ulp
+        torch.testing.assert_close(y.float(), g["y"].float(), rtol=2 ** -7, atol=1e-6)
+        xf = g["x"].float()
+        y32 = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + g["eps"]) * g["w"].float()
+        assert (trunc_bf16(y32) != g["y"]).float().mean() < 1e-3
+    g = golden_ref["residual_add"]
+    assert torch.equal(trunc_bf16(g["a"].float() + g["b"].float()), g["out"])
+    torch.testing.assert_close(O.residual_add(g["a"], g["b"]).float(), g["out"].float(), rtol=2 ** -7, atol=0)
+    g = golden_ref["silu_mul"]
+    gf = g["gate"].float()
+    s32 = gf * torch.sigmoid(gf) * g["up"].float()
+    assert (trunc_bf16(s32) != g["out"]).float().mean() < 1e-3
+    torch.testing.assert_close(O.silu_mul(g["gate"], g["up"]).float(), g["out"].float(), rtol=2 ** -7, atol=1e-6)
+
+
+def test_oracle_router_vs_reference_golden(golden_ref):
+    g = golden_ref["router_topk6"]
+    ids, w = O.softmax_topk6(g["logits"], g["scaling"])
+    assert torch.equal(ids, g["ids"])  # including the exact tie in row 0 (lowest index first)
+    torch.testing.assert_close(w, g["weights"], rtol=1e-6, atol=1e-8)
+
+
+def test_oracle_prepare_inputs_and_cache_copy_vs_golden(golden_ref):
+    g = golden_ref["prepare_decode_inputs"]
+    mask, pid = O.prepare_decode_inputs(g["cache_position"], g["attention_mask_index"], g["batch"])
+    assert torch.equal(mask, g["attention_mask"]) and torch.equal(pid, g["position_ids"])
+    g = golden_ref["copy_single_token_to_cache"]
+    dst = O.copy_single_token_to_cache(g["src"], g["dst_before"].clone(), g["cache_position"])
+    assert torch.equal(dst, g["dst_after"])
+
+
+def test_oracle_rope_vs_reference_golden(golden_ref):
+    g = golden_ref["build_qkv_rope"]
+    p = int(g["position"])
+    c, s = g["cos"][p, :32], g["sin"][p, :32]
+    torch.testing.assert_close(O.rope_half_split(g["q_proj"][:, 128:], c, s).float(), g["q_out"][:, 128:].float(),
+                               rtol=2 ** -7, atol=1e-6)
+    assert torch.equal(g["q_out"][:, :128], g["q_proj"][:, :128])
+    torch.testing.assert_close(O.rope_half_split(g["k_pe"], c, s).float(), g["k_new"][0, 128:].float(),
+                               rtol=2 ** -7, atol=1e-6)
+    # interleaved and half-split layouts give the same q.k
+    qi = O.rope_interleaved(g["q_proj"][:, 128:], c, s).float()
+    ki = O.rope_interleaved(g["k_pe"], c, s).float()
+    qh = O.rope_half_split(g["q_proj"][:, 128:], c, s).float()
+    kh = O.rope_half_split(g["k_pe"], c, s).float()
+    torch.testing.assert_close(qi @ ki, qh @ kh, rtol=1e-5, atol=1e-4)
+
+
+def test_oracle_attention_vs_reference_golden(golden_ref):
+    g = golden_ref["batched_attention"]
+    n = int(g["cache_position"]) + 1
+    out = O.expanded_attention_decode(g["q"][:, :, 0], g["k"], g["v"], [n] * g["q"].shape[0], g["scale"])
+    err = (out - g["out"][:, :, 0].double()).abs().max() / g["out"].double().abs().max()
+    assert err < 1e-2
+
+
+def test_absorbed_attention_equals_expanded():
+    """Absorbed MLA over the latent cache == expanded attention with K = [W_UK c | k_pe], V = W_UV c."""
+    g = torch.Generator().manual_seed(0)
+    B, S, L = 2, 40, 33
+    cache = torch.randn(B, S, 576, generator=g).double()
+    w_uk = torch.randn(16, 128, 512, generator=g).double() * 0.05
+    w_uv = torch.randn(16, 128, 512, generator=g).double() * 0.05
+    q_nope = torch.randn(B, 16, 128, generator=g).double()
+    q_pe = torch.randn(B, 16, 64, generator=g).double()
+    k = torch.cat([torch.einsum("hdc,bsc->bhsd", w_uk, cache[..., :512]),
+                   cache[:, None, :, 512:].expand(B, 16, S, 64)], -1)
+    v = torch.einsum("hvc,bsc->bhsv", w_uv, cache[..., :512])
+    ref = O.expanded_attention_decode(torch.cat([q_nope, q_pe], -1), k, v, [L] * B, 0.07)
+    o_lat = O.mla_decode(torch.einsum("bhd,hdc->bhc", q_nope, w_uk), q_pe, cache, [L] * B, 0.07)
+    out = torch.einsum("bhc,hvc->bhv", o_lat, w_uv)
+    torch.testing.assert_close(out, ref, rtol=1e-9, atol=1e-9)
+
+
+def test_bucket_is_stable_and_complete():
+    g = torch.Generator().manual_seed(1)
+    ids = torch.stack([torch.randperm(64, generator=g)[:6] for _ in range(10)])
+    w = torch.rand(10, 6, generator=g)
+    go, tok, slot, wt = O.bucket(ids, w, 0, 64, 0, 10)
+    assert int(go[-1]) == 10 * 8
+    for e in range(64):
+        a, b = int(go[e]), int(go[e + 1])
+        assert all(int(ids.view(-1)[int(slot[i]) // 8 * 6 + int(slot[i]) % 8]) == e for i in range(a, b))
+        assert tok[a:b].tolist() == sorted(tok[a:b].tolist())
+    assert slot[int(go[64]):].tolist() == [b * 8 + 6 for b in range(10)] + [b * 8 + 7 for b in range(10)]
+
+
+@pytest.fixture(scope="module")
+def hf2():
+    from oracle.hf_model import build_model, dsv2_lite_config
+    return build_model(dsv2_lite_config(num_layers=2), seed=0, device="cpu", dtype=torch.float32)
+
+
+def test_hf_oracle_reproduces_config1_golden(hf2, golden_hf):
+    """BASELINE config 1 (2 layers, fp32, seed 0, 128-token prompt): the HF oracle's greedy
+    tokens, hidden states and router choices are reproducible from the seed."""
+    from transformers import DynamicCache
+    cache = DynamicCache(config=hf2.config)
+    with torch.no_grad():
+        out = hf2(input_ids=golden_hf["prompt"].view(1, -1), past_key_values=cache, use_cache=True)
+        tok = out.logits[:, -1].argmax(-1, keepdim=True)
+        assert int(tok) == int(golden_hf["generated"][0])
+        out = hf2(input_ids=tok, past_key_values=cache, use_cache=True, output_hidden_states=True)
+    hid = torch.stack([h[0, -1] for h in out.hidden_states])
+    torch.testing.assert_close(hid, golden_hf["hidden_step1"], rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(out.logits[0, -1], golden_hf["logits_step1"], rtol=1e-4, atol=1e-4)
+
+
+def test_oracle_restatement_matches_hf_decode_layer(hf2, golden_hf):
+    """The absorbed-latent attention and the MoE restatement reproduce HF's own decode of
+    config 1 (first decode step, both layers) to bf16-level tolerance."""
+    from transformers import DynamicCache
+    from dsv2.model import rope_tables  # pure torch helper (no kernels)
+    m = hf2
+    prompt = golden_hf["prompt"]
+    T = prompt.numel()
+    cos, sin = rope_tables(m, T + 4, "cpu")
+    # latent cache of the prompt from HF's own kv_a projections
+    caps = {}
+    hooks = [l.self_attn.kv_a_proj_with_mqa.register_forward_hook(
+        lambda mod, i, o, li=li: caps.__setitem__(li, o)) for li, l in enumerate(m.model.layers)]
+    cache = DynamicCache(config=m.config)
+    with torch.no_grad():
+        m(input_ids=prompt.view(1, -1), past_key_values=cache, use_cache=True)
+    for h in hooks:
+        h.remove()
+    lat = []
+    for li, layer in enumerate(m.model.layers):
+        a = layer.self_attn
+        rows = torch.zeros(1, T + 4, 576, dtype=torch.bfloat16)
+        rows[0, :T] = O.latent_row(caps[li][0].to(torch.bfloat16), a.kv_a_layernorm.weight.to(torch.bfloat16),
+                                   a.kv_a_layernorm.variance_epsilon, cos[:T], sin[:T])
+        lat.append(rows)
+    tok = golden_hf["generated"][0]
+    h = m.model.embed_tokens.weight[tok].view(1, -1).float()
+    pos = torch.tensor([T])
+    hidden = [h.clone()]
+    for li, layer in enumerate(m.model.layers):
+        x = O.rmsnorm(h.to(torch.bfloat16), layer.input_layernorm.weight.to(torch.bfloat16), 1e-6)
+        a = layer.self_attn
+        attn = O.absorbed_attention_layer(x, a, lat[li], pos, cos, sin, a.scaling)
+        h = h + attn.float()
+        x = O.rmsnorm(h.to(torch.bfloat16), layer.post_attention_layernorm.weight.to(torch.bfloat16), 1e-6)
+        mlp = layer.mlp
+        if hasattr(mlp, "experts"):
+            _, ids, w = O.router(x, mlp.gate.weight, float(mlp.routed_scaling_factor))
+            assert set(ids[0].tolist()) == set(golden_hf["routes"][0].tolist())
+            sh = mlp.shared_experts
+            y = O.moe(x, ids, w, mlp.experts.gate_up_proj, mlp.experts.down_proj, sh.gate_proj.weight,
+                      sh.up_proj.weight, sh.down_proj.weight)
+        else:
+            y = O.expert_mlp(x, torch.cat([mlp.gate_proj.weight, mlp.up_proj.weight]), mlp.down_proj.weight).float()
+        h = h + y
+        hidden.append(h.clone())
+    ref = golden_hf["hidden_step1"]
+    # HF replaces hidden_states[-1] with the final-norm output (capture_outputs tie_last_hidden_states)
+    hidden[-1] = m.model.norm(hidden[-1])
+    for li in range(len(hidden)):
+        err = float((hidden[li][0] - ref[li]).abs().max() / ref[li].abs().max())
+        assert err < 2e-2, (li, err)
