@@ -70,10 +70,10 @@ class DecodeEngine:
             for l in model.model.layers
         ]
         self.L = len(self.layers)
-        self.embed = model.model.embed_tokens.weight
-        self.final_norm_w = model.model.norm.weight
+        self.embed = model.model.embed_tokens.weight.detach()
+        self.final_norm_w = model.model.norm.weight.detach()
         self.final_eps = float(model.model.norm.variance_epsilon)
-        self.lm_head = model.lm_head.weight
+        self.lm_head = model.lm_head.weight.detach()
         self.vocab = int(self.lm_head.shape[0])
         self.scale = float(model.model.layers[0].self_attn.scaling)
         self.cos, self.sin = rope_tables(model, self.max_len, self.dev)
@@ -261,6 +261,7 @@ class DecodeEngine:
         return ms, float(nbytes), 2 * len(moe_layers)
 
     # ------------------------------------------------------------------ step
+    @torch.no_grad()
     def step(self, trace: dict | None = None) -> None:
         """One q_len = 1 decode step for every row (kernel launches only; graph-capturable).
 

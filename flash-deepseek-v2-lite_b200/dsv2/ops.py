@@ -213,10 +213,24 @@ def gather_rows(x: torch.Tensor, route_token: torch.Tensor, group_offsets: torch
               group_offsets.data_ptr(), n_groups, out.data_ptr(), x.shape[1], max_routes, stream())
 
 
+def _check_cache(cache: torch.Tensor) -> None:
+    _cuda(cache, "cache")
+    if cache.dim() != 3 or cache.shape[2] != 576 or cache.stride(2) != 1 or cache.stride(1) != 576:
+        raise NotImplementedError("latent cache must be [B, max_len, 576] with contiguous 576-wide rows")
+
+
 def mla_prep(*, qkva: torch.Tensor, kv_norm_w: torch.Tensor, eps: float, cos: torch.Tensor,
              sin: torch.Tensor, positions: torch.Tensor, cache: torch.Tensor,
              q_pe_out: torch.Tensor) -> None:
     """cache: [B, max_len, 576] (one layer, any batch stride); positions int64 [1] or [B]."""
+    _cuda(qkva, "qkva")
+    if qkva.dtype != torch.bfloat16 or qkva.stride(1) != 1 or qkva.shape[1] != 3648:
+        raise NotImplementedError("mla_prep expects bf16 qkva [B, 3648] with contiguous rows")
+    if not q_pe_out.is_contiguous() or cos.stride(1) != 1 or sin.stride(1) != 1:
+        raise NotImplementedError("mla_prep requires contiguous q_pe_out and rope tables")
+    if cos.dtype != torch.float32 or sin.dtype != torch.float32:
+        raise NotImplementedError("rope tables must be fp32")
+    _check_cache(cache)
     a = MlaPrepArgs()
     a.qkva = qkva.data_ptr()
     a.qkva_row_stride = qkva.stride(0)
@@ -239,6 +253,15 @@ def mla_prep(*, qkva: torch.Tensor, kv_norm_w: torch.Tensor, eps: float, cos: to
 def mla_decode(*, q_abs: torch.Tensor, q_pe: torch.Tensor, cache: torch.Tensor, positions: torch.Tensor,
                softmax_scale: float, split_len: int, o_part: torch.Tensor, ml_part: torch.Tensor,
                o_lat: torch.Tensor) -> None:
+    for name, t in (("q_abs", q_abs), ("q_pe", q_pe), ("o_part", o_part), ("ml_part", ml_part), ("o_lat", o_lat)):
+        _cuda(t, name)
+        if not t.is_contiguous():
+            raise NotImplementedError(f"mla_decode requires a contiguous {name}")
+    if q_abs.dtype != torch.bfloat16 or q_pe.dtype != torch.bfloat16 or cache.dtype != torch.bfloat16:
+        raise NotImplementedError("mla_decode supports bf16 queries and cache only")
+    if tuple(q_abs.shape[1:]) != (16, 512) or tuple(q_pe.shape[1:]) != (16, 64):
+        raise ValueError("q_abs must be [B, 16, 512] and q_pe [B, 16, 64]")
+    _check_cache(cache)
     a = MlaDecodeArgs()
     a.q_abs = q_abs.data_ptr()
     a.q_pe = q_pe.data_ptr()

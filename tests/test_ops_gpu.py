@@ -219,7 +219,7 @@ def test_mla_decode_matches_reference_expanded_attention(D, golden_ref):
     q = torch.cat([q_nope, q_pe.float()], -1)
     scale = 192 ** -0.5
     ref = O.expanded_attention_decode(q, k, v, [L] * B, scale)
-    q_abs = torch.einsum("bhd,hdc->bhc", q_nope, w_uk).to(torch.bfloat16)
+    q_abs = torch.einsum("bhd,hdc->bhc", q_nope, w_uk).to(torch.bfloat16).contiguous()
     o_part = torch.zeros(B, 2, 16, 512, device=DEV)
     ml = torch.zeros(B, 2, 16, 2, device=DEV)
     o_lat = torch.zeros(B, 16, 512, dtype=torch.bfloat16, device=DEV)
