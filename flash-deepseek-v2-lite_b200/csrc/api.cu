@@ -492,4 +492,53 @@ int dsv2_mla_decode(const dsv2_mla_decode_args* a, void* stream) {
                       "mla_combine");
 }
 
+// Same computation as dsv2_mla_decode, with the split partials kept in the library's
+// fixed device array instead of caller buffers (no allocation of any kind here).
+int dsv2_mla_decode_noalloc(const void* q_abs, const void* q_pe, const void* cache,
+                            int64_t cache_b_stride, int max_len, const int64_t* positions,
+                            int pos_numel, float softmax_scale, int split_len, void* o_lat,
+                            int batch, void* stream) {
+  if (!q_abs || !q_pe || !cache || !positions || !o_lat)
+    return fail(DSV2_ERR_INVALID, "mla_decode_noalloc: null pointer");
+  if (split_len <= 0 || split_len % 64 || max_len <= 0)
+    return fail(DSV2_ERR_INVALID, "mla_decode_noalloc: split_len %d must be a positive multiple of 64",
+                split_len);
+  if (pos_numel != 1 && pos_numel != batch)
+    return fail(DSV2_ERR_INVALID, "mla_decode_noalloc: positions numel %d for batch %d", pos_numel, batch);
+  if (!aligned16(q_abs) || !aligned16(q_pe) || !aligned16(cache) || cache_b_stride % 8)
+    return fail(DSV2_ERR_INVALID, "mla_decode_noalloc: operands must be 16-byte aligned");
+  if (batch <= 0) return DSV2_OK;
+  const long long n_splits = (static_cast<long long>(max_len) + split_len - 1) / split_len;
+  if (static_cast<long long>(batch) * n_splits > kNoAllocMaxParts)
+    return fail(DSV2_ERR_INVALID,
+                "mla_decode_noalloc: batch * ceil(max_len / split_len) = %lld exceeds the %d split "
+                "partials of the built-in scratch; raise split_len or use dsv2_mla_decode",
+                static_cast<long long>(batch) * n_splits, kNoAllocMaxParts);
+  int rc = ensure_init(nullptr);
+  if (rc) return rc;
+  float* scratch = nullptr;
+  cudaError_t e = mla_noalloc_scratch(&scratch);
+  if (e != cudaSuccess) return check_launch(e, "mla_decode_noalloc: scratch address");
+  float* o_part = scratch;
+  float* ml_part = scratch + static_cast<size_t>(kNoAllocMaxParts) * kHeads * kLatent;
+  MlaDecodeParams p;
+  p.q_abs = reinterpret_cast<const bf16*>(q_abs);
+  p.q_pe = reinterpret_cast<const bf16*>(q_pe);
+  p.cache = reinterpret_cast<const bf16*>(cache);
+  p.cache_b_stride = cache_b_stride;
+  p.max_len = max_len;
+  p.positions = reinterpret_cast<const long long*>(positions);
+  p.pos_numel = pos_numel;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.split_len = split_len;
+  p.n_splits = static_cast<int>(n_splits);
+  p.o_part = o_part;
+  p.ml_part = ml_part;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = check_launch(launch_mla_decode(p, batch, st), "mla_decode_noalloc");
+  if (rc) return rc;
+  return check_launch(launch_mla_combine(o_part, ml_part, p.n_splits, o_lat, batch, st),
+                      "mla_decode_noalloc: combine");
+}
+
 }  // extern "C"

@@ -338,6 +338,36 @@ __global__ __launch_bounds__(128) void mla_combine_kernel(const float* __restric
   *reinterpret_cast<uint2*>(o_lat + (static_cast<long long>(b) * kHeads + h) * kLatent + d) = o;
 }
 
+// ----------------------------------------------------------------------------
+// Scratch for dsv2_mla_decode_noalloc: the split partials (o: [parts, 16, 512] then
+// (m, l): [parts, 16, 2], parts = batch * n_splits <= kNoAllocMaxParts) in one
+// fixed file-scope device array, so that entry point allocates nothing.  Every GPU
+// that loads the library holds these 8.4 MB until the process exits.  Host code
+// must not use the symbol as a pointer: its device address is looked up once per
+// device with cudaGetSymbolAddress (below) and passed to the kernels.
+// ----------------------------------------------------------------------------
+constexpr int kNoAllocMaxParts = 256;
+constexpr size_t kNoAllocFloats =
+    static_cast<size_t>(kNoAllocMaxParts) * kHeads * (kLatent + 2);
+static __device__ __align__(256) float g_mla_noalloc_scratch[kNoAllocFloats];
+static float* g_mla_noalloc_ptr[128];
+
+// Device address of the scratch array on the current device (looked up on first use).
+cudaError_t mla_noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+  if (!g_mla_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_mla_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    g_mla_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_mla_noalloc_ptr[dev];
+  return cudaSuccess;
+}
+
 constexpr size_t mla_decode_smem_bytes() {
   return kQBytes + kStages * kTileBytes + 4 * kHeads * kSRedStride * sizeof(float) +
          kHeads * kPStride * sizeof(bf16) + kHeads * sizeof(float);

@@ -102,6 +102,8 @@ _SIGNATURES = {
     "dsv2_gather_rows": ([c_vp, c_i64, c_vp, c_vp, c_i32, c_vp, c_i32, c_i32, c_vp], c_i32),
     "dsv2_mla_prep": ([ctypes.POINTER(MlaPrepArgs), c_vp], c_i32),
     "dsv2_mla_decode": ([ctypes.POINTER(MlaDecodeArgs), c_vp], c_i32),
+    "dsv2_mla_decode_noalloc": ([c_vp, c_vp, c_vp, c_i64, c_i32, c_vp, c_i32, c_f32, c_i32, c_vp, c_i32, c_vp],
+                                c_i32),
 }
 
 EXPORTED = tuple(_SIGNATURES)

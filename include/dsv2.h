@@ -277,6 +277,28 @@ typedef struct dsv2_mla_decode_args {
 
 DSV2_API int dsv2_mla_decode(const dsv2_mla_decode_args* args, void* stream);
 
+/* Allocation-free form of dsv2_mla_decode, for callers that cannot call cudaMalloc:
+ * an embedding runtime that has already handed all device memory to its own pool,
+ * a foreign-language host (through an FFI) with no CUDA allocator of its own, or a
+ * latency-critical decode thread where cudaMalloc's implicit device synchronisation
+ * is not acceptable.  No counterpart in the reference (its attention wrappers
+ * allocate their outputs and workspaces with torch).
+ * The split-KV partials live in a fixed device array inside libdsv2.so (8.4 MB,
+ * held by every GPU that loads the library until the process exits): at most 256
+ * split partials, i.e. batch * ceil(max_len / split_len) <= 256; larger requests
+ * return DSV2_ERR_INVALID with a message.  The caller still passes every input and
+ * the o_lat output, laid out as for dsv2_mla_decode.
+ * The first call on each device looks up that array's device address
+ * (cudaGetSymbolAddress) and the kernels' shared-memory attributes; make that first
+ * call before any stream capture.  Nothing needs clearing between calls (every
+ * partial the merge reads is written earlier in the same call), but all calls share
+ * the one array, so calls that overlap on the GPU (different streams, or several
+ * host threads) race and corrupt each other's results: serialise them. */
+DSV2_API int dsv2_mla_decode_noalloc(const void* q_abs, const void* q_pe, const void* cache,
+                                     int64_t cache_b_stride, int max_len, const int64_t* positions,
+                                     int pos_numel, float softmax_scale, int split_len, void* o_lat,
+                                     int batch, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
