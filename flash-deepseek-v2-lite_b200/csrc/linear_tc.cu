@@ -7,10 +7,11 @@
 // around silu_mul.
 //
 // Y[token, n] = sum_k W[n, k] * X[token, k].  Weights are the A operand (M = 128
-// weight rows per tile, K-major), tokens are the B operand (N = up to 256 tokens,
-// padded to a multiple of 16), the fp32 accumulator lives in TMEM.  Decode is
-// weight-bandwidth bound, so each 128-row weight tile is streamed from HBM exactly
-// once per 256 tokens; TMA moves 64-wide K slices of W and X (128-byte swizzle)
+// weight rows per tile, K-major), tokens are the B operand (an N tile of 16..256
+// tokens chosen per launch, padded to a multiple of 16), the fp32 accumulator lives
+// in TMEM.  Decode is weight-bandwidth bound, so each 128-row weight tile is streamed
+// from HBM once per N tile (the CTAs sharing a weight tile run side by side, so the
+// repeats are served by L2); TMA moves 64-wide K slices of W and X (128-byte swizzle)
 // through a multi-stage shared-memory ring.
 //
 // Warp roles (192 threads, persistent CTAs, one per SM):
@@ -19,7 +20,9 @@
 //   warps 2..5  epilogue: tcgen05.ld of the accumulator, fused SwiGLU / route-weight
 //               scaling / bf16 or fp32 store (TMEM lane quadrant = warp % 4)
 // SwiGLU tiles issue two MMAs per K step (gate rows and the matching up rows) into
-// two TMEM accumulators, so silu(gate) * up is computed in registers.
+// two TMEM accumulators, so silu(gate) * up is computed in registers.  When two
+// accumulator sets fit in TMEM's 512 columns they are double-buffered: the MMAs of
+// the next work item run while the epilogue drains the previous one.
 //
 // Grouped (MoE) mode: group g owns rows [group_offsets[g], group_offsets[g+1]) of X
 // (activations gathered in expert order), read on the device; work items of empty
@@ -34,16 +37,19 @@ namespace dsv2 {
 constexpr int kTcThreads = 192;
 constexpr int kTcM = 128;
 constexpr int kTcK = 64;                 // K per stage (one 128-byte swizzle row)
-constexpr int kTcNMax = 256;
 constexpr int kTcABytes = kTcM * 128;    // 16 KB
 constexpr int kTcBoxRows = 16;           // token rows per TMA box
-constexpr int kTcSmemBudget = 200 * 1024;
+constexpr int kTcSmemBudget = 216 * 1024;
+constexpr int kTcTmemCols = 512;
+constexpr int kTcMaxGroups = 256;
 
 struct TcShape {
   int stages;
-  int b_bytes;       // B region per stage (n_max_pad * 128)
-  int stage_bytes;   // A (+A_up) + B
-  int tmem_cols;
+  int n_tile;        // tokens per work item (multiple of 16, <= 256)
+  int stage_bytes;   // A (+A_up) + n_tile * 128
+  int acc_cols;      // TMEM columns of one accumulator set (n_tile or 2 * n_tile)
+  int acc_bufs;      // 1 or 2 (double-buffered accumulators)
+  int tmem_cols;     // power of two >= acc_bufs * acc_cols
 };
 
 __host__ __device__ inline int round_up(int a, int b) { return (a + b - 1) / b * b; }
@@ -58,10 +64,12 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + shp.stages * shp.stage_bytes);
   uint64_t* empty_bar = full_bar + shp.stages;
-  uint64_t* tfull_bar = empty_bar + shp.stages;
-  uint64_t* tempty_bar = tfull_bar + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 1);
+  uint64_t* tfull_bar = empty_bar + shp.stages;   // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;            // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  __shared__ int s_r0[kTcMaxGroups], s_cnt[kTcMaxGroups], s_nts[kTcMaxGroups];
+  __shared__ int s_first[kTcMaxGroups + 1];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -69,8 +77,10 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(tfull_bar, 1);
-    mbar_init(tempty_bar, 128);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 128);
+    }
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmap_w);
@@ -85,31 +95,57 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int n_groups = p.n_groups;
-  const long long total_items = static_cast<long long>(n_groups) * mt_count * nt_count;
   const int nkb = p.k / kTcK;
   const int a_tiles = SWIGLU ? 2 : 1;
+  const int n_tile = shp.n_tile;
 
-  // decode an item into (group, m tile, n tile, first route, tokens); false if empty
-  auto decode = [&](long long it, int& g, int& mt, int& nt, int& r0, int& ntok) -> bool {
-    nt = static_cast<int>(it % nt_count);
-    long long rest = it / nt_count;
-    mt = static_cast<int>(rest % mt_count);
-    g = static_cast<int>(rest / mt_count);
-    int cnt;
+  // Compacted work list: group g contributes mt_count * ceil(cnt_g / n_tile) items
+  // (none when empty).  Every CTA builds the same prefix from the device-side group
+  // offsets, then takes items blockIdx.x, blockIdx.x + gridDim.x, ... so the work is
+  // spread evenly over the CTAs whatever the routing.
+  const int G = p.n_groups;
+  for (int gi = threadIdx.x; gi < G; gi += kTcThreads) {
+    int r0 = 0, cnt = p.n_tokens;
     if (p.group_offsets) {
-      r0 = p.group_offsets[g];
-      cnt = p.group_offsets[g + 1] - r0;
-    } else {
-      r0 = 0;
-      cnt = p.n_tokens;
+      r0 = p.group_offsets[gi];
+      cnt = p.group_offsets[gi + 1] - r0;
     }
-    ntok = min(kTcNMax, cnt - nt * kTcNMax);
-    const int cap = shp.b_bytes / 128;
-    if (ntok > cap) {  // more tokens than the host-side bound: clamp and flag
+    int nts = (max(cnt, 0) + n_tile - 1) / n_tile;
+    if (nts > nt_count) {  // more tokens than the host-side bound: clamp and flag
       set_device_error(kErrIndex);
-      ntok = cap;
+      nts = nt_count;
     }
+    s_r0[gi] = r0;
+    s_cnt[gi] = cnt;
+    s_nts[gi] = nts;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int gi = 0; gi < G; ++gi) {
+      s_first[gi] = acc;
+      acc += s_nts[gi] * mt_count;
+    }
+    s_first[G] = acc;
+  }
+  __syncthreads();
+  const int total_items = s_first[G];
+
+  // item -> (group, m tile, n tile, first route, tokens); n tiles vary fastest so the
+  // CTAs that share a weight tile run side by side (repeat reads hit L2)
+  auto decode = [&](int it, int& g, int& mt, int& nt, int& r0, int& ntok) -> bool {
+    int lo = 0, hi = G - 1;
+    while (lo < hi) {  // last group with s_first[g] <= it
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_first[mid] <= it) lo = mid; else hi = mid - 1;
+    }
+    g = lo;
+    const int local = it - s_first[g];
+    const int nts = s_nts[g];
+    mt = local / nts;
+    nt = local - mt * nts;
+    r0 = s_r0[g];
+    ntok = min(n_tile, s_cnt[g] - nt * n_tile);
     return ntok > 0;
   };
 
@@ -118,12 +154,12 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (long long it = blockIdx.x; it < total_items && !*abort_flag; it += gridDim.x) {
+      for (int it = blockIdx.x; it < total_items && !*abort_flag; it += gridDim.x) {
         int g, mt, nt, r0, ntok;
         if (!decode(it, g, mt, nt, r0, ntok)) continue;
         const int npad = round_up(ntok, 16);
         const int nbox = npad / kTcBoxRows;
-        const int xrow0 = r0 + nt * kTcNMax;
+        const int xrow0 = r0 + nt * n_tile;
         const int gx = x_grouped ? g : 0;
         const uint32_t bytes = a_tiles * kTcABytes + nbox * kTcBoxRows * 128;
         for (int kb = 0; kb < nkb; ++kb) {
@@ -148,13 +184,16 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
       int stage = 0;
       uint32_t phase = 0;
       uint32_t local = 0;
-      for (long long it = blockIdx.x; it < total_items && !*abort_flag; it += gridDim.x) {
+      for (int it = blockIdx.x; it < total_items && !*abort_flag; it += gridDim.x) {
         int g, mt, nt, r0, ntok;
         if (!decode(it, g, mt, nt, r0, ntok)) continue;
         const int npad = round_up(ntok, 16);
         const uint32_t idesc = make_idesc_bf16(kTcM, npad);
-        if (!mbar_wait(tempty_bar, (local & 1) ^ 1)) { *abort_flag = 1; break; }
+        const uint32_t buf = local % shp.acc_bufs;
+        const uint32_t use = local / shp.acc_bufs;
+        if (!mbar_wait(&tempty_bar[buf], (use & 1) ^ 1)) { *abort_flag = 1; break; }
         tc_fence_after();
+        const uint32_t dacc = tmem_base + buf * shp.acc_cols;
         bool ok = true;
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase)) { ok = false; break; }
@@ -167,14 +206,14 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
           for (int k = 0; k < kTcK / 16; ++k) {
             const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
             // advance 16 bf16 (32 bytes) along K inside the swizzle row: +2 in addr>>4 units
-            tc_mma_bf16(tmem_base, da + 2 * k, db + 2 * k, idesc, acc);
-            if (SWIGLU) tc_mma_bf16(tmem_base + npad, du + 2 * k, db + 2 * k, idesc, acc);
+            tc_mma_bf16(dacc, da + 2 * k, db + 2 * k, idesc, acc);
+            if (SWIGLU) tc_mma_bf16(dacc + npad, du + 2 * k, db + 2 * k, idesc, acc);
           }
           tc_commit(&empty_bar[stage]);
           if (++stage == shp.stages) { stage = 0; phase ^= 1; }
         }
         if (!ok) { *abort_flag = 1; break; }
-        tc_commit(tfull_bar);
+        tc_commit(&tfull_bar[buf]);
         ++local;
       }
     }
@@ -183,30 +222,37 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
     const int quad = warp & 3;
     const int row_in_tile = quad * 32 + lane;
     uint32_t local = 0;
-    for (long long it = blockIdx.x; it < total_items; it += gridDim.x) {
+    for (int it = blockIdx.x; it < total_items; it += gridDim.x) {
       int g, mt, nt, r0, ntok;
       if (!decode(it, g, mt, nt, r0, ntok)) continue;
       const int npad = round_up(ntok, 16);
-      const bool ok = mbar_wait(tfull_bar, local & 1);
+      const uint32_t buf = local % shp.acc_bufs;
+      const uint32_t use = local / shp.acc_bufs;
+      const bool ok = mbar_wait(&tfull_bar[buf], use & 1);
       if (!ok || *abort_flag) { *abort_flag = 1; break; }
       tc_fence_after();
       const int n = mt * kTcM + row_in_tile;
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+      const uint32_t tbase =
+          tmem_base + buf * shp.acc_cols + (static_cast<uint32_t>(quad * 32) << 16);
+      const int rbase = r0 + nt * n_tile;
       for (int c0 = 0; c0 < npad; c0 += 16) {
         float acc[16], accu[16];
         tmem_ld16(tbase + c0, acc);
         if (SWIGLU) tmem_ld16(tbase + npad + c0, accu);
         tmem_ld_wait();
+        if (c0 + 16 >= npad) {
+          // accumulator fully read: hand the buffer back to the MMA warp before storing
+          tc_fence_before();
+          mbar_arrive(&tempty_bar[buf]);
+        }
         if (n < p.n_rows) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int tok = c0 + j;
-            if (tok < ntok) linear_store(p, g, r0 + nt * kTcNMax + tok, n, acc[j], SWIGLU ? accu[j] : 0.f);
+            if (tok < ntok) linear_store(p, g, rbase + tok, n, acc[j], SWIGLU ? accu[j] : 0.f);
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive(tempty_bar);
       ++local;
     }
   }
@@ -218,33 +264,45 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
   }
 }
 
-static int tmem_cols_for(int n) {
+static int pow2_at_least(int n) {
   int c = 32;
   while (c < n) c <<= 1;
   return c;
 }
 
-TcShape tc_shape(bool swiglu, int n_max) {
+// Tile shape for one launch.  n_tile: tokens per work item, shrunk (down to 32) until
+// the launch has work for about two thirds of the SMs, and capped at 128 for SwiGLU so
+// that two accumulator sets (gate + up) fit in TMEM.
+TcShape tc_shape(bool swiglu, int n_max, long long base_items, int num_sms, bool grouped) {
   TcShape s;
-  const int npad = round_up(min(max(n_max, 1), kTcNMax), 16);
-  s.b_bytes = npad * 128;
-  s.stage_bytes = (swiglu ? 2 : 1) * kTcABytes + s.b_bytes;
+  // grouped (MoE) launches: most groups hold a few dozen tokens, so a 128-token tile
+  // leaves shared memory for a deeper ring; the rare larger group takes two tiles
+  const int n_cap = (swiglu || grouped) ? 128 : 256;
+  int n_tile = round_up(min(max(n_max, 1), n_cap), 16);
+  if (!grouped) {
+    while (n_tile > 16 && base_items * ((n_max + n_tile - 1) / n_tile) * 3 < 2LL * num_sms)
+      n_tile = round_up(n_tile / 2, 16);
+  }
+  s.n_tile = n_tile;
+  s.stage_bytes = (swiglu ? 2 : 1) * kTcABytes + n_tile * 128;
   s.stages = min(8, (kTcSmemBudget - 2048) / s.stage_bytes);
-  s.tmem_cols = tmem_cols_for(npad * (swiglu ? 2 : 1));
+  s.acc_cols = n_tile * (swiglu ? 2 : 1);
+  s.acc_bufs = (2 * s.acc_cols <= kTcTmemCols) ? 2 : 1;
+  s.tmem_cols = pow2_at_least(s.acc_bufs * s.acc_cols);
   return s;
 }
 
 size_t tc_smem_bytes(const TcShape& s) {
   return 1024 /*alignment slack*/ + static_cast<size_t>(s.stages) * s.stage_bytes +
-         (2 * s.stages + 2) * sizeof(uint64_t) + 16;
+         (2 * s.stages + 4) * sizeof(uint64_t) + 16;
 }
 
 cudaError_t linear_tc_init() {
   cudaError_t e = cudaFuncSetAttribute(linear_tc_kernel<false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
   if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(linear_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              227 * 1024);
+                              220 * 1024);
 }
 
 // tmap_w / tmap_x: CUtensorMap built by the caller (api.cu) for W and X
@@ -252,12 +310,15 @@ cudaError_t launch_linear_tc_impl(const LinearParams& p, const CUtensorMap& tmap
                                   const CUtensorMap& tmap_x, int up_rows, int x_grouped,
                                   int num_sms, cudaStream_t st) {
   const bool swiglu = (p.epilogue == kEpiSwiglu);
-  const int n_max = p.group_offsets ? p.max_routes_per_group : p.n_tokens;
-  const TcShape shp = tc_shape(swiglu, n_max);
+  const bool grouped = p.group_offsets != nullptr;
+  const int n_max = grouped ? p.max_routes_per_group : p.n_tokens;
   const int mt_count = (p.n_rows + kTcM - 1) / kTcM;
-  const int nt_count = max(1, (n_max + kTcNMax - 1) / kTcNMax);
+  const TcShape shp = tc_shape(swiglu, n_max, static_cast<long long>(p.n_groups) * mt_count,
+                               num_sms, grouped);
+  const int nt_count = max(1, (n_max + shp.n_tile - 1) / shp.n_tile);
   const long long items = static_cast<long long>(p.n_groups) * mt_count * nt_count;
   if (items <= 0) return cudaSuccess;
+  if (p.n_groups > kTcMaxGroups || items > 0x7fffffffLL) return cudaErrorInvalidValue;
   const int grid = static_cast<int>(items < num_sms ? items : static_cast<long long>(num_sms));
   const size_t smem = tc_smem_bytes(shp);
   if (swiglu)
