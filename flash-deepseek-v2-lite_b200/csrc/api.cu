@@ -306,6 +306,14 @@ int dsv2_linear(const dsv2_linear_args* a, int family, void* stream) {
   p.route_y_row = a->route_y_row;
   p.route_scale = a->route_scale;
   p.max_routes_per_group = a->max_routes_per_group;
+  p.k_splits = a->k_splits > 1 ? a->k_splits : 1;
+  p.y_split_stride = a->y_split_stride;
+  if (p.k_splits > 1) {
+    if (family != DSV2_FAMILY_BATCH || a->group_offsets || a->epilogue != DSV2_EPI_STORE_F32)
+      return fail(DSV2_ERR_UNSUPPORTED, "linear: a K split needs the batch family, dense mode and fp32 output");
+    if (p.k_splits > a->k / 64)
+      return fail(DSV2_ERR_INVALID, "linear: k_splits %d exceeds k/64 = %d", p.k_splits, a->k / 64);
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (family == DSV2_FAMILY_SMALL) {
     if (a->k % 32) return fail(DSV2_ERR_UNSUPPORTED, "linear(small): k=%d not a multiple of 32", a->k);
@@ -340,7 +348,15 @@ int dsv2_linear(const dsv2_linear_args* a, int family, void* stream) {
                           : xrs * static_cast<uint64_t>(a->x_group_rows);
   rc = tensor_map_3d(a->x, a->k, a->x_group_rows, xg ? a->n_groups : 1, xrs, xgs, 16, &mx);
   if (rc) return rc;
-  return check_launch(launch_linear_tc_impl(p, mw, mx, up_rows, xg ? 1 : 0, sms, st),
+  TcShape shp;
+  int mt_count = 0, nt_count = 0;
+  const long long items = tc_launch_shape(p, sms, &shp, &mt_count, &nt_count);
+  CUtensorMap mxb;
+  rc = tensor_map_3d(a->x, a->k, a->x_group_rows, xg ? a->n_groups : 1, xrs, xgs,
+                     static_cast<uint32_t>(shp.x_box), &mxb);
+  if (rc) return rc;
+  return check_launch(launch_linear_tc_impl(p, mw, mx, mxb, shp, mt_count, nt_count, items, up_rows,
+                                            xg ? 1 : 0, sms, st),
                       "linear(batch)");
 }
 
@@ -440,7 +456,17 @@ int dsv2_mla_prep(const dsv2_mla_prep_args* a, void* stream) {
   if (a->rope_stride < 32) return fail(DSV2_ERR_INVALID, "mla_prep: rope table stride %lld < 32", (long long)a->rope_stride);
   if (a->batch <= 0) return DSV2_OK;
   MlaPrepParams p;
-  p.qkva = reinterpret_cast<const bf16*>(a->qkva);
+  if (a->qkva_dtype != DSV2_BF16 && a->qkva_dtype != DSV2_F32)
+    return fail(DSV2_ERR_UNSUPPORTED, "mla_prep: qkva dtype %d", a->qkva_dtype);
+  if (a->qkva_dtype == DSV2_F32 && (a->qkva_parts < 1 || a->qkva_part_stride % 4))
+    return fail(DSV2_ERR_INVALID, "mla_prep: fp32 qkva needs >= 1 part and 16-byte part stride");
+  if (a->q_nope_out && !aligned16(a->q_nope_out))
+    return fail(DSV2_ERR_INVALID, "mla_prep: q_nope_out must be 16-byte aligned");
+  p.qkva = a->qkva;
+  p.qkva_f32 = a->qkva_dtype == DSV2_F32 ? 1 : 0;
+  p.qkva_parts = a->qkva_dtype == DSV2_F32 ? a->qkva_parts : 1;
+  p.qkva_part_stride = a->qkva_part_stride;
+  p.q_nope_out = reinterpret_cast<bf16*>(a->q_nope_out);
   p.qkva_row_stride = a->qkva_row_stride;
   p.kv_norm_w = reinterpret_cast<const bf16*>(a->kv_norm_w);
   p.eps = a->eps;

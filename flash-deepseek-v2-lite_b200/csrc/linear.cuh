@@ -33,15 +33,18 @@ struct LinearParams {
   const int* route_y_row;
   const float* route_scale;
   int max_routes_per_group;
+  int k_splits;                 // batch family, dense fp32 output: K split across CTAs
+  long long y_split_stride;     // elements between the fp32 partial outputs of the splits
 };
 
 __device__ __forceinline__ float silu_ref(float g) { return g / (1.f + expf(-g)); }
 
 // Epilogue for one output element (row n, route r, accumulators acc/acc_up).
 __device__ __forceinline__ void linear_store(const LinearParams& p, int g, int r, int n, float acc,
-                                             float acc_up) {
+                                             float acc_up, long long split_off = 0) {
   const int yrow = p.route_y_row ? p.route_y_row[r] : r;
-  const long long off = g * p.y_group_stride + static_cast<long long>(yrow) * p.y_row_stride + n;
+  const long long off =
+      split_off + g * p.y_group_stride + static_cast<long long>(yrow) * p.y_row_stride + n;
   switch (p.epilogue) {
     case kEpiStoreBf16:
       reinterpret_cast<bf16*>(p.y)[off] = __float2bfloat16_rn(acc);

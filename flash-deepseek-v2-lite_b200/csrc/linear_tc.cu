@@ -30,6 +30,8 @@
 // CUDA-graph safe.  All mbarrier waits are bounded (see common.cuh).
 #include <cudaTypedefs.h>
 
+#include <type_traits>
+
 #include "linear.cuh"
 
 namespace dsv2 {
@@ -50,15 +52,23 @@ struct TcShape {
   int acc_cols;      // TMEM columns of one accumulator set (n_tile or 2 * n_tile)
   int acc_bufs;      // 1 or 2 (double-buffered accumulators)
   int tmem_cols;     // power of two >= acc_bufs * acc_cols
+  int x_box;         // rows of the large activation box (tmap_xb)
 };
 
 __host__ __device__ inline int round_up(int a, int b) { return (a + b - 1) / b * b; }
 
-template <bool SWIGLU>
+__device__ __forceinline__ void store_out(bf16* p, float v) { *p = __float2bfloat16_rn(v); }
+__device__ __forceinline__ void store_out(float* p, float v) { *p = v; }
+
+// EPI: epilogue (compile time); ROUTED: output rows come from route_y_row
+template <int EPI, bool ROUTED>
 __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
     const LinearParams p, const __grid_constant__ CUtensorMap tmap_w,
-    const __grid_constant__ CUtensorMap tmap_x, const TcShape shp, int mt_count, int nt_count,
-    int up_rows, int x_grouped) {
+    const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_xb,
+    const TcShape shp, int mt_count, int nt_count, int up_rows, int x_grouped) {
+  constexpr bool SWIGLU = (EPI == kEpiSwiglu);
+  using OutT = typename std::conditional<(EPI == kEpiStoreF32 || EPI == kEpiScaleF32), float,
+                                         bf16>::type;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -85,6 +95,7 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
     fence_mbar_init();
     prefetch_tmap(&tmap_w);
     prefetch_tmap(&tmap_x);
+    prefetch_tmap(&tmap_xb);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, static_cast<uint32_t>(shp.tmem_cols));
@@ -103,7 +114,9 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
   // (none when empty).  Every CTA builds the same prefix from the device-side group
   // offsets, then takes items blockIdx.x, blockIdx.x + gridDim.x, ... so the work is
   // spread evenly over the CTAs whatever the routing.
-  const int G = p.n_groups;
+  // With a K split (dense mode only) every (group, split) pair is one "virtual group".
+  const int S = max(p.k_splits, 1);
+  const int G = p.n_groups * S;
   for (int gi = threadIdx.x; gi < G; gi += kTcThreads) {
     int r0 = 0, cnt = p.n_tokens;
     if (p.group_offsets) {
@@ -133,19 +146,24 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
 
   // item -> (group, m tile, n tile, first route, tokens); n tiles vary fastest so the
   // CTAs that share a weight tile run side by side (repeat reads hit L2)
-  auto decode = [&](int it, int& g, int& mt, int& nt, int& r0, int& ntok) -> bool {
+  auto decode = [&](int it, int& g, int& mt, int& nt, int& r0, int& ntok, int& kb0,
+                    int& kb1, int& sp) -> bool {
     int lo = 0, hi = G - 1;
-    while (lo < hi) {  // last group with s_first[g] <= it
+    while (lo < hi) {  // last virtual group with s_first[vg] <= it
       const int mid = (lo + hi + 1) >> 1;
       if (s_first[mid] <= it) lo = mid; else hi = mid - 1;
     }
-    g = lo;
-    const int local = it - s_first[g];
-    const int nts = s_nts[g];
+    const int vg = lo;
+    const int local = it - s_first[vg];
+    const int nts = s_nts[vg];
     mt = local / nts;
     nt = local - mt * nts;
-    r0 = s_r0[g];
-    ntok = min(n_tile, s_cnt[g] - nt * n_tile);
+    r0 = s_r0[vg];
+    ntok = min(n_tile, s_cnt[vg] - nt * n_tile);
+    g = vg / S;
+    sp = vg - g * S;
+    kb0 = sp * nkb / S;
+    kb1 = (sp + 1) * nkb / S;
     return ntok > 0;
   };
 
@@ -155,14 +173,17 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
       int stage = 0;
       uint32_t phase = 0;
       for (int it = blockIdx.x; it < total_items && !*abort_flag; it += gridDim.x) {
-        int g, mt, nt, r0, ntok;
-        if (!decode(it, g, mt, nt, r0, ntok)) continue;
+        int g, mt, nt, r0, ntok, kb0, kb1, sp;
+        if (!decode(it, g, mt, nt, r0, ntok, kb0, kb1, sp)) continue;
         const int npad = round_up(ntok, 16);
-        const int nbox = npad / kTcBoxRows;
+        // activation rows: as many large boxes as fit, 16-row boxes for the rest
+        // (few large TMA requests per stage instead of many 2 KB ones)
+        const int nbig = npad / shp.x_box;
+        const int nsmall = (npad - nbig * shp.x_box) / kTcBoxRows;
         const int xrow0 = r0 + nt * n_tile;
         const int gx = x_grouped ? g : 0;
-        const uint32_t bytes = a_tiles * kTcABytes + nbox * kTcBoxRows * 128;
-        for (int kb = 0; kb < nkb; ++kb) {
+        const uint32_t bytes = a_tiles * kTcABytes + npad * 128;
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { *abort_flag = 1; break; }
           unsigned char* st = smem + stage * shp.stage_bytes;
           mbar_arrive_expect_tx(&full_bar[stage], bytes);
@@ -171,9 +192,12 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
             tma_load_3d(smem_u32(st + kTcABytes), &tmap_w, &full_bar[stage], kb * kTcK,
                         mt * kTcM + up_rows, g);
           unsigned char* sb = st + a_tiles * kTcABytes;
-          for (int bx = 0; bx < nbox; ++bx)
-            tma_load_3d(smem_u32(sb + bx * kTcBoxRows * 128), &tmap_x, &full_bar[stage], kb * kTcK,
-                        xrow0 + bx * kTcBoxRows, gx);
+          for (int bx = 0; bx < nbig; ++bx)
+            tma_load_3d(smem_u32(sb + bx * shp.x_box * 128), &tmap_xb, &full_bar[stage], kb * kTcK,
+                        xrow0 + bx * shp.x_box, gx);
+          for (int bx = 0; bx < nsmall; ++bx)
+            tma_load_3d(smem_u32(sb + (nbig * shp.x_box + bx * kTcBoxRows) * 128), &tmap_x,
+                        &full_bar[stage], kb * kTcK, xrow0 + nbig * shp.x_box + bx * kTcBoxRows, gx);
           if (++stage == shp.stages) { stage = 0; phase ^= 1; }
         }
       }
@@ -185,8 +209,8 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
       uint32_t phase = 0;
       uint32_t local = 0;
       for (int it = blockIdx.x; it < total_items && !*abort_flag; it += gridDim.x) {
-        int g, mt, nt, r0, ntok;
-        if (!decode(it, g, mt, nt, r0, ntok)) continue;
+        int g, mt, nt, r0, ntok, kb0, kb1, sp;
+        if (!decode(it, g, mt, nt, r0, ntok, kb0, kb1, sp)) continue;
         const int npad = round_up(ntok, 16);
         const uint32_t idesc = make_idesc_bf16(kTcM, npad);
         const uint32_t buf = local % shp.acc_bufs;
@@ -195,7 +219,7 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
         tc_fence_after();
         const uint32_t dacc = tmem_base + buf * shp.acc_cols;
         bool ok = true;
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase)) { ok = false; break; }
           tc_fence_after();
           unsigned char* st = smem + stage * shp.stage_bytes;
@@ -204,7 +228,7 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
           const uint64_t db = sw128_kmajor_desc(smem_u32(st + a_tiles * kTcABytes));
 #pragma unroll
           for (int k = 0; k < kTcK / 16; ++k) {
-            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
             // advance 16 bf16 (32 bytes) along K inside the swizzle row: +2 in addr>>4 units
             tc_mma_bf16(dacc, da + 2 * k, db + 2 * k, idesc, acc);
             if (SWIGLU) tc_mma_bf16(dacc + npad, du + 2 * k, db + 2 * k, idesc, acc);
@@ -223,33 +247,59 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
     const int row_in_tile = quad * 32 + lane;
     uint32_t local = 0;
     for (int it = blockIdx.x; it < total_items; it += gridDim.x) {
-      int g, mt, nt, r0, ntok;
-      if (!decode(it, g, mt, nt, r0, ntok)) continue;
+      int g, mt, nt, r0, ntok, kb0, kb1, sp;
+      if (!decode(it, g, mt, nt, r0, ntok, kb0, kb1, sp)) continue;
       const int npad = round_up(ntok, 16);
+      const long long split_off = static_cast<long long>(sp) * p.y_split_stride;
       const uint32_t buf = local % shp.acc_bufs;
       const uint32_t use = local / shp.acc_bufs;
       const bool ok = mbar_wait(&tfull_bar[buf], use & 1);
       if (!ok || *abort_flag) { *abort_flag = 1; break; }
       tc_fence_after();
       const int n = mt * kTcM + row_in_tile;
+      const bool row_ok = n < p.n_rows;
       const uint32_t tbase =
           tmem_base + buf * shp.acc_cols + (static_cast<uint32_t>(quad * 32) << 16);
       const int rbase = r0 + nt * n_tile;
+      // output column n of group g (dense rows advance by y_row_stride per token)
+      OutT* ybase = reinterpret_cast<OutT*>(p.y) + split_off + g * p.y_group_stride + n;
       for (int c0 = 0; c0 < npad; c0 += 16) {
         float acc[16], accu[16];
         tmem_ld16(tbase + c0, acc);
         if (SWIGLU) tmem_ld16(tbase + npad + c0, accu);
+        // routed rows: lanes 0..15 fetch this chunk's (row, scale) once, shuffled out below
+        int my_row = 0;
+        float my_scale = 1.f;
+        if (ROUTED) {
+          const int r = rbase + c0 + (lane & 15);
+          if (c0 + (lane & 15) < ntok) {
+            my_row = p.route_y_row[r];
+            if (EPI == kEpiScaleF32) my_scale = p.route_scale[r];
+          }
+        }
         tmem_ld_wait();
         if (c0 + 16 >= npad) {
           // accumulator fully read: hand the buffer back to the MMA warp before storing
           tc_fence_before();
           mbar_arrive(&tempty_bar[buf]);
         }
-        if (n < p.n_rows) {
+        OutT* yp = ybase + static_cast<long long>(rbase + c0) * p.y_row_stride;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int tok = c0 + j;
-            if (tok < ntok) linear_store(p, g, rbase + tok, n, acc[j], SWIGLU ? accu[j] : 0.f);
+        for (int j = 0; j < 16; ++j) {
+          const bool ok_j = row_ok && (c0 + j < ntok);
+          float v = acc[j];
+          if (EPI == kEpiSwiglu) {
+            const float gt = bf16_round(acc[j]), up = bf16_round(accu[j]);
+            v = silu_ref(gt) * up;
+          }
+          if (ROUTED) {
+            const int yrow = __shfl_sync(0xffffffffu, my_row, j);
+            const float sc = __shfl_sync(0xffffffffu, my_scale, j);
+            if (EPI == kEpiScaleF32) v = bf16_round(v) * sc;
+            if (ok_j) store_out(reinterpret_cast<OutT*>(p.y) + g * p.y_group_stride +
+                                    static_cast<long long>(yrow) * p.y_row_stride + n, v);
+          } else {
+            if (ok_j) store_out(yp + j * p.y_row_stride, v);
           }
         }
       }
@@ -273,13 +323,14 @@ static int pow2_at_least(int n) {
 // Tile shape for one launch.  n_tile: tokens per work item, shrunk (down to 32) until
 // the launch has work for about two thirds of the SMs, and capped at 128 for SwiGLU so
 // that two accumulator sets (gate + up) fit in TMEM.
-TcShape tc_shape(bool swiglu, int n_max, long long base_items, int num_sms, bool grouped) {
+TcShape tc_shape(bool swiglu, int n_max, long long base_items, int num_sms, bool grouped,
+                 bool keep_n) {
   TcShape s;
   // grouped (MoE) launches: most groups hold a few dozen tokens, so a 128-token tile
   // leaves shared memory for a deeper ring; the rare larger group takes two tiles
   const int n_cap = (swiglu || grouped) ? 128 : 256;
   int n_tile = round_up(min(max(n_max, 1), n_cap), 16);
-  if (!grouped) {
+  if (!grouped && !keep_n) {
     while (n_tile > 16 && base_items * ((n_max + n_tile - 1) / n_tile) * 3 < 2LL * num_sms)
       n_tile = round_up(n_tile / 2, 16);
   }
@@ -297,36 +348,74 @@ size_t tc_smem_bytes(const TcShape& s) {
          (2 * s.stages + 4) * sizeof(uint64_t) + 16;
 }
 
-cudaError_t linear_tc_init() {
-  cudaError_t e = cudaFuncSetAttribute(linear_tc_kernel<false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(linear_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              220 * 1024);
+template <int EPI, bool ROUTED>
+static cudaError_t tc_set_smem() {
+  return cudaFuncSetAttribute(linear_tc_kernel<EPI, ROUTED>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
 }
 
-// tmap_w / tmap_x: CUtensorMap built by the caller (api.cu) for W and X
-cudaError_t launch_linear_tc_impl(const LinearParams& p, const CUtensorMap& tmap_w,
-                                  const CUtensorMap& tmap_x, int up_rows, int x_grouped,
-                                  int num_sms, cudaStream_t st) {
+cudaError_t linear_tc_init() {
+  const cudaError_t errs[] = {
+      tc_set_smem<kEpiStoreBf16, false>(), tc_set_smem<kEpiStoreBf16, true>(),
+      tc_set_smem<kEpiStoreF32, false>(),  tc_set_smem<kEpiStoreF32, true>(),
+      tc_set_smem<kEpiSwiglu, false>(),    tc_set_smem<kEpiSwiglu, true>(),
+      tc_set_smem<kEpiScaleF32, false>(),  tc_set_smem<kEpiScaleF32, true>()};
+  for (cudaError_t e : errs)
+    if (e != cudaSuccess) return e;
+  return cudaSuccess;
+}
+
+template <int EPI, bool ROUTED>
+static void tc_launch(int grid, size_t smem, cudaStream_t st, const LinearParams& p,
+                      const CUtensorMap& w, const CUtensorMap& x, const CUtensorMap& xb,
+                      const TcShape& shp, int mt_count, int nt_count, int up_rows, int x_grouped) {
+  linear_tc_kernel<EPI, ROUTED><<<grid, kTcThreads, smem, st>>>(p, w, x, xb, shp, mt_count,
+                                                                 nt_count, up_rows, x_grouped);
+}
+
+// Launch geometry, shared with the tensor-map builder in api.cu (the large activation
+// box must match the token tile).  Returns the number of work items (0 = nothing to do).
+long long tc_launch_shape(const LinearParams& p, int num_sms, TcShape* shp, int* mt_count,
+                          int* nt_count) {
   const bool swiglu = (p.epilogue == kEpiSwiglu);
   const bool grouped = p.group_offsets != nullptr;
   const int n_max = grouped ? p.max_routes_per_group : p.n_tokens;
-  const int mt_count = (p.n_rows + kTcM - 1) / kTcM;
-  const TcShape shp = tc_shape(swiglu, n_max, static_cast<long long>(p.n_groups) * mt_count,
-                               num_sms, grouped);
-  const int nt_count = max(1, (n_max + shp.n_tile - 1) / shp.n_tile);
-  const long long items = static_cast<long long>(p.n_groups) * mt_count * nt_count;
+  *mt_count = (p.n_rows + kTcM - 1) / kTcM;
+  const int S = max(p.k_splits, 1);
+  // a K split keeps every token in one tile (weights read once); without one, small
+  // launches shrink the token tile to spread over more SMs
+  *shp = tc_shape(swiglu, n_max, static_cast<long long>(p.n_groups) * S * *mt_count, num_sms,
+                  grouped, S > 1);
+  shp->x_box = grouped ? min(64, shp->n_tile) : shp->n_tile;
+  *nt_count = max(1, (n_max + shp->n_tile - 1) / shp->n_tile);
+  return static_cast<long long>(p.n_groups) * S * *mt_count * *nt_count;
+}
+
+// tmap_w / tmap_x / tmap_xb: tensor maps built by the caller (api.cu) for W and for X
+// with 16-row and shp.x_box-row boxes
+cudaError_t launch_linear_tc_impl(const LinearParams& p, const CUtensorMap& tmap_w,
+                                  const CUtensorMap& tmap_x, const CUtensorMap& tmap_xb,
+                                  const TcShape& shp, int mt_count, int nt_count, long long items,
+                                  int up_rows, int x_grouped, int num_sms, cudaStream_t st) {
   if (items <= 0) return cudaSuccess;
-  if (p.n_groups > kTcMaxGroups || items > 0x7fffffffLL) return cudaErrorInvalidValue;
+  const int S = max(p.k_splits, 1);
+  if (static_cast<long long>(p.n_groups) * S > kTcMaxGroups || items > 0x7fffffffLL)
+    return cudaErrorInvalidValue;
   const int grid = static_cast<int>(items < num_sms ? items : static_cast<long long>(num_sms));
   const size_t smem = tc_smem_bytes(shp);
-  if (swiglu)
-    linear_tc_kernel<true><<<grid, kTcThreads, smem, st>>>(p, tmap_w, tmap_x, shp, mt_count,
-                                                           nt_count, up_rows, x_grouped);
-  else
-    linear_tc_kernel<false><<<grid, kTcThreads, smem, st>>>(p, tmap_w, tmap_x, shp, mt_count,
-                                                            nt_count, up_rows, x_grouped);
+  const bool routed = p.route_y_row != nullptr;
+#define DSV2_TC_LAUNCH(E)                                                                       \
+  (routed ? tc_launch<E, true>(grid, smem, st, p, tmap_w, tmap_x, tmap_xb, shp, mt_count,       \
+                               nt_count, up_rows, x_grouped)                                    \
+          : tc_launch<E, false>(grid, smem, st, p, tmap_w, tmap_x, tmap_xb, shp, mt_count,      \
+                                nt_count, up_rows, x_grouped))
+  switch (p.epilogue) {
+    case kEpiStoreBf16: DSV2_TC_LAUNCH(kEpiStoreBf16); break;
+    case kEpiStoreF32: DSV2_TC_LAUNCH(kEpiStoreF32); break;
+    case kEpiSwiglu: DSV2_TC_LAUNCH(kEpiSwiglu); break;
+    default: DSV2_TC_LAUNCH(kEpiScaleF32); break;
+  }
+#undef DSV2_TC_LAUNCH
   return cudaGetLastError();
 }
 

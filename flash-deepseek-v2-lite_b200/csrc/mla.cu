@@ -45,8 +45,36 @@ constexpr int kMlaThreads = 128;
 
 __global__ __launch_bounds__(256) void mla_prep_kernel(const MlaPrepParams p) {
   __shared__ float red[8];
+  __shared__ __align__(16) bf16 s_row[kHeads * 192 + kRow];  // this row of qkva, bf16
   const int b = blockIdx.x;
-  const bf16* row = p.qkva + b * p.qkva_row_stride;
+  // stage the row (summing fp32 split-K partials and rounding to bf16, like a bf16 linear)
+  if (p.qkva_f32) {
+    const float* src = reinterpret_cast<const float*>(p.qkva) + b * p.qkva_row_stride;
+    for (int i = threadIdx.x; i < (kHeads * 192 + kRow) / 4; i += blockDim.x) {
+      float4 acc = *reinterpret_cast<const float4*>(src + 4 * i);
+      for (int s = 1; s < p.qkva_parts; ++s) {
+        const float4 v = *reinterpret_cast<const float4*>(src + s * p.qkva_part_stride + 4 * i);
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+      }
+      uint2 o;
+      o.x = pack_bf16x2(acc.x, acc.y);
+      o.y = pack_bf16x2(acc.z, acc.w);
+      *reinterpret_cast<uint2*>(s_row + 4 * i) = o;
+    }
+  } else {
+    const bf16* src = reinterpret_cast<const bf16*>(p.qkva) + b * p.qkva_row_stride;
+    for (int i = threadIdx.x; i < (kHeads * 192 + kRow) / 8; i += blockDim.x)
+      *reinterpret_cast<uint4*>(s_row + 8 * i) = *reinterpret_cast<const uint4*>(src + 8 * i);
+  }
+  __syncthreads();
+  const bf16* row = s_row;
+  if (p.q_nope_out) {
+    for (int i = threadIdx.x; i < kHeads * 16; i += blockDim.x) {
+      const int h = i / 16, c = i % 16;
+      *reinterpret_cast<uint4*>(p.q_nope_out + (static_cast<long long>(b) * kHeads + h) * 128 + c * 8) =
+          *reinterpret_cast<const uint4*>(row + h * 192 + c * 8);
+    }
+  }
   long long pos = p.positions[p.pos_numel == 1 ? 0 : b];
   const bool pos_ok = (pos >= 0 && pos < p.max_len && pos < p.rope_rows);
   if (!pos_ok) {

@@ -32,7 +32,11 @@ struct RouterParams {
 };
 
 struct MlaPrepParams {
-  const bf16* qkva;            // [B, 3072 + 576]: q (16 x 192) | c_kv (512) | k_pe (64)
+  const void* qkva;            // [B, 3072 + 576]: q (16 x 192) | c_kv (512) | k_pe (64)
+  int qkva_f32;                // 1: fp32 split-K partials (qkva_parts of them), 0: bf16
+  int qkva_parts;
+  long long qkva_part_stride;  // elements
+  bf16* q_nope_out;            // optional [B, 16, 128]
   long long qkva_row_stride;
   const bf16* kv_norm_w;       // [512]
   float eps;
@@ -91,9 +95,8 @@ cudaError_t launch_mla_prep(const MlaPrepParams&, int, cudaStream_t);
 cudaError_t mla_decode_init();
 cudaError_t launch_mla_decode(const MlaDecodeParams&, int, cudaStream_t);
 cudaError_t launch_mla_combine(const float*, const float*, int, void*, int, cudaStream_t);
-// linear_tc.cu
+// linear_tc.cu (TcShape, tc_launch_shape and launch_linear_tc_impl are defined there; the
+// unity build includes it before api.cu)
 cudaError_t linear_tc_init();
-cudaError_t launch_linear_tc_impl(const LinearParams&, const CUtensorMap&, const CUtensorMap&, int,
-                                  int, int, cudaStream_t);
 
 }  // namespace dsv2

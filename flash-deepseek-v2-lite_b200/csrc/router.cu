@@ -147,14 +147,21 @@ __global__ __launch_bounds__(kRouterThreads) void router_kernel(const RouterPara
   const int e_end = min(p.n_experts, e_beg + p.experts_per_cta);
   for (int e = e_beg + warp; e < e_end; e += kRouterThreads / 32) {
     float acc = 0.f;
-    for (int c = lane; c < nch; c += 32) {
-      const uint4 u = *reinterpret_cast<const uint4*>(xr + c * 8);
-      const uint32_t* up = reinterpret_cast<const uint32_t*>(&u);
-      const long long wo = static_cast<long long>(e) * p.hidden + c * 8;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        acc = fmaf(bf16lo(up[j]), load_gate_w(p.w, p.w_dtype, wo + 2 * j), acc);
-        acc = fmaf(bf16hi(up[j]), load_gate_w(p.w, p.w_dtype, wo + 2 * j + 1), acc);
+    if (p.w_dtype == 0) {
+      const bf16* wr = reinterpret_cast<const bf16*>(p.w) + static_cast<long long>(e) * p.hidden;
+      for (int c = lane; c < nch; c += 32)
+        acc = dot8(*reinterpret_cast<const uint4*>(xr + c * 8), *reinterpret_cast<const uint4*>(wr + c * 8), acc);
+    } else {
+      const float* wr = reinterpret_cast<const float*>(p.w) + static_cast<long long>(e) * p.hidden;
+      for (int c = lane; c < nch; c += 32) {
+        const uint4 u = *reinterpret_cast<const uint4*>(xr + c * 8);
+        const uint32_t* up = reinterpret_cast<const uint32_t*>(&u);
+        const float4 w0 = *reinterpret_cast<const float4*>(wr + c * 8);
+        const float4 w1 = *reinterpret_cast<const float4*>(wr + c * 8 + 4);
+        acc = fmaf(bf16lo(up[0]), w0.x, acc); acc = fmaf(bf16hi(up[0]), w0.y, acc);
+        acc = fmaf(bf16lo(up[1]), w0.z, acc); acc = fmaf(bf16hi(up[1]), w0.w, acc);
+        acc = fmaf(bf16lo(up[2]), w1.x, acc); acc = fmaf(bf16hi(up[2]), w1.y, acc);
+        acc = fmaf(bf16lo(up[3]), w1.z, acc); acc = fmaf(bf16hi(up[3]), w1.w, acc);
       }
     }
     acc = warp_sum(acc);

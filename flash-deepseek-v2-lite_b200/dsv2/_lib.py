@@ -46,6 +46,7 @@ class LinearArgs(ctypes.Structure):
         ("epilogue", c_i32), ("n_groups", c_i32), ("n_tokens", c_i32), ("max_routes_per_group", c_i32),
         ("group_offsets", c_vp), ("route_x_row", c_vp), ("route_y_row", c_vp), ("route_scale", c_vp),
         ("w_group_rows", c_i64), ("x_group_rows", c_i64),
+        ("k_splits", c_i32), ("y_split_stride", c_i64),
     ]
 
 
@@ -68,6 +69,7 @@ class MlaPrepArgs(ctypes.Structure):
         ("positions", c_vp), ("pos_numel", c_i32),
         ("cache", c_vp), ("cache_b_stride", c_i64), ("max_len", c_i32),
         ("q_pe_out", c_vp), ("batch", c_i32),
+        ("qkva_dtype", c_i32), ("qkva_parts", c_i32), ("qkva_part_stride", c_i64), ("q_nope_out", c_vp),
     ]
 
 

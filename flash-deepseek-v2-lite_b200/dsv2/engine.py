@@ -37,6 +37,14 @@ def choose_split_len(batch: int, max_len: int, num_sms: int) -> int:
     return int(min(max(s, 64), 4096))
 
 
+def split_count(n_rows: int, k: int, num_sms: int) -> int:
+    """K splits for a dense batch-family linear: about one 128-row tile per SM, at least
+    two 64-wide K blocks per split."""
+    m_tiles = (n_rows + 127) // 128
+    s = max(1, round(num_sms / m_tiles))
+    return int(min(s, max(1, (k // 64) // 2), 16))
+
+
 @dataclass
 class DecodeState:
     positions: torch.Tensor   # [B] int64: write position of the next token
@@ -97,6 +105,17 @@ class DecodeEngine:
         self.x = torch.zeros((B, HIDDEN), device=dev, dtype=bf)
         self.qkva = torch.zeros((B, QKVA_ROWS), device=dev, dtype=bf)
         self.q_pe = torch.zeros((B, N_HEADS, 64), device=dev, dtype=bf)
+        self.q_nope = torch.zeros((B, N_HEADS, QK_NOPE), device=dev, dtype=bf)
+        # batch family: split-K fp32 partials for the dense linears whose consumers sum them
+        self.split_k = self.family == ops.FAMILY_BATCH
+        if self.split_k:
+            s_q = split_count(QKVA_ROWS, HIDDEN, self.num_sms)
+            s_o = split_count(HIDDEN, N_HEADS * V_DIM, self.num_sms)
+            self.qkva_part = torch.zeros((s_q, B, QKVA_ROWS), device=dev, dtype=f32)
+            self.o_proj_part = torch.zeros((s_o, B, HIDDEN), device=dev, dtype=f32)
+            dense_k = max([lp.dense.inter for lp in self.layers if lp.dense is not None], default=0)
+            s_d = split_count(HIDDEN, dense_k, self.num_sms) if dense_k else 1
+            self.dense_part = torch.zeros((s_d, B, HIDDEN), device=dev, dtype=f32)
         self.q_abs = torch.zeros((B, N_HEADS, KV_LORA), device=dev, dtype=bf)
         self.o_lat = torch.zeros((B, N_HEADS, KV_LORA), device=dev, dtype=bf)
         self.attn_o = torch.zeros((B, N_HEADS * V_DIM), device=dev, dtype=bf)
@@ -141,16 +160,31 @@ class DecodeEngine:
     def _linear(self, **kw):
         ops.linear(family=self.family, **kw)
 
-    def _attention(self, li: int, lp: LayerPack) -> None:
+    def _split_linear(self, *, w, n_rows, k, x, out, **kw) -> torch.Tensor:
+        """Dense linear into fp32 split-K partials out[S, B, n_rows] (batch family): every
+        token stays in one tile, so the weights are streamed once, and the K split spreads
+        the launch over the SMs.  Returns the [B, S, n_rows] view the consumers sum."""
+        S = out.shape[0]
+        self._linear(w=w, n_rows=n_rows, k=k, x=x, y=out[0], epilogue=ops.EPI_STORE_F32, n_tokens=self.B,
+                     x_group_rows=self.B, k_splits=S, y_split_stride=out.stride(0), **kw)
+        return out.permute(1, 0, 2)
+
+    def _attention(self, li: int, lp: LayerPack) -> torch.Tensor:
+        """Attention sublayer; returns its output (bf16 [B, 2048] or fp32 partials [B, S, 2048])."""
         a, B = lp.attn, self.B
-        self._linear(w=a.qkva, n_rows=QKVA_ROWS, k=HIDDEN, x=self.x, y=self.qkva, n_tokens=B,
-                     x_group_rows=B)
-        ops.mla_prep(qkva=self.qkva, kv_norm_w=a.kv_norm_w, eps=a.kv_norm_eps, cos=self.cos, sin=self.sin,
-                     positions=self.positions, cache=self.cache[li], q_pe_out=self.q_pe)
+        if self.split_k:
+            self._split_linear(w=a.qkva, n_rows=QKVA_ROWS, k=HIDDEN, x=self.x, out=self.qkva_part)
+            qkva = self.qkva_part
+        else:
+            self._linear(w=a.qkva, n_rows=QKVA_ROWS, k=HIDDEN, x=self.x, y=self.qkva, n_tokens=B,
+                         x_group_rows=B)
+            qkva = self.qkva
+        ops.mla_prep(qkva=qkva, kv_norm_w=a.kv_norm_w, eps=a.kv_norm_eps, cos=self.cos, sin=self.sin,
+                     positions=self.positions, cache=self.cache[li], q_pe_out=self.q_pe, q_nope_out=self.q_nope)
         # q_abs[b, h] = q_nope[b, h] @ W_UK[h]
         self._linear(w=a.w_uk_t, n_rows=KV_LORA, k=QK_NOPE, w_row_stride=QK_NOPE,
-                     w_group_stride=KV_LORA * QK_NOPE, x=self.qkva, x_row_stride=QKVA_ROWS,
-                     x_group_stride=Q_DIM, y=self.q_abs, y_row_stride=N_HEADS * KV_LORA,
+                     w_group_stride=KV_LORA * QK_NOPE, x=self.q_nope, x_row_stride=N_HEADS * QK_NOPE,
+                     x_group_stride=QK_NOPE, y=self.q_abs, y_row_stride=N_HEADS * KV_LORA,
                      y_group_stride=KV_LORA, n_groups=N_HEADS, n_tokens=B, w_group_rows=KV_LORA,
                      x_group_rows=B)
         ops.mla_decode(q_abs=self.q_abs, q_pe=self.q_pe, cache=self.cache[li], positions=self.positions,
@@ -162,14 +196,19 @@ class DecodeEngine:
                      x_group_stride=KV_LORA, y=self.attn_o, y_row_stride=N_HEADS * V_DIM,
                      y_group_stride=V_DIM, n_groups=N_HEADS, n_tokens=B, w_group_rows=V_DIM,
                      x_group_rows=B)
+        if self.split_k:
+            return self._split_linear(w=a.o, n_rows=HIDDEN, k=N_HEADS * V_DIM, x=self.attn_o, out=self.o_proj_part)
         self._linear(w=a.o, n_rows=HIDDEN, k=N_HEADS * V_DIM, x=self.attn_o, y=self.attn_out, n_tokens=B,
                      x_group_rows=B)
+        return self.attn_out
 
     def _dense_mlp(self, lp: LayerPack) -> torch.Tensor:
         d, B = lp.dense, self.B
         h = self.mlp_h[:, :d.inter]
         self._linear(w=d.gate_up, n_rows=d.inter, k=HIDDEN, up_offset=d.inter * HIDDEN, x=self.x, y=h,
                      epilogue=ops.EPI_SWIGLU, n_tokens=B, w_group_rows=2 * d.inter, x_group_rows=B)
+        if self.split_k:
+            return self._split_linear(w=d.down, n_rows=HIDDEN, k=d.inter, x=h, out=self.dense_part)
         self._linear(w=d.down, n_rows=HIDDEN, k=d.inter, x=h, y=self.mlp_out, n_tokens=B, x_group_rows=B)
         return self.mlp_out
 
@@ -277,8 +316,8 @@ class DecodeEngine:
         for li, lp in enumerate(self.layers):
             if li > 0:
                 ops.add_rmsnorm(self.h, delta, lp.in_norm_w, lp.eps, self.x)
-            self._attention(li, lp)
-            ops.add_rmsnorm(self.h, self.attn_out, lp.post_norm_w, lp.eps, self.x)
+            attn = self._attention(li, lp)
+            ops.add_rmsnorm(self.h, attn, lp.post_norm_w, lp.eps, self.x)
             delta = self._dense_mlp(lp) if lp.dense is not None else self._moe(li, lp)
             if trace is not None:
                 d = delta.float().sum(1) if delta.dim() == 3 else delta.float()

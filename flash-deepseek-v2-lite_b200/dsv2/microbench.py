@@ -31,7 +31,8 @@ def _routing(B, n_exp, g, dev):
     return ids.contiguous(), w.contiguous()
 
 
-def build_case(kernel: str, B: int, family: int, ctx: int, split_len: int | None, dev="cuda"):
+def build_case(kernel: str, B: int, family: int, ctx: int, split_len: int | None, dev="cuda",
+               k_splits: int = 1):
     g = torch.Generator(device=dev).manual_seed(0)
     H, I, E = 2048, 1408, 64
     calls = []
@@ -83,10 +84,17 @@ def build_case(kernel: str, B: int, family: int, ctx: int, split_len: int | None
                         "dense_gate_up": (10944, 2048, True), "dense_down": (2048, 10944, False)}[kernel]
         wt = _rnd(((2 if swiglu else 1) * N, K), g, 0.02)
         x = _rnd((B, K), g)
-        y = torch.zeros(B, N, dtype=torch.bfloat16, device=dev)
-        calls.append(lambda: ops.linear(w=wt, n_rows=N, k=K, up_offset=N * K if swiglu else 0, x=x, y=y,
-                                        epilogue=ops.EPI_SWIGLU if swiglu else ops.EPI_STORE_BF16, n_tokens=B,
-                                        family=family, w_group_rows=(2 if swiglu else 1) * N, x_group_rows=B))
+        if k_splits > 1 and not swiglu:
+            yp = torch.zeros(k_splits, B, N, device=dev)
+            calls.append(lambda: ops.linear(w=wt, n_rows=N, k=K, x=x, y=yp[0], epilogue=ops.EPI_STORE_F32,
+                                            n_tokens=B, family=family, x_group_rows=B, k_splits=k_splits,
+                                            y_split_stride=yp.stride(0)))
+        else:
+            y = torch.zeros(B, N, dtype=torch.bfloat16, device=dev)
+            calls.append(lambda: ops.linear(w=wt, n_rows=N, k=K, up_offset=N * K if swiglu else 0, x=x, y=y,
+                                            epilogue=ops.EPI_SWIGLU if swiglu else ops.EPI_STORE_BF16,
+                                            n_tokens=B, family=family, w_group_rows=(2 if swiglu else 1) * N,
+                                            x_group_rows=B))
         nbytes = wt.numel() * 2
     elif kernel in ("absorb", "unabsorb"):
         kv_b = _rnd((4096, 512), g, 0.05)
@@ -134,21 +142,37 @@ def main():
     ap.add_argument("--family", default="batch", choices=["small", "batch"])
     ap.add_argument("--ctx", type=int, default=576)
     ap.add_argument("--split-len", type=int, default=None)
+    ap.add_argument("--k-splits", type=int, default=1)
+    ap.add_argument("--no-graph", action="store_true", help="issue launches from Python (host-bound)")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args()
     fam = ops.FAMILY_BATCH if a.family == "batch" else ops.FAMILY_SMALL
-    calls, nbytes = build_case(a.kernel, a.batch, fam, a.ctx, a.split_len)
+    calls, nbytes = build_case(a.kernel, a.batch, fam, a.ctx, a.split_len, k_splits=a.k_splits)
     for _ in range(a.warmup):
         for c in calls:
             c()
     torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(a.iters):
-        for c in calls:
-            c()
-    e.record()
+    if a.no_graph:
+        s.record()
+        for _ in range(a.iters):
+            for c in calls:
+                c()
+        e.record()
+    else:
+        # replay the launches from a CUDA graph (as the decode step does), so the timing
+        # is device time, not the host's launch rate
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(a.iters):
+                for c in calls:
+                    c()
+        graph.replay()
+        torch.cuda.synchronize()
+        s.record()
+        graph.replay()
+        e.record()
     torch.cuda.synchronize()
     us = s.elapsed_time(e) * 1000 / a.iters
     print(json.dumps({"kernel": a.kernel, "batch": a.batch, "family": a.family, "ctx": a.ctx, "us": round(us, 2),

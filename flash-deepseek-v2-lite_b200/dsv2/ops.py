@@ -132,7 +132,7 @@ def linear(*, w: torch.Tensor, n_rows: int, k: int, x: torch.Tensor, y: torch.Te
            route_x_row: torch.Tensor | None = None, route_y_row: torch.Tensor | None = None,
            route_scale: torch.Tensor | None = None,
            w_group_rows: int | None = None, x_group_rows: int | None = None,
-           x_base: int | None = None) -> None:
+           x_base: int | None = None, k_splits: int = 1, y_split_stride: int = 0) -> None:
     """Generic linear (see dsv2_linear_args in include/dsv2.h).
 
     Strides are in elements; defaults take them from the 2-D views of w / x / y.
@@ -161,6 +161,8 @@ def linear(*, w: torch.Tensor, n_rows: int, k: int, x: torch.Tensor, y: torch.Te
     a.route_scale = _ptr(route_scale)
     a.w_group_rows = n_rows if w_group_rows is None else w_group_rows
     a.x_group_rows = (n_tokens if x_group_rows is None else x_group_rows)
+    a.k_splits = k_splits
+    a.y_split_stride = y_split_stride
     _lib.call("dsv2_linear", ctypes.byref(a), family, stream())
 
 
@@ -221,19 +223,31 @@ def _check_cache(cache: torch.Tensor) -> None:
 
 def mla_prep(*, qkva: torch.Tensor, kv_norm_w: torch.Tensor, eps: float, cos: torch.Tensor,
              sin: torch.Tensor, positions: torch.Tensor, cache: torch.Tensor,
-             q_pe_out: torch.Tensor) -> None:
-    """cache: [B, max_len, 576] (one layer, any batch stride); positions int64 [1] or [B]."""
+             q_pe_out: torch.Tensor, q_nope_out: torch.Tensor | None = None) -> None:
+    """New-token preparation for one layer.
+
+    qkva: bf16 [B, 3648], or fp32 split-K partial sums [S, B, 3648] (summed here);
+    cache: [B, max_len, 576] (one layer); positions int64 [1] or [B];
+    q_nope_out (optional): bf16 [B, 16, 128] copy of the (summed) q_nope."""
     _cuda(qkva, "qkva")
-    if qkva.dtype != torch.bfloat16 or qkva.stride(1) != 1 or qkva.shape[1] != 3648:
-        raise NotImplementedError("mla_prep expects bf16 qkva [B, 3648] with contiguous rows")
+    if qkva.dim() == 2 and qkva.dtype == torch.bfloat16:
+        dt, parts, pstride, rstride, batch = DSV2_BF16, 1, 0, qkva.stride(0), qkva.shape[0]
+    elif qkva.dim() == 3 and qkva.dtype == torch.float32:
+        dt, parts, pstride, rstride, batch = DSV2_F32, qkva.shape[0], qkva.stride(0), qkva.stride(1), qkva.shape[1]
+    else:
+        raise NotImplementedError("mla_prep expects bf16 qkva [B, 3648] or fp32 partials [S, B, 3648]")
+    if qkva.stride(-1) != 1 or qkva.shape[-1] != 3648:
+        raise NotImplementedError("mla_prep expects 3648-wide rows with a contiguous last dimension")
     if not q_pe_out.is_contiguous() or cos.stride(1) != 1 or sin.stride(1) != 1:
         raise NotImplementedError("mla_prep requires contiguous q_pe_out and rope tables")
+    if q_nope_out is not None and (not q_nope_out.is_contiguous() or q_nope_out.dtype != torch.bfloat16):
+        raise NotImplementedError("q_nope_out must be a contiguous bf16 [B, 16, 128] tensor")
     if cos.dtype != torch.float32 or sin.dtype != torch.float32:
         raise NotImplementedError("rope tables must be fp32")
     _check_cache(cache)
     a = MlaPrepArgs()
     a.qkva = qkva.data_ptr()
-    a.qkva_row_stride = qkva.stride(0)
+    a.qkva_row_stride = rstride
     a.kv_norm_w = kv_norm_w.data_ptr()
     a.eps = float(eps)
     a.cos_tab = cos.data_ptr()
@@ -246,7 +260,11 @@ def mla_prep(*, qkva: torch.Tensor, kv_norm_w: torch.Tensor, eps: float, cos: to
     a.cache_b_stride = cache.stride(0)
     a.max_len = cache.shape[1]
     a.q_pe_out = q_pe_out.data_ptr()
-    a.batch = qkva.shape[0]
+    a.batch = batch
+    a.qkva_dtype = dt
+    a.qkva_parts = parts
+    a.qkva_part_stride = pstride
+    a.q_nope_out = _ptr(q_nope_out)
     _lib.call("dsv2_mla_prep", ctypes.byref(a), stream())
 
 

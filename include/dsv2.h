@@ -157,6 +157,11 @@ typedef struct dsv2_linear_args {
   const float* route_scale;
   int64_t w_group_rows;
   int64_t x_group_rows;
+  /* batch family, dense mode, DSV2_EPI_STORE_F32 only: split K over k_splits CTAs
+   * (1 <= k_splits <= k/64); split s writes its fp32 partial sum at y + s * y_split_stride,
+   * the caller sums the partials (e.g. dsv2_add_rmsnorm with fp32 parts).  0 or 1 = no split. */
+  int32_t k_splits;
+  int64_t y_split_stride;
 } dsv2_linear_args;
 
 DSV2_API int dsv2_linear(const dsv2_linear_args* args, int family, void* stream);
@@ -245,6 +250,13 @@ typedef struct dsv2_mla_prep_args {
   int32_t max_len;
   void* q_pe_out;
   int32_t batch;
+  /* qkva element type: DSV2_BF16 (one [B, 3648] matrix) or DSV2_F32 (qkva_parts split-K
+   * partial sums at qkva + p * qkva_part_stride, summed and rounded to bf16 here) */
+  int32_t qkva_dtype;
+  int32_t qkva_parts;
+  int64_t qkva_part_stride;
+  /* optional [B, 16, 128] bf16 copy of q_nope (the input of the absorbed projection) */
+  void* q_nope_out;
 } dsv2_mla_prep_args;
 
 DSV2_API int dsv2_mla_prep(const dsv2_mla_prep_args* args, void* stream);
