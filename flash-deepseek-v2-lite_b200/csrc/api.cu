@@ -365,14 +365,16 @@ int dsv2_router(const dsv2_router_args* a, void* stream) {
     return fail(DSV2_ERR_INVALID, "router: null pointer");
   if (a->n_experts <= 0 || a->n_experts > 64)
     return fail(DSV2_ERR_UNSUPPORTED, "router: n_experts=%d (max 64)", a->n_experts);
-  if (a->hidden % 8 || !aligned16(a->x) || a->x_row_stride % 8)
+  if (a->hidden > 2048 || a->hidden % 64)
+    return fail(DSV2_ERR_UNSUPPORTED, "router: hidden %d (need a multiple of 64, <= 2048)", a->hidden);
+  if (a->rows > 4096) return fail(DSV2_ERR_UNSUPPORTED, "router: at most 4096 rows (got %d)", a->rows);
+  if (!aligned16(a->x) || a->x_row_stride % 8)
     return fail(DSV2_ERR_INVALID, "router: activations must be 16-byte aligned rows");
   if (a->w_dtype != DSV2_BF16 && a->w_dtype != DSV2_F32)
     return fail(DSV2_ERR_UNSUPPORTED, "router: gate dtype %d", a->w_dtype);
+  if (a->gather_out && (!a->group_offsets || !aligned16(a->gather_out)))
+    return fail(DSV2_ERR_INVALID, "router: gather_out needs bucketing and 16-byte alignment");
   if (a->rows <= 0) return DSV2_OK;
-  const int experts_per_cta = a->rows <= 16 ? 8 : a->n_experts;
-  const bool need_ticket = experts_per_cta < a->n_experts || a->group_offsets;
-  if (need_ticket && !a->ticket) return fail(DSV2_ERR_INVALID, "router: ticket buffer required");
   if (a->group_offsets) {
     if (!a->route_token || !a->route_slot || !a->route_weight)
       return fail(DSV2_ERR_INVALID, "router: bucketing outputs missing");
@@ -394,8 +396,10 @@ int dsv2_router(const dsv2_router_args* a, void* stream) {
   p.topk_ids = reinterpret_cast<long long*>(a->topk_ids64);
   p.topk_ids32 = a->topk_ids32;
   p.topk_w = a->topk_weights;
-  p.ticket = a->ticket;
-  p.experts_per_cta = experts_per_cta;
+  p.ticket = nullptr;
+  p.experts_per_cta = a->n_experts;
+  p.gather_x = a->gather_out ? 1 : 0;
+  p.gather_out = a->gather_out;
   p.expert_lo = a->expert_lo;
   p.n_local = a->n_local;
   p.shared_lo = a->shared_lo;
@@ -423,14 +427,21 @@ int dsv2_softmax_topk(const float* logits, int rows, int n_experts, float scalin
 int dsv2_moe_bucket(const int32_t* topk_ids32, const float* topk_weights, int rows,
                     int expert_lo, int n_local, int shared_lo, int shared_hi,
                     int32_t* group_offsets, int32_t* route_token, int32_t* route_slot,
-                    float* route_weight, void* stream) {
+                    float* route_weight, const void* gather_src, int64_t gather_src_stride,
+                    void* gather_out, int cols, void* stream) {
   if (!topk_ids32 || !topk_weights || !group_offsets || !route_token || !route_slot || !route_weight)
     return fail(DSV2_ERR_INVALID, "moe_bucket: null pointer");
+  if (rows > 4096) return fail(DSV2_ERR_UNSUPPORTED, "moe_bucket: at most 4096 rows (got %d)", rows);
   if (n_local < 0 || n_local > 64 || shared_lo < 0 || shared_hi < shared_lo || shared_hi > rows)
     return fail(DSV2_ERR_INVALID, "moe_bucket: bad ranges");
+  if (gather_out && (!gather_src || cols % 8 || gather_src_stride % 8 || !aligned16(gather_src) ||
+                     !aligned16(gather_out)))
+    return fail(DSV2_ERR_INVALID, "moe_bucket: gather rows must be 16-byte aligned");
+  if (rows <= 0) return DSV2_OK;
   return check_launch(launch_bucket(topk_ids32, topk_weights, rows, expert_lo, n_local, shared_lo,
-                                    shared_hi, group_offsets, route_token, route_slot,
-                                    route_weight, static_cast<cudaStream_t>(stream)),
+                                    shared_hi, group_offsets, route_token, route_slot, route_weight,
+                                    gather_out ? gather_src : nullptr, gather_src_stride, gather_out,
+                                    cols, static_cast<cudaStream_t>(stream)),
                       "moe_bucket");
 }
 
@@ -511,11 +522,11 @@ int dsv2_mla_decode(const dsv2_mla_decode_args* a, void* stream) {
   p.n_splits = a->n_splits;
   p.o_part = a->o_part;
   p.ml_part = a->ml_part;
+  p.o_lat = reinterpret_cast<bf16*>(a->o_lat);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   rc = check_launch(launch_mla_decode(p, a->batch, st), "mla_decode");
   if (rc) return rc;
-  return check_launch(launch_mla_combine(a->o_part, a->ml_part, a->n_splits, a->o_lat, a->batch, st),
-                      "mla_combine");
+  return check_launch(launch_mla_combine(p, a->batch, st), "mla_combine");
 }
 
 // Same computation as dsv2_mla_decode, with the split partials kept in the library's
@@ -560,11 +571,11 @@ int dsv2_mla_decode_noalloc(const void* q_abs, const void* q_pe, const void* cac
   p.n_splits = static_cast<int>(n_splits);
   p.o_part = o_part;
   p.ml_part = ml_part;
+  p.o_lat = reinterpret_cast<bf16*>(o_lat);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   rc = check_launch(launch_mla_decode(p, batch, st), "mla_decode_noalloc");
   if (rc) return rc;
-  return check_launch(launch_mla_combine(o_part, ml_part, p.n_splits, o_lat, batch, st),
-                      "mla_decode_noalloc: combine");
+  return check_launch(launch_mla_combine(p, batch, st), "mla_decode_noalloc: combine");
 }
 
 }  // extern "C"

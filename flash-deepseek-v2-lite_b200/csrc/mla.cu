@@ -31,7 +31,7 @@ constexpr int kRope = 64;
 constexpr int kRow = kLatent + kRope;           // 576
 constexpr int kRowBytes = kRow * 2;             // 1152
 constexpr int kChunks = kRow / 64;              // 9 swizzle chunks of 64 dims
-constexpr int kTile = 64;                       // positions per tile
+constexpr int kTile = 32;                       // positions per tile (two CTAs per SM)
 constexpr int kStages = 2;
 constexpr int kTileBytes = kTile * kRowBytes;   // 73728
 constexpr int kQBytes = kHeads * kRowBytes;     // 18432
@@ -143,7 +143,7 @@ __device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, 
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n));
 }
 
-__global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDecodeParams p) {
+__global__ __launch_bounds__(kMlaThreads, 2) void mla_decode_kernel(const MlaDecodeParams p) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* s_q = smem;                                     // 9 chunks x 16 rows x 128 B
   unsigned char* s_kv = smem + kQBytes;                          // stages x 9 chunks x 64 rows x 128 B
@@ -225,15 +225,15 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
     cp_async_commit();
     const unsigned char* kv = s_kv + stage * kTileBytes;
 
-    // --- partial scores over this warp's 144 dims for all 64 positions
-    float sc[8][4];
+    // --- partial scores over this warp's 144 dims for all positions of the tile
+    float sc[kTile / 8][4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+    for (int j = 0; j < kTile / 8; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
 #pragma unroll
     for (int ks = 0; ks < 9; ++ks) {
       const int d0 = warp * 144 + ks * 16;
 #pragma unroll
-      for (int np = 0; np < 4; ++np) {  // pairs of n8 tiles (16 positions)
+      for (int np = 0; np < kTile / 16; ++np) {  // pairs of n8 tiles (16 positions)
         const int mi = lane >> 3, ri = lane & 7;
         const int r = np * 16 + (mi >> 1) * 8 + ri;
         const int d = d0 + (mi & 1) * 8;
@@ -245,7 +245,7 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
     }
     float* red_w = s_red + warp * kHeads * kSRedStride;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < kTile / 8; ++j) {
       const int c = j * 8 + 2 * tq;
       red_w[gq * kSRedStride + c] = sc[j][0];
       red_w[gq * kSRedStride + c + 1] = sc[j][1];
@@ -254,14 +254,15 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
     }
     __syncthreads();
 
-    // --- online softmax (log2 domain) for head hs, positions [8*js, 8*js+8)
+    // --- online softmax (log2 domain) for head hs, positions [kPT*js, kPT*js + kPT)
     {
+      constexpr int kPT = kTile / 8;
       const int t0 = s_beg + ti * kTile;
-      float s[8];
+      float s[kPT];
       float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int c = js * 8 + i;
+      for (int i = 0; i < kPT; ++i) {
+        const int c = js * kPT + i;
         float v = 0.f;
 #pragma unroll
         for (int w = 0; w < 4; ++w) v += s_red[(w * kHeads + hs) * kSRedStride + c];
@@ -274,9 +275,9 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
       const float m_new = fmaxf(m_run, mx);
       const float alpha = exp2f(m_run - m_new);
       float sum = 0.f;
-      uint32_t pk[4];
+      uint32_t pk[kPT / 2];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < kPT / 2; ++i) {
         const float p0 = exp2f(s[2 * i] - m_new), p1 = exp2f(s[2 * i + 1] - m_new);
         pk[i] = pack_bf16x2(p0, p1);
         sum += p0 + p1;
@@ -285,7 +286,9 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
       for (int o = 1; o < 8; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
       l_run = l_run * alpha + sum;
       m_run = m_new;
-      *reinterpret_cast<uint4*>(s_p + hs * kPStride + js * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      uint32_t* prow = reinterpret_cast<uint32_t*>(s_p + hs * kPStride + js * kPT);
+#pragma unroll
+      for (int i = 0; i < kPT / 2; ++i) prow[i] = pk[i];
       if (js == 0) s_alpha[hs] = alpha;
     }
     __syncthreads();
@@ -322,6 +325,22 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
   }
   cp_async_wait<0>();
 
+  if (len <= p.split_len) {
+    // the whole row fitted in this one split: normalise and write o_lat directly
+    // (no partials, and the merge kernel skips the row)
+    if (js == 0) s_alpha[hs] = 1.f / l_run;
+    __syncthreads();
+    const float i0 = s_alpha[gq], i1 = s_alpha[gq + 8];
+    bf16* ob = p.o_lat + static_cast<long long>(b) * kHeads * kLatent;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int d = warp * 128 + j * 8 + 2 * tq;
+      *reinterpret_cast<uint32_t*>(ob + gq * kLatent + d) = pack_bf16x2(o_acc[j][0] * i0, o_acc[j][1] * i0);
+      *reinterpret_cast<uint32_t*>(ob + (gq + 8) * kLatent + d) =
+          pack_bf16x2(o_acc[j][2] * i1, o_acc[j][3] * i1);
+    }
+    return;
+  }
   // --- write partial results
   float* op = p.o_part + ((static_cast<long long>(b) * p.n_splits + split) * kHeads) * kLatent;
 #pragma unroll
@@ -337,10 +356,15 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
 }
 
 // o_lat[b, h, :] = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s   (bf16 out)
+// (rows whose length fits one split were written directly by mla_decode_kernel)
 __global__ __launch_bounds__(128) void mla_combine_kernel(const float* __restrict__ o_part,
                                                           const float* __restrict__ ml_part,
-                                                          int n_splits, bf16* __restrict__ o_lat) {
+                                                          int n_splits, bf16* __restrict__ o_lat,
+                                                          const long long* __restrict__ positions,
+                                                          int pos_numel, int max_len, int split_len) {
   const int b = blockIdx.x, h = blockIdx.y;
+  const long long len = min(static_cast<long long>(max_len), positions[pos_numel == 1 ? 0 : b] + 1);
+  if (len <= split_len) return;
   const float* ml = ml_part + (static_cast<long long>(b) * n_splits) * kHeads * 2;
   float M = -INFINITY;
   for (int s = 0; s < n_splits; ++s) {
@@ -416,10 +440,10 @@ cudaError_t launch_mla_decode(const MlaDecodeParams& p, int batch, cudaStream_t 
   return cudaGetLastError();
 }
 
-cudaError_t launch_mla_combine(const float* o_part, const float* ml_part, int n_splits, void* o_lat,
-                               int batch, cudaStream_t st) {
-  mla_combine_kernel<<<dim3(batch, kHeads), 128, 0, st>>>(o_part, ml_part, n_splits,
-                                                           reinterpret_cast<bf16*>(o_lat));
+cudaError_t launch_mla_combine(const MlaDecodeParams& p, int batch, cudaStream_t st) {
+  mla_combine_kernel<<<dim3(batch, kHeads), 128, 0, st>>>(p.o_part, p.ml_part, p.n_splits, p.o_lat,
+                                                           p.positions, p.pos_numel, p.max_len,
+                                                           p.split_len);
   return cudaGetLastError();
 }
 

@@ -29,6 +29,8 @@ struct RouterParams {
   int* route_token;        // [rows*6 + 2*(shared_hi-shared_lo)]
   int* route_slot;
   float* route_weight;
+  int gather_x;            // copy each route's x row into gather_out (expert order)
+  void* gather_out;
 };
 
 struct MlaPrepParams {
@@ -65,6 +67,7 @@ struct MlaDecodeParams {
   int n_splits;
   float* o_part;               // [B, n_splits, 16, 512]
   float* ml_part;              // [B, n_splits, 16, 2]  (m in log2 domain, l)
+  bf16* o_lat;                 // [B, 16, 512] output
 };
 
 // norm.cu
@@ -85,7 +88,7 @@ cudaError_t launch_advance_positions(long long*, int, cudaStream_t);
 // router.cu
 cudaError_t launch_router(const RouterParams&, cudaStream_t);
 cudaError_t launch_bucket(const int*, const float*, int, int, int, int, int, int*, int*, int*,
-                          float*, cudaStream_t);
+                          float*, const void*, long long, void*, int, cudaStream_t);
 cudaError_t launch_softmax_topk(const float*, int, int, float, long long*, int*, float*,
                                 cudaStream_t);
 cudaError_t launch_gather_rows(const void*, long long, const int*, const int*, int, void*, int,
@@ -94,7 +97,7 @@ cudaError_t launch_gather_rows(const void*, long long, const int*, const int*, i
 cudaError_t launch_mla_prep(const MlaPrepParams&, int, cudaStream_t);
 cudaError_t mla_decode_init();
 cudaError_t launch_mla_decode(const MlaDecodeParams&, int, cudaStream_t);
-cudaError_t launch_mla_combine(const float*, const float*, int, void*, int, cudaStream_t);
+cudaError_t launch_mla_combine(const MlaDecodeParams&, int, cudaStream_t);
 // linear_tc.cu (TcShape, tc_launch_shape and launch_linear_tc_impl are defined there; the
 // unity build includes it before api.cu)
 cudaError_t linear_tc_init();

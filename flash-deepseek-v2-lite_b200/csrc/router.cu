@@ -1,4 +1,4 @@
-// Fused MoE router: fp32 gate GEMV + softmax + top-6 + token-to-expert bucketing.
+// Fused MoE router: fp32 gate GEMV + softmax + top-6, then token-to-expert bucketing.
 //
 // Replaces (Flash-DeepSeeek-V2-Lite):
 //   moe_router.py:8-60          _router_softmax_topk6_kernel (softmax over 64 logits, six
@@ -9,27 +9,32 @@
 // The gate logits follow the HF MoE gate (fp32 linear over bf16 inputs; softmax in
 // fp32; greedy top-k; no renormalisation; weights scaled by routed_scaling_factor).
 //
-// Bucketing is a stable counting sort: routes are ranked inside each warp with
-// __match_any_sync + popc and across warps with a per-expert scan, so the route
-// order inside every expert bucket is ascending in (token, k) and identical from
-// run to run.  Two extra "shared" groups carry every local token with weight 1,
-// which lets the MoE kernels run the two shared experts in the same launch as
-// the routed ones.  The bucketing stage runs in the last CTA to finish (atomic
-// ticket), so routing plus bucketing is one launch.
+// router_topk_kernel: one CTA per 8 tokens computes all 64 logits on the tensor cores
+// (mma.sync m16n8k16, experts as M, tokens as N; bf16 products are exact in fp32, so
+// this is the fp32 linear up to summation order), warps split K and meet in shared
+// memory, then one warp per token does the softmax and the six argmax rounds
+// (lowest index first on ties).
+//
+// route_kernel: stable counting sort of the routes by local expert.  Every CTA counts
+// all routes per expert (the top-k ids are a few KB) and the routes of earlier tokens,
+// so it knows where its own tokens' routes go without any grid-wide synchronisation;
+// inside a CTA, routes are ranked in (token, k) order.  Two extra "shared" groups
+// carry the local tokens with weight 1 (slots 6 and 7), so the MoE kernels run the two
+// shared experts in the same launch as the routed ones.  Optionally the same kernel
+// copies each route's activation row into expert-contiguous order for the TMA path.
 #include "params.cuh"
 
 namespace dsv2 {
 
-constexpr int kRouterThreads = 256;
 constexpr int kTopK = 6;
 constexpr int kMaxExperts = 64;
-constexpr int kSlots = 8;  // 6 routed + 2 shared-expert halves per token
-
-
-__device__ __forceinline__ float load_gate_w(const void* w, int dt, long long i) {
-  return dt == 2 ? reinterpret_cast<const float*>(w)[i]
-                 : __bfloat162float(reinterpret_cast<const bf16*>(w)[i]);
-}
+constexpr int kSlots = 8;              // 6 routed + 2 shared-expert halves per token
+constexpr int kRtTok = 8;              // tokens per CTA (the mma N dimension)
+constexpr int kRtThreads = 256;        // 8 warps: 4 expert blocks of 16 x 2 K halves
+constexpr int kRtMaxHidden = 2048;
+constexpr int kRouteTok = 8;           // tokens per route_kernel CTA
+constexpr int kRouteThreads = 256;
+constexpr int kRouteMaxRows = 4096;
 
 // softmax + top-6 for one token with one warp; logits in shared/global memory.
 __device__ void softmax_topk_warp(const float* lg, int n_experts, float scaling, int row,
@@ -64,152 +69,205 @@ __device__ void softmax_topk_warp(const float* lg, int n_experts, float scaling,
   }
 }
 
-// Stable bucketing of all routes by local expert (+ the two shared groups).
-// Must be called by every thread of one CTA (blockDim.x == kRouterThreads).
-__device__ void bucket_routes(const int* ids32, const float* tw, int rows, int expert_lo,
-                              int n_local, int shared_lo, int shared_hi, int* group_offsets,
-                              int* route_token, int* route_slot, float* route_weight) {
-  constexpr int NW = kRouterThreads / 32;
-  __shared__ int s_cnt[kMaxExperts];
-  __shared__ int s_off[kMaxExperts + 3];
-  __shared__ int s_run[kMaxExperts];
-  __shared__ int s_wh[NW][kMaxExperts];
+// ---------------------------------------------------------------------------------
+// logits + softmax + top-6
+// ---------------------------------------------------------------------------------
+__global__ __launch_bounds__(kRtThreads) void router_topk_kernel(const RouterParams p) {
+  constexpr int XS = kRtMaxHidden + 8;  // padded row (bank spread for the 16-byte reads)
+  __shared__ __align__(16) bf16 s_x[kRtTok][XS];
+  __shared__ float s_part[2][kMaxExperts][kRtTok];
+  __shared__ float s_logits[kRtTok][kMaxExperts];
+  const int row0 = blockIdx.x * kRtTok;
+  const int nt = min(kRtTok, p.rows - row0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int i = tid; i < kMaxExperts; i += kRouterThreads) { s_cnt[i] = 0; s_run[i] = 0; }
-  __syncthreads();
-  const int n_routes = rows * kTopK;
-  for (int r = tid; r < n_routes; r += kRouterThreads) {
-    const int e = __ldcg(ids32 + r) - expert_lo;
-    if (e >= 0 && e < n_local) atomicAdd(&s_cnt[e], 1);
-  }
-  __syncthreads();
-  if (tid == 0) {
-    int acc = 0;
-    for (int e = 0; e < n_local; ++e) { s_off[e] = acc; acc += s_cnt[e]; }
-    const int nsh = shared_hi - shared_lo;
-    s_off[n_local] = acc;
-    s_off[n_local + 1] = acc + nsh;
-    s_off[n_local + 2] = acc + 2 * nsh;
-    for (int e = 0; e <= n_local + 2; ++e) group_offsets[e] = s_off[e];
-  }
-  __syncthreads();
-  for (int base = 0; base < n_routes; base += kRouterThreads) {
-    const int r = base + tid;
-    int key = -1;
-    if (r < n_routes) {
-      const int e = __ldcg(ids32 + r) - expert_lo;
-      if (e >= 0 && e < n_local) key = e;
-    }
-    const unsigned peers = __match_any_sync(0xffffffffu, key);
-    const int rank = __popc(peers & ((1u << lane) - 1u));
-    for (int i = tid; i < NW * kMaxExperts; i += kRouterThreads) (&s_wh[0][0])[i] = 0;
-    __syncthreads();
-    if (key >= 0 && rank == 0) s_wh[warp][key] = __popc(peers);
-    __syncthreads();
-    // exclusive scan over warps per expert; the chunk total goes to s_run afterwards
-    if (tid < n_local) {
-      int acc = 0;
-      for (int w = 0; w < NW; ++w) { const int c = s_wh[w][tid]; s_wh[w][tid] = acc; acc += c; }
-      s_cnt[tid] = acc;  // reuse as chunk total
-    }
-    __syncthreads();
-    if (key >= 0) {
-      const int pos = s_off[key] + s_run[key] + s_wh[warp][key] + rank;
-      const int b = r / kTopK, k = r % kTopK;
-      route_token[pos] = b;
-      route_slot[pos] = b * kSlots + k;
-      route_weight[pos] = __ldcg(tw + r);
-    }
-    __syncthreads();
-    if (tid < n_local) s_run[tid] += s_cnt[tid];
-    __syncthreads();
-  }
-  // shared-expert groups: every local row, weight 1
-  const int nsh = shared_hi - shared_lo;
-  for (int i = tid; i < 2 * nsh; i += kRouterThreads) {
-    const int s = i / nsh, b = shared_lo + (i % nsh);
-    const int pos = s_off[n_local + s] + (i % nsh);
-    route_token[pos] = b;
-    route_slot[pos] = b * kSlots + kTopK + s;
-    route_weight[pos] = 1.f;
-  }
-}
-
-__global__ __launch_bounds__(kRouterThreads) void router_kernel(const RouterParams p) {
-  __shared__ float s_logits[kMaxExperts];
-  __shared__ bool s_last;
-  const int row = blockIdx.x;
-  const int eg = blockIdx.y;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const bf16* xr = p.x + row * p.x_row_stride;
   const int nch = p.hidden / 8;
-  const int e_beg = eg * p.experts_per_cta;
-  const int e_end = min(p.n_experts, e_beg + p.experts_per_cta);
-  for (int e = e_beg + warp; e < e_end; e += kRouterThreads / 32) {
-    float acc = 0.f;
-    if (p.w_dtype == 0) {
-      const bf16* wr = reinterpret_cast<const bf16*>(p.w) + static_cast<long long>(e) * p.hidden;
-      for (int c = lane; c < nch; c += 32)
-        acc = dot8(*reinterpret_cast<const uint4*>(xr + c * 8), *reinterpret_cast<const uint4*>(wr + c * 8), acc);
-    } else {
-      const float* wr = reinterpret_cast<const float*>(p.w) + static_cast<long long>(e) * p.hidden;
-      for (int c = lane; c < nch; c += 32) {
-        const uint4 u = *reinterpret_cast<const uint4*>(xr + c * 8);
-        const uint32_t* up = reinterpret_cast<const uint32_t*>(&u);
-        const float4 w0 = *reinterpret_cast<const float4*>(wr + c * 8);
-        const float4 w1 = *reinterpret_cast<const float4*>(wr + c * 8 + 4);
-        acc = fmaf(bf16lo(up[0]), w0.x, acc); acc = fmaf(bf16hi(up[0]), w0.y, acc);
-        acc = fmaf(bf16lo(up[1]), w0.z, acc); acc = fmaf(bf16hi(up[1]), w0.w, acc);
-        acc = fmaf(bf16lo(up[2]), w1.x, acc); acc = fmaf(bf16hi(up[2]), w1.y, acc);
-        acc = fmaf(bf16lo(up[3]), w1.z, acc); acc = fmaf(bf16hi(up[3]), w1.w, acc);
+  for (int i = tid; i < kRtTok * nch; i += kRtThreads) {
+    const int t = i / nch, c = i % nch;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (t < nt) v = *reinterpret_cast<const uint4*>(p.x + (row0 + t) * p.x_row_stride + c * 8);
+    *reinterpret_cast<uint4*>(&s_x[t][c * 8]) = v;
+  }
+  __syncthreads();
+  // warp -> experts [16*eb, 16*eb + 16), K half kh
+  const int eb = warp & 3, kh = warp >> 2;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int eA = eb * 16 + gq, eB = eA + 8;
+  const bool okA = eA < p.n_experts, okB = eB < p.n_experts;
+  float c[4] = {0.f, 0.f, 0.f, 0.f};
+  const int nkb = p.hidden / 32;              // 32-wide K blocks
+  const int kb_beg = kh * (nkb / 2), kb_end = kh ? nkb : nkb / 2;
+  const bf16* xr = &s_x[gq][tq * 8];
+  if (p.w_dtype == 0) {
+    const bf16* wA = reinterpret_cast<const bf16*>(p.w) + static_cast<long long>(okA ? eA : 0) * p.hidden + tq * 8;
+    const bf16* wB = reinterpret_cast<const bf16*>(p.w) + static_cast<long long>(okB ? eB : 0) * p.hidden + tq * 8;
+    for (int kb0 = kb_beg; kb0 < kb_end; kb0 += 8) {
+      uint4 a[8], b[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int kb = kb0 + u;
+        a[u] = (kb < kb_end && okA) ? *reinterpret_cast<const uint4*>(wA + kb * 32) : make_uint4(0, 0, 0, 0);
+        b[u] = (kb < kb_end && okB) ? *reinterpret_cast<const uint4*>(wB + kb * 32) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int kb = kb0 + u;
+        if (kb >= kb_end) break;
+        const uint4 xv = *reinterpret_cast<const uint4*>(xr + kb * 32);
+        const uint32_t a0[4] = {a[u].x, b[u].x, a[u].y, b[u].y};
+        mma_bf16_16816(c, a0, xv.x, xv.y);
+        const uint32_t a1[4] = {a[u].z, b[u].z, a[u].w, b[u].w};
+        mma_bf16_16816(c, a1, xv.z, xv.w);
       }
     }
-    acc = warp_sum(acc);
-    if (p.bias) acc += p.bias[e];
-    if (lane == 0) {
-      s_logits[e - e_beg] = acc;
-      p.logits[row * p.n_experts + e] = acc;
+  } else {
+    // fp32 gate weights: CUDA-core path (exact fp32 products); thread (gq, tq) owns the
+    // same (expert, token) outputs as its mma fragment would
+    const float* wf = reinterpret_cast<const float*>(p.w);
+    for (int k = kb_beg * 32; k < kb_end * 32; ++k) {
+      const float x0 = __bfloat162float(s_x[2 * tq][k]), x1 = __bfloat162float(s_x[2 * tq + 1][k]);
+      const float wa = okA ? wf[static_cast<long long>(eA) * p.hidden + k] : 0.f;
+      const float wb = okB ? wf[static_cast<long long>(eB) * p.hidden + k] : 0.f;
+      c[0] = fmaf(wa, x0, c[0]); c[1] = fmaf(wa, x1, c[1]);
+      c[2] = fmaf(wb, x0, c[2]); c[3] = fmaf(wb, x1, c[3]);
+    }
+  }
+  // C fragment: (expert gq, tokens 2tq, 2tq+1), (expert gq+8, ...)
+  s_part[kh][eb * 16 + gq][2 * tq] = c[0];
+  s_part[kh][eb * 16 + gq][2 * tq + 1] = c[1];
+  s_part[kh][eb * 16 + gq + 8][2 * tq] = c[2];
+  s_part[kh][eb * 16 + gq + 8][2 * tq + 1] = c[3];
+  __syncthreads();
+  for (int i = tid; i < kRtTok * kMaxExperts; i += kRtThreads) {
+    const int t = i / kMaxExperts, e = i % kMaxExperts;
+    if (e < p.n_experts && t < nt) {
+      float v = s_part[0][e][t] + s_part[1][e][t];
+      if (p.bias) v += p.bias[e];
+      s_logits[t][e] = v;
+      p.logits[(row0 + t) * p.n_experts + e] = v;
     }
   }
   __syncthreads();
-  const bool full = (p.experts_per_cta >= p.n_experts);
-  if (full && warp == 0)
-    softmax_topk_warp(s_logits, p.n_experts, p.scaling, row, p.topk_ids, p.topk_ids32, p.topk_w);
-  if (full && p.group_offsets == nullptr) return;
-  // ticket: the last CTA finishes top-k (when split) and bucketing
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned total = gridDim.x * gridDim.y;
-    const unsigned t = atomicAdd(p.ticket, 1u);
-    s_last = (t == total - 1);
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  if (!full) {
-    for (int r = warp; r < p.rows; r += kRouterThreads / 32) {
-      __shared__ float lg[kRouterThreads / 32][kMaxExperts];
-      for (int e = lane; e < p.n_experts; e += 32) lg[warp][e] = __ldcg(p.logits + r * p.n_experts + e);
-      __syncwarp();
-      softmax_topk_warp(lg[warp], p.n_experts, p.scaling, r, p.topk_ids, p.topk_ids32, p.topk_w);
-      __syncwarp();
-    }
-    __threadfence();
-    __syncthreads();
-  }
-  if (p.group_offsets)
-    bucket_routes(p.topk_ids32, p.topk_w, p.rows, p.expert_lo, p.n_local, p.shared_lo,
-                  p.shared_hi, p.group_offsets, p.route_token, p.route_slot, p.route_weight);
-  if (threadIdx.x == 0) *p.ticket = 0u;
+  if (warp < nt)
+    softmax_topk_warp(s_logits[warp], p.n_experts, p.scaling, row0 + warp, p.topk_ids, p.topk_ids32,
+                      p.topk_w);
 }
 
-// Standalone bucketing (expert parallel: runs after the all-gather of top-k results).
-__global__ __launch_bounds__(kRouterThreads) void bucket_kernel(
-    const int* ids32, const float* tw, int rows, int expert_lo, int n_local, int shared_lo,
-    int shared_hi, int* group_offsets, int* route_token, int* route_slot, float* route_weight) {
-  bucket_routes(ids32, tw, rows, expert_lo, n_local, shared_lo, shared_hi, group_offsets,
-                route_token, route_slot, route_weight);
+// ---------------------------------------------------------------------------------
+// bucketing (+ optional gather of activation rows)
+// ---------------------------------------------------------------------------------
+struct RouteParams {
+  const int* ids32;        // [rows, 6]
+  const float* tw;         // [rows, 6]
+  int rows;
+  int expert_lo, n_local;
+  int shared_lo, shared_hi;
+  int* group_offsets;      // [n_local + 3]
+  int* route_token;
+  int* route_slot;
+  float* route_weight;
+  const bf16* gx;          // optional gather source [rows, cols]
+  long long gx_stride;
+  bf16* gout;              // optional gather destination [routes, cols]
+  int cols;
+};
+
+__global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams p) {
+  __shared__ int s_total[kMaxExperts];
+  __shared__ int s_before[kMaxExperts];
+  __shared__ int s_off[kMaxExperts + 3];
+  __shared__ int s_e[kRouteTok * kTopK];
+  __shared__ int s_pos[kRouteTok * kTopK + 2 * kRouteTok];
+  __shared__ int s_tok[kRouteTok * kTopK + 2 * kRouteTok];
+  const int tid = threadIdx.x;
+  const int tok0 = blockIdx.x * kRouteTok;
+  const int ntok = min(kRouteTok, p.rows - tok0);
+  for (int i = tid; i < kMaxExperts; i += kRouteThreads) { s_total[i] = 0; s_before[i] = 0; }
+  __syncthreads();
+  const int n_routes = p.rows * kTopK;
+  const int r_first = tok0 * kTopK;
+  for (int r = tid; r < n_routes; r += kRouteThreads) {
+    const int e = p.ids32[r] - p.expert_lo;
+    if (e >= 0 && e < p.n_local) {
+      atomicAdd(&s_total[e], 1);
+      if (r < r_first) atomicAdd(&s_before[e], 1);
+    }
+  }
+  __syncthreads();
+  if (tid < 32) {  // exclusive scan of the expert totals (64 = 2 per lane)
+    const int lane = tid;
+    const int a = lane * 2 < p.n_local ? s_total[lane * 2] : 0;
+    const int b = lane * 2 + 1 < p.n_local ? s_total[lane * 2 + 1] : 0;
+    int incl = a + b;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const int excl = incl - a - b;
+    if (lane * 2 < p.n_local) s_off[lane * 2] = excl;
+    if (lane * 2 + 1 < p.n_local) s_off[lane * 2 + 1] = excl + a;
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    if (lane == 0) {
+      const int nsh = p.shared_hi - p.shared_lo;
+      s_off[p.n_local] = total;
+      s_off[p.n_local + 1] = total + nsh;
+      s_off[p.n_local + 2] = total + 2 * nsh;
+    }
+  }
+  // this CTA's routes, in (token, k) order
+  const int my_routes = ntok * kTopK;
+  if (tid < my_routes) {
+    const int e = p.ids32[r_first + tid] - p.expert_lo;
+    s_e[tid] = (e >= 0 && e < p.n_local) ? e : -1;
+  }
+  __syncthreads();
+  if (blockIdx.x == 0)
+    for (int g = tid; g <= p.n_local + 2; g += kRouteThreads) p.group_offsets[g] = s_off[g];
+  if (tid < my_routes) {
+    const int e = s_e[tid];
+    if (e >= 0) {
+      int rank = 0;
+      for (int j = 0; j < tid; ++j) rank += (s_e[j] == e);
+      const int pos = s_off[e] + s_before[e] + rank;
+      const int r = r_first + tid;
+      const int b = r / kTopK, k = r % kTopK;
+      p.route_token[pos] = b;
+      p.route_slot[pos] = b * kSlots + k;
+      p.route_weight[pos] = p.tw[r];
+      s_pos[tid] = pos;
+      s_tok[tid] = b;
+    } else {
+      s_pos[tid] = -1;
+    }
+  }
+  // shared-expert routes of this CTA's tokens
+  if (tid >= 64 && tid < 64 + 2 * kRouteTok) {
+    const int i = tid - 64, s = i / kRouteTok, t = i % kRouteTok;
+    const int b = tok0 + t;
+    int pos = -1;
+    if (t < ntok && b >= p.shared_lo && b < p.shared_hi) {
+      pos = s_off[p.n_local + s] + (b - p.shared_lo);
+      p.route_token[pos] = b;
+      p.route_slot[pos] = b * kSlots + kTopK + s;
+      p.route_weight[pos] = 1.f;
+    }
+    s_pos[kRouteTok * kTopK + i] = pos;
+    s_tok[kRouteTok * kTopK + i] = b;
+  }
+  if (!p.gout) return;
+  __syncthreads();
+  // gather: one warp per placed route row
+  const int warp = tid >> 5, lane = tid & 31;
+  const int nslots = kRouteTok * kTopK + 2 * kRouteTok;
+  for (int i = warp; i < nslots; i += kRouteThreads / 32) {
+    const bool routed = i < kRouteTok * kTopK;
+    if (routed && i >= my_routes) continue;
+    const int pos = s_pos[i];
+    if (pos < 0) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(p.gx + s_tok[i] * p.gx_stride);
+    uint4* dst = reinterpret_cast<uint4*>(p.gout + static_cast<long long>(pos) * p.cols);
+    for (int c = lane; c < p.cols / 8; c += 32) dst[c] = src[c];
+  }
 }
 
 // Softmax/top-6 over precomputed logits (the reference's router_softmax_topk6_triton).
@@ -221,8 +279,7 @@ __global__ void softmax_topk_kernel(const float* logits, int rows, int n_experts
                     ids64, ids32, tw);
 }
 
-// x_sorted[r] = x[route_token[r]] for r < group_offsets[n_groups]  (gathers the
-// activations of every route into expert-contiguous rows for the TMA path)
+// x_sorted[r] = x[route_token[r]] for r < group_offsets[n_groups]
 __global__ void gather_rows_kernel(const bf16* __restrict__ x, long long x_row_stride,
                                    const int* __restrict__ route_token,
                                    const int* __restrict__ group_offsets, int n_groups,
@@ -235,18 +292,45 @@ __global__ void gather_rows_kernel(const bf16* __restrict__ x, long long x_row_s
   for (int c = threadIdx.x; c < cols / 8; c += blockDim.x) dst[c] = src[c];
 }
 
-cudaError_t launch_router(const RouterParams& p, cudaStream_t st) {
-  const int eg = (p.n_experts + p.experts_per_cta - 1) / p.experts_per_cta;
-  router_kernel<<<dim3(p.rows, eg), kRouterThreads, 0, st>>>(p);
+static cudaError_t launch_route(const int* ids32, const float* tw, int rows, int expert_lo,
+                                int n_local, int shared_lo, int shared_hi, int* go, int* rt,
+                                int* rs, float* rw, const bf16* gx, long long gxs, bf16* gout,
+                                int cols, cudaStream_t st) {
+  RouteParams q;
+  q.ids32 = ids32;
+  q.tw = tw;
+  q.rows = rows;
+  q.expert_lo = expert_lo;
+  q.n_local = n_local;
+  q.shared_lo = shared_lo;
+  q.shared_hi = shared_hi;
+  q.group_offsets = go;
+  q.route_token = rt;
+  q.route_slot = rs;
+  q.route_weight = rw;
+  q.gx = gx;
+  q.gx_stride = gxs;
+  q.gout = gout;
+  q.cols = cols;
+  route_kernel<<<(rows + kRouteTok - 1) / kRouteTok, kRouteThreads, 0, st>>>(q);
   return cudaGetLastError();
+}
+
+cudaError_t launch_router(const RouterParams& p, cudaStream_t st) {
+  router_topk_kernel<<<(p.rows + kRtTok - 1) / kRtTok, kRtThreads, 0, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || !p.group_offsets) return e;
+  return launch_route(p.topk_ids32, p.topk_w, p.rows, p.expert_lo, p.n_local, p.shared_lo,
+                      p.shared_hi, p.group_offsets, p.route_token, p.route_slot, p.route_weight,
+                      p.gather_x ? p.x : nullptr, p.x_row_stride, reinterpret_cast<bf16*>(p.gather_out),
+                      p.hidden, st);
 }
 
 cudaError_t launch_bucket(const int* ids32, const float* tw, int rows, int expert_lo, int n_local,
                           int shared_lo, int shared_hi, int* go, int* rt, int* rs, float* rw,
-                          cudaStream_t st) {
-  bucket_kernel<<<1, kRouterThreads, 0, st>>>(ids32, tw, rows, expert_lo, n_local, shared_lo,
-                                               shared_hi, go, rt, rs, rw);
-  return cudaGetLastError();
+                          const void* gx, long long gxs, void* gout, int cols, cudaStream_t st) {
+  return launch_route(ids32, tw, rows, expert_lo, n_local, shared_lo, shared_hi, go, rt, rs, rw,
+                      reinterpret_cast<const bf16*>(gx), gxs, reinterpret_cast<bf16*>(gout), cols, st);
 }
 
 cudaError_t launch_softmax_topk(const float* logits, int rows, int n_experts, float scaling,

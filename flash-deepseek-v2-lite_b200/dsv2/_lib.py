@@ -56,7 +56,7 @@ class RouterArgs(ctypes.Structure):
         ("rows", c_i32), ("hidden", c_i32), ("n_experts", c_i32),
         ("bias", c_vp), ("scaling", c_f32),
         ("logits", c_vp), ("topk_ids64", c_vp), ("topk_ids32", c_vp), ("topk_weights", c_vp),
-        ("ticket", c_vp),
+        ("gather_out", c_vp),
         ("expert_lo", c_i32), ("n_local", c_i32), ("shared_lo", c_i32), ("shared_hi", c_i32),
         ("group_offsets", c_vp), ("route_token", c_vp), ("route_slot", c_vp), ("route_weight", c_vp),
     ]
@@ -100,7 +100,8 @@ _SIGNATURES = {
     "dsv2_linear": ([ctypes.POINTER(LinearArgs), c_i32, c_vp], c_i32),
     "dsv2_router": ([ctypes.POINTER(RouterArgs), c_vp], c_i32),
     "dsv2_softmax_topk": ([c_vp, c_i32, c_i32, c_f32, c_vp, c_vp, c_vp, c_vp], c_i32),
-    "dsv2_moe_bucket": ([c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp], c_i32),
+    "dsv2_moe_bucket": ([c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp,
+                         c_vp, c_i64, c_vp, c_i32, c_vp], c_i32),
     "dsv2_gather_rows": ([c_vp, c_i64, c_vp, c_vp, c_i32, c_vp, c_i32, c_i32, c_vp], c_i32),
     "dsv2_mla_prep": ([ctypes.POINTER(MlaPrepArgs), c_vp], c_i32),
     "dsv2_mla_decode": ([ctypes.POINTER(MlaDecodeArgs), c_vp], c_i32),

@@ -30,9 +30,12 @@ FAMILIES = {"small": ops.FAMILY_SMALL, "batch": ops.FAMILY_BATCH}
 
 
 def choose_split_len(batch: int, max_len: int, num_sms: int) -> int:
-    """Positions per split-KV CTA: about two CTAs per SM over the whole batch."""
-    target = max(1, 2 * num_sms)
-    s = math.ceil(batch * max_len / target)
+    """Positions per split-KV CTA.  With at least ~1.5 rows per SM every row is one CTA
+    (a single-split row writes its output directly, no partials); otherwise rows are
+    split so the batch yields about four CTAs per SM (two resident per SM)."""
+    if batch * 2 >= 3 * num_sms:
+        return int((max_len + 63) // 64 * 64)
+    s = math.ceil(batch * max_len / (4 * num_sms))
     s = (s + 63) // 64 * 64
     return int(min(max(s, 64), 4096))
 
@@ -138,7 +141,6 @@ class DecodeEngine:
             self.topk_w = torch.zeros((Ball, TOPK), device=dev, dtype=f32)
             self.ids_local = torch.zeros((B, TOPK), device=dev, dtype=i32)
             self.w_local = torch.zeros((B, TOPK), device=dev, dtype=f32)
-            self.ticket = torch.zeros(4, device=dev, dtype=i32)
             # per-MoE-layer group offsets (kept per layer so the routing of the last step
             # can be inspected: distinct experts per layer for the roofline)
             self.moe_index = {li: i for i, li in enumerate(l for l, lp in enumerate(self.layers)
@@ -215,10 +217,12 @@ class DecodeEngine:
     def _moe(self, li: int, lp: LayerPack) -> torch.Tensor:
         m, B = lp.moe, self.B
         go = self.group_offsets_hist[self.moe_index[li]]
+        # batch family: the routing kernel also copies x into expert order for the TMA loads
+        gather = self.x_sorted if self.family == ops.FAMILY_BATCH else None
         if self.world == 1:
             ops.router(x=self.x, w=m.gate_w, scaling=m.scaling, bias=m.gate_bias, logits=self.logits_r,
                        topk_ids32=self.topk_ids32, topk_weights=self.topk_w, topk_ids64=self.topk_ids64,
-                       ticket=self.ticket, expert_lo=m.expert_lo, n_local=m.n_local, shared_lo=0,
+                       gather_out=gather, expert_lo=m.expert_lo, n_local=m.n_local, shared_lo=0,
                        shared_hi=B, group_offsets=go, route_token=self.route_token,
                        route_slot=self.route_slot, route_weight=self.route_weight)
             x_src = self.x
@@ -226,17 +230,15 @@ class DecodeEngine:
             import torch.distributed as dist
             r0 = self.rank * B
             ops.router(x=self.x, w=m.gate_w, scaling=m.scaling, bias=m.gate_bias, logits=self.logits_r,
-                       topk_ids32=self.ids_local, topk_weights=self.w_local, topk_ids64=self.topk_ids64,
-                       ticket=self.ticket)
+                       topk_ids32=self.ids_local, topk_weights=self.w_local, topk_ids64=self.topk_ids64)
             dist.all_gather_into_tensor(self.x_all, self.x, group=self.group)
             dist.all_gather_into_tensor(self.topk_ids32, self.ids_local, group=self.group)
             dist.all_gather_into_tensor(self.topk_w, self.w_local, group=self.group)
             ops.moe_bucket(self.topk_ids32, self.topk_w, m.expert_lo, m.n_local, r0, r0 + B,
-                           go, self.route_token, self.route_slot, self.route_weight)
+                           go, self.route_token, self.route_slot, self.route_weight,
+                           gather_src=self.x_all if gather is not None else None, gather_out=gather)
             self.partial.zero_()
             x_src = self.x_all
-        if self.family == ops.FAMILY_BATCH:
-            ops.gather_rows(x_src, self.route_token, go, self.n_groups, self.x_sorted, self.r_max)
         self._moe_gemms(m, go, x_src)
         if self.world == 1:
             return self.partial

@@ -37,7 +37,7 @@ def build_case(kernel: str, B: int, family: int, ctx: int, split_len: int | None
     H, I, E = 2048, 1408, 64
     calls = []
     nbytes = 0
-    if kernel in ("moe_gate_up", "moe_down", "router"):
+    if kernel in ("moe_gate_up", "moe_down", "router", "router_topk", "moe_bucket"):
         G = E + 2
         gate_up = _rnd((G, 2 * I, H), g, 0.02)
         down = _rnd((G, H, I), g, 0.02)
@@ -68,15 +68,20 @@ def build_case(kernel: str, B: int, family: int, ctx: int, split_len: int | None
                 n_groups=G, group_offsets=go, max_routes_per_group=B, route_y_row=rs, route_scale=rw,
                 family=family, w_group_rows=H, x_group_rows=R))
             nbytes = (distinct + 2) * H * I * 2
+        elif kernel == "moe_bucket":
+            calls.append(lambda: ops.moe_bucket(ids, w, 0, E, 0, B, go, rt, rs, rw))
+            nbytes = B * 6 * 8
         else:
             logits = torch.zeros(B, E, device=dev)
             i32 = torch.zeros(B, 6, dtype=torch.int32, device=dev)
             i64 = torch.zeros(B, 6, dtype=torch.int64, device=dev)
             tw = torch.zeros(B, 6, device=dev)
-            ticket = torch.zeros(4, dtype=torch.int32, device=dev)
+            bucket = kernel == "router"
             calls.append(lambda: ops.router(x=x, w=gate_w, scaling=1.0, logits=logits, topk_ids32=i32,
-                                            topk_weights=tw, topk_ids64=i64, ticket=ticket, expert_lo=0,
-                                            n_local=E, shared_lo=0, shared_hi=B, group_offsets=go,
+                                            topk_weights=tw, topk_ids64=i64,
+                                            gather_out=xs if (bucket and batch) else None, expert_lo=0,
+                                            n_local=E, shared_lo=0, shared_hi=B,
+                                            group_offsets=go if bucket else None,
                                             route_token=rt, route_slot=rs, route_weight=rw))
             nbytes = E * H * 2 + B * H * 2
     elif kernel in ("qkva", "o_proj", "dense_gate_up", "dense_down"):

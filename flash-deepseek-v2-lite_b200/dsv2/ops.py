@@ -168,10 +168,12 @@ def linear(*, w: torch.Tensor, n_rows: int, k: int, x: torch.Tensor, y: torch.Te
 
 def router(*, x: torch.Tensor, w: torch.Tensor, scaling: float, logits: torch.Tensor,
            topk_ids32: torch.Tensor, topk_weights: torch.Tensor, topk_ids64: torch.Tensor | None = None,
-           bias: torch.Tensor | None = None, ticket: torch.Tensor | None = None,
+           bias: torch.Tensor | None = None, gather_out: torch.Tensor | None = None,
            expert_lo: int = 0, n_local: int = 0, shared_lo: int = 0, shared_hi: int = 0,
            group_offsets: torch.Tensor | None = None, route_token: torch.Tensor | None = None,
            route_slot: torch.Tensor | None = None, route_weight: torch.Tensor | None = None) -> None:
+    """Gate logits + softmax + top-6 (+ bucketing when group_offsets is given, + the
+    expert-ordered copy of x into gather_out when given)."""
     a = RouterArgs()
     a.x = x.data_ptr()
     a.x_row_stride = x.stride(0)
@@ -186,7 +188,7 @@ def router(*, x: torch.Tensor, w: torch.Tensor, scaling: float, logits: torch.Te
     a.topk_ids64 = _ptr(topk_ids64)
     a.topk_ids32 = topk_ids32.data_ptr()
     a.topk_weights = topk_weights.data_ptr()
-    a.ticket = _ptr(ticket)
+    a.gather_out = _ptr(gather_out)
     a.expert_lo, a.n_local, a.shared_lo, a.shared_hi = expert_lo, n_local, shared_lo, shared_hi
     a.group_offsets = _ptr(group_offsets)
     a.route_token = _ptr(route_token)
@@ -203,10 +205,13 @@ def softmax_topk(logits: torch.Tensor, scaling: float, topk_ids64: torch.Tensor 
 
 def moe_bucket(topk_ids32: torch.Tensor, topk_weights: torch.Tensor, expert_lo: int, n_local: int,
                shared_lo: int, shared_hi: int, group_offsets: torch.Tensor, route_token: torch.Tensor,
-               route_slot: torch.Tensor, route_weight: torch.Tensor) -> None:
+               route_slot: torch.Tensor, route_weight: torch.Tensor, gather_src: torch.Tensor | None = None,
+               gather_out: torch.Tensor | None = None) -> None:
     _lib.call("dsv2_moe_bucket", topk_ids32.data_ptr(), topk_weights.data_ptr(), topk_ids32.shape[0],
               expert_lo, n_local, shared_lo, shared_hi, group_offsets.data_ptr(), route_token.data_ptr(),
-              route_slot.data_ptr(), route_weight.data_ptr(), stream())
+              route_slot.data_ptr(), route_weight.data_ptr(), _ptr(gather_src),
+              gather_src.stride(0) if gather_src is not None else 0, _ptr(gather_out),
+              gather_src.shape[1] if gather_src is not None else 0, stream())
 
 
 def gather_rows(x: torch.Tensor, route_token: torch.Tensor, group_offsets: torch.Tensor,

@@ -167,7 +167,7 @@ typedef struct dsv2_linear_args {
 DSV2_API int dsv2_linear(const dsv2_linear_args* args, int family, void* stream);
 
 /* ---- MoE routing ------------------------------------------------------------ */
-/* Fused gate GEMV (fp32 over bf16 activations) + softmax + top-6 + bucketing, one launch.
+/* Gate GEMV (fp32 over bf16 activations) + softmax + top-6, then bucketing (two launches).
  *   logits[r, e] = sum_k x[r, k] * w[e, k] (+ bias[e]);  p = softmax(logits[r]);
  *   topk_ids / topk_weights = 6 largest p (descending, lowest index first on ties),
  *   weights multiplied by `scaling` (routed_scaling_factor).
@@ -176,8 +176,10 @@ DSV2_API int dsv2_linear(const dsv2_linear_args* args, int family, void* stream)
  * shared-expert groups holding rows [shared_lo, shared_hi) with weight 1:
  *   group_offsets[n_local + 3], route_token / route_slot / route_weight[6*rows + 2*shared rows],
  *   route_slot = token * 8 + k (k = 0..5 routed, 6..7 the two shared-expert halves).
- * ticket: one int32 in device memory, zero before the first call; the kernel leaves it zero.
- * logits: [rows, n_experts] fp32 work buffer.  topk_ids64 may be NULL.
+ * gather_out (optional, needs bucketing): [routes, hidden] bf16, row i = x[route_token[i]]
+ * (the expert-ordered activations the batch-family MoE GEMMs read with TMA).
+ * logits: [rows, n_experts] fp32 work buffer.  topk_ids64 may be NULL.  hidden % 64 == 0,
+ * hidden <= 2048, rows <= 4096.
  * Reference: router_softmax_topk6_triton (moe_router.py:63-86) with the fp32 gate linear of
  * src/run.py:257-275, and the bucketing of packed_routed_moe (moe_batch.py:101-148, 425-470). */
 typedef struct dsv2_router_args {
@@ -194,7 +196,7 @@ typedef struct dsv2_router_args {
   int64_t* topk_ids64;
   int32_t* topk_ids32;
   float* topk_weights;
-  uint32_t* ticket;
+  void* gather_out;
   int32_t expert_lo;
   int32_t n_local;
   int32_t shared_lo;
@@ -214,11 +216,13 @@ DSV2_API int dsv2_softmax_topk(const float* logits, int rows, int n_experts, flo
                       void* stream);
 
 /* Bucketing alone (expert parallel: after the all-gather of the top-k results); same
- * outputs as dsv2_router.  Reference: moe_batch.py:101-148. */
+ * outputs as dsv2_router.  gather_out (optional): row i = gather_src[route_token[i]]
+ * (row stride gather_src_stride, cols columns).  Reference: moe_batch.py:101-148. */
 DSV2_API int dsv2_moe_bucket(const int32_t* topk_ids32, const float* topk_weights, int rows,
                     int expert_lo, int n_local, int shared_lo, int shared_hi,
                     int32_t* group_offsets, int32_t* route_token, int32_t* route_slot,
-                    float* route_weight, void* stream);
+                    float* route_weight, const void* gather_src, int64_t gather_src_stride,
+                    void* gather_out, int cols, void* stream);
 
 /* out[r] = x[route_token[r]] for r < group_offsets[n_groups] (r < max_routes): gathers
  * activations into expert-contiguous rows for the batch family.  cols % 8 == 0. */

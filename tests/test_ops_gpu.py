@@ -122,15 +122,15 @@ def test_router_topk_and_bucketing(D, B):
     lg, ids, wts = O.router(x, w, 1.0, bias)
     dev = {k: torch.zeros(s, dtype=t, device=DEV) for k, s, t in (
         ("logits", (B, 64), torch.float32), ("ids32", (B, 6), torch.int32), ("ids64", (B, 6), torch.int64),
-        ("tw", (B, 6), torch.float32), ("ticket", (4,), torch.int32), ("go", (67,), torch.int32),
+        ("tw", (B, 6), torch.float32), ("go", (67,), torch.int32), ("xs", (8 * B, 2048), torch.bfloat16),
         ("rt", (8 * B,), torch.int32), ("rs", (8 * B,), torch.int32), ("rw", (8 * B,), torch.float32))}
-    for _ in range(2):  # twice: the ticket must be left at zero
-        D.router(x=x.to(DEV), w=w.to(DEV), scaling=1.0, bias=None if bias is None else bias.to(DEV),
+    xd = x.to(DEV)
+    for _ in range(2):  # twice: nothing may depend on state left by the previous call
+        D.router(x=xd, w=w.to(DEV), scaling=1.0, bias=None if bias is None else bias.to(DEV),
                  logits=dev["logits"], topk_ids32=dev["ids32"], topk_weights=dev["tw"], topk_ids64=dev["ids64"],
-                 ticket=dev["ticket"], expert_lo=0, n_local=64, shared_lo=0, shared_hi=B,
+                 gather_out=dev["xs"], expert_lo=0, n_local=64, shared_lo=0, shared_hi=B,
                  group_offsets=dev["go"], route_token=dev["rt"], route_slot=dev["rs"], route_weight=dev["rw"])
     torch.cuda.synchronize()
-    assert int(dev["ticket"][0]) == 0
     torch.testing.assert_close(dev["logits"].cpu(), lg, rtol=1e-4, atol=1e-5)
     got = dev["ids64"].cpu()
     p = torch.softmax(lg, -1)
@@ -147,6 +147,7 @@ def test_router_topk_and_bucketing(D, B):
     n = int(go[-1])
     assert torch.equal(dev["rt"].cpu()[:n], rt) and torch.equal(dev["rs"].cpu()[:n], rs)
     assert torch.equal(dev["rw"].cpu()[:n], rw)
+    assert torch.equal(dev["xs"].cpu()[:n], x[rt.long()])  # expert-ordered activation copy
 
 
 def test_router_golden_topk6(D, golden_ref):
@@ -170,11 +171,14 @@ def test_moe_bucket_expert_parallel_slice(D):
     go = torch.zeros(16 + 3, dtype=torch.int32, device=DEV)
     rt = torch.zeros(8 * B, dtype=torch.int32, device=DEV)
     rs, rw = torch.zeros_like(rt), torch.zeros(8 * B, device=DEV)
-    D.moe_bucket(ids.to(DEV), tw.to(DEV), 16, 16, 10, 20, go, rt, rs, rw)
+    xsrc = torch.randn(B, 2048, generator=g).to(torch.bfloat16)
+    xs = torch.zeros(8 * B, 2048, dtype=torch.bfloat16, device=DEV)
+    D.moe_bucket(ids.to(DEV), tw.to(DEV), 16, 16, 10, 20, go, rt, rs, rw, gather_src=xsrc.to(DEV), gather_out=xs)
     eg, et, es, ew = O.bucket(ids, tw, 16, 16, 10, 20)
     assert torch.equal(go.cpu(), eg)
     n = int(eg[-1])
     assert torch.equal(rt.cpu()[:n], et) and torch.equal(rs.cpu()[:n], es) and torch.equal(rw.cpu()[:n], ew)
+    assert torch.equal(xs.cpu()[:n], xsrc[et.long()])
 
 
 def _mla_inputs(B, S, lengths, seed):
