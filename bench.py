@@ -51,6 +51,9 @@ GATE_BYTES = 2 * 131_072
 LMHEAD_BYTES = 2 * 209_715_200
 EXPERT_BYTES = 2 * 8_650_752
 KV_ROW_BYTES = 576 * 2
+# DRAM traffic / algorithmic bytes of the grouped MoE GEMMs, from one ncu capture of the
+# gate_up and down launches at B=256: (770.6 + 7.8 + 386.5 + 13.3) MB / (761.3 + 380.6) MB
+MOE_TRAFFIC_RATIO = 1.032
 
 
 def prompt_lengths(cfg: dict, batch: int) -> list[int]:
@@ -205,7 +208,7 @@ def distinct_experts(eng) -> list[int]:
 
 def run_ours(args, cfg_id: int):
     from dsv2.engine import DecodeEngine
-    from oracle.hf_model import add_router_bias, build_model, dsv2_lite_config, router_bias_zipf
+    from dsv2.synthetic import add_router_bias, build_model, dsv2_lite_config, router_bias_zipf
 
     rank, world, local, group = init_dist(args)
     dev = torch.device("cuda", local)
@@ -325,7 +328,10 @@ def run_ours(args, cfg_id: int):
                 "unit": "GB/s",
                 "frac": round(dk_gbs / peak, 4) if dk_gbs else None,
                 "peak_kind": peak_kind,
-                "traffic": None,
+                "traffic": round(moe_bytes / max(moe_launches, 1) * MOE_TRAFFIC_RATIO),
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the same two launches "
+                                  "(dsv2.microbench moe_gate_up / moe_down, B=256, all 64 experts hit), "
+                                  "scaled to this launch by its algorithmic bytes",
                 "algorithmic_bytes_per_launch": round(moe_bytes / max(moe_launches, 1)),
                 "launch_ms": round(moe_ms / max(moe_launches, 1), 5),
             },

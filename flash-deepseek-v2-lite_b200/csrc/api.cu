@@ -222,6 +222,23 @@ int dsv2_silu_mul(const void* gate, const void* up, void* out, int64_t n, void* 
                       "silu_mul");
 }
 
+int dsv2_sum_partials(const float* part, int n_parts, int64_t part_stride, int64_t row_stride, void* out,
+                      int out_dtype, int64_t out_row_stride, int rows, int cols, void* stream) {
+  if (!part || !out) return fail(DSV2_ERR_INVALID, "sum_partials: null pointer");
+  if (out_dtype != DSV2_BF16 && out_dtype != DSV2_F32)
+    return fail(DSV2_ERR_UNSUPPORTED, "sum_partials: output dtype %d", out_dtype);
+  if (cols < 0 || cols % 8 || n_parts < 0 || rows < 0 || rows > 65535)
+    return fail(DSV2_ERR_UNSUPPORTED, "sum_partials: rows=%d cols=%d parts=%d", rows, cols, n_parts);
+  if (!aligned16(part) || !aligned16(out) || part_stride % 4 || row_stride % 4 ||
+      out_row_stride % (out_dtype == DSV2_F32 ? 4 : 8))
+    return fail(DSV2_ERR_INVALID, "sum_partials: operands and strides must be 16-byte aligned");
+  if (rows == 0 || cols == 0) return DSV2_OK;
+  return check_launch(launch_sum_partials(part, n_parts, part_stride, row_stride, out,
+                                          out_dtype == DSV2_F32, out_row_stride, rows, cols,
+                                          static_cast<cudaStream_t>(stream)),
+                      "sum_partials");
+}
+
 int dsv2_prepare_decode_inputs(const int64_t* cache_position, int pos_numel,
                                int64_t* attention_mask, int64_t mask_stride_b,
                                int64_t* position_ids, int64_t position_ids_stride_b,

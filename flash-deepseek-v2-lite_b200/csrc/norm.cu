@@ -221,6 +221,38 @@ __global__ void residual_add_kernel(const bf16* __restrict__ a, const bf16* __re
   reinterpret_cast<uint4*>(out)[i] = o;
 }
 
+// out[r, c] = sum_{p < n_parts} part[r * rs + p * ps + c], summed in part order (fp32),
+// stored as bf16 (out_f32 == 0) or fp32.  8 columns per thread; grid (col chunks, rows).
+__global__ void sum_partials_kernel(const float* __restrict__ part, int n_parts, long long ps,
+                                    long long rs, void* __restrict__ out, int out_f32,
+                                    long long ors, int cols) {
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c >= cols) return;
+  const long long r = blockIdx.y;
+  const float* src = part + r * rs + c;
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  for (int p = 0; p < n_parts; ++p) {
+    const float4 a = *reinterpret_cast<const float4*>(src + p * ps);
+    const float4 b = *reinterpret_cast<const float4*>(src + p * ps + 4);
+    acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+    acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+  }
+  if (out_f32) {
+    float* o = reinterpret_cast<float*>(out) + r * ors + c;
+    *reinterpret_cast<float4*>(o) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    *reinterpret_cast<float4*>(o + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  } else {
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(out) + r * ors + c) = o;
+  }
+}
+
 __device__ __forceinline__ float silu_f(float g) { return g / (1.f + expf(-g)); }
 
 // out = bf16(silu(gate) * up)
@@ -318,6 +350,14 @@ cudaError_t launch_residual_add(const void* a, const void* b, void* out, long lo
   residual_add_kernel<<<static_cast<unsigned>((n8 + thr - 1) / thr), thr, 0, st>>>(
       reinterpret_cast<const bf16*>(a), reinterpret_cast<const bf16*>(b),
       reinterpret_cast<bf16*>(out), n8);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sum_partials(const float* part, int n_parts, long long ps, long long rs, void* out,
+                               int out_f32, long long ors, int rows, int cols, cudaStream_t st) {
+  const int thr = 128;
+  dim3 grid((cols / 8 + thr - 1) / thr, rows);
+  sum_partials_kernel<<<grid, thr, 0, st>>>(part, n_parts, ps, rs, out, out_f32, ors, cols);
   return cudaGetLastError();
 }
 

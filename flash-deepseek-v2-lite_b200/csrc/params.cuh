@@ -79,6 +79,8 @@ cudaError_t launch_embed_rmsnorm(const long long*, const void*, long long, const
                                  void*, int, int, float, cudaStream_t);
 cudaError_t launch_residual_add(const void*, const void*, void*, long long, cudaStream_t);
 cudaError_t launch_silu_mul(const void*, const void*, void*, long long, cudaStream_t);
+cudaError_t launch_sum_partials(const float* part, int n_parts, long long ps, long long rs, void* out,
+                               int out_f32, long long ors, int rows, int cols, cudaStream_t st);
 cudaError_t launch_prepare_decode_inputs(const long long*, int, long long*, long long, long long*,
                                          long long, const long long*, int, int, cudaStream_t);
 cudaError_t launch_copy_token_to_cache(const void*, const long long*, void*, const long long*,

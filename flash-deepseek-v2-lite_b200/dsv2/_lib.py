@@ -93,6 +93,7 @@ _SIGNATURES = {
     "dsv2_embed_rmsnorm": ([c_vp, c_vp, c_i64, c_vp, c_i32, c_vp, c_vp, c_i32, c_i32, c_f32, c_vp], c_i32),
     "dsv2_residual_add": ([c_vp, c_vp, c_vp, c_i64, c_vp], c_i32),
     "dsv2_silu_mul": ([c_vp, c_vp, c_vp, c_i64, c_vp], c_i32),
+    "dsv2_sum_partials": ([c_vp, c_i32, c_i64, c_i64, c_vp, c_i32, c_i64, c_i32, c_i32, c_vp], c_i32),
     "dsv2_prepare_decode_inputs": ([c_vp, c_i32, c_vp, c_i64, c_vp, c_i64, c_vp, c_i32, c_i32, c_vp], c_i32),
     "dsv2_copy_token_to_cache": ([c_vp, c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
                                   c_vp], c_i32),

@@ -23,6 +23,7 @@ from dataclasses import dataclass
 import torch
 
 from . import ops
+from .expert_parallel import ep_shard, gather_routing, scatter_sum
 from .model import (HIDDEN, KV_LORA, LATENT_ROW, N_HEADS, QK_NOPE, QKVA_ROWS, Q_DIM, SLOTS, TOPK,
                     V_DIM, LayerPack, check_config, pack_layer, rope_tables)
 
@@ -62,8 +63,6 @@ class DecodeEngine:
         check_config(cfg)
         if family not in FAMILIES:
             raise ValueError(f"Unknown kernel family: {family}")
-        if world > 1 and cfg.n_routed_experts % world:
-            raise ValueError("expert count must divide the world size")
         self.model = model
         self.cfg = cfg
         self.family_name = family
@@ -73,9 +72,9 @@ class DecodeEngine:
         self.max_len = int(max_len)
         self.rank, self.world, self.group = rank, world, group
         self.B_all = self.B * world
-        n_exp = int(cfg.n_routed_experts)
-        self.n_local = n_exp // world
-        self.expert_lo = rank * self.n_local
+        self.shard = ep_shard(int(cfg.n_routed_experts), self.B_all, rank, world)
+        self.n_local = self.shard.n_local
+        self.expert_lo = self.shard.expert_lo
         self.layers: list[LayerPack] = [
             pack_layer(l, self.expert_lo, self.n_local, alias_hf=alias_hf and world == 1, gate_bias=gate_bias)
             for l in model.model.layers
@@ -227,14 +226,12 @@ class DecodeEngine:
                        route_slot=self.route_slot, route_weight=self.route_weight)
             x_src = self.x
         else:
-            import torch.distributed as dist
-            r0 = self.rank * B
+            sh = self.shard
             ops.router(x=self.x, w=m.gate_w, scaling=m.scaling, bias=m.gate_bias, logits=self.logits_r,
                        topk_ids32=self.ids_local, topk_weights=self.w_local, topk_ids64=self.topk_ids64)
-            dist.all_gather_into_tensor(self.x_all, self.x, group=self.group)
-            dist.all_gather_into_tensor(self.topk_ids32, self.ids_local, group=self.group)
-            dist.all_gather_into_tensor(self.topk_w, self.w_local, group=self.group)
-            ops.moe_bucket(self.topk_ids32, self.topk_w, m.expert_lo, m.n_local, r0, r0 + B,
+            gather_routing(self.x, self.ids_local, self.w_local, self.x_all, self.topk_ids32, self.topk_w,
+                           group=self.group)
+            ops.moe_bucket(self.topk_ids32, self.topk_w, m.expert_lo, m.n_local, sh.row_lo, sh.row_hi,
                            go, self.route_token, self.route_slot, self.route_weight,
                            gather_src=self.x_all if gather is not None else None, gather_out=gather)
             self.partial.zero_()
@@ -242,9 +239,8 @@ class DecodeEngine:
         self._moe_gemms(m, go, x_src)
         if self.world == 1:
             return self.partial
-        import torch.distributed as dist
-        torch.sum(self.partial, dim=1, out=self.moe_sum)
-        dist.reduce_scatter_tensor(self.moe_local.view(B, HIDDEN), self.moe_sum, group=self.group)
+        ops.sum_partials(self.partial, self.moe_sum)
+        scatter_sum(self.moe_sum, self.moe_local.view(B, HIDDEN), group=self.group)
         return self.moe_local
 
     def _moe_gemms(self, m, go: torch.Tensor, x_src: torch.Tensor) -> None:

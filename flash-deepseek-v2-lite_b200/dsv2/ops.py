@@ -18,7 +18,7 @@ from ._lib import (
 )
 
 __all__ = [
-    "stream", "rmsnorm", "add_rmsnorm", "embed_rmsnorm", "residual_add", "silu_mul",
+    "stream", "rmsnorm", "add_rmsnorm", "embed_rmsnorm", "residual_add", "silu_mul", "sum_partials",
     "prepare_decode_inputs", "copy_token_to_cache", "advance_positions", "linear",
     "router", "softmax_topk", "moe_bucket", "gather_rows", "mla_prep", "mla_decode",
     "EPI_STORE_BF16", "EPI_STORE_F32", "EPI_SWIGLU", "EPI_SCALE_F32", "FAMILY_SMALL", "FAMILY_BATCH",
@@ -97,6 +97,26 @@ def residual_add(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor) -> torch.T
 
 def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
     _lib.call("dsv2_silu_mul", gate.data_ptr(), up.data_ptr(), out.data_ptr(), gate.numel(), stream())
+    return out
+
+
+def sum_partials(part: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out[r] = sum_p part[r, p] (fp32 partials [rows, parts, cols], summed in part order)
+    stored as out's dtype (bf16 or fp32)."""
+    _cuda(part, "part")
+    if part.dtype != torch.float32 or part.dim() != 3 or part.stride(2) != 1:
+        raise NotImplementedError("sum_partials expects fp32 partials [rows, parts, cols] with contiguous cols")
+    rows, parts, cols = part.shape
+    if tuple(out.shape) != (rows, cols) or out.stride(1) != 1:
+        raise ValueError("out must be [rows, cols] with contiguous cols")
+    if out.dtype == torch.bfloat16:
+        odt = DSV2_BF16
+    elif out.dtype == torch.float32:
+        odt = DSV2_F32
+    else:
+        raise NotImplementedError(f"sum_partials output dtype {out.dtype}")
+    _lib.call("dsv2_sum_partials", part.data_ptr(), parts, part.stride(1), part.stride(0), out.data_ptr(), odt,
+              out.stride(0), rows, cols, stream())
     return out
 
 

@@ -95,6 +95,16 @@ DSV2_API int dsv2_residual_add(const void* a, const void* b, void* out, int64_t 
  * Reference: silu_mul_triton, triton_kernels/mlp_elementwise.py:24-45. */
 DSV2_API int dsv2_silu_mul(const void* gate, const void* up, void* out, int64_t n, void* stream);
 
+/* Deterministic sum of fp32 partials: out[r, c] = sum_{p < n_parts} part[r*row_stride +
+ * p*part_stride + c], added in part order, stored as out_dtype (DSV2_BF16 or DSV2_F32)
+ * at out_row_stride.  Strides in elements; cols % 8 == 0; rows <= 65535.
+ * Reference: the top-k route reduction _down_reduce_topk6_kernel /
+ * _batched_down_reduce_topk6_kernel (moe_small_gemv.py:162-192, :311-348), here over
+ * partials already scaled by the route weight (the down GEMM's epilogue). */
+DSV2_API int dsv2_sum_partials(const float* part, int n_parts, int64_t part_stride, int64_t row_stride,
+                      void* out, int out_dtype, int64_t out_row_stride, int rows, int cols,
+                      void* stream);
+
 /* attention_mask[b, s] = (attention_mask_index[s] <= pos_b), position_ids[b] = pos_b,
  * pos_b = cache_position[pos_numel == 1 ? 0 : b] (int64 everywhere).  Either output
  * may be NULL.  Reference: prepare_decode_inputs_triton, attention_prepost.py:152-188. */

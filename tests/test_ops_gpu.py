@@ -266,3 +266,17 @@ def test_mla_prep_vs_oracle(D, golden_ref):
     torch.testing.assert_close(hs.float(), gg["q_out"][:, 128:].float(), rtol=2 ** -7, atol=1e-6)
     torch.testing.assert_close(O.rope_half_split(gg["k_pe"], c, s).float(), gg["k_new"][0, 128:].float(),
                                rtol=2 ** -7, atol=1e-6)
+
+
+def test_sum_partials_fixed_order(D):
+    g = torch.Generator().manual_seed(9)
+    part = torch.randn(6, 8, 2048, generator=g)
+    ref = torch.zeros(6, 2048)
+    for p in range(5):          # sum the first five slots in slot order
+        ref += part[:, p]
+    out32 = torch.empty(6, 2048, device=DEV)
+    D.sum_partials(part.to(DEV)[:, :5], out32)
+    assert torch.equal(out32.cpu(), ref)
+    out16 = torch.empty(6, 2048, dtype=torch.bfloat16, device=DEV)
+    D.sum_partials(part.to(DEV)[:, :5], out16)
+    assert torch.equal(out16.cpu(), ref.to(torch.bfloat16))
