@@ -174,20 +174,11 @@ def barrier(world: int):
 
 
 def count_launches(fn) -> int:
-    """Number of libdsv2 kernels one call of fn launches (C-ABI calls, mla_decode = 2)."""
+    """Number of libdsv2 kernels one call of fn enqueues (the library's own launch counter)."""
     from dsv2 import _lib
-    orig = _lib.call
-    n = [0]
-
-    def counting(name, *a):
-        n[0] += 2 if name == "dsv2_mla_decode" else 1
-        return orig(name, *a)
-    _lib.call = counting
-    try:
-        fn()
-    finally:
-        _lib.call = orig
-    return n[0]
+    n0 = _lib.kernel_launches()
+    fn()
+    return _lib.kernel_launches() - n0
 
 
 def step_bytes(eng, lens_now: list[int], distinct: list[int]) -> float:

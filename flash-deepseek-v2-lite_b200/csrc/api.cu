@@ -7,6 +7,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -50,6 +51,12 @@ int ensure_init(int* sms_out) {
   if (e != cudaSuccess) return fail(DSV2_ERR_LAUNCH, "cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= 128) return fail(DSV2_ERR_INVALID, "device index %d out of range", dev);
   std::lock_guard<std::mutex> lk(g_mu);
+  static bool env_read = false;
+  if (!env_read) {  // DSV2_PDL=0 turns programmatic dependent launch off
+    const char* v = getenv("DSV2_PDL");
+    if (v && v[0] == '0') g_pdl_enabled = false;
+    env_read = true;
+  }
   if (!g_dev_init[dev]) {
     int major = 0, minor = 0, sms = 0;
     cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
@@ -140,6 +147,14 @@ int dsv2_version(void) { return 100; }
 const char* dsv2_last_error(void) { return g_last_error.c_str(); }
 
 int dsv2_init(void) { return ensure_init(nullptr); }
+
+int dsv2_set_programmatic_launch(int enable) {
+  const int prev = g_pdl_enabled ? 1 : 0;
+  g_pdl_enabled = enable != 0;
+  return prev;
+}
+
+int64_t dsv2_kernel_launches(void) { return g_kernel_launches.load(std::memory_order_relaxed); }
 
 int dsv2_get_device_error(int* code, int clear) {
   if (!code) return fail(DSV2_ERR_INVALID, "code is NULL");
@@ -302,7 +317,7 @@ int dsv2_linear(const dsv2_linear_args* a, int family, void* stream) {
     return fail(DSV2_ERR_INVALID, "linear: W/X rows must be 16-byte aligned");
   const int n_tok = a->group_offsets ? a->max_routes_per_group : a->n_tokens;
   if (n_tok <= 0) return DSV2_OK;
-  LinearParams p;
+  LinearParams p = {};
   p.w = reinterpret_cast<const bf16*>(a->w);
   p.w_row_stride = a->w_row_stride;
   p.w_group_stride = a->w_group_stride;
@@ -325,6 +340,7 @@ int dsv2_linear(const dsv2_linear_args* a, int family, void* stream) {
   p.max_routes_per_group = a->max_routes_per_group;
   p.k_splits = a->k_splits > 1 ? a->k_splits : 1;
   p.y_split_stride = a->y_split_stride;
+  p.offsets_prior = a->offsets_prior != 0;
   if (p.k_splits > 1) {
     if (family != DSV2_FAMILY_BATCH || a->group_offsets || a->epilogue != DSV2_EPI_STORE_F32)
       return fail(DSV2_ERR_UNSUPPORTED, "linear: a K split needs the batch family, dense mode and fp32 output");
@@ -526,7 +542,7 @@ int dsv2_mla_decode(const dsv2_mla_decode_args* a, void* stream) {
   if (a->batch <= 0) return DSV2_OK;
   int rc = ensure_init(nullptr);
   if (rc) return rc;
-  MlaDecodeParams p;
+  MlaDecodeParams p = {};
   p.q_abs = reinterpret_cast<const bf16*>(a->q_abs);
   p.q_pe = reinterpret_cast<const bf16*>(a->q_pe);
   p.cache = reinterpret_cast<const bf16*>(a->cache);
@@ -540,6 +556,7 @@ int dsv2_mla_decode(const dsv2_mla_decode_args* a, void* stream) {
   p.o_part = a->o_part;
   p.ml_part = a->ml_part;
   p.o_lat = reinterpret_cast<bf16*>(a->o_lat);
+  p.inputs_prior = a->inputs_prior != 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   rc = check_launch(launch_mla_decode(p, a->batch, st), "mla_decode");
   if (rc) return rc;
@@ -575,7 +592,7 @@ int dsv2_mla_decode_noalloc(const void* q_abs, const void* q_pe, const void* cac
   if (e != cudaSuccess) return check_launch(e, "mla_decode_noalloc: scratch address");
   float* o_part = scratch;
   float* ml_part = scratch + static_cast<size_t>(kNoAllocMaxParts) * kHeads * kLatent;
-  MlaDecodeParams p;
+  MlaDecodeParams p = {};
   p.q_abs = reinterpret_cast<const bf16*>(q_abs);
   p.q_pe = reinterpret_cast<const bf16*>(q_pe);
   p.cache = reinterpret_cast<const bf16*>(cache);

@@ -38,6 +38,34 @@ __device__ __forceinline__ void set_device_error(int code) {
 }
 
 // ----------------------------------------------------------------------------
+// Programmatic dependent launch
+// ----------------------------------------------------------------------------
+// Every kernel of the library is launched with programmatic stream serialization
+// (launch_kernel below): the next kernel of the stream may be scheduled before this
+// one completes.  Protocol, followed by every kernel:
+//   1. work that touches no data written by the last two kernels of the stream
+//      (weights, tensor maps, shared memory / TMEM setup, and inputs the caller
+//      states were written earlier) may run first;
+//   2. pdl_wait() before reading anything the previous kernel wrote or writing
+//      anything it may still read (griddepcontrol.wait: the previous grid has
+//      completed and its writes are visible);
+//   3. pdl_launch_dependents() only after that wait, so the next kernel starts once
+//      every CTA of this one is past its wait, i.e. once the kernel before this one
+//      has completed.  That is what makes inputs written two launches back safe to
+//      read in step 1, and it keeps at most one early grid waiting per kernel.
+// Every CTA reaches pdl_wait() on every path, early exits included, so a grid never
+// completes before its predecessor and completion stays ordered along the stream.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// steps 2 and 3, at the top of a kernel that has nothing to do before its inputs are ready
+__device__ __forceinline__ void pdl_enter() {
+  pdl_wait();
+  pdl_launch_dependents();
+}
+
+// ----------------------------------------------------------------------------
 // bf16 <-> fp32
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ float bf16lo(uint32_t u) { return __uint_as_float(u << 16); }
@@ -262,6 +290,37 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N) {
          | (1u << 10)                               // B format: bf16
          | (static_cast<uint32_t>(N >> 3) << 17)    // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24);   // M / 16
+}
+
+}  // namespace dsv2
+
+// ----------------------------------------------------------------------------
+// Host-side launch helper
+// ----------------------------------------------------------------------------
+#include <atomic>
+
+namespace dsv2 {
+
+// Programmatic stream serialization for every launch (on unless DSV2_PDL=0 in the
+// environment when the library initialises) and a count of the kernels enqueued.
+inline bool g_pdl_enabled = true;
+inline std::atomic<long long> g_kernel_launches{0};
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = g_pdl_enabled ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 }  // namespace dsv2

@@ -35,6 +35,7 @@ struct LinearParams {
   int max_routes_per_group;
   int k_splits;                 // batch family, dense fp32 output: K split across CTAs
   long long y_split_stride;     // elements between the fp32 partial outputs of the splits
+  int offsets_prior;            // group_offsets were written at least two launches earlier
 };
 
 __device__ __forceinline__ float silu_ref(float g) { return g / (1.f + expf(-g)); }

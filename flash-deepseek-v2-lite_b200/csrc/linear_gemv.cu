@@ -28,6 +28,12 @@ constexpr int kGemvTok = 8;
 template <bool SWIGLU, int U>
 __global__ __launch_bounds__(kGemvWarps * 32) void gemv_mma_kernel(const LinearParams p,
                                                                     int rb_count, int tc_count) {
+  // Dense launches, and grouped ones whose routing is older than the previous launch
+  // (offsets_prior), request their first weight chunks before waiting for the previous
+  // kernel; the activations are loaded after the wait.
+  const bool early = p.group_offsets == nullptr || p.offsets_prior;
+  bool waited = !early;
+  if (!early) pdl_enter();
   __shared__ float red[kGemvWarps][32][SWIGLU ? 8 : 4];
   int item = blockIdx.x;
   const int tc = item % tc_count;
@@ -44,7 +50,10 @@ __global__ __launch_bounds__(kGemvWarps * 32) void gemv_mma_kernel(const LinearP
     cnt = p.n_tokens;
   }
   const int tbeg = tc * kGemvTok;
-  if (tbeg >= cnt) return;
+  if (tbeg >= cnt) {
+    if (!waited) pdl_enter();
+    return;
+  }
   const int tn = min(kGemvTok, cnt - tbeg);
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -79,8 +88,16 @@ __global__ __launch_bounds__(kGemvWarps * 32) void gemv_mma_kernel(const LinearP
           if (okA) ua[u] = ld_stream_v4(wA + p.up_offset + kb * 32);
           if (okB) ub[u] = ld_stream_v4(wB + p.up_offset + kb * 32);
         }
-        if (okT) xv[u] = *reinterpret_cast<const uint4*>(xp + kb * 32);
       }
+    }
+    if (!waited) {
+      pdl_enter();
+      waited = true;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int kb = kb0 + u * kGemvWarps;
+      if (kb < nkb && okT) xv[u] = *reinterpret_cast<const uint4*>(xp + kb * 32);
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -103,6 +120,7 @@ __global__ __launch_bounds__(kGemvWarps * 32) void gemv_mma_kernel(const LinearP
     red[warp][lane][i] = c[i];
     if (SWIGLU) red[warp][lane][4 + i] = cu[i];
   }
+  if (!waited) pdl_enter();  // warps without K blocks
   __syncthreads();
   // 128 output elements (16 rows x 8 tokens): thread i -> lane i/4, fragment slot i%4
   if (threadIdx.x < 128) {
@@ -128,9 +146,9 @@ cudaError_t launch_linear_gemv(const LinearParams& p, cudaStream_t st) {
   if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
   const dim3 grid(static_cast<unsigned>(items));
   if (p.epilogue == kEpiSwiglu)
-    gemv_mma_kernel<true, 4><<<grid, kGemvWarps * 32, 0, st>>>(p, rb_count, tc_count);
+    launch_kernel(gemv_mma_kernel<true, 4>, grid, kGemvWarps * 32, 0, st, p, rb_count, tc_count);
   else
-    gemv_mma_kernel<false, 8><<<grid, kGemvWarps * 32, 0, st>>>(p, rb_count, tc_count);
+    launch_kernel(gemv_mma_kernel<false, 8>, grid, kGemvWarps * 32, 0, st, p, rb_count, tc_count);
   return cudaGetLastError();
 }
 

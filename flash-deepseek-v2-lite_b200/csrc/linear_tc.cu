@@ -44,6 +44,7 @@ constexpr int kTcBoxRows = 16;           // token rows per TMA box
 constexpr int kTcSmemBudget = 216 * 1024;
 constexpr int kTcTmemCols = 512;
 constexpr int kTcMaxGroups = 256;
+constexpr int kTcMaxStages = 8;
 
 struct TcShape {
   int stages;
@@ -109,6 +110,12 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
   const int nkb = p.k / kTcK;
   const int a_tiles = SWIGLU ? 2 : 1;
   const int n_tile = shp.n_tile;
+  // Grouped launches whose group offsets the previous kernel wrote wait for it here.
+  // Dense launches (static work list) and grouped launches whose offsets are older
+  // (p.offsets_prior) wait in the producer, after requesting the weight tiles of the
+  // first pass over the ring.
+  const bool early = p.group_offsets == nullptr || p.offsets_prior;
+  if (!early) pdl_enter();
 
   // Compacted work list: group g contributes mt_count * ceil(cnt_g / n_tile) items
   // (none when empty).  Every CTA builds the same prefix from the device-side group
@@ -170,14 +177,36 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
+      // activation rows of one stage: as many large boxes as fit, 16-row boxes for the
+      // rest (few large TMA requests per stage instead of many 2 KB ones)
+      auto load_x = [&](int stage, int kb, int xrow0, int gx, int nbig, int nsmall) {
+        unsigned char* sb = smem + stage * shp.stage_bytes + a_tiles * kTcABytes;
+        for (int bx = 0; bx < nbig; ++bx)
+          tma_load_3d(smem_u32(sb + bx * shp.x_box * 128), &tmap_xb, &full_bar[stage], kb * kTcK,
+                      xrow0 + bx * shp.x_box, gx);
+        for (int bx = 0; bx < nsmall; ++bx)
+          tma_load_3d(smem_u32(sb + (nbig * shp.x_box + bx * kTcBoxRows) * 128), &tmap_x,
+                      &full_bar[stage], kb * kTcK, xrow0 + nbig * shp.x_box + bx * kTcBoxRows, gx);
+      };
+      // early launches: the stages of the first ring pass get their weight tiles before
+      // pdl_wait() and their activation tiles after it
+      bool waited = !early;
+      int npend = 0;
+      int pend_kb[kTcMaxStages], pend_row[kTcMaxStages], pend_gx[kTcMaxStages];
+      int pend_big[kTcMaxStages], pend_small[kTcMaxStages];
+      auto release = [&]() {
+        pdl_enter();
+        waited = true;
+        for (int i = 0; i < npend; ++i)
+          load_x(i, pend_kb[i], pend_row[i], pend_gx[i], pend_big[i], pend_small[i]);
+        npend = 0;
+      };
       int stage = 0;
       uint32_t phase = 0;
       for (int it = blockIdx.x; it < total_items && !*abort_flag; it += gridDim.x) {
         int g, mt, nt, r0, ntok, kb0, kb1, sp;
         if (!decode(it, g, mt, nt, r0, ntok, kb0, kb1, sp)) continue;
         const int npad = round_up(ntok, 16);
-        // activation rows: as many large boxes as fit, 16-row boxes for the rest
-        // (few large TMA requests per stage instead of many 2 KB ones)
         const int nbig = npad / shp.x_box;
         const int nsmall = (npad - nbig * shp.x_box) / kTcBoxRows;
         const int xrow0 = r0 + nt * n_tile;
@@ -191,16 +220,20 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
           if (SWIGLU)
             tma_load_3d(smem_u32(st + kTcABytes), &tmap_w, &full_bar[stage], kb * kTcK,
                         mt * kTcM + up_rows, g);
-          unsigned char* sb = st + a_tiles * kTcABytes;
-          for (int bx = 0; bx < nbig; ++bx)
-            tma_load_3d(smem_u32(sb + bx * shp.x_box * 128), &tmap_xb, &full_bar[stage], kb * kTcK,
-                        xrow0 + bx * shp.x_box, gx);
-          for (int bx = 0; bx < nsmall; ++bx)
-            tma_load_3d(smem_u32(sb + (nbig * shp.x_box + bx * kTcBoxRows) * 128), &tmap_x,
-                        &full_bar[stage], kb * kTcK, xrow0 + nbig * shp.x_box + bx * kTcBoxRows, gx);
+          if (waited) {
+            load_x(stage, kb, xrow0, gx, nbig, nsmall);
+          } else {  // first ring pass: stage == npend
+            pend_kb[npend] = kb;
+            pend_row[npend] = xrow0;
+            pend_gx[npend] = gx;
+            pend_big[npend] = nbig;
+            pend_small[npend] = nsmall;
+            if (++npend == shp.stages) release();
+          }
           if (++stage == shp.stages) { stage = 0; phase ^= 1; }
         }
       }
+      if (!waited) release();
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -336,7 +369,7 @@ TcShape tc_shape(bool swiglu, int n_max, long long base_items, int num_sms, bool
   }
   s.n_tile = n_tile;
   s.stage_bytes = (swiglu ? 2 : 1) * kTcABytes + n_tile * 128;
-  s.stages = min(8, (kTcSmemBudget - 2048) / s.stage_bytes);
+  s.stages = min(kTcMaxStages, (kTcSmemBudget - 2048) / s.stage_bytes);
   s.acc_cols = n_tile * (swiglu ? 2 : 1);
   s.acc_bufs = (2 * s.acc_cols <= kTcTmemCols) ? 2 : 1;
   s.tmem_cols = pow2_at_least(s.acc_bufs * s.acc_cols);
@@ -369,8 +402,7 @@ template <int EPI, bool ROUTED>
 static void tc_launch(int grid, size_t smem, cudaStream_t st, const LinearParams& p,
                       const CUtensorMap& w, const CUtensorMap& x, const CUtensorMap& xb,
                       const TcShape& shp, int mt_count, int nt_count, int up_rows, int x_grouped) {
-  linear_tc_kernel<EPI, ROUTED><<<grid, kTcThreads, smem, st>>>(p, w, x, xb, shp, mt_count,
-                                                                 nt_count, up_rows, x_grouped);
+  launch_kernel(linear_tc_kernel<EPI, ROUTED>, grid, kTcThreads, smem, st, p, w, x, xb, shp, mt_count, nt_count, up_rows, x_grouped);
 }
 
 // Launch geometry, shared with the tensor-map builder in api.cu (the large activation

@@ -44,6 +44,7 @@ constexpr int kMlaThreads = 128;
 // ----------------------------------------------------------------------------
 
 __global__ __launch_bounds__(256) void mla_prep_kernel(const MlaPrepParams p) {
+  pdl_enter();
   __shared__ float red[8];
   __shared__ __align__(16) bf16 s_row[kHeads * 192 + kRow];  // this row of qkva, bf16
   const int b = blockIdx.x;
@@ -144,6 +145,10 @@ __device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, 
 }
 
 __global__ __launch_bounds__(kMlaThreads, 2) void mla_decode_kernel(const MlaDecodeParams p) {
+  // inputs_prior: positions, q_pe and the cache are older than the previous launch, so
+  // the first cache tile is requested before waiting for it (it writes q_abs)
+  const bool early = p.inputs_prior != 0;
+  if (!early) pdl_enter();
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* s_q = smem;                                     // 9 chunks x 16 rows x 128 B
   unsigned char* s_kv = smem + kQBytes;                          // stages x 9 chunks x 64 rows x 128 B
@@ -160,6 +165,7 @@ __global__ __launch_bounds__(kMlaThreads, 2) void mla_decode_kernel(const MlaDec
   const int s_end = min(len, s_beg + p.split_len);
   float* mlp = p.ml_part + ((static_cast<long long>(b) * p.n_splits + split) * kHeads) * 2;
   if (s_beg >= s_end) {
+    if (early) pdl_enter();
     if (tid < kHeads) {
       mlp[tid * 2] = -INFINITY;
       mlp[tid * 2 + 1] = 0.f;
@@ -167,18 +173,6 @@ __global__ __launch_bounds__(kMlaThreads, 2) void mla_decode_kernel(const MlaDec
     return;
   }
   const bf16* cache_b = p.cache + b * p.cache_b_stride;
-
-  // --- stage Q = [q_abs | q_pe] (16 x 576) into swizzled smem
-  for (int i = tid; i < kHeads * kChunks * 8; i += kMlaThreads) {
-    const int h = i / (kChunks * 8), rem = i % (kChunks * 8);
-    const int ch = rem / 8, c16 = rem % 8;
-    const int d = ch * 64 + c16 * 8;
-    const bf16* src = (d < kLatent)
-                          ? p.q_abs + (static_cast<long long>(b) * kHeads + h) * kLatent + d
-                          : p.q_pe + (static_cast<long long>(b) * kHeads + h) * kRope + (d - kLatent);
-    *reinterpret_cast<uint4*>(s_q + ch * (kHeads * 128) + swz(h, c16)) = *reinterpret_cast<const uint4*>(src);
-  }
-
   const int n_tiles = (s_end - s_beg + kTile - 1) / kTile;
   auto load_tile = [&](int ti, int stage) {
     const int t0 = s_beg + ti * kTile;
@@ -192,9 +186,21 @@ __global__ __launch_bounds__(kMlaThreads, 2) void mla_decode_kernel(const MlaDec
       cp_async16_zfill(base + ch * (kTile * 128) + swz(r, c16), src, valid);
     }
   };
-
   load_tile(0, 0);
   cp_async_commit();
+  if (early) pdl_enter();
+
+  // --- stage Q = [q_abs | q_pe] (16 x 576) into swizzled smem
+  for (int i = tid; i < kHeads * kChunks * 8; i += kMlaThreads) {
+    const int h = i / (kChunks * 8), rem = i % (kChunks * 8);
+    const int ch = rem / 8, c16 = rem % 8;
+    const int d = ch * 64 + c16 * 8;
+    const bf16* src = (d < kLatent)
+                          ? p.q_abs + (static_cast<long long>(b) * kHeads + h) * kLatent + d
+                          : p.q_pe + (static_cast<long long>(b) * kHeads + h) * kRope + (d - kLatent);
+    *reinterpret_cast<uint4*>(s_q + ch * (kHeads * 128) + swz(h, c16)) = *reinterpret_cast<const uint4*>(src);
+  }
+
   __syncthreads();  // Q visible
 
   // --- query fragments for this warp's 9 k-steps (dims [144*warp, 144*warp + 144))
@@ -362,6 +368,7 @@ __global__ __launch_bounds__(128) void mla_combine_kernel(const float* __restric
                                                           int n_splits, bf16* __restrict__ o_lat,
                                                           const long long* __restrict__ positions,
                                                           int pos_numel, int max_len, int split_len) {
+  pdl_enter();
   const int b = blockIdx.x, h = blockIdx.y;
   const long long len = min(static_cast<long long>(max_len), positions[pos_numel == 1 ? 0 : b] + 1);
   if (len <= split_len) return;
@@ -426,7 +433,7 @@ constexpr size_t mla_decode_smem_bytes() {
 }
 
 cudaError_t launch_mla_prep(const MlaPrepParams& p, int batch, cudaStream_t st) {
-  mla_prep_kernel<<<batch, 256, 0, st>>>(p);
+  launch_kernel(mla_prep_kernel, batch, 256, 0, st, p);
   return cudaGetLastError();
 }
 
@@ -436,14 +443,14 @@ cudaError_t mla_decode_init() {
 }
 
 cudaError_t launch_mla_decode(const MlaDecodeParams& p, int batch, cudaStream_t st) {
-  mla_decode_kernel<<<dim3(p.n_splits, batch), kMlaThreads, mla_decode_smem_bytes(), st>>>(p);
+  launch_kernel(mla_decode_kernel, dim3(p.n_splits, batch), kMlaThreads, mla_decode_smem_bytes(), st, p);
   return cudaGetLastError();
 }
 
 cudaError_t launch_mla_combine(const MlaDecodeParams& p, int batch, cudaStream_t st) {
-  mla_combine_kernel<<<dim3(batch, kHeads), 128, 0, st>>>(p.o_part, p.ml_part, p.n_splits, p.o_lat,
-                                                           p.positions, p.pos_numel, p.max_len,
-                                                           p.split_len);
+  // one split covers the whole cache: every row wrote its output directly
+  if (static_cast<long long>(p.split_len) >= p.max_len) return cudaSuccess;
+  launch_kernel(mla_combine_kernel, dim3(batch, kHeads), 128, 0, st, p.o_part, p.ml_part, p.n_splits, p.o_lat, p.positions, p.pos_numel, p.max_len, p.split_len);
   return cudaGetLastError();
 }
 

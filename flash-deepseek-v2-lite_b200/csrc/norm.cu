@@ -63,6 +63,7 @@ __global__ __launch_bounds__(kNormThreads) void rmsnorm_kernel(const bf16* __res
                                                                int w_dtype, bf16* __restrict__ y,
                                                                long long y_stride, int cols,
                                                                float eps) {
+  pdl_enter();
   __shared__ float red[kNormThreads / 32];
   const int row = blockIdx.x;
   const bf16* xr = x + row * x_stride;
@@ -98,6 +99,7 @@ __global__ __launch_bounds__(kNormThreads) void add_rmsnorm_kernel(
     bf16* __restrict__ h, bf16* __restrict__ h_out, const void* __restrict__ delta, int delta_dtype,
     int n_delta, long long delta_part_stride, long long delta_row_stride,
     const void* __restrict__ w, int w_dtype, bf16* __restrict__ y, int cols, float eps) {
+  pdl_enter();
   __shared__ float red[kNormThreads / 32];
   const int row = blockIdx.x;
   bf16* hr = h + static_cast<long long>(row) * cols;
@@ -169,6 +171,7 @@ __global__ __launch_bounds__(kNormThreads) void embed_rmsnorm_kernel(
     const long long* __restrict__ ids, const bf16* __restrict__ table, long long vocab,
     const void* __restrict__ w, int w_dtype, bf16* __restrict__ h, bf16* __restrict__ y, int cols,
     float eps) {
+  pdl_enter();
   __shared__ float red[kNormThreads / 32];
   const int row = blockIdx.x;
   long long id = ids[row];
@@ -207,6 +210,7 @@ __global__ __launch_bounds__(kNormThreads) void embed_rmsnorm_kernel(
 // out = bf16(a + b), 8 elements per thread
 __global__ void residual_add_kernel(const bf16* __restrict__ a, const bf16* __restrict__ b,
                                     bf16* __restrict__ out, long long n8) {
+  pdl_enter();
   const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (i >= n8) return;
   const uint4 x = reinterpret_cast<const uint4*>(a)[i];
@@ -226,6 +230,7 @@ __global__ void residual_add_kernel(const bf16* __restrict__ a, const bf16* __re
 __global__ void sum_partials_kernel(const float* __restrict__ part, int n_parts, long long ps,
                                     long long rs, void* __restrict__ out, int out_f32,
                                     long long ors, int cols) {
+  pdl_enter();
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (c >= cols) return;
   const long long r = blockIdx.y;
@@ -258,6 +263,7 @@ __device__ __forceinline__ float silu_f(float g) { return g / (1.f + expf(-g)); 
 // out = bf16(silu(gate) * up)
 __global__ void silu_mul_kernel(const bf16* __restrict__ gate, const bf16* __restrict__ up,
                                 bf16* __restrict__ out, long long n8) {
+  pdl_enter();
   const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (i >= n8) return;
   const uint4 x = reinterpret_cast<const uint4*>(gate)[i];
@@ -279,6 +285,7 @@ __global__ void prepare_decode_inputs_kernel(const long long* __restrict__ cache
                                              long long mask_stride_b, long long* __restrict__ pos_ids,
                                              long long pos_ids_stride_b,
                                              const long long* __restrict__ mask_index, int max_len) {
+  pdl_enter();
   const int b = blockIdx.y;
   const long long pos = cache_position[pos_numel == 1 ? 0 : b];
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
@@ -293,6 +300,7 @@ __global__ void copy_token_to_cache_kernel(const char* __restrict__ src, long lo
                                            const long long* __restrict__ cache_position,
                                            int pos_numel, int heads, int dim, int esize,
                                            int max_len) {
+  pdl_enter();
   const int b = blockIdx.x, h = blockIdx.y;
   long long pos = cache_position[pos_numel == 1 ? 0 : b];
   if (pos < 0 || pos >= max_len) {
@@ -311,6 +319,7 @@ __global__ void copy_token_to_cache_kernel(const char* __restrict__ src, long lo
 
 // Advance per-row decode state after a step: pos[b] += 1 (int64 positions).
 __global__ void advance_positions_kernel(long long* __restrict__ pos, int n) {
+  pdl_enter();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) pos[i] += 1;
 }
@@ -320,26 +329,21 @@ __global__ void advance_positions_kernel(long long* __restrict__ pos, int n) {
 // ---------------------------------------------------------------------------
 cudaError_t launch_rmsnorm(const void* x, long long xs, const void* w, int wd, void* y,
                            long long ys, int rows, int cols, float eps, cudaStream_t st) {
-  rmsnorm_kernel<<<rows, kNormThreads, 0, st>>>(reinterpret_cast<const bf16*>(x), xs, w, wd,
-                                                reinterpret_cast<bf16*>(y), ys, cols, eps);
+  launch_kernel(rmsnorm_kernel, rows, kNormThreads, 0, st, reinterpret_cast<const bf16*>(x), xs, w, wd, reinterpret_cast<bf16*>(y), ys, cols, eps);
   return cudaGetLastError();
 }
 
 cudaError_t launch_add_rmsnorm(void* h, void* h_out, const void* delta, int dd, int nd,
                                long long dps, long long drs, const void* w, int wd, void* y,
                                int rows, int cols, float eps, cudaStream_t st) {
-  add_rmsnorm_kernel<<<rows, kNormThreads, 0, st>>>(
-      reinterpret_cast<bf16*>(h), reinterpret_cast<bf16*>(h_out), delta, dd, nd, dps, drs, w, wd,
-      reinterpret_cast<bf16*>(y), cols, eps);
+  launch_kernel(add_rmsnorm_kernel, rows, kNormThreads, 0, st, reinterpret_cast<bf16*>(h), reinterpret_cast<bf16*>(h_out), delta, dd, nd, dps, drs, w, wd, reinterpret_cast<bf16*>(y), cols, eps);
   return cudaGetLastError();
 }
 
 cudaError_t launch_embed_rmsnorm(const long long* ids, const void* table, long long vocab,
                                  const void* w, int wd, void* h, void* y, int rows, int cols,
                                  float eps, cudaStream_t st) {
-  embed_rmsnorm_kernel<<<rows, kNormThreads, 0, st>>>(ids, reinterpret_cast<const bf16*>(table),
-                                                      vocab, w, wd, reinterpret_cast<bf16*>(h),
-                                                      reinterpret_cast<bf16*>(y), cols, eps);
+  launch_kernel(embed_rmsnorm_kernel, rows, kNormThreads, 0, st, ids, reinterpret_cast<const bf16*>(table), vocab, w, wd, reinterpret_cast<bf16*>(h), reinterpret_cast<bf16*>(y), cols, eps);
   return cudaGetLastError();
 }
 
@@ -347,9 +351,7 @@ cudaError_t launch_residual_add(const void* a, const void* b, void* out, long lo
                                 cudaStream_t st) {
   const long long n8 = n / 8;
   const int thr = 256;
-  residual_add_kernel<<<static_cast<unsigned>((n8 + thr - 1) / thr), thr, 0, st>>>(
-      reinterpret_cast<const bf16*>(a), reinterpret_cast<const bf16*>(b),
-      reinterpret_cast<bf16*>(out), n8);
+  launch_kernel(residual_add_kernel, static_cast<unsigned>((n8 + thr - 1) / thr), thr, 0, st, reinterpret_cast<const bf16*>(a), reinterpret_cast<const bf16*>(b), reinterpret_cast<bf16*>(out), n8);
   return cudaGetLastError();
 }
 
@@ -357,16 +359,14 @@ cudaError_t launch_sum_partials(const float* part, int n_parts, long long ps, lo
                                int out_f32, long long ors, int rows, int cols, cudaStream_t st) {
   const int thr = 128;
   dim3 grid((cols / 8 + thr - 1) / thr, rows);
-  sum_partials_kernel<<<grid, thr, 0, st>>>(part, n_parts, ps, rs, out, out_f32, ors, cols);
+  launch_kernel(sum_partials_kernel, grid, thr, 0, st, part, n_parts, ps, rs, out, out_f32, ors, cols);
   return cudaGetLastError();
 }
 
 cudaError_t launch_silu_mul(const void* g, const void* u, void* out, long long n, cudaStream_t st) {
   const long long n8 = n / 8;
   const int thr = 256;
-  silu_mul_kernel<<<static_cast<unsigned>((n8 + thr - 1) / thr), thr, 0, st>>>(
-      reinterpret_cast<const bf16*>(g), reinterpret_cast<const bf16*>(u),
-      reinterpret_cast<bf16*>(out), n8);
+  launch_kernel(silu_mul_kernel, static_cast<unsigned>((n8 + thr - 1) / thr), thr, 0, st, reinterpret_cast<const bf16*>(g), reinterpret_cast<const bf16*>(u), reinterpret_cast<bf16*>(out), n8);
   return cudaGetLastError();
 }
 
@@ -374,7 +374,7 @@ cudaError_t launch_prepare_decode_inputs(const long long* cp, int pn, long long*
                                          long long* pid, long long psb, const long long* mi,
                                          int batch, int max_len, cudaStream_t st) {
   dim3 grid((max_len + 255) / 256, batch);
-  prepare_decode_inputs_kernel<<<grid, 256, 0, st>>>(cp, pn, mask, msb, pid, psb, mi, max_len);
+  launch_kernel(prepare_decode_inputs_kernel, grid, 256, 0, st, cp, pn, mask, msb, pid, psb, mi, max_len);
   return cudaGetLastError();
 }
 
@@ -383,14 +383,12 @@ cudaError_t launch_copy_token_to_cache(const void* src, const long long* ss, voi
                                        int heads, int dim, int esize, int max_len,
                                        cudaStream_t st) {
   dim3 grid(batch, heads);
-  copy_token_to_cache_kernel<<<grid, 128, 0, st>>>(
-      reinterpret_cast<const char*>(src), ss[0], ss[1], ss[2], reinterpret_cast<char*>(dst), ds[0],
-      ds[1], ds[2], ds[3], cp, pn, heads, dim, esize, max_len);
+  launch_kernel(copy_token_to_cache_kernel, grid, 128, 0, st, reinterpret_cast<const char*>(src), ss[0], ss[1], ss[2], reinterpret_cast<char*>(dst), ds[0], ds[1], ds[2], ds[3], cp, pn, heads, dim, esize, max_len);
   return cudaGetLastError();
 }
 
 cudaError_t launch_advance_positions(long long* pos, int n, cudaStream_t st) {
-  advance_positions_kernel<<<(n + 255) / 256, 256, 0, st>>>(pos, n);
+  launch_kernel(advance_positions_kernel, (n + 255) / 256, 256, 0, st, pos, n);
   return cudaGetLastError();
 }
 

@@ -68,6 +68,7 @@ struct MlaDecodeParams {
   float* o_part;               // [B, n_splits, 16, 512]
   float* ml_part;              // [B, n_splits, 16, 2]  (m in log2 domain, l)
   bf16* o_lat;                 // [B, 16, 512] output
+  int inputs_prior;            // q_pe / positions / cache written >= 2 launches earlier
 };
 
 // norm.cu

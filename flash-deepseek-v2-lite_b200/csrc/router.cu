@@ -32,7 +32,7 @@ constexpr int kSlots = 8;              // 6 routed + 2 shared-expert halves per 
 constexpr int kRtTok = 8;              // tokens per CTA (the mma N dimension)
 constexpr int kRtThreads = 256;        // 8 warps: 4 expert blocks of 16 x 2 K halves
 constexpr int kRtMaxHidden = 2048;
-constexpr int kRouteTok = 8;           // tokens per route_kernel CTA
+constexpr int kRouteTokMax = 32;       // tokens per route_kernel CTA (upper bound)
 constexpr int kRouteThreads = 256;
 constexpr int kRouteMaxRows = 4096;
 
@@ -73,6 +73,7 @@ __device__ void softmax_topk_warp(const float* lg, int n_experts, float scaling,
 // logits + softmax + top-6
 // ---------------------------------------------------------------------------------
 __global__ __launch_bounds__(kRtThreads) void router_topk_kernel(const RouterParams p) {
+  pdl_enter();
   constexpr int XS = kRtMaxHidden + 8;  // padded row (bank spread for the 16-byte reads)
   __shared__ __align__(16) bf16 s_x[kRtTok][XS];
   __shared__ float s_part[2][kMaxExperts][kRtTok];
@@ -169,18 +170,21 @@ struct RouteParams {
   long long gx_stride;
   bf16* gout;              // optional gather destination [routes, cols]
   int cols;
+  int tok_per_cta;
 };
 
 __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams p) {
+  pdl_enter();
   __shared__ int s_total[kMaxExperts];
   __shared__ int s_before[kMaxExperts];
   __shared__ int s_off[kMaxExperts + 3];
-  __shared__ int s_e[kRouteTok * kTopK];
-  __shared__ int s_pos[kRouteTok * kTopK + 2 * kRouteTok];
-  __shared__ int s_tok[kRouteTok * kTopK + 2 * kRouteTok];
+  __shared__ int s_e[kRouteTokMax * kTopK];
+  __shared__ int s_pos[kRouteTokMax * kSlots];
+  __shared__ int s_tok[kRouteTokMax * kSlots];
   const int tid = threadIdx.x;
-  const int tok0 = blockIdx.x * kRouteTok;
-  const int ntok = min(kRouteTok, p.rows - tok0);
+  const int tpc = p.tok_per_cta;
+  const int tok0 = blockIdx.x * tpc;
+  const int ntok = min(tpc, p.rows - tok0);
   for (int i = tid; i < kMaxExperts; i += kRouteThreads) { s_total[i] = 0; s_before[i] = 0; }
   __syncthreads();
   const int n_routes = p.rows * kTopK;
@@ -216,63 +220,75 @@ __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams 
   }
   // this CTA's routes, in (token, k) order
   const int my_routes = ntok * kTopK;
-  if (tid < my_routes) {
-    const int e = p.ids32[r_first + tid] - p.expert_lo;
-    s_e[tid] = (e >= 0 && e < p.n_local) ? e : -1;
+  for (int i = tid; i < my_routes; i += kRouteThreads) {
+    const int e = p.ids32[r_first + i] - p.expert_lo;
+    s_e[i] = (e >= 0 && e < p.n_local) ? e : -1;
   }
   __syncthreads();
   if (blockIdx.x == 0)
     for (int g = tid; g <= p.n_local + 2; g += kRouteThreads) p.group_offsets[g] = s_off[g];
-  if (tid < my_routes) {
-    const int e = s_e[tid];
+  for (int i = tid; i < my_routes; i += kRouteThreads) {
+    const int e = s_e[i];
+    int pos = -1;
     if (e >= 0) {
       int rank = 0;
-      for (int j = 0; j < tid; ++j) rank += (s_e[j] == e);
-      const int pos = s_off[e] + s_before[e] + rank;
-      const int r = r_first + tid;
+      for (int j = 0; j < i; ++j) rank += (s_e[j] == e);
+      pos = s_off[e] + s_before[e] + rank;
+      const int r = r_first + i;
       const int b = r / kTopK, k = r % kTopK;
       p.route_token[pos] = b;
       p.route_slot[pos] = b * kSlots + k;
       p.route_weight[pos] = p.tw[r];
-      s_pos[tid] = pos;
-      s_tok[tid] = b;
-    } else {
-      s_pos[tid] = -1;
+      s_tok[i] = b;
     }
+    s_pos[i] = pos;
   }
-  // shared-expert routes of this CTA's tokens
-  if (tid >= 64 && tid < 64 + 2 * kRouteTok) {
-    const int i = tid - 64, s = i / kRouteTok, t = i % kRouteTok;
+  // shared-expert routes of this CTA's tokens (slots 6 and 7)
+  for (int i = tid; i < 2 * tpc; i += kRouteThreads) {
+    const int sh = i / tpc, t = i % tpc;
     const int b = tok0 + t;
     int pos = -1;
     if (t < ntok && b >= p.shared_lo && b < p.shared_hi) {
-      pos = s_off[p.n_local + s] + (b - p.shared_lo);
+      pos = s_off[p.n_local + sh] + (b - p.shared_lo);
       p.route_token[pos] = b;
-      p.route_slot[pos] = b * kSlots + kTopK + s;
+      p.route_slot[pos] = b * kSlots + kTopK + sh;
       p.route_weight[pos] = 1.f;
     }
-    s_pos[kRouteTok * kTopK + i] = pos;
-    s_tok[kRouteTok * kTopK + i] = b;
+    s_pos[tpc * kTopK + i] = pos;
+    s_tok[tpc * kTopK + i] = b;
   }
   if (!p.gout) return;
   __syncthreads();
-  // gather: one warp per placed route row
+  // gather: one warp per placed row; each lane holds up to 8 16-byte chunks in flight
   const int warp = tid >> 5, lane = tid & 31;
-  const int nslots = kRouteTok * kTopK + 2 * kRouteTok;
+  const int nslots = tpc * kSlots;
+  const int n16 = p.cols / 8;
   for (int i = warp; i < nslots; i += kRouteThreads / 32) {
-    const bool routed = i < kRouteTok * kTopK;
-    if (routed && i >= my_routes) continue;
+    if (i < tpc * kTopK && i >= my_routes) continue;
     const int pos = s_pos[i];
     if (pos < 0) continue;
     const uint4* src = reinterpret_cast<const uint4*>(p.gx + s_tok[i] * p.gx_stride);
     uint4* dst = reinterpret_cast<uint4*>(p.gout + static_cast<long long>(pos) * p.cols);
-    for (int c = lane; c < p.cols / 8; c += 32) dst[c] = src[c];
+    for (int c0 = 0; c0 < n16; c0 += 8 * 32) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < n16) v[u] = src[c];
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < n16) dst[c] = v[u];
+      }
+    }
   }
 }
 
 // Softmax/top-6 over precomputed logits (the reference's router_softmax_topk6_triton).
 __global__ void softmax_topk_kernel(const float* logits, int rows, int n_experts, float scaling,
                                     long long* ids64, int* ids32, float* tw) {
+  pdl_enter();
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (row >= rows) return;
   softmax_topk_warp(logits + static_cast<long long>(row) * n_experts, n_experts, scaling, row,
@@ -284,6 +300,7 @@ __global__ void gather_rows_kernel(const bf16* __restrict__ x, long long x_row_s
                                    const int* __restrict__ route_token,
                                    const int* __restrict__ group_offsets, int n_groups,
                                    bf16* __restrict__ out, int cols, int max_routes) {
+  pdl_enter();
   const int r = blockIdx.x;
   if (r >= max_routes || r >= group_offsets[n_groups]) return;
   const int t = route_token[r];
@@ -312,12 +329,15 @@ static cudaError_t launch_route(const int* ids32, const float* tw, int rows, int
   q.gx_stride = gxs;
   q.gout = gout;
   q.cols = cols;
-  route_kernel<<<(rows + kRouteTok - 1) / kRouteTok, kRouteThreads, 0, st>>>(q);
+  // about one CTA per SM (the counting pass is repeated by every CTA; the placement and
+  // the row copies are split between them)
+  q.tok_per_cta = min(kRouteTokMax, max(1, (rows + 147) / 148));
+  launch_kernel(route_kernel, (rows + q.tok_per_cta - 1) / q.tok_per_cta, kRouteThreads, 0, st, q);
   return cudaGetLastError();
 }
 
 cudaError_t launch_router(const RouterParams& p, cudaStream_t st) {
-  router_topk_kernel<<<(p.rows + kRtTok - 1) / kRtTok, kRtThreads, 0, st>>>(p);
+  launch_kernel(router_topk_kernel, (p.rows + kRtTok - 1) / kRtTok, kRtThreads, 0, st, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || !p.group_offsets) return e;
   return launch_route(p.topk_ids32, p.topk_w, p.rows, p.expert_lo, p.n_local, p.shared_lo,
@@ -336,17 +356,14 @@ cudaError_t launch_bucket(const int* ids32, const float* tw, int rows, int exper
 cudaError_t launch_softmax_topk(const float* logits, int rows, int n_experts, float scaling,
                                 long long* ids64, int* ids32, float* tw, cudaStream_t st) {
   const int warps = 4;
-  softmax_topk_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, st>>>(logits, rows, n_experts,
-                                                                          scaling, ids64, ids32, tw);
+  launch_kernel(softmax_topk_kernel, (rows + warps - 1) / warps, warps * 32, 0, st, logits, rows, n_experts, scaling, ids64, ids32, tw);
   return cudaGetLastError();
 }
 
 cudaError_t launch_gather_rows(const void* x, long long xs, const int* rt, const int* go,
                                int n_groups, void* out, int cols, int max_routes, cudaStream_t st) {
   if (max_routes <= 0) return cudaSuccess;
-  gather_rows_kernel<<<max_routes, 128, 0, st>>>(reinterpret_cast<const bf16*>(x), xs, rt, go,
-                                                 n_groups, reinterpret_cast<bf16*>(out), cols,
-                                                 max_routes);
+  launch_kernel(gather_rows_kernel, max_routes, 128, 0, st, reinterpret_cast<const bf16*>(x), xs, rt, go, n_groups, reinterpret_cast<bf16*>(out), cols, max_routes);
   return cudaGetLastError();
 }
 

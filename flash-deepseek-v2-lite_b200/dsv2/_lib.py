@@ -46,7 +46,7 @@ class LinearArgs(ctypes.Structure):
         ("epilogue", c_i32), ("n_groups", c_i32), ("n_tokens", c_i32), ("max_routes_per_group", c_i32),
         ("group_offsets", c_vp), ("route_x_row", c_vp), ("route_y_row", c_vp), ("route_scale", c_vp),
         ("w_group_rows", c_i64), ("x_group_rows", c_i64),
-        ("k_splits", c_i32), ("y_split_stride", c_i64),
+        ("k_splits", c_i32), ("y_split_stride", c_i64), ("offsets_prior", c_i32),
     ]
 
 
@@ -78,7 +78,7 @@ class MlaDecodeArgs(ctypes.Structure):
         ("q_abs", c_vp), ("q_pe", c_vp), ("cache", c_vp), ("cache_b_stride", c_i64), ("max_len", c_i32),
         ("positions", c_vp), ("pos_numel", c_i32), ("softmax_scale", c_f32),
         ("split_len", c_i32), ("n_splits", c_i32), ("o_part", c_vp), ("ml_part", c_vp),
-        ("o_lat", c_vp), ("batch", c_i32),
+        ("o_lat", c_vp), ("batch", c_i32), ("inputs_prior", c_i32),
     ]
 
 
@@ -86,6 +86,8 @@ _SIGNATURES = {
     "dsv2_version": ([], c_i32),
     "dsv2_last_error": ([], ctypes.c_char_p),
     "dsv2_init": ([], c_i32),
+    "dsv2_set_programmatic_launch": ([c_i32], c_i32),
+    "dsv2_kernel_launches": ([], c_i64),
     "dsv2_get_device_error": ([ctypes.POINTER(c_i32), c_i32], c_i32),
     "dsv2_rmsnorm": ([c_vp, c_i64, c_vp, c_i32, c_vp, c_i64, c_i32, c_i32, c_f32, c_vp], c_i32),
     "dsv2_add_rmsnorm": ([c_vp, c_vp, c_vp, c_i32, c_i32, c_i64, c_i64, c_vp, c_i32, c_vp, c_i32, c_i32,
@@ -152,6 +154,16 @@ def check(rc: int, what: str) -> None:
 
 def call(name: str, *args) -> None:
     check(getattr(load(), name)(*args), name)
+
+
+def kernel_launches() -> int:
+    """Kernels enqueued by libdsv2 so far in this process."""
+    return int(load().dsv2_kernel_launches())
+
+
+def set_programmatic_launch(enable: bool) -> bool:
+    """Turn programmatic dependent launch on or off for later launches; returns the old setting."""
+    return bool(load().dsv2_set_programmatic_launch(1 if enable else 0))
 
 
 def device_error(clear: bool = True) -> int:

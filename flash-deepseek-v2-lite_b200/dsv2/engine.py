@@ -190,7 +190,7 @@ class DecodeEngine:
                      x_group_rows=B)
         ops.mla_decode(q_abs=self.q_abs, q_pe=self.q_pe, cache=self.cache[li], positions=self.positions,
                        softmax_scale=self.scale, split_len=self.split_len, o_part=self.o_part,
-                       ml_part=self.ml_part, o_lat=self.o_lat)
+                       ml_part=self.ml_part, o_lat=self.o_lat, inputs_prior=True)
         # o[b, h] = o_lat[b, h] @ W_UV[h]^T,  W_UV[h] = kv_b[h*256 + 128 : h*256 + 256]
         self._linear(w=a.kv_b[QK_NOPE:], n_rows=V_DIM, k=KV_LORA, w_row_stride=KV_LORA,
                      w_group_stride=(QK_NOPE + V_DIM) * KV_LORA, x=self.o_lat, x_row_stride=N_HEADS * KV_LORA,
@@ -258,7 +258,7 @@ class DecodeEngine:
                      y=self.partial.view(-1, HIDDEN), epilogue=ops.EPI_SCALE_F32, n_groups=G,
                      group_offsets=go, max_routes_per_group=self.B_all,
                      route_y_row=self.route_slot, route_scale=self.route_weight, w_group_rows=HIDDEN,
-                     x_group_rows=self.r_max)
+                     x_group_rows=self.r_max, offsets_prior=True)
 
     def time_moe_gemms(self, iters: int = 10) -> tuple[float, float, int]:
         """Replay only the grouped MoE GEMMs of every MoE layer (routing of the last step's

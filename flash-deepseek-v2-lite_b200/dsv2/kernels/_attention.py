@@ -171,7 +171,8 @@ def mla_decode_layer(name: str, hidden_states, cos, sin, position_ids, cache_pos
                x_group_stride=QK_NOPE, y=ws.q_abs, y_row_stride=HEADS * KV_LORA, y_group_stride=KV_LORA,
                n_groups=HEADS, n_tokens=B, family=family, w_group_rows=KV_LORA, x_group_rows=B)
     ops.mla_decode(q_abs=ws.q_abs, q_pe=ws.q_pe, cache=key_cache, positions=pos, softmax_scale=softmax_scale,
-                   split_len=ws.split_len, o_part=ws.o_part, ml_part=ws.ml_part, o_lat=ws.o_lat)
+                   split_len=ws.split_len, o_part=ws.o_part, ml_part=ws.ml_part, o_lat=ws.o_lat,
+                   inputs_prior=True)
     kv_b = packed.kv_b_weight
     ops.linear(w=kv_b[QK_NOPE:], n_rows=V_DIM, k=KV_LORA, w_row_stride=KV_LORA,
                w_group_stride=(QK_NOPE + V_DIM) * KV_LORA, x=ws.o_lat, x_row_stride=HEADS * KV_LORA,

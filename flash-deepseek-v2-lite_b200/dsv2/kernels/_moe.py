@@ -133,6 +133,7 @@ def routed_moe(name: str, x: torch.Tensor, topk_ids: torch.Tensor, topk_weight: 
                w_group_rows=2 * I, x_group_rows=R if batch else B)
     ops.linear(w=packed.down_weights, n_rows=H, k=I, w_group_stride=H * I, x=h, y=partial.view(-1, H),
                epilogue=ops.EPI_SCALE_F32, n_groups=E, group_offsets=go, max_routes_per_group=B,
-               route_y_row=rs, route_scale=rw, family=family, w_group_rows=H, x_group_rows=R)
+               route_y_row=rs, route_scale=rw, family=family, w_group_rows=H, x_group_rows=R,
+               offsets_prior=True)
     ops.sum_partials(partial[:, :K], out)
     return out

@@ -152,11 +152,14 @@ def linear(*, w: torch.Tensor, n_rows: int, k: int, x: torch.Tensor, y: torch.Te
            route_x_row: torch.Tensor | None = None, route_y_row: torch.Tensor | None = None,
            route_scale: torch.Tensor | None = None,
            w_group_rows: int | None = None, x_group_rows: int | None = None,
-           x_base: int | None = None, k_splits: int = 1, y_split_stride: int = 0) -> None:
+           x_base: int | None = None, k_splits: int = 1, y_split_stride: int = 0,
+           offsets_prior: bool = False) -> None:
     """Generic linear (see dsv2_linear_args in include/dsv2.h).
 
     Strides are in elements; defaults take them from the 2-D views of w / x / y.
     x_base overrides x's data pointer (strided column views such as q_nope).
+    offsets_prior: group_offsets / route arrays were written at least two launches earlier
+    on this stream (lets the kernel start before the previous one completes).
     """
     a = LinearArgs()
     a.w = w.data_ptr()
@@ -183,6 +186,7 @@ def linear(*, w: torch.Tensor, n_rows: int, k: int, x: torch.Tensor, y: torch.Te
     a.x_group_rows = (n_tokens if x_group_rows is None else x_group_rows)
     a.k_splits = k_splits
     a.y_split_stride = y_split_stride
+    a.offsets_prior = 1 if offsets_prior else 0
     _lib.call("dsv2_linear", ctypes.byref(a), family, stream())
 
 
@@ -295,7 +299,10 @@ def mla_prep(*, qkva: torch.Tensor, kv_norm_w: torch.Tensor, eps: float, cos: to
 
 def mla_decode(*, q_abs: torch.Tensor, q_pe: torch.Tensor, cache: torch.Tensor, positions: torch.Tensor,
                softmax_scale: float, split_len: int, o_part: torch.Tensor, ml_part: torch.Tensor,
-               o_lat: torch.Tensor) -> None:
+               o_lat: torch.Tensor, inputs_prior: bool = False) -> None:
+    """Latent attention for every row (see dsv2_mla_decode_args in include/dsv2.h).
+    inputs_prior: q_pe, positions and the cache were written at least two launches earlier
+    on this stream (only q_abs by the previous one)."""
     for name, t in (("q_abs", q_abs), ("q_pe", q_pe), ("o_part", o_part), ("ml_part", ml_part), ("o_lat", o_lat)):
         _cuda(t, name)
         if not t.is_contiguous():
@@ -320,4 +327,5 @@ def mla_decode(*, q_abs: torch.Tensor, q_pe: torch.Tensor, cache: torch.Tensor, 
     a.ml_part = ml_part.data_ptr()
     a.o_lat = o_lat.data_ptr()
     a.batch = q_abs.shape[0]
+    a.inputs_prior = 1 if inputs_prior else 0
     _lib.call("dsv2_mla_decode", ctypes.byref(a), stream())

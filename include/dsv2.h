@@ -58,6 +58,18 @@ DSV2_API const char* dsv2_last_error(void);
  * points call it lazily. */
 DSV2_API int dsv2_init(void);
 
+/* Programmatic dependent launch: every kernel is enqueued with programmatic stream
+ * serialization, so it is scheduled while its predecessor in the stream drains and
+ * waits on the device (griddepcontrol.wait) before touching that predecessor's outputs.
+ * On by default; DSV2_PDL=0 in the environment or this call turns it off.  Returns the
+ * previous setting.  Applies to launches made after the call (a captured graph keeps
+ * the setting it was captured with).  No reference counterpart. */
+DSV2_API int dsv2_set_programmatic_launch(int enable);
+
+/* Number of kernels this library has enqueued in the process (all devices, all
+ * streams), for launch accounting.  No reference counterpart. */
+DSV2_API int64_t dsv2_kernel_launches(void);
+
 /* Reads (and optionally clears) the device error word of the current device.
  * Synchronous (cudaMemcpyFromSymbol); call outside the hot loop. */
 DSV2_API int dsv2_get_device_error(int* code, int clear);
@@ -172,6 +184,11 @@ typedef struct dsv2_linear_args {
    * the caller sums the partials (e.g. dsv2_add_rmsnorm with fp32 parts).  0 or 1 = no split. */
   int32_t k_splits;
   int64_t y_split_stride;
+  /* batch family, grouped mode: nonzero when group_offsets (and the route arrays) were
+   * written by a kernel at least two launches earlier on this stream, e.g. the MoE down
+   * GEMM after bucketing -> gate_up.  The kernel then reads them, and starts streaming
+   * weights, while the previous kernel is still running.  0 = no such guarantee. */
+  int32_t offsets_prior;
 } dsv2_linear_args;
 
 DSV2_API int dsv2_linear(const dsv2_linear_args* args, int family, void* stream);
@@ -299,6 +316,11 @@ typedef struct dsv2_mla_decode_args {
   float* ml_part;
   void* o_lat;
   int32_t batch;
+  /* nonzero when q_pe, positions and the cache were written at least two launches earlier
+   * on this stream (only q_abs may come from the previous launch, e.g. prep -> absorb ->
+   * decode): the kernel then starts loading cache tiles while the previous kernel is still
+   * running.  0 = no such guarantee. */
+  int32_t inputs_prior;
 } dsv2_mla_decode_args;
 
 DSV2_API int dsv2_mla_decode(const dsv2_mla_decode_args* args, void* stream);

@@ -26,6 +26,10 @@ def test_library_loads_and_exports_every_declared_symbol():
         assert hasattr(lib, s), s
     assert set(syms) == set(_lib.EXPORTED)
     assert lib.dsv2_version() >= 100
+    # host-only entry points: the launch counter and the programmatic-launch switch
+    assert _lib.kernel_launches() >= 0
+    prev = _lib.set_programmatic_launch(False)
+    assert _lib.set_programmatic_launch(prev) is False
 
 
 def test_ops_fail_loudly_without_valid_args():

@@ -130,3 +130,42 @@ def test_graph_replay_matches_eager(models):
     torch.cuda.synchronize()
     for a, b in zip(eager, graph):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("family,batch", [("batch", 8), ("small", 2)])
+def test_programmatic_launch_matches_serialized(models, family, batch):
+    """Graph replays with programmatic dependent launch (default) and with plain stream
+    serialization give bit-identical logits and tokens; the launch counter sees every kernel."""
+    from dsv2 import _lib
+    from dsv2.engine import DecodeEngine
+    model, _ = models
+    g = torch.Generator().manual_seed(4)
+    prompts = [torch.randint(0, model.config.vocab_size, (int(n),), generator=g)
+               for n in torch.randint(5, 60, (batch,), generator=g)]
+    eng = DecodeEngine(model, batch=batch, max_len=96, family=family, alias_hf=False)
+    eng.prefill(prompts)
+    n0 = _lib.kernel_launches()
+    eng.step()
+    per_step = _lib.kernel_launches() - n0
+    assert per_step >= 3 * 9
+    eng.restore()
+    outs = {}
+    for pdl in (True, False):
+        prev = _lib.set_programmatic_launch(pdl)
+        try:
+            eng.capture()
+            logits, toks = [], []
+            for _ in range(3):
+                eng.replay()
+                logits.append(eng.logits.clone())
+                toks.append(eng.next_ids.clone())
+            torch.cuda.synchronize()
+            eng.release()
+            eng.restore()
+        finally:
+            _lib.set_programmatic_launch(prev)
+        outs[pdl] = (logits, toks)
+    for a, b in zip(outs[True][0], outs[False][0]):
+        assert torch.equal(a, b)
+    for a, b in zip(outs[True][1], outs[False][1]):
+        assert torch.equal(a, b)
