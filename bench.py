@@ -313,7 +313,9 @@ def run_ours(args, cfg_id: int):
             },
             "roofline": {
                 "bound": "hbm",
-                "kernel": "linear_tc_kernel/gemv_mma_kernel grouped MoE gate_up+down (all MoE layers)",
+                "kernel": ("moe_tc_kernel: fused grouped MoE gate_up+SwiGLU+down (all MoE layers)"
+                           if family == "batch" else
+                           "gemv_mma_kernel: grouped MoE gate_up+SwiGLU and down (all MoE layers)"),
                 "achieved": round(dk_gbs, 1) if dk_gbs else None,
                 "peak": peak,
                 "unit": "GB/s",

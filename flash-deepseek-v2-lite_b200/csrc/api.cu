@@ -69,6 +69,8 @@ int ensure_init(int* sms_out) {
       return fail(DSV2_ERR_LAUNCH, "mla_decode_init: %s", cudaGetErrorString(e));
     if ((e = linear_tc_init()) != cudaSuccess)
       return fail(DSV2_ERR_LAUNCH, "linear_tc_init: %s", cudaGetErrorString(e));
+    if ((e = moe_tc_init()) != cudaSuccess)
+      return fail(DSV2_ERR_LAUNCH, "moe_tc_init: %s", cudaGetErrorString(e));
     g_dev_sms[dev] = sms;
     g_dev_init[dev] = true;
   }
@@ -391,6 +393,51 @@ int dsv2_linear(const dsv2_linear_args* a, int family, void* stream) {
   return check_launch(launch_linear_tc_impl(p, mw, mx, mxb, shp, mt_count, nt_count, items, up_rows,
                                             xg ? 1 : 0, sms, st),
                       "linear(batch)");
+}
+
+int dsv2_moe(const dsv2_moe_args* a, void* stream) {
+  if (!a || !a->gate_up || !a->down || !a->x_sorted || !a->h || !a->group_offsets || !a->route_slot ||
+      !a->route_weight || !a->y || !a->sync)
+    return fail(DSV2_ERR_INVALID, "moe: null pointer");
+  if (a->n_groups <= 0 || a->n_groups + 1 > kTcMaxGroups)
+    return fail(DSV2_ERR_UNSUPPORTED, "moe: n_groups=%d (max %d)", a->n_groups, kTcMaxGroups - 1);
+  if (a->hidden <= 0 || a->inter <= 0 || a->hidden % 64 || a->inter % 64)
+    return fail(DSV2_ERR_UNSUPPORTED, "moe: hidden %d / inter %d must be multiples of 64", a->hidden,
+                a->inter);
+  if (a->x_rows <= 0 || a->max_routes_per_group <= 0) return DSV2_OK;
+  if (!aligned16(a->gate_up) || !aligned16(a->down) || !aligned16(a->x_sorted) || !aligned16(a->h) ||
+      !aligned16(a->y))
+    return fail(DSV2_ERR_INVALID, "moe: operands must be 16-byte aligned");
+  int sms = 0;
+  int rc = ensure_init(&sms);
+  if (rc) return rc;
+  const uint64_t H = static_cast<uint64_t>(a->hidden), I = static_cast<uint64_t>(a->inter);
+  const uint64_t G = static_cast<uint64_t>(a->n_groups), R = static_cast<uint64_t>(a->x_rows);
+  if (a->tile_tokens < 0 || a->tile_tokens > 128 || a->tile_tokens % 16)
+    return fail(DSV2_ERR_INVALID, "moe: tile_tokens %d (0, or a multiple of 16 up to 128)", a->tile_tokens);
+  const MoeShape shp = moe_shape(a->max_routes_per_group, a->tile_tokens);
+  CUtensorMap w1, x1, x1b, w2, hm, hb;
+  if ((rc = tensor_map_3d(a->gate_up, H, 2 * I, G, H * 2, 2 * I * H * 2, 128, &w1))) return rc;
+  if ((rc = tensor_map_3d(a->x_sorted, H, R, 1, H * 2, R * H * 2, 16, &x1))) return rc;
+  if ((rc = tensor_map_3d(a->x_sorted, H, R, 1, H * 2, R * H * 2, shp.x_box, &x1b))) return rc;
+  if ((rc = tensor_map_3d(a->down, I, H, G, I * 2, H * I * 2, 128, &w2))) return rc;
+  if ((rc = tensor_map_3d(a->h, I, R, 1, I * 2, R * I * 2, 16, &hm))) return rc;
+  if ((rc = tensor_map_3d(a->h, I, R, 1, I * 2, R * I * 2, shp.x_box, &hb))) return rc;
+  MoeParams p = {};
+  p.n_groups = a->n_groups;
+  p.hidden = a->hidden;
+  p.inter = a->inter;
+  p.x_rows = a->x_rows;
+  p.group_offsets = a->group_offsets;
+  p.max_routes_per_group = a->max_routes_per_group;
+  p.route_slot = a->route_slot;
+  p.route_weight = a->route_weight;
+  p.h = reinterpret_cast<bf16*>(a->h);
+  p.y = a->y;
+  p.sync = a->sync;
+  return check_launch(launch_moe_tc(p, w1, x1, x1b, w2, hm, hb, shp, sms,
+                                    static_cast<cudaStream_t>(stream)),
+                      "moe");
 }
 
 int dsv2_router(const dsv2_router_args* a, void* stream) {

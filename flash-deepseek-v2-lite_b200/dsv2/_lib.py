@@ -50,6 +50,15 @@ class LinearArgs(ctypes.Structure):
     ]
 
 
+class MoeArgs(ctypes.Structure):
+    _fields_ = [
+        ("gate_up", c_vp), ("down", c_vp), ("n_groups", c_i32), ("hidden", c_i32), ("inter", c_i32),
+        ("x_sorted", c_vp), ("h", c_vp), ("x_rows", c_i32), ("group_offsets", c_vp),
+        ("max_routes_per_group", c_i32), ("route_slot", c_vp), ("route_weight", c_vp), ("y", c_vp),
+        ("sync", c_vp), ("tile_tokens", c_i32),
+    ]
+
+
 class RouterArgs(ctypes.Structure):
     _fields_ = [
         ("x", c_vp), ("x_row_stride", c_i64), ("w", c_vp), ("w_dtype", c_i32),
@@ -101,6 +110,7 @@ _SIGNATURES = {
                                   c_vp], c_i32),
     "dsv2_advance_positions": ([c_vp, c_i32, c_vp], c_i32),
     "dsv2_linear": ([ctypes.POINTER(LinearArgs), c_i32, c_vp], c_i32),
+    "dsv2_moe": ([ctypes.POINTER(MoeArgs), c_vp], c_i32),
     "dsv2_router": ([ctypes.POINTER(RouterArgs), c_vp], c_i32),
     "dsv2_softmax_topk": ([c_vp, c_i32, c_i32, c_f32, c_vp, c_vp, c_vp, c_vp], c_i32),
     "dsv2_moe_bucket": ([c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp,

@@ -58,7 +58,7 @@ class DecodeState:
 class DecodeEngine:
     def __init__(self, model, batch: int, max_len: int, family: str = "batch", *,
                  rank: int = 0, world: int = 1, group=None, gate_bias: torch.Tensor | None = None,
-                 alias_hf: bool = True):
+                 alias_hf: bool = True, fused_moe: bool = True):
         cfg = model.config
         check_config(cfg)
         if family not in FAMILIES:
@@ -71,6 +71,7 @@ class DecodeEngine:
         self.B = int(batch)                  # rows owned by this rank
         self.max_len = int(max_len)
         self.rank, self.world, self.group = rank, world, group
+        self.fused_moe = fused_moe
         self.B_all = self.B * world
         self.shard = ep_shard(int(cfg.n_routed_experts), self.B_all, rank, world)
         self.n_local = self.shard.n_local
@@ -150,6 +151,7 @@ class DecodeEngine:
             self.route_weight = torch.zeros(self.r_max, device=dev, dtype=f32)
             self.x_sorted = torch.zeros((self.r_max, HIDDEN), device=dev, dtype=bf)
             self.h_moe = torch.zeros((self.r_max, m0.inter), device=dev, dtype=bf)
+            self.moe_sync = torch.zeros(self.n_groups + 1, device=dev, dtype=i32)
             self.partial = torch.zeros((Ball, SLOTS, HIDDEN), device=dev, dtype=f32)
             if self.world > 1:
                 self.x_all = torch.zeros((Ball, HIDDEN), device=dev, dtype=bf)
@@ -244,7 +246,13 @@ class DecodeEngine:
         return self.moe_local
 
     def _moe_gemms(self, m, go: torch.Tensor, x_src: torch.Tensor) -> None:
-        """gate_up + SwiGLU and down + route-weight scaling over local experts + shared halves."""
+        """gate_up + SwiGLU and down + route-weight scaling over local experts + shared halves
+        (batch family: one fused persistent launch; small family: two GEMV launches)."""
+        if self.family == ops.FAMILY_BATCH and self.fused_moe:
+            ops.moe(gate_up=m.gate_up, down=m.down, x_sorted=self.x_sorted, h=self.h_moe, group_offsets=go,
+                    max_routes_per_group=self.B_all, route_slot=self.route_slot,
+                    route_weight=self.route_weight, y=self.partial.view(-1, HIDDEN), sync=self.moe_sync)
+            return
         if self.family == ops.FAMILY_BATCH:
             gx, rx = self.x_sorted, None
         else:
@@ -273,9 +281,12 @@ class DecodeEngine:
         g = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream(device=self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
+        from . import _lib
+        n0 = _lib.kernel_launches()
         with torch.cuda.stream(s):
             for lp in moe_layers:
                 self._moe_gemms(lp.moe, go, x_src)
+        launches = _lib.kernel_launches() - n0
         torch.cuda.current_stream(self.dev).wait_stream(s)
         with torch.cuda.graph(g):
             for lp in moe_layers:
@@ -295,7 +306,7 @@ class DecodeEngine:
         per_expert = (2 * m0.inter * HIDDEN + HIDDEN * m0.inter) * 2
         nbytes = len(moe_layers) * int((counts > 0).sum()) * per_expert
         del g
-        return ms, float(nbytes), 2 * len(moe_layers)
+        return ms, float(nbytes), launches
 
     # ------------------------------------------------------------------ step
     @torch.no_grad()

@@ -103,10 +103,10 @@ def routed_moe(name: str, x: torch.Tensor, topk_ids: torch.Tensor, topk_weight: 
     """out[b] = sum_k w[b,k] * down_e(silu(gate_e(x[b])) * up_e(x[b])), e = ids[b,k].
 
     Launches: bucket routes by expert (stable, + expert-ordered copy of x for the
-    batch family) -> grouped gate_up GEMM with the SwiGLU epilogue -> grouped down GEMM
-    scaling each route by its weight into per-slot fp32 partials -> fixed-order sum of
-    the six slots.  ``family`` selects the mma.sync GEMV (small) or tcgen05 (batch)
-    kernels."""
+    batch family) -> grouped gate_up GEMM with the SwiGLU epilogue and grouped down GEMM
+    scaling each route by its weight into per-slot fp32 partials (batch family: one fused
+    tcgen05 launch; small family: two mma.sync GEMV launches) -> fixed-order sum of the
+    six slots."""
     out_dtype = _check(name, x, topk_ids, topk_weight, packed, output_dtype)
     x = x.contiguous()
     B, H = (int(s) for s in x.shape)
@@ -127,6 +127,12 @@ def routed_moe(name: str, x: torch.Tensor, topk_ids: torch.Tensor, topk_weight: 
     batch = family == ops.FAMILY_BATCH
     xs = torch.empty((R, H), device=dev, dtype=torch.bfloat16) if batch else None
     ops.moe_bucket(ids32, tw, 0, E, 0, 0, go, rt, rs, rw, gather_src=x if batch else None, gather_out=xs)
+    if batch:
+        sync = torch.zeros(E + 1, device=dev, dtype=torch.int32)
+        ops.moe(gate_up=packed.gate_up_weights, down=packed.down_weights, x_sorted=xs, h=h, group_offsets=go,
+                max_routes_per_group=B, route_slot=rs, route_weight=rw, y=partial.view(-1, H), sync=sync)
+        ops.sum_partials(partial[:, :K], out)
+        return out
     ops.linear(w=packed.gate_up_weights, n_rows=I, k=H, up_offset=I * H, w_group_stride=2 * I * H,
                x=xs if batch else x, y=h, epilogue=ops.EPI_SWIGLU, n_groups=E, group_offsets=go,
                max_routes_per_group=B, route_x_row=None if batch else rt, family=family,

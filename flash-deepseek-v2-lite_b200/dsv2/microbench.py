@@ -2,8 +2,8 @@
 
     python -m dsv2.microbench --kernel moe_gate_up --batch 256 [--family batch] [--iters 20]
 
-Kernels: moe_gate_up, moe_down (one MoE layer: 64 routed experts + 2 shared halves,
-uniform random routing), qkva, absorb, unabsorb, o_proj, dense_gate_up, dense_down,
+Kernels: moe (fused gate_up + down, batch family), moe_gate_up, moe_down (one MoE layer:
+64 routed experts + 2 shared halves, uniform random routing), qkva, absorb, unabsorb, o_proj, dense_gate_up, dense_down,
 mla_decode (ctx = --ctx positions per row), router.  Prints one JSON line with the
 CUDA-event time per launch and the algorithmic bytes / s.  The footprint of every
 case is at most ~1.5 GB, so it can run under `ncu --set full` on one launch.
@@ -32,12 +32,12 @@ def _routing(B, n_exp, g, dev):
 
 
 def build_case(kernel: str, B: int, family: int, ctx: int, split_len: int | None, dev="cuda",
-               k_splits: int = 1):
+               k_splits: int = 1, tile_tokens: int = 0):
     g = torch.Generator(device=dev).manual_seed(0)
     H, I, E = 2048, 1408, 64
     calls = []
     nbytes = 0
-    if kernel in ("moe_gate_up", "moe_down", "router", "router_topk", "moe_bucket"):
+    if kernel in ("moe", "moe_gate_up", "moe_down", "router", "router_topk", "moe_bucket"):
         G = E + 2
         gate_up = _rnd((G, 2 * I, H), g, 0.02)
         down = _rnd((G, H, I), g, 0.02)
@@ -56,7 +56,13 @@ def build_case(kernel: str, B: int, family: int, ctx: int, split_len: int | None
         part = torch.zeros(B, 8, H, device=dev)
         distinct = int((torch.bincount(ids.view(-1).long(), minlength=E) > 0).sum())
         batch = family == ops.FAMILY_BATCH
-        if kernel == "moe_gate_up":
+        if kernel == "moe":
+            sync = torch.zeros(G + 1, dtype=torch.int32, device=dev)
+            calls.append(lambda: ops.moe(gate_up=gate_up, down=down, x_sorted=xs, h=h, group_offsets=go,
+                                         max_routes_per_group=B, route_slot=rs, route_weight=rw,
+                                         y=part.view(-1, H), sync=sync, tile_tokens=tile_tokens))
+            nbytes = (distinct + 2) * 3 * I * H * 2
+        elif kernel == "moe_gate_up":
             calls.append(lambda: ops.linear(
                 w=gate_up, n_rows=I, k=H, up_offset=I * H, w_group_stride=2 * I * H, x=xs if batch else x,
                 y=h, epilogue=ops.EPI_SWIGLU, n_groups=G, group_offsets=go, max_routes_per_group=B,
@@ -148,12 +154,14 @@ def main():
     ap.add_argument("--ctx", type=int, default=576)
     ap.add_argument("--split-len", type=int, default=None)
     ap.add_argument("--k-splits", type=int, default=1)
+    ap.add_argument("--tile-tokens", type=int, default=0, help="moe: tokens per work item (0 = auto)")
     ap.add_argument("--no-graph", action="store_true", help="issue launches from Python (host-bound)")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args()
     fam = ops.FAMILY_BATCH if a.family == "batch" else ops.FAMILY_SMALL
-    calls, nbytes = build_case(a.kernel, a.batch, fam, a.ctx, a.split_len, k_splits=a.k_splits)
+    calls, nbytes = build_case(a.kernel, a.batch, fam, a.ctx, a.split_len, k_splits=a.k_splits,
+                               tile_tokens=a.tile_tokens)
     for _ in range(a.warmup):
         for c in calls:
             c()

@@ -14,13 +14,13 @@ import torch
 from . import _lib
 from ._lib import (
     DSV2_BF16, DSV2_F32, EPI_STORE_BF16, EPI_STORE_F32, EPI_SWIGLU, EPI_SCALE_F32,
-    FAMILY_SMALL, FAMILY_BATCH, LinearArgs, MlaDecodeArgs, MlaPrepArgs, RouterArgs,
+    FAMILY_SMALL, FAMILY_BATCH, LinearArgs, MlaDecodeArgs, MlaPrepArgs, MoeArgs, RouterArgs,
 )
 
 __all__ = [
     "stream", "rmsnorm", "add_rmsnorm", "embed_rmsnorm", "residual_add", "silu_mul", "sum_partials",
     "prepare_decode_inputs", "copy_token_to_cache", "advance_positions", "linear",
-    "router", "softmax_topk", "moe_bucket", "gather_rows", "mla_prep", "mla_decode",
+    "router", "softmax_topk", "moe_bucket", "gather_rows", "moe", "mla_prep", "mla_decode",
     "EPI_STORE_BF16", "EPI_STORE_F32", "EPI_SWIGLU", "EPI_SCALE_F32", "FAMILY_SMALL", "FAMILY_BATCH",
 ]
 
@@ -188,6 +188,39 @@ def linear(*, w: torch.Tensor, n_rows: int, k: int, x: torch.Tensor, y: torch.Te
     a.y_split_stride = y_split_stride
     a.offsets_prior = 1 if offsets_prior else 0
     _lib.call("dsv2_linear", ctypes.byref(a), family, stream())
+
+
+def moe(*, gate_up: torch.Tensor, down: torch.Tensor, x_sorted: torch.Tensor, h: torch.Tensor,
+        group_offsets: torch.Tensor, max_routes_per_group: int, route_slot: torch.Tensor,
+        route_weight: torch.Tensor, y: torch.Tensor, sync: torch.Tensor, tile_tokens: int = 0) -> None:
+    """Fused grouped MoE of one layer (batch family): gate_up + SwiGLU -> h, then down scaled
+    by the route weight into y[route_slot] (fp32 rows).  See dsv2_moe_args in include/dsv2.h.
+    gate_up [G, 2I, H], down [G, H, I] bf16; x_sorted [R, H], h [R, I] bf16; sync int32 [G + 1]
+    (zero-initialised once, left zero by every call)."""
+    for name, t in (("gate_up", gate_up), ("down", down), ("x_sorted", x_sorted), ("h", h), ("y", y)):
+        _cuda(t, name)
+        if not t.is_contiguous():
+            raise NotImplementedError(f"moe requires a contiguous {name}")
+    if gate_up.dtype != torch.bfloat16 or down.dtype != torch.bfloat16 or x_sorted.dtype != torch.bfloat16:
+        raise NotImplementedError("moe supports bf16 weights and activations")
+    if y.dtype != torch.float32 or sync.dtype != torch.int32 or group_offsets.dtype != torch.int32:
+        raise NotImplementedError("moe: y must be fp32, sync and group_offsets int32")
+    G, two_i, H = gate_up.shape
+    inter = two_i // 2
+    if tuple(down.shape) != (G, H, inter) or x_sorted.shape[1] != H or tuple(h.shape) != (x_sorted.shape[0], inter):
+        raise ValueError("moe: inconsistent shapes")
+    if sync.numel() < G + 1 or group_offsets.numel() < G + 1:
+        raise ValueError("moe: sync and group_offsets need n_groups + 1 entries")
+    a = MoeArgs()
+    a.gate_up, a.down = gate_up.data_ptr(), down.data_ptr()
+    a.n_groups, a.hidden, a.inter = G, H, inter
+    a.x_sorted, a.h, a.x_rows = x_sorted.data_ptr(), h.data_ptr(), x_sorted.shape[0]
+    a.group_offsets = group_offsets.data_ptr()
+    a.max_routes_per_group = max_routes_per_group
+    a.route_slot, a.route_weight = route_slot.data_ptr(), route_weight.data_ptr()
+    a.y, a.sync = y.data_ptr(), sync.data_ptr()
+    a.tile_tokens = tile_tokens
+    _lib.call("dsv2_moe", ctypes.byref(a), stream())
 
 
 def router(*, x: torch.Tensor, w: torch.Tensor, scaling: float, logits: torch.Tensor,

@@ -193,6 +193,42 @@ typedef struct dsv2_linear_args {
 
 DSV2_API int dsv2_linear(const dsv2_linear_args* args, int family, void* stream);
 
+/* ---- fused MoE (batch family) ------------------------------------------------ */
+/* One layer's routed + shared experts in one persistent tcgen05 launch:
+ *   h[r, :]            = bf16(silu(bf16(W_gate[g] x_sorted[r])) * bf16(W_up[g] x_sorted[r]))
+ *   y[route_slot[r], :] = bf16(W_down[g] h[r]) * route_weight[r]
+ * for every route r of group g (rows [group_offsets[g], group_offsets[g+1]) of x_sorted,
+ * as the router's bucketing lays them out).  gate_up: [n_groups, 2*inter, hidden] (gate
+ * rows then up rows), down: [n_groups, hidden, inter], bf16.  x_sorted / h: [x_rows,
+ * hidden] / [x_rows, inter] bf16; y rows are hidden wide, fp32 (the per-slot partials the
+ * next fused add+RMSNorm sums).  sync: int32[n_groups + 1], zero before the first call
+ * and left zero by every call (per-group progress counters between the two GEMMs).
+ * hidden % 64 == 0, inter % 64 == 0, n_groups <= 255.  Calls that share `sync` must not
+ * overlap on the GPU.
+ * Reference: the grouped gate/up + SwiGLU and down kernels of packed_routed_moe
+ * (moe_batch.py:151-307, launched at :425-557). */
+typedef struct dsv2_moe_args {
+  const void* gate_up;
+  const void* down;
+  int32_t n_groups;
+  int32_t hidden;
+  int32_t inter;
+  const void* x_sorted;
+  void* h;
+  int32_t x_rows;
+  const int32_t* group_offsets;
+  int32_t max_routes_per_group;
+  const int32_t* route_slot;
+  const float* route_weight;
+  float* y;
+  int32_t* sync;
+  /* tokens per work item (16..128, multiple of 16); 0 = the largest group's size capped
+   * at 128 */
+  int32_t tile_tokens;
+} dsv2_moe_args;
+
+DSV2_API int dsv2_moe(const dsv2_moe_args* args, void* stream);
+
 /* ---- MoE routing ------------------------------------------------------------ */
 /* Gate GEMV (fp32 over bf16 activations) + softmax + top-6, then bucketing (two launches).
  *   logits[r, e] = sum_k x[r, k] * w[e, k] (+ bias[e]);  p = softmax(logits[r]);

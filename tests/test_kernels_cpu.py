@@ -102,3 +102,19 @@ def test_run_cli_arguments():
     if not torch.cuda.is_available():
         with pytest.raises(RuntimeError):
             run.main(["--layers", "1"])
+
+
+def test_torch_custom_ops_registered():
+    import dsv2.torch_ops  # noqa: F401  (registers torch.ops.dsv2.*)
+    for name in ("rmsnorm", "silu_mul", "residual_add", "copy_single_token_to_cache", "prepare_decode_inputs",
+                 "router_softmax_topk6", "routed_moe", "attention_decode"):
+        assert hasattr(torch.ops.dsv2, name), name
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    with FakeTensorMode():
+        x = torch.empty(3, 1, 2048, dtype=torch.bfloat16)
+        y = torch.ops.dsv2.rmsnorm(x, torch.empty(2048, dtype=torch.bfloat16), 1e-6)
+        assert y.shape == x.shape and y.dtype == x.dtype
+        ids, w = torch.ops.dsv2.router_softmax_topk6(torch.empty(5, 64), 1.0)
+        assert ids.shape == (5, 6) and ids.dtype == torch.long and w.dtype == torch.float32
+    with pytest.raises(NotImplementedError):   # real implementation: CUDA only
+        torch.ops.dsv2.rmsnorm(torch.zeros(2, 2048, dtype=torch.bfloat16), torch.ones(2048), 1e-6)

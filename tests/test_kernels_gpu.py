@@ -244,3 +244,34 @@ def test_run_cli_json(capsys):
     assert [e["step"] for e in r1["step_trace"]] == list(range(5))
     assert r1["step_trace"][1]["cache_position"] == 17
     assert doc["hardware"]["gpu"]["capability"] == "sm100"
+
+
+def test_torch_ops_match_python_api(K, experts):
+    """torch.ops.dsv2.* (custom operators) return what the reference-named functions return."""
+    import dsv2.torch_ops  # noqa: F401
+    gate_up, down = experts
+    gud, dnd = gate_up.to(DEV), down.to(DEV)
+    x, ids, w = _moe_case(9, seed=9)
+    packed = K.moe_batch.PackedRoutedExperts(gate_up_weights=gud, down_weights=dnd, hidden_size=H,
+                                             intermediate_size=I, num_experts=E, topk=6)
+    for fam, fn in ((1, K.moe_batch.packed_routed_moe), (0, K.moe_small.batched_grouped_routed_moe_route_gemv)):
+        a = fn(x.to(DEV), ids.to(DEV), w.to(DEV), packed)
+        b = torch.ops.dsv2.routed_moe(x.to(DEV), ids.to(DEV), w.to(DEV), gud, dnd, fam)
+        assert torch.equal(a, b)
+    g = torch.Generator().manual_seed(3)
+    y = torch.randn(4, 1, 2048, generator=g).to(torch.bfloat16).to(DEV)
+    wt = torch.rand(2048, generator=g).to(torch.bfloat16).to(DEV)
+    assert torch.equal(torch.ops.dsv2.rmsnorm(y, wt, 1e-6), K.rmsnorm.rmsnorm_triton(y, wt, 1e-6))
+    attn = _to_dev(_attn_module(seed=21))
+    p = K.attn_batch.pack_attention_weights(attn)
+    B, S = 3, 64
+    xh = torch.randn(B, 1, 2048, generator=g).to(torch.bfloat16).to(DEV)
+    cache = torch.randn(B, S, 576, generator=g).to(torch.bfloat16).to(DEV)
+    pos = torch.tensor([5, 30, 63], device=DEV)
+    _, _, cos64, sin64 = _rope(S)
+    c1, c2 = cache.clone(), cache.clone()
+    a = K.attn_batch.attention_decode_triton(xh, cos64.to(DEV), sin64.to(DEV), pos.view(B, 1), pos, c1, None, p,
+                                             0.07).clone()
+    b = torch.ops.dsv2.attention_decode(xh, cos64.to(DEV), sin64.to(DEV), pos.view(B, 1), pos, c2, p.q_kv_a_weight,
+                                        p.kv_b_weight, p.o_weight, p.w_uk_t, p.kv_a_ln_weight, p.kv_a_ln_eps, 0.07, 1)
+    assert torch.equal(a, b) and torch.equal(c1, c2)

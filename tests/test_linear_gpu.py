@@ -146,6 +146,19 @@ def test_grouped_moe(D, family, B):
         p_ref[rs[a:b].long()] = O.linear(down[gi], h_ref[a:b], "scale", scale=rw[a:b])
     assert relerr(h, h_ref) < 1e-2
     assert relerr(partial.view(-1, H), p_ref) < 1e-2
+    if family == "batch":
+        # the fused single-launch MoE computes the same values bit for bit, and leaves its
+        # progress counters at zero (checked by running it twice)
+        sync = torch.zeros(G + 1, dtype=torch.int32, device=DEV)
+        for tt in (0, 0, 32):   # auto token tile (twice), and a fixed 32-token tile
+            h2 = torch.full((R, I), float("nan"), dtype=torch.bfloat16, device=DEV)
+            p2 = torch.zeros(B, 8, H, device=DEV)
+            D.moe(gate_up=gud, down=dnd, x_sorted=gx, h=h2, group_offsets=god, max_routes_per_group=B,
+                  route_slot=rsd, route_weight=rwd, y=p2.view(-1, H), sync=sync, tile_tokens=tt)
+            torch.cuda.synchronize()
+            assert torch.equal(h2, h)
+            assert torch.equal(p2, partial)
+            assert int(sync.abs().sum()) == 0
     # and the combined output equals the HF-semantics MoE
     moe_ref = O.moe(x, ids, wts, gate_up[:E], down[:E], torch.cat([gate_up[E, :I], gate_up[E + 1, :I]]),
                     torch.cat([gate_up[E, I:], gate_up[E + 1, I:]]), torch.cat([down[E], down[E + 1]], 1))
