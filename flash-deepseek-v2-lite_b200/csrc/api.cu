@@ -140,6 +140,12 @@ int tensor_map_3d(const void* base, uint64_t inner, uint64_t rows, uint64_t grou
   return DSV2_OK;
 }
 
+// Latent cache [batch][max_len][576] bf16 as a TMA map: boxes of 64 dims x 32 positions.
+int mla_cache_map(const void* cache, int64_t cache_b_stride, int max_len, int batch, CUtensorMap* out) {
+  return tensor_map_3d(cache, 576, static_cast<uint64_t>(max_len), static_cast<uint64_t>(batch), 576 * 2,
+                       static_cast<uint64_t>(cache_b_stride) * 2, 32, out);
+}
+
 }  // namespace
 
 extern "C" {
@@ -604,8 +610,11 @@ int dsv2_mla_decode(const dsv2_mla_decode_args* a, void* stream) {
   p.ml_part = a->ml_part;
   p.o_lat = reinterpret_cast<bf16*>(a->o_lat);
   p.inputs_prior = a->inputs_prior != 0;
+  p.row_sync = a->row_sync;
+  CUtensorMap tm_kv;
+  if ((rc = mla_cache_map(a->cache, a->cache_b_stride, a->max_len, a->batch, &tm_kv))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  rc = check_launch(launch_mla_decode(p, a->batch, st), "mla_decode");
+  rc = check_launch(launch_mla_decode(p, tm_kv, a->batch, st), "mla_decode");
   if (rc) return rc;
   return check_launch(launch_mla_combine(p, a->batch, st), "mla_combine");
 }
@@ -653,8 +662,10 @@ int dsv2_mla_decode_noalloc(const void* q_abs, const void* q_pe, const void* cac
   p.o_part = o_part;
   p.ml_part = ml_part;
   p.o_lat = reinterpret_cast<bf16*>(o_lat);
+  CUtensorMap tm_kv;
+  if ((rc = mla_cache_map(cache, cache_b_stride, max_len, batch, &tm_kv))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  rc = check_launch(launch_mla_decode(p, batch, st), "mla_decode_noalloc");
+  rc = check_launch(launch_mla_decode(p, tm_kv, batch, st), "mla_decode_noalloc");
   if (rc) return rc;
   return check_launch(launch_mla_combine(p, batch, st), "mla_decode_noalloc: combine");
 }

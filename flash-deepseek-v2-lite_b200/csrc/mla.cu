@@ -15,12 +15,14 @@
 // half-split layout.
 //
 // mla_decode_kernel: split-KV flash-decode.  One CTA = (split, sequence), 4 warps.
-// 64-position tiles of the latent cache are staged through a 2-deep cp.async ring in
+// 32-position tiles of the latent cache are staged through a 2-deep cp.async ring in
 // a 128-byte-swizzled layout (conflict-free ldmatrix).  Scores use mma.sync with
 // the 16 heads as M: each warp owns a 144-wide slice of the 576 dims and keeps its
 // query fragments in registers for the whole kernel; slices are summed through
 // shared memory.  P @ V (the latent part) uses mma.sync with each warp owning 128
-// latent dims.  Partial (o, m, l) per split are merged by mla_combine_kernel.
+// latent dims.  A row that fits one split writes o_lat directly; otherwise the split
+// partials (o, m, l) are merged by the last split of the row to finish (row_sync
+// counters) or, without counters, by mla_combine_kernel.
 #include "params.cuh"
 
 namespace dsv2 {
@@ -33,11 +35,12 @@ constexpr int kRowBytes = kRow * 2;             // 1152
 constexpr int kChunks = kRow / 64;              // 9 swizzle chunks of 64 dims
 constexpr int kTile = 32;                       // positions per tile (two CTAs per SM)
 constexpr int kStages = 2;
-constexpr int kTileBytes = kTile * kRowBytes;   // 73728
+constexpr int kTileBytes = kTile * kRowBytes;   // 36864
 constexpr int kQBytes = kHeads * kRowBytes;     // 18432
 constexpr int kSRedStride = kTile + 4;          // fp32 row stride of the score-reduction buffer
 constexpr int kPStride = kTile + 8;             // bf16 row stride of P
-constexpr int kMlaThreads = 128;
+constexpr int kMlaPvWarps = 8;                 // warps doing P @ V (64 latent dims each)
+constexpr int kMlaThreads = (kChunks) * 32;     // 9 warps: one 64-dim chunk of the scores each
 
 // ----------------------------------------------------------------------------
 // mla_prep: latent RMSNorm + RoPE + cache write for the new token, RoPE of q_pe
@@ -144,17 +147,51 @@ __device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, 
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n));
 }
 
-__global__ __launch_bounds__(kMlaThreads, 2) void mla_decode_kernel(const MlaDecodeParams p) {
+// o_lat[b] = merge of the first n_active split partials of row b (the splits of a row are
+// contiguous from 0): o = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s, per head.
+// Partials written by other CTAs are read with L1-bypassing loads.
+__device__ __forceinline__ void mla_merge_row(const float* o_part, const float* ml_part, int n_splits,
+                                              int n_active, bf16* o_lat, int b, int tid, int nthreads) {
+  const float* ml = ml_part + (static_cast<long long>(b) * n_splits) * kHeads * 2;
+  for (int i = tid; i < kHeads * kLatent / 4; i += nthreads) {
+    const int h = i / (kLatent / 4), d = (i % (kLatent / 4)) * 4;
+    float M = -INFINITY;
+    for (int s = 0; s < n_active; ++s) {
+      const float l = __ldcg(ml + (s * kHeads + h) * 2 + 1);
+      if (l > 0.f) M = fmaxf(M, __ldcg(ml + (s * kHeads + h) * 2));
+    }
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, den = 0.f;
+    for (int s = 0; s < n_active; ++s) {
+      const float l = __ldcg(ml + (s * kHeads + h) * 2 + 1);
+      if (!(l > 0.f)) continue;
+      const float w = exp2f(__ldcg(ml + (s * kHeads + h) * 2) - M);
+      den += w * l;
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(
+          o_part + ((static_cast<long long>(b) * n_splits + s) * kHeads + h) * kLatent + d));
+      a0 += w * v.x; a1 += w * v.y; a2 += w * v.z; a3 += w * v.w;
+    }
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+    uint2 o;
+    o.x = pack_bf16x2(a0 * inv, a1 * inv);
+    o.y = pack_bf16x2(a2 * inv, a3 * inv);
+    *reinterpret_cast<uint2*>(o_lat + (static_cast<long long>(b) * kHeads + h) * kLatent + d) = o;
+  }
+}
+
+__global__ __launch_bounds__(kMlaThreads, 2) void mla_decode_kernel(const MlaDecodeParams p,
+                                                                   const __grid_constant__ CUtensorMap tm_kv) {
   // inputs_prior: positions, q_pe and the cache are older than the previous launch, so
-  // the first cache tile is requested before waiting for it (it writes q_abs)
+  // the first cache tiles are requested before waiting for it (it writes q_abs)
   const bool early = p.inputs_prior != 0;
   if (!early) pdl_enter();
   extern __shared__ __align__(1024) unsigned char smem[];
-  unsigned char* s_q = smem;                                     // 9 chunks x 16 rows x 128 B
-  unsigned char* s_kv = smem + kQBytes;                          // stages x 9 chunks x 64 rows x 128 B
-  float* s_red = reinterpret_cast<float*>(s_kv + kStages * kTileBytes);  // [4][16][kSRedStride]
-  bf16* s_p = reinterpret_cast<bf16*>(s_red + 4 * kHeads * kSRedStride); // [16][kPStride]
-  float* s_alpha = reinterpret_cast<float*>(s_p + kHeads * kPStride);    // [16]
+  unsigned char* s_kv = smem;                                    // stages x 9 chunks x 32 rows x 128 B
+  unsigned char* s_q = smem + kStages * kTileBytes;              // 9 chunks x 16 rows x 128 B
+  float* s_red = reinterpret_cast<float*>(s_q + kQBytes);        // [9][16][kSRedStride]
+  bf16* s_p = reinterpret_cast<bf16*>(s_red + kChunks * kHeads * kSRedStride);  // [16][kPStride]
+  float* s_alpha = reinterpret_cast<float*>(s_p + kHeads * kPStride);           // [16]
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(s_alpha + kHeads);           // [kStages]
+  uint64_t* empty_bar = full_bar + kStages;                                      // [kStages]
 
   const int split = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -172,22 +209,27 @@ __global__ __launch_bounds__(kMlaThreads, 2) void mla_decode_kernel(const MlaDec
     }
     return;
   }
-  const bf16* cache_b = p.cache + b * p.cache_b_stride;
   const int n_tiles = (s_end - s_beg + kTile - 1) / kTile;
-  auto load_tile = [&](int ti, int stage) {
-    const int t0 = s_beg + ti * kTile;
-    const uint32_t base = smem_u32(s_kv + stage * kTileBytes);
-    for (int i = tid; i < kTile * kChunks * 8; i += kMlaThreads) {
-      const int r = i / (kChunks * 8), rem = i % (kChunks * 8);
-      const int ch = rem / 8, c16 = rem % 8;
-      const int sp = t0 + r;
-      const bool valid = sp < s_end;
-      const bf16* src = cache_b + static_cast<long long>(valid ? sp : s_beg) * kRow + ch * 64 + c16 * 8;
-      cp_async16_zfill(base + ch * (kTile * 128) + swz(r, c16), src, valid);
-    }
+  const bool producer = (warp == kMlaPvWarps && lane == 0);
+  // tile ti -> stage ti % 2: 9 TMA boxes of 64 dims x 32 positions (128-byte swizzle);
+  // positions past the split are masked below, past the cache they read as zeros
+  auto load_tile = [&](int ti) {
+    const int st = ti % kStages;
+    mbar_arrive_expect_tx(&full_bar[st], kTileBytes);
+    for (int c = 0; c < kChunks; ++c)
+      tma_load_3d(smem_u32(s_kv + st * kTileBytes + c * (kTile * 128)), &tm_kv, &full_bar[st], c * 64,
+                  s_beg + ti * kTile, b);
   };
-  load_tile(0, 0);
-  cp_async_commit();
+  if (producer) {
+    for (int st = 0; st < kStages; ++st) {
+      mbar_init(&full_bar[st], 1);
+      mbar_init(&empty_bar[st], kMlaPvWarps);
+    }
+    fence_mbar_init();
+    prefetch_tmap(&tm_kv);
+    load_tile(0);
+    if (n_tiles > 1) load_tile(1);
+  }
   if (early) pdl_enter();
 
   // --- stage Q = [q_abs | q_pe] (16 x 576) into swizzled smem
@@ -200,113 +242,101 @@ __global__ __launch_bounds__(kMlaThreads, 2) void mla_decode_kernel(const MlaDec
                           : p.q_pe + (static_cast<long long>(b) * kHeads + h) * kRope + (d - kLatent);
     *reinterpret_cast<uint4*>(s_q + ch * (kHeads * 128) + swz(h, c16)) = *reinterpret_cast<const uint4*>(src);
   }
+  __syncthreads();  // Q and the barriers visible
 
-  __syncthreads();  // Q visible
-
-  // --- query fragments for this warp's 9 k-steps (dims [144*warp, 144*warp + 144))
-  uint32_t qa[9][4];
+  // --- query fragments of this warp's 64-dim chunk (warp w scores dims [64w, 64w + 64))
+  uint32_t qa[4][4];
 #pragma unroll
-  for (int ks = 0; ks < 9; ++ks) {
-    const int d0 = warp * 144 + ks * 16;
+  for (int ks = 0; ks < 4; ++ks) {
     const int mi = lane >> 3, ri = lane & 7;
     const int row = (mi & 1) * 8 + ri;
-    const int d = d0 + (mi >> 1) * 8;
-    const uint32_t addr = smem_u32(s_q + (d / 64) * (kHeads * 128) + swz(row, (d % 64) / 8));
-    ldmatrix_x4(addr, qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+    const int c16 = ks * 2 + (mi >> 1);
+    ldmatrix_x4(smem_u32(s_q + warp * (kHeads * 128) + swz(row, c16)), qa[ks][0], qa[ks][1], qa[ks][2],
+                qa[ks][3]);
   }
 
-  // softmax state: thread tid owns head hs = tid / 8 and positions [8*(tid%8), +8) of a tile
-  const int hs = tid >> 3, js = tid & 7;
+  // softmax state: threads 0..255, head hs = tid / 16, positions 2*js, 2*js + 1 of a tile
+  const int hs = (tid >> 4) & 15, js = tid & 15;
   float m_run = -INFINITY, l_run = 0.f;
-  float o_acc[16][4];
+  // P @ V accumulators: warps 0..7 own latent dims [64w, 64w + 64)
+  float o_acc[8][4];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) o_acc[j][0] = o_acc[j][1] = o_acc[j][2] = o_acc[j][3] = 0.f;
+  for (int j = 0; j < 8; ++j) o_acc[j][0] = o_acc[j][1] = o_acc[j][2] = o_acc[j][3] = 0.f;
+  bool ok = true;
 
   for (int ti = 0; ti < n_tiles; ++ti) {
     const int stage = ti % kStages;
-    // tile ti has landed and every warp has finished with the buffer refilled below
-    cp_async_wait<0>();
-    __syncthreads();
-    if (ti + 1 < n_tiles) load_tile(ti + 1, (ti + 1) % kStages);
-    cp_async_commit();
+    const uint32_t par = static_cast<uint32_t>((ti / kStages) & 1);
+    if (!mbar_wait(&full_bar[stage], par)) ok = false;
     const unsigned char* kv = s_kv + stage * kTileBytes;
 
-    // --- partial scores over this warp's 144 dims for all positions of the tile
-    float sc[kTile / 8][4];
+    // --- partial scores over this warp's 64 dims for the 32 positions of the tile
+    {
+      float sc[kTile / 8][4];
 #pragma unroll
-    for (int j = 0; j < kTile / 8; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+      for (int j = 0; j < kTile / 8; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+      const unsigned char* kc = kv + warp * (kTile * 128);
 #pragma unroll
-    for (int ks = 0; ks < 9; ++ks) {
-      const int d0 = warp * 144 + ks * 16;
+      for (int ks = 0; ks < 4; ++ks) {
 #pragma unroll
-      for (int np = 0; np < kTile / 16; ++np) {  // pairs of n8 tiles (16 positions)
-        const int mi = lane >> 3, ri = lane & 7;
-        const int r = np * 16 + (mi >> 1) * 8 + ri;
-        const int d = d0 + (mi & 1) * 8;
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4(smem_u32(kv + (d / 64) * (kTile * 128) + swz(r, (d % 64) / 8)), b0, b1, b2, b3);
-        mma_bf16_16816(sc[2 * np], qa[ks], b0, b1);
-        mma_bf16_16816(sc[2 * np + 1], qa[ks], b2, b3);
+        for (int np = 0; np < kTile / 16; ++np) {  // pairs of n8 tiles (16 positions)
+          const int mi = lane >> 3, ri = lane & 7;
+          const int r = np * 16 + (mi >> 1) * 8 + ri;
+          const int c16 = ks * 2 + (mi & 1);
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(smem_u32(kc + swz(r, c16)), b0, b1, b2, b3);
+          mma_bf16_16816(sc[2 * np], qa[ks], b0, b1);
+          mma_bf16_16816(sc[2 * np + 1], qa[ks], b2, b3);
+        }
       }
-    }
-    float* red_w = s_red + warp * kHeads * kSRedStride;
+      float* red_w = s_red + warp * kHeads * kSRedStride;
 #pragma unroll
-    for (int j = 0; j < kTile / 8; ++j) {
-      const int c = j * 8 + 2 * tq;
-      red_w[gq * kSRedStride + c] = sc[j][0];
-      red_w[gq * kSRedStride + c + 1] = sc[j][1];
-      red_w[(gq + 8) * kSRedStride + c] = sc[j][2];
-      red_w[(gq + 8) * kSRedStride + c + 1] = sc[j][3];
+      for (int j = 0; j < kTile / 8; ++j) {
+        const int c = j * 8 + 2 * tq;
+        *reinterpret_cast<float2*>(red_w + gq * kSRedStride + c) = make_float2(sc[j][0], sc[j][1]);
+        *reinterpret_cast<float2*>(red_w + (gq + 8) * kSRedStride + c) = make_float2(sc[j][2], sc[j][3]);
+      }
     }
     __syncthreads();
 
-    // --- online softmax (log2 domain) for head hs, positions [kPT*js, kPT*js + kPT)
-    {
-      constexpr int kPT = kTile / 8;
+    // --- online softmax (log2 domain) for head hs, positions 2*js, 2*js + 1
+    if (tid < 256) {
       const int t0 = s_beg + ti * kTile;
-      float s[kPT];
-      float mx = -INFINITY;
+      const int c = 2 * js;
+      float v0 = 0.f, v1 = 0.f;
 #pragma unroll
-      for (int i = 0; i < kPT; ++i) {
-        const int c = js * kPT + i;
-        float v = 0.f;
-#pragma unroll
-        for (int w = 0; w < 4; ++w) v += s_red[(w * kHeads + hs) * kSRedStride + c];
-        v = (t0 + c < s_end) ? v * p.scale_log2 : -INFINITY;
-        s[i] = v;
-        mx = fmaxf(mx, v);
+      for (int w = 0; w < kChunks; ++w) {
+        const float2 r2 = *reinterpret_cast<const float2*>(s_red + (w * kHeads + hs) * kSRedStride + c);
+        v0 += r2.x;
+        v1 += r2.y;
       }
+      v0 = (t0 + c < s_end) ? v0 * p.scale_log2 : -INFINITY;
+      v1 = (t0 + c + 1 < s_end) ? v1 * p.scale_log2 : -INFINITY;
+      float mx = fmaxf(v0, v1);
 #pragma unroll
-      for (int o = 1; o < 8; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      for (int o = 1; o < 16; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       const float m_new = fmaxf(m_run, mx);
       const float alpha = exp2f(m_run - m_new);
-      float sum = 0.f;
-      uint32_t pk[kPT / 2];
+      const float p0 = exp2f(v0 - m_new), p1 = exp2f(v1 - m_new);
+      float sum = p0 + p1;
 #pragma unroll
-      for (int i = 0; i < kPT / 2; ++i) {
-        const float p0 = exp2f(s[2 * i] - m_new), p1 = exp2f(s[2 * i + 1] - m_new);
-        pk[i] = pack_bf16x2(p0, p1);
-        sum += p0 + p1;
-      }
-#pragma unroll
-      for (int o = 1; o < 8; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      for (int o = 1; o < 16; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
       l_run = l_run * alpha + sum;
       m_run = m_new;
-      uint32_t* prow = reinterpret_cast<uint32_t*>(s_p + hs * kPStride + js * kPT);
-#pragma unroll
-      for (int i = 0; i < kPT / 2; ++i) prow[i] = pk[i];
+      *reinterpret_cast<uint32_t*>(s_p + hs * kPStride + c) = pack_bf16x2(p0, p1);
       if (js == 0) s_alpha[hs] = alpha;
     }
     __syncthreads();
 
-    // --- O[:, 128*warp .. +128] = alpha * O + P @ V
-    {
+    if (warp < kMlaPvWarps) {
+      // --- O[:, 64*warp .. +64] = alpha * O + P @ V
       const float a0 = s_alpha[gq], a1 = s_alpha[gq + 8];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
+      for (int j = 0; j < 8; ++j) {
         o_acc[j][0] *= a0; o_acc[j][1] *= a0;
         o_acc[j][2] *= a1; o_acc[j][3] *= a1;
       }
+      const unsigned char* vc = kv + warp * (kTile * 128);
 #pragma unroll
       for (int kk = 0; kk < kTile / 16; ++kk) {
         uint32_t pa[4];
@@ -317,48 +347,79 @@ __global__ __launch_bounds__(kMlaThreads, 2) void mla_decode_kernel(const MlaDec
           ldmatrix_x4(smem_u32(s_p + row * kPStride + col), pa[0], pa[1], pa[2], pa[3]);
         }
 #pragma unroll
-        for (int np = 0; np < 8; ++np) {
+        for (int np = 0; np < 4; ++np) {
           const int mi = lane >> 3, ri = lane & 7;
           const int r = kk * 16 + (mi & 1) * 8 + ri;
-          const int d = warp * 128 + np * 16 + (mi >> 1) * 8;
+          const int c16 = np * 2 + (mi >> 1);
           uint32_t b0, b1, b2, b3;
-          ldmatrix_x4_trans(smem_u32(kv + (d / 64) * (kTile * 128) + swz(r, (d % 64) / 8)), b0, b1, b2, b3);
+          ldmatrix_x4_trans(smem_u32(vc + swz(r, c16)), b0, b1, b2, b3);
           mma_bf16_16816(o_acc[2 * np], pa, b0, b1);
           mma_bf16_16816(o_acc[2 * np + 1], pa, b2, b3);
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[stage]);  // this warp is done with the tile
+    } else if (producer && ti + kStages < n_tiles) {
+      // refill this stage once the P @ V warps have released it
+      if (!mbar_wait(&empty_bar[stage], par)) ok = false;
+      else load_tile(ti + kStages);
     }
   }
-  cp_async_wait<0>();
+  if (!ok) set_device_error(kErrMbarTimeout);
 
   if (len <= p.split_len) {
     // the whole row fitted in this one split: normalise and write o_lat directly
-    // (no partials, and the merge kernel skips the row)
-    if (js == 0) s_alpha[hs] = 1.f / l_run;
+    // (no partials, and the merge skips the row)
+    if (tid < 256 && js == 0) s_alpha[hs] = 1.f / l_run;
     __syncthreads();
-    const float i0 = s_alpha[gq], i1 = s_alpha[gq + 8];
-    bf16* ob = p.o_lat + static_cast<long long>(b) * kHeads * kLatent;
+    if (warp < kMlaPvWarps) {
+      const float i0 = s_alpha[gq], i1 = s_alpha[gq + 8];
+      bf16* ob = p.o_lat + static_cast<long long>(b) * kHeads * kLatent;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int d = warp * 128 + j * 8 + 2 * tq;
-      *reinterpret_cast<uint32_t*>(ob + gq * kLatent + d) = pack_bf16x2(o_acc[j][0] * i0, o_acc[j][1] * i0);
-      *reinterpret_cast<uint32_t*>(ob + (gq + 8) * kLatent + d) =
-          pack_bf16x2(o_acc[j][2] * i1, o_acc[j][3] * i1);
+      for (int j = 0; j < 8; ++j) {
+        const int d = warp * 64 + j * 8 + 2 * tq;
+        *reinterpret_cast<uint32_t*>(ob + gq * kLatent + d) = pack_bf16x2(o_acc[j][0] * i0, o_acc[j][1] * i0);
+        *reinterpret_cast<uint32_t*>(ob + (gq + 8) * kLatent + d) =
+            pack_bf16x2(o_acc[j][2] * i1, o_acc[j][3] * i1);
+      }
     }
     return;
   }
   // --- write partial results
-  float* op = p.o_part + ((static_cast<long long>(b) * p.n_splits + split) * kHeads) * kLatent;
+  if (warp < kMlaPvWarps) {
+    float* op = p.o_part + ((static_cast<long long>(b) * p.n_splits + split) * kHeads) * kLatent;
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const int d = warp * 128 + j * 8 + 2 * tq;
-    *reinterpret_cast<float2*>(op + gq * kLatent + d) = make_float2(o_acc[j][0], o_acc[j][1]);
-    *reinterpret_cast<float2*>(op + (gq + 8) * kLatent + d) = make_float2(o_acc[j][2], o_acc[j][3]);
+    for (int j = 0; j < 8; ++j) {
+      const int d = warp * 64 + j * 8 + 2 * tq;
+      *reinterpret_cast<float2*>(op + gq * kLatent + d) = make_float2(o_acc[j][0], o_acc[j][1]);
+      *reinterpret_cast<float2*>(op + (gq + 8) * kLatent + d) = make_float2(o_acc[j][2], o_acc[j][3]);
+    }
   }
-  if (js == 0) {
+  if (tid < 256 && js == 0) {
     mlp[hs * 2] = m_run;
     mlp[hs * 2 + 1] = l_run;
   }
+  if (!p.row_sync) return;  // mla_combine_kernel merges the splits
+  // The last split of the row to finish merges all of them (no separate launch): the
+  // partial stores above are published by a fence + counter increment, the last
+  // arriver reads the others' partials through L2 and returns the counter to zero.
+  __syncthreads();
+  int* s_flag = reinterpret_cast<int*>(s_alpha);
+  if (tid == 0) {
+    const int n_active = (len + p.split_len - 1) / p.split_len;
+    __threadfence();
+    const int t = atomicAdd(&p.row_sync[b], 1);
+    const bool last = (t == n_active - 1);
+    if (last) {
+      p.row_sync[b] = 0;
+      __threadfence();
+    }
+    *s_flag = last ? n_active : 0;
+  }
+  __syncthreads();
+  const int n_active = *s_flag;
+  if (n_active == 0) return;
+  mla_merge_row(p.o_part, p.ml_part, p.n_splits, n_active, p.o_lat, b, tid, kMlaThreads);
 }
 
 // o_lat[b, h, :] = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s   (bf16 out)
@@ -428,8 +489,8 @@ cudaError_t mla_noalloc_scratch(float** out) {
 }
 
 constexpr size_t mla_decode_smem_bytes() {
-  return kQBytes + kStages * kTileBytes + 4 * kHeads * kSRedStride * sizeof(float) +
-         kHeads * kPStride * sizeof(bf16) + kHeads * sizeof(float);
+  return kStages * kTileBytes + kQBytes + kChunks * kHeads * kSRedStride * sizeof(float) +
+         kHeads * kPStride * sizeof(bf16) + kHeads * sizeof(float) + 2 * kStages * sizeof(uint64_t);
 }
 
 cudaError_t launch_mla_prep(const MlaPrepParams& p, int batch, cudaStream_t st) {
@@ -442,14 +503,17 @@ cudaError_t mla_decode_init() {
                               static_cast<int>(mla_decode_smem_bytes()));
 }
 
-cudaError_t launch_mla_decode(const MlaDecodeParams& p, int batch, cudaStream_t st) {
-  launch_kernel(mla_decode_kernel, dim3(p.n_splits, batch), kMlaThreads, mla_decode_smem_bytes(), st, p);
+cudaError_t launch_mla_decode(const MlaDecodeParams& p, const CUtensorMap& tm_kv, int batch,
+                              cudaStream_t st) {
+  launch_kernel(mla_decode_kernel, dim3(p.n_splits, batch), kMlaThreads, mla_decode_smem_bytes(), st, p,
+                tm_kv);
   return cudaGetLastError();
 }
 
 cudaError_t launch_mla_combine(const MlaDecodeParams& p, int batch, cudaStream_t st) {
-  // one split covers the whole cache: every row wrote its output directly
-  if (static_cast<long long>(p.split_len) >= p.max_len) return cudaSuccess;
+  // one split covers the whole cache: every row wrote its output directly; with
+  // row_sync the decode kernel merged the splits itself
+  if (static_cast<long long>(p.split_len) >= p.max_len || p.row_sync) return cudaSuccess;
   launch_kernel(mla_combine_kernel, dim3(batch, kHeads), 128, 0, st, p.o_part, p.ml_part, p.n_splits, p.o_lat, p.positions, p.pos_numel, p.max_len, p.split_len);
   return cudaGetLastError();
 }

@@ -69,6 +69,7 @@ struct MlaDecodeParams {
   float* ml_part;              // [B, n_splits, 16, 2]  (m in log2 domain, l)
   bf16* o_lat;                 // [B, 16, 512] output
   int inputs_prior;            // q_pe / positions / cache written >= 2 launches earlier
+  int* row_sync;               // [B] split counters (merge in the decode kernel), or nullptr
 };
 
 // norm.cu
@@ -99,7 +100,7 @@ cudaError_t launch_gather_rows(const void*, long long, const int*, const int*, i
 // mla.cu
 cudaError_t launch_mla_prep(const MlaPrepParams&, int, cudaStream_t);
 cudaError_t mla_decode_init();
-cudaError_t launch_mla_decode(const MlaDecodeParams&, int, cudaStream_t);
+cudaError_t launch_mla_decode(const MlaDecodeParams&, const CUtensorMap&, int, cudaStream_t);
 cudaError_t launch_mla_combine(const MlaDecodeParams&, int, cudaStream_t);
 // linear_tc.cu (TcShape, tc_launch_shape and launch_linear_tc_impl are defined there; the
 // unity build includes it before api.cu)

@@ -31,11 +31,12 @@ FAMILIES = {"small": ops.FAMILY_SMALL, "batch": ops.FAMILY_BATCH}
 
 
 def choose_split_len(batch: int, max_len: int, num_sms: int) -> int:
-    """Positions per split-KV CTA.  With at least ~1.5 rows per SM every row is one CTA
-    (a single-split row writes its output directly, no partials); otherwise rows are
-    split so the batch yields about four CTAs per SM (two resident per SM)."""
+    """Positions per split-KV CTA.  Large batches use 256-position splits, so that rows of
+    very different lengths (ragged batches) spread over the SMs and a row of up to 256
+    positions writes its output directly; smaller batches are split so that they yield
+    about four CTAs per SM (two resident per SM)."""
     if batch * 2 >= 3 * num_sms:
-        return int((max_len + 63) // 64 * 64)
+        return int(min(256, (max_len + 63) // 64 * 64))
     s = math.ceil(batch * max_len / (4 * num_sms))
     s = (s + 63) // 64 * 64
     return int(min(max(s, 64), 4096))

@@ -32,7 +32,8 @@ def _routing(B, n_exp, g, dev):
 
 
 def build_case(kernel: str, B: int, family: int, ctx: int, split_len: int | None, dev="cuda",
-               k_splits: int = 1, tile_tokens: int = 0):
+               k_splits: int = 1, tile_tokens: int = 0, ragged: tuple[int, int] | None = None,
+               merge_in_kernel: bool = True):
     g = torch.Generator(device=dev).manual_seed(0)
     H, I, E = 2048, 1408, 64
     calls = []
@@ -127,20 +128,27 @@ def build_case(kernel: str, B: int, family: int, ctx: int, split_len: int | None
                                             x_group_rows=B))
         nbytes = 16 * 128 * 512 * 2
     elif kernel == "mla_decode":
-        S = ctx + 64
+        # ctx: fixed length per row; ragged=(lo, hi): lengths uniform in [lo, hi) per row
+        hi = ragged[1] if ragged else ctx
+        S = hi + 64
         cache = _rnd((B, S, 576), g)
         q_abs = _rnd((B, 16, 512), g, 0.1)
         q_pe = _rnd((B, 16, 64), g, 0.1)
-        pos = torch.full((B,), ctx - 1, dtype=torch.int64, device=dev)
+        if ragged:
+            gg = torch.Generator().manual_seed(3)
+            pos = torch.randint(ragged[0], ragged[1], (B,), generator=gg).to(dev) - 1
+        else:
+            pos = torch.full((B,), ctx - 1, dtype=torch.int64, device=dev)
         from .engine import choose_split_len
         sl = split_len or choose_split_len(B, S, torch.cuda.get_device_properties(dev).multi_processor_count)
         ns = math.ceil(S / sl)
         o_part = torch.zeros(B, ns, 16, 512, device=dev)
         ml = torch.zeros(B, ns, 16, 2, device=dev)
         o_lat = torch.zeros(B, 16, 512, dtype=torch.bfloat16, device=dev)
+        sync = torch.zeros(B, dtype=torch.int32, device=dev) if merge_in_kernel else None
         calls.append(lambda: ops.mla_decode(q_abs=q_abs, q_pe=q_pe, cache=cache, positions=pos, softmax_scale=0.07,
-                                            split_len=sl, o_part=o_part, ml_part=ml, o_lat=o_lat))
-        nbytes = B * ctx * 576 * 2
+                                            split_len=sl, o_part=o_part, ml_part=ml, o_lat=o_lat, row_sync=sync))
+        nbytes = int((pos + 1).sum()) * 576 * 2
     else:
         raise ValueError(kernel)
     return calls, nbytes
@@ -155,13 +163,16 @@ def main():
     ap.add_argument("--split-len", type=int, default=None)
     ap.add_argument("--k-splits", type=int, default=1)
     ap.add_argument("--tile-tokens", type=int, default=0, help="moe: tokens per work item (0 = auto)")
+    ap.add_argument("--ragged", default=None, help="mla_decode: lo,hi row lengths uniform in [lo, hi)")
+    ap.add_argument("--merge-launch", action="store_true", help="mla_decode: merge splits in a second launch")
     ap.add_argument("--no-graph", action="store_true", help="issue launches from Python (host-bound)")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     a = ap.parse_args()
     fam = ops.FAMILY_BATCH if a.family == "batch" else ops.FAMILY_SMALL
+    ragged = tuple(int(v) for v in a.ragged.split(",")) if a.ragged else None
     calls, nbytes = build_case(a.kernel, a.batch, fam, a.ctx, a.split_len, k_splits=a.k_splits,
-                               tile_tokens=a.tile_tokens)
+                               tile_tokens=a.tile_tokens, ragged=ragged, merge_in_kernel=not a.merge_launch)
     for _ in range(a.warmup):
         for c in calls:
             c()
@@ -188,7 +199,8 @@ def main():
         e.record()
     torch.cuda.synchronize()
     us = s.elapsed_time(e) * 1000 / a.iters
-    print(json.dumps({"kernel": a.kernel, "batch": a.batch, "family": a.family, "ctx": a.ctx, "us": round(us, 2),
+    print(json.dumps({"kernel": a.kernel, "batch": a.batch, "family": a.family, "ctx": a.ragged or a.ctx,
+                      "split_len": a.split_len, "us": round(us, 2),
                       "bytes": nbytes, "GBps": round(nbytes / us / 1e3, 1)}))
 
 

@@ -357,6 +357,10 @@ typedef struct dsv2_mla_decode_args {
    * decode): the kernel then starts loading cache tiles while the previous kernel is still
    * running.  0 = no such guarantee. */
   int32_t inputs_prior;
+  /* optional int32[batch], zero before the first call and left zero by every call: the
+   * last split of each row to finish merges the row's partials, so no merge launch
+   * follows.  NULL = merge in a second launch. */
+  int32_t* row_sync;
 } dsv2_mla_decode_args;
 
 DSV2_API int dsv2_mla_decode(const dsv2_mla_decode_args* args, void* stream);

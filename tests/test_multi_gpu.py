@@ -1,0 +1,87 @@
+"""Expert-parallel decode on 2 GPUs (NCCL) against the single-GPU engine.
+
+Runs only where at least two GPUs are visible (skipped otherwise).  Each rank owns half
+of the routed experts and half of the rows; the MoE activations are all-gathered and
+the expert outputs reduce-scattered inside the captured decode graph.  The logits of
+every row must match the single-GPU engine's (cosine >= 0.999; the fp32 sums over
+experts are associated differently across ranks) and the greedy tokens of the first
+step must be identical.
+"""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+B_ALL, LAYERS, STEPS = 8, 3, 3
+
+
+def _prompts():
+    g = torch.Generator().manual_seed(5)
+    lens = torch.randint(5, 70, (B_ALL,), generator=g)
+    return [torch.randint(0, 102400, (int(n),), generator=g) for n in lens]
+
+
+def _run_engine(model, prompts, family, rank=0, world=1, group=None):
+    from dsv2.engine import DecodeEngine
+    B = len(prompts) // world
+    eng = DecodeEngine(model, B, 96, family, rank=rank, world=world, group=group, alias_hf=(world == 1))
+    eng.prefill(prompts[rank * B:(rank + 1) * B])
+    eng.capture()
+    logits, toks = [], []
+    for _ in range(STEPS):
+        eng.replay()
+        logits.append(eng.logits.float().cpu())
+        toks.append(eng.next_ids.cpu())
+    torch.cuda.synchronize()
+    eng.release()
+    return torch.stack(logits), torch.stack(toks)
+
+
+def _rank_main(rank, world, port, family, ref_path, out_path):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from dsv2.synthetic import build_model, dsv2_lite_config
+        model = build_model(dsv2_lite_config(num_layers=LAYERS), seed=1, device=f"cuda:{rank}",
+                            dtype=torch.bfloat16)
+        logits, toks = _run_engine(model, _prompts(), family, rank, world, dist.group.WORLD)
+        torch.save({"logits": logits, "toks": toks}, f"{out_path}.{rank}")
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("family", ["batch", "small"])
+def test_expert_parallel_matches_single_gpu(family, tmp_path):
+    import torch.multiprocessing as mp
+    from dsv2.synthetic import build_model, dsv2_lite_config
+    model = build_model(dsv2_lite_config(num_layers=LAYERS), seed=1, device="cuda:0", dtype=torch.bfloat16)
+    ref_logits, ref_toks = _run_engine(model, _prompts(), family)
+    del model
+    torch.cuda.empty_cache()
+    out = str(tmp_path / "ep")
+    mp.start_processes(_rank_main, args=(2, _free_port(), family, None, out), nprocs=2, start_method="spawn")
+    half = B_ALL // 2
+    for r in range(2):
+        got = torch.load(f"{out}.{r}")
+        rows = slice(r * half, (r + 1) * half)
+        assert torch.equal(got["toks"][0], ref_toks[0, rows])
+        for s in range(STEPS):
+            a, b = got["logits"][s].double(), ref_logits[s, rows].double()
+            cos = (a * b).sum(-1) / (a.norm(dim=-1) * b.norm(dim=-1))
+            assert float(cos.min()) >= 0.999, (r, s, cos)

@@ -205,6 +205,16 @@ def test_mla_decode_vs_oracle(D, B, S, lengths, split):
     ref = O.mla_decode(q_abs, q_pe, cache, pos + 1, scale)
     # bf16 P (as the reference's P.V) and bf16 output: 1e-2 relative bound
     assert relerr(o_lat.cpu(), ref) < 1e-2
+    # merging the splits inside the decode launch (row counters) gives the same bits as
+    # the separate merge launch, and leaves the counters at zero (run twice)
+    sync = torch.zeros(B, dtype=torch.int32, device=DEV)
+    for _ in range(2):
+        o2 = torch.zeros_like(o_lat)
+        D.mla_decode(q_abs=q_abs.to(DEV), q_pe=q_pe.to(DEV), cache=cache.to(DEV), positions=pos.to(DEV),
+                     softmax_scale=scale, split_len=split, o_part=o_part, ml_part=ml, o_lat=o2, row_sync=sync)
+        torch.cuda.synchronize()
+        assert torch.equal(o2, o_lat)
+        assert int(sync.abs().sum()) == 0
 
 
 def test_mla_decode_matches_reference_expanded_attention(D, golden_ref):
