@@ -71,6 +71,8 @@ int ensure_init(int* sms_out) {
       return fail(DSV2_ERR_LAUNCH, "linear_tc_init: %s", cudaGetErrorString(e));
     if ((e = moe_tc_init()) != cudaSuccess)
       return fail(DSV2_ERR_LAUNCH, "moe_tc_init: %s", cudaGetErrorString(e));
+    if ((e = mla_tc_init()) != cudaSuccess)
+      return fail(DSV2_ERR_LAUNCH, "mla_tc_init: %s", cudaGetErrorString(e));
     g_dev_sms[dev] = sms;
     g_dev_init[dev] = true;
   }
@@ -140,10 +142,11 @@ int tensor_map_3d(const void* base, uint64_t inner, uint64_t rows, uint64_t grou
   return DSV2_OK;
 }
 
-// Latent cache [batch][max_len][576] bf16 as a TMA map: boxes of 64 dims x 32 positions.
-int mla_cache_map(const void* cache, int64_t cache_b_stride, int max_len, int batch, CUtensorMap* out) {
+// Latent cache [batch][max_len][576] bf16 as a TMA map: boxes of 64 dims x box_rows positions.
+int mla_cache_map(const void* cache, int64_t cache_b_stride, int max_len, int batch, uint32_t box_rows,
+                  CUtensorMap* out) {
   return tensor_map_3d(cache, 576, static_cast<uint64_t>(max_len), static_cast<uint64_t>(batch), 576 * 2,
-                       static_cast<uint64_t>(cache_b_stride) * 2, 32, out);
+                       static_cast<uint64_t>(cache_b_stride) * 2, box_rows, out);
 }
 
 }  // namespace
@@ -611,10 +614,17 @@ int dsv2_mla_decode(const dsv2_mla_decode_args* a, void* stream) {
   p.o_lat = reinterpret_cast<bf16*>(a->o_lat);
   p.inputs_prior = a->inputs_prior != 0;
   p.row_sync = a->row_sync;
-  CUtensorMap tm_kv;
-  if ((rc = mla_cache_map(a->cache, a->cache_b_stride, a->max_len, a->batch, &tm_kv))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  rc = check_launch(launch_mla_decode(p, tm_kv, a->batch, st), "mla_decode");
+  CUtensorMap tm_kv;
+  if (a->family == DSV2_FAMILY_BATCH) {
+    if (a->row_sync) return fail(DSV2_ERR_UNSUPPORTED, "mla_decode(batch): row_sync is not supported");
+    if ((rc = mla_cache_map(a->cache, a->cache_b_stride, a->max_len, a->batch, 64, &tm_kv))) return rc;
+    rc = check_launch(launch_mla_tc(p, tm_kv, a->batch, st), "mla_decode(batch)");
+  } else {
+    if (a->family != DSV2_FAMILY_SMALL) return fail(DSV2_ERR_INVALID, "mla_decode: family %d", a->family);
+    if ((rc = mla_cache_map(a->cache, a->cache_b_stride, a->max_len, a->batch, 32, &tm_kv))) return rc;
+    rc = check_launch(launch_mla_decode(p, tm_kv, a->batch, st), "mla_decode");
+  }
   if (rc) return rc;
   return check_launch(launch_mla_combine(p, a->batch, st), "mla_combine");
 }
@@ -663,7 +673,7 @@ int dsv2_mla_decode_noalloc(const void* q_abs, const void* q_pe, const void* cac
   p.ml_part = ml_part;
   p.o_lat = reinterpret_cast<bf16*>(o_lat);
   CUtensorMap tm_kv;
-  if ((rc = mla_cache_map(cache, cache_b_stride, max_len, batch, &tm_kv))) return rc;
+  if ((rc = mla_cache_map(cache, cache_b_stride, max_len, batch, 32, &tm_kv))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   rc = check_launch(launch_mla_decode(p, tm_kv, batch, st), "mla_decode_noalloc");
   if (rc) return rc;

@@ -268,6 +268,40 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// 32 lanes x 16 columns of 32-bit from registers (the inverse of tmem_ld16)
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%"
+      "16};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+// make this thread's generic-proxy shared-memory writes visible to the async proxy
+// (tensor-core operand reads)
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor for an MN-major operand stored with the 128-byte
+// swizzle: rows of 64 MN-contiguous bf16 (one K index each), 8-row atoms of 1024 B along
+// K (stride sbo between atoms), the next 64 MN elements lbo bytes further.
+__device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3fffu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3fffu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3fffu) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;             // descriptor version for sm_100
+  d |= static_cast<uint64_t>(2u) << 61;             // SWIZZLE_128B
+  return d;
+}
 
 // Shared-memory matrix descriptor for a K-major operand tile stored with the
 // 128-byte swizzle (rows of 64 bf16, 8-row atoms of 1024 B).  Field layout:
@@ -283,11 +317,13 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
   return d;
 }
 
-// Instruction descriptor for kind::f16 with bf16 A/B, fp32 D, both K-major.
-__host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N) {
+// Instruction descriptor for kind::f16 with bf16 A/B, fp32 D, both K-major
+// (a_mn_major: A is MN-major instead, bit 15).
+__host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, bool a_mn_major = false) {
   return (1u << 4)                                  // D format: f32
          | (1u << 7)                                // A format: bf16
          | (1u << 10)                               // B format: bf16
+         | (a_mn_major ? (1u << 15) : 0u)           // A major-ness
          | (static_cast<uint32_t>(N >> 3) << 17)    // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24);   // M / 16
 }

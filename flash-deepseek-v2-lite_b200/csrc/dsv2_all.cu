@@ -6,4 +6,5 @@
 #include "moe_tc.cu"
 #include "router.cu"
 #include "mla.cu"
+#include "mla_tc.cu"
 #include "api.cu"

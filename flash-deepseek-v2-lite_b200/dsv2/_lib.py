@@ -87,7 +87,7 @@ class MlaDecodeArgs(ctypes.Structure):
         ("q_abs", c_vp), ("q_pe", c_vp), ("cache", c_vp), ("cache_b_stride", c_i64), ("max_len", c_i32),
         ("positions", c_vp), ("pos_numel", c_i32), ("softmax_scale", c_f32),
         ("split_len", c_i32), ("n_splits", c_i32), ("o_part", c_vp), ("ml_part", c_vp),
-        ("o_lat", c_vp), ("batch", c_i32), ("inputs_prior", c_i32), ("row_sync", c_vp),
+        ("o_lat", c_vp), ("batch", c_i32), ("inputs_prior", c_i32), ("row_sync", c_vp), ("family", c_i32),
     ]
 
 

@@ -30,16 +30,17 @@ from .model import (HIDDEN, KV_LORA, LATENT_ROW, N_HEADS, QK_NOPE, QKVA_ROWS, Q_
 FAMILIES = {"small": ops.FAMILY_SMALL, "batch": ops.FAMILY_BATCH}
 
 
-def choose_split_len(batch: int, max_len: int, num_sms: int) -> int:
+def choose_split_len(batch: int, max_len: int, num_sms: int, family: int = ops.FAMILY_SMALL) -> int:
     """Positions per split-KV CTA.  Large batches use 256-position splits, so that rows of
     very different lengths (ragged batches) spread over the SMs and a row of up to 256
     positions writes its output directly; smaller batches are split so that they yield
-    about four CTAs per SM (two resident per SM)."""
+    about four CTAs per SM.  Splits are multiples of 64 positions."""
+    unit = 64
     if batch * 2 >= 3 * num_sms:
-        return int(min(256, (max_len + 63) // 64 * 64))
+        return int(min(256, (max_len + unit - 1) // unit * unit))
     s = math.ceil(batch * max_len / (4 * num_sms))
-    s = (s + 63) // 64 * 64
-    return int(min(max(s, 64), 4096))
+    s = (s + unit - 1) // unit * unit
+    return int(min(max(s, unit), 4096))
 
 
 def split_count(n_rows: int, k: int, num_sms: int) -> int:

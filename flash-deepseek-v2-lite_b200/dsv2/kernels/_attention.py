@@ -89,14 +89,15 @@ def pack_attention_weights(attn: torch.nn.Module) -> AttentionPackedWeights:
     )
 
 
-def _workspace(packed: AttentionPackedWeights, dev: torch.device, B: int, max_len: int) -> AttentionDecodeWorkspace:
-    key = (dev.index if dev.index is not None else 0, B, max_len)
+def _workspace(packed: AttentionPackedWeights, dev: torch.device, B: int, max_len: int,
+               family: int) -> AttentionDecodeWorkspace:
+    key = (dev.index if dev.index is not None else 0, B, max_len, family)
     ws = packed.workspace_by_device.get(key)
     if ws is not None:
         return ws
     from ..engine import choose_split_len
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    split_len = choose_split_len(B, max_len, sms)
+    split_len = choose_split_len(B, max_len, sms, family)
     n_splits = math.ceil(max_len / split_len)
     bf, f32 = torch.bfloat16, torch.float32
     ws = AttentionDecodeWorkspace(
@@ -158,7 +159,7 @@ def mla_decode_layer(name: str, hidden_states, cos, sin, position_ids, cache_pos
         x = x.contiguous()
     dev = x.device
     max_len = int(key_cache.shape[1])
-    ws = _workspace(packed, dev, B, max_len)
+    ws = _workspace(packed, dev, B, max_len, family)
     pos = cache_position.reshape(-1)
     if not pos.is_contiguous():
         pos = pos.contiguous()

@@ -140,14 +140,17 @@ def build_case(kernel: str, B: int, family: int, ctx: int, split_len: int | None
         else:
             pos = torch.full((B,), ctx - 1, dtype=torch.int64, device=dev)
         from .engine import choose_split_len
-        sl = split_len or choose_split_len(B, S, torch.cuda.get_device_properties(dev).multi_processor_count)
+        sl = split_len or choose_split_len(B, S, torch.cuda.get_device_properties(dev).multi_processor_count,
+                                           family)
         ns = math.ceil(S / sl)
         o_part = torch.zeros(B, ns, 16, 512, device=dev)
         ml = torch.zeros(B, ns, 16, 2, device=dev)
         o_lat = torch.zeros(B, 16, 512, dtype=torch.bfloat16, device=dev)
-        sync = torch.zeros(B, dtype=torch.int32, device=dev) if merge_in_kernel else None
+        sync = (torch.zeros(B, dtype=torch.int32, device=dev)
+                if merge_in_kernel and family == ops.FAMILY_SMALL else None)
         calls.append(lambda: ops.mla_decode(q_abs=q_abs, q_pe=q_pe, cache=cache, positions=pos, softmax_scale=0.07,
-                                            split_len=sl, o_part=o_part, ml_part=ml, o_lat=o_lat, row_sync=sync))
+                                            split_len=sl, o_part=o_part, ml_part=ml, o_lat=o_lat, row_sync=sync,
+                                            family=family))
         nbytes = int((pos + 1).sum()) * 576 * 2
     else:
         raise ValueError(kernel)

@@ -332,11 +332,13 @@ def mla_prep(*, qkva: torch.Tensor, kv_norm_w: torch.Tensor, eps: float, cos: to
 
 def mla_decode(*, q_abs: torch.Tensor, q_pe: torch.Tensor, cache: torch.Tensor, positions: torch.Tensor,
                softmax_scale: float, split_len: int, o_part: torch.Tensor, ml_part: torch.Tensor,
-               o_lat: torch.Tensor, inputs_prior: bool = False, row_sync: torch.Tensor | None = None) -> None:
+               o_lat: torch.Tensor, inputs_prior: bool = False, row_sync: torch.Tensor | None = None,
+               family: int = FAMILY_SMALL) -> None:
     """Latent attention for every row (see dsv2_mla_decode_args in include/dsv2.h).
     inputs_prior: q_pe, positions and the cache were written at least two launches earlier
     on this stream (only q_abs by the previous one).  row_sync: int32 [B] zero-initialised
-    counters; when given, the splits of a row are merged inside the decode launch."""
+    counters; when given, the splits of a row are merged inside the decode launch.
+    family: FAMILY_SMALL (mma.sync kernel) or FAMILY_BATCH (tcgen05 kernel)."""
     for name, t in (("q_abs", q_abs), ("q_pe", q_pe), ("o_part", o_part), ("ml_part", ml_part), ("o_lat", o_lat)):
         _cuda(t, name)
         if not t.is_contiguous():
@@ -362,6 +364,7 @@ def mla_decode(*, q_abs: torch.Tensor, q_pe: torch.Tensor, cache: torch.Tensor, 
     a.o_lat = o_lat.data_ptr()
     a.batch = q_abs.shape[0]
     a.inputs_prior = 1 if inputs_prior else 0
+    a.family = family
     if row_sync is not None:
         if row_sync.dtype != torch.int32 or row_sync.numel() < q_abs.shape[0]:
             raise ValueError("row_sync must be int32 with one entry per row")

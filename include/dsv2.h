@@ -361,6 +361,9 @@ typedef struct dsv2_mla_decode_args {
    * last split of each row to finish merges the row's partials, so no merge launch
    * follows.  NULL = merge in a second launch. */
   int32_t* row_sync;
+  /* DSV2_FAMILY_SMALL: mma.sync kernel (32-position tiles);
+   * DSV2_FAMILY_BATCH: tcgen05/TMEM kernel (64-position tiles; row_sync must be NULL). */
+  int32_t family;
 } dsv2_mla_decode_args;
 
 DSV2_API int dsv2_mla_decode(const dsv2_mla_decode_args* args, void* stream);

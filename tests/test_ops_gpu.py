@@ -217,6 +217,25 @@ def test_mla_decode_vs_oracle(D, B, S, lengths, split):
         assert int(sync.abs().sum()) == 0
 
 
+@pytest.mark.parametrize("B,S,lengths,split", [
+    (1, 128, [1], 128), (1, 700, [613], 128), (3, 300, [5, 300, 129], 128), (4, 1100, [1100, 64, 65, 700], 256),
+    (5, 256, [128, 129, 256, 1, 200], 256), (2, 8300, [8292, 4000], 1024), (2, 640, [640, 639], 640)])
+def test_mla_decode_tcgen05_vs_oracle(D, B, S, lengths, split):
+    """Batch-family latent attention on the tensor cores (128-position tiles)."""
+    cache, q_abs, q_pe, pos = _mla_inputs(B, S, lengths, seed=S + 7 * B)
+    scale = 192 ** -0.5
+    n_splits = math.ceil(S / split)
+    o_part = torch.zeros(B, n_splits, 16, 512, device=DEV)
+    ml = torch.zeros(B, n_splits, 16, 2, device=DEV)
+    o_tc = torch.zeros(B, 16, 512, dtype=torch.bfloat16, device=DEV)
+    D.mla_decode(q_abs=q_abs.to(DEV), q_pe=q_pe.to(DEV), cache=cache.to(DEV), positions=pos.to(DEV),
+                 softmax_scale=scale, split_len=split, o_part=o_part, ml_part=ml, o_lat=o_tc, family=D.FAMILY_BATCH)
+    ref = O.mla_decode(q_abs, q_pe, cache, pos + 1, scale)
+    assert relerr(o_tc.cpu(), ref) < 1e-2
+    # the cache is only read
+    assert torch.equal(cache.to(DEV).cpu(), cache)
+
+
 def test_mla_decode_matches_reference_expanded_attention(D, golden_ref):
     """The absorbed kernel reproduces the reference's expanded-cache attention when the
     expanded K/V are built from a latent cache through W_UK / W_UV."""
