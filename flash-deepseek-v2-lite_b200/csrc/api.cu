@@ -313,11 +313,56 @@ int dsv2_advance_positions(int64_t* pos, int n, void* stream) {
                       "advance_positions");
 }
 
+static int linear_impl(const dsv2_linear_args* a, int family, void* stream, bool argmax);
+
 int dsv2_linear(const dsv2_linear_args* a, int family, void* stream) {
+  return linear_impl(a, family, stream, false);
+}
+
+int dsv2_lm_head_argmax(const void* w, int vocab, int hidden, const void* x, int64_t x_row_stride,
+                        int n_tokens, uint64_t* keys, int64_t keys_capacity, int64_t* next_ids,
+                        int64_t* input_ids, int64_t* positions, int pos_numel, int family, void* stream) {
+  if (!w || !x || !keys || !next_ids) return fail(DSV2_ERR_INVALID, "lm_head_argmax: null pointer");
+  if (vocab <= 0 || hidden <= 0 || n_tokens < 0)
+    return fail(DSV2_ERR_INVALID, "lm_head_argmax: vocab %d hidden %d tokens %d", vocab, hidden, n_tokens);
+  if (positions && pos_numel != 1 && pos_numel != n_tokens)
+    return fail(DSV2_ERR_INVALID, "lm_head_argmax: positions numel %d for %d tokens", pos_numel, n_tokens);
+  if (n_tokens == 0) return DSV2_OK;
+  const long long n_blocks = family == DSV2_FAMILY_BATCH ? (static_cast<long long>(vocab) + 127) / 128 * 4
+                                                         : (static_cast<long long>(vocab) + 15) / 16;
+  if (keys_capacity < n_blocks * n_tokens)
+    return fail(DSV2_ERR_INVALID, "lm_head_argmax: keys hold %lld entries, %lld needed",
+                static_cast<long long>(keys_capacity), n_blocks * n_tokens);
+  dsv2_linear_args a = {};
+  a.w = w;
+  a.w_row_stride = hidden;
+  a.n_rows = vocab;
+  a.k = hidden;
+  a.x = x;
+  a.x_row_stride = x_row_stride;
+  a.y = keys;
+  a.y_row_stride = n_tokens;
+  a.epilogue = DSV2_EPI_ARGMAX;
+  a.n_groups = 1;
+  a.n_tokens = n_tokens;
+  a.w_group_rows = vocab;
+  a.x_group_rows = n_tokens;
+  int rc = linear_impl(&a, family, stream, true);
+  if (rc) return rc;
+  return check_launch(launch_argmax_finalize(reinterpret_cast<const unsigned long long*>(keys),
+                                             static_cast<int>(n_blocks), n_tokens, n_tokens,
+                                             reinterpret_cast<long long*>(next_ids),
+                                             reinterpret_cast<long long*>(input_ids),
+                                             reinterpret_cast<long long*>(positions), pos_numel,
+                                             static_cast<cudaStream_t>(stream)),
+                      "lm_head_argmax: finalize");
+}
+
+static int linear_impl(const dsv2_linear_args* a, int family, void* stream, bool argmax) {
   if (!a || !a->w || !a->x || !a->y) return fail(DSV2_ERR_INVALID, "linear: null pointer");
   if (a->n_rows <= 0 || a->k <= 0 || a->n_groups <= 0)
     return fail(DSV2_ERR_INVALID, "linear: n_rows=%d k=%d n_groups=%d", a->n_rows, a->k, a->n_groups);
-  if (a->epilogue < DSV2_EPI_STORE_BF16 || a->epilogue > DSV2_EPI_SCALE_F32)
+  if (a->epilogue < DSV2_EPI_STORE_BF16 || a->epilogue > (argmax ? DSV2_EPI_ARGMAX : DSV2_EPI_SCALE_F32))
     return fail(DSV2_ERR_INVALID, "linear: epilogue %d", a->epilogue);
   if (a->epilogue == DSV2_EPI_SCALE_F32 && !a->route_scale)
     return fail(DSV2_ERR_INVALID, "linear: SCALE epilogue needs route_scale");

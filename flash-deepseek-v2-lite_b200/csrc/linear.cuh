@@ -10,7 +10,19 @@ enum Epilogue : int {
   kEpiStoreF32 = 1,    // y = acc
   kEpiSwiglu = 2,      // y = bf16(silu(bf16(acc_gate)) * bf16(acc_up)) computed in fp32
   kEpiScaleF32 = 3,    // y = bf16(acc) * route_scale[route]   (fp32 store)
+  kEpiArgmax = 4,      // y = per-row-block arg-max keys of bf16(acc) (uint64, see argmax_key)
 };
+
+// Arg-max key of output row n with value v (rounded to bf16 first, like bf16 logits):
+// the value's bits in an order-preserving form above, and ~n below, so the largest key
+// is the largest value and, among equal values, the lowest row.
+__device__ __forceinline__ uint32_t argmax_ord(float v) {
+  const uint32_t u = __float_as_uint(bf16_round(v));
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ unsigned long long argmax_key(uint32_t ord, uint32_t row) {
+  return (static_cast<unsigned long long>(ord) << 32) | (0xffffffffu - row);
+}
 
 struct LinearParams {
   const bf16* w;

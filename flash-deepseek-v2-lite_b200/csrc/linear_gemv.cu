@@ -35,6 +35,7 @@ __global__ __launch_bounds__(kGemvWarps * 32) void gemv_mma_kernel(const LinearP
   bool waited = !early;
   if (!early) pdl_enter();
   __shared__ float red[kGemvWarps][32][SWIGLU ? 8 : 4];
+  __shared__ unsigned long long s_key[kGemvRows * kGemvTok];  // arg-max epilogue only
   int item = blockIdx.x;
   const int tc = item % tc_count;
   item /= tc_count;
@@ -133,7 +134,22 @@ __global__ __launch_bounds__(kGemvWarps * 32) void gemv_mma_kernel(const LinearP
     }
     const int n = n0 + (l >> 2) + ((s & 2) ? 8 : 0);
     const int j = 2 * (l & 3) + (s & 1);
-    if (j < tn && n < p.n_rows) linear_store(p, g, r0 + tbeg + j, n, acc, accu);
+    if (p.epilogue == kEpiArgmax) {
+      s_key[(n - n0) * kGemvTok + j] = (n < p.n_rows) ? argmax_key(argmax_ord(acc), n) : 0ull;
+    } else if (j < tn && n < p.n_rows) {
+      linear_store(p, g, r0 + tbeg + j, n, acc, accu);
+    }
+  }
+  if (p.epilogue == kEpiArgmax) {
+    // one key per (16-row block, token): the block's largest value, lowest row on ties
+    __syncthreads();
+    if (threadIdx.x < tn) {
+      unsigned long long best = 0;
+#pragma unroll
+      for (int r = 0; r < kGemvRows; ++r) best = max(best, s_key[r * kGemvTok + threadIdx.x]);
+      reinterpret_cast<unsigned long long*>(p.y)[static_cast<long long>(rb) * p.y_row_stride + tbeg +
+                                                 threadIdx.x] = best;
+    }
   }
 }
 

@@ -316,6 +316,21 @@ __global__ __launch_bounds__(kTcThreads, 1) void linear_tc_kernel(
           tc_fence_before();
           mbar_arrive(&tempty_bar[buf]);
         }
+        if (EPI == kEpiArgmax) {
+          // per token: the largest bf16 value of this warp's 32 rows, lowest row on ties;
+          // lane 0 stores one key per (32-row block, token)
+          unsigned long long* kp = reinterpret_cast<unsigned long long*>(p.y) +
+                                   static_cast<long long>(mt * 4 + quad) * p.y_row_stride + rbase + c0;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const uint32_t ord = row_ok ? argmax_ord(acc[j]) : 0u;
+            const uint32_t best = __reduce_max_sync(0xffffffffu, ord);
+            const uint32_t cand = (row_ok && ord == best) ? (0xffffffffu - static_cast<uint32_t>(n)) : 0u;
+            const uint32_t low = __reduce_max_sync(0xffffffffu, cand);
+            if (lane == 0 && c0 + j < ntok) kp[j] = (static_cast<unsigned long long>(best) << 32) | low;
+          }
+          continue;
+        }
         OutT* yp = ybase + static_cast<long long>(rbase + c0) * p.y_row_stride;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -392,7 +407,8 @@ cudaError_t linear_tc_init() {
       tc_set_smem<kEpiStoreBf16, false>(), tc_set_smem<kEpiStoreBf16, true>(),
       tc_set_smem<kEpiStoreF32, false>(),  tc_set_smem<kEpiStoreF32, true>(),
       tc_set_smem<kEpiSwiglu, false>(),    tc_set_smem<kEpiSwiglu, true>(),
-      tc_set_smem<kEpiScaleF32, false>(),  tc_set_smem<kEpiScaleF32, true>()};
+      tc_set_smem<kEpiScaleF32, false>(),  tc_set_smem<kEpiScaleF32, true>(),
+      tc_set_smem<kEpiArgmax, false>()};
   for (cudaError_t e : errs)
     if (e != cudaSuccess) return e;
   return cudaSuccess;
@@ -445,6 +461,10 @@ cudaError_t launch_linear_tc_impl(const LinearParams& p, const CUtensorMap& tmap
     case kEpiStoreBf16: DSV2_TC_LAUNCH(kEpiStoreBf16); break;
     case kEpiStoreF32: DSV2_TC_LAUNCH(kEpiStoreF32); break;
     case kEpiSwiglu: DSV2_TC_LAUNCH(kEpiSwiglu); break;
+    case kEpiArgmax:
+      tc_launch<kEpiArgmax, false>(grid, smem, st, p, tmap_w, tmap_x, tmap_xb, shp, mt_count, nt_count,
+                                   up_rows, x_grouped);
+      break;
     default: DSV2_TC_LAUNCH(kEpiScaleF32); break;
   }
 #undef DSV2_TC_LAUNCH

@@ -258,6 +258,34 @@ __global__ void sum_partials_kernel(const float* __restrict__ part, int n_parts,
   }
 }
 
+// Greedy token per row from the per-block arg-max keys [n_blocks][key_stride] (largest
+// key = largest bf16 logit, lowest vocabulary index on ties): next_ids[t] = index; also
+// input_ids[t] = index and positions[t] += 1 when given (the end of a decode step).
+__global__ __launch_bounds__(256) void argmax_finalize_kernel(const unsigned long long* __restrict__ keys,
+                                                              int n_blocks, long long key_stride,
+                                                              long long* __restrict__ next_ids,
+                                                              long long* __restrict__ input_ids,
+                                                              long long* __restrict__ positions,
+                                                              int pos_numel) {
+  pdl_enter();
+  __shared__ unsigned long long s_best[8];
+  const int t = blockIdx.x;
+  unsigned long long best = 0;
+  for (int i = threadIdx.x; i < n_blocks; i += blockDim.x) best = max(best, keys[i * key_stride + t]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+  if ((threadIdx.x & 31) == 0) s_best[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) best = max(best, s_best[w]);
+    best = max(best, s_best[0]);
+    const long long idx = static_cast<long long>(0xffffffffu - static_cast<uint32_t>(best & 0xffffffffu));
+    next_ids[t] = idx;
+    if (input_ids) input_ids[t] = idx;
+    if (positions && (pos_numel != 1 || t == 0)) positions[pos_numel == 1 ? 0 : t] += 1;
+  }
+}
+
 __device__ __forceinline__ float silu_f(float g) { return g / (1.f + expf(-g)); }
 
 // out = bf16(silu(gate) * up)
@@ -360,6 +388,14 @@ cudaError_t launch_sum_partials(const float* part, int n_parts, long long ps, lo
   const int thr = 128;
   dim3 grid((cols / 8 + thr - 1) / thr, rows);
   launch_kernel(sum_partials_kernel, grid, thr, 0, st, part, n_parts, ps, rs, out, out_f32, ors, cols);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_argmax_finalize(const unsigned long long* keys, int n_blocks, long long key_stride,
+                                   int n_tokens, long long* next_ids, long long* input_ids,
+                                   long long* positions, int pos_numel, cudaStream_t st) {
+  launch_kernel(argmax_finalize_kernel, n_tokens, 256, 0, st, keys, n_blocks, key_stride, next_ids, input_ids,
+                positions, pos_numel);
   return cudaGetLastError();
 }
 

@@ -89,6 +89,9 @@ cudaError_t launch_copy_token_to_cache(const void*, const long long*, void*, con
                                        const long long*, int, int, int, int, int, int,
                                        cudaStream_t);
 cudaError_t launch_advance_positions(long long*, int, cudaStream_t);
+cudaError_t launch_argmax_finalize(const unsigned long long* keys, int n_blocks, long long key_stride,
+                                   int n_tokens, long long* next_ids, long long* input_ids,
+                                   long long* positions, int pos_numel, cudaStream_t st);
 // router.cu
 cudaError_t launch_router(const RouterParams&, cudaStream_t);
 cudaError_t launch_bucket(const int*, const float*, int, int, int, int, int, int*, int*, int*,

@@ -111,6 +111,8 @@ _SIGNATURES = {
     "dsv2_advance_positions": ([c_vp, c_i32, c_vp], c_i32),
     "dsv2_linear": ([ctypes.POINTER(LinearArgs), c_i32, c_vp], c_i32),
     "dsv2_moe": ([ctypes.POINTER(MoeArgs), c_vp], c_i32),
+    "dsv2_lm_head_argmax": ([c_vp, c_i32, c_i32, c_vp, c_i64, c_i32, c_vp, c_i64, c_vp, c_vp, c_vp, c_i32, c_i32,
+                             c_vp], c_i32),
     "dsv2_router": ([ctypes.POINTER(RouterArgs), c_vp], c_i32),
     "dsv2_softmax_topk": ([c_vp, c_i32, c_i32, c_f32, c_vp, c_vp, c_vp, c_vp], c_i32),
     "dsv2_moe_bucket": ([c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp,

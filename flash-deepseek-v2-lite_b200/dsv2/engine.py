@@ -60,7 +60,7 @@ class DecodeState:
 class DecodeEngine:
     def __init__(self, model, batch: int, max_len: int, family: str = "batch", *,
                  rank: int = 0, world: int = 1, group=None, gate_bias: torch.Tensor | None = None,
-                 alias_hf: bool = True, fused_moe: bool = True):
+                 alias_hf: bool = True, fused_moe: bool = True, keep_logits: bool = False):
         cfg = model.config
         check_config(cfg)
         if family not in FAMILIES:
@@ -74,6 +74,7 @@ class DecodeEngine:
         self.max_len = int(max_len)
         self.rank, self.world, self.group = rank, world, group
         self.fused_moe = fused_moe
+        self.keep_logits = keep_logits   # also materialise the bf16 logits every step
         self.B_all = self.B * world
         self.shard = ep_shard(int(cfg.n_routed_experts), self.B_all, rank, world)
         self.n_local = self.shard.n_local
@@ -159,7 +160,8 @@ class DecodeEngine:
                 self.x_all = torch.zeros((Ball, HIDDEN), device=dev, dtype=bf)
                 self.moe_sum = torch.zeros((Ball, HIDDEN), device=dev, dtype=f32)
                 self.moe_local = torch.zeros((B, 1, HIDDEN), device=dev, dtype=f32)
-        self.logits = torch.zeros((B, self.vocab), device=dev, dtype=bf)
+        self.logits = torch.zeros((B if self.keep_logits else 1, self.vocab), device=dev, dtype=bf)
+        self.argmax_keys = torch.zeros(((self.vocab + 15) // 16) * B, device=dev, dtype=i64)
 
     # ------------------------------------------------------------------ layers
     def _linear(self, **kw):
@@ -336,10 +338,12 @@ class DecodeEngine:
                 if lp.moe is not None:
                     trace["routes"].append(self.topk_ids64.clone())
         ops.add_rmsnorm(self.h, delta, self.final_norm_w, self.final_eps, self.x)
-        torch.mm(self.x, self.lm_head.t(), out=self.logits)
-        torch.argmax(self.logits, dim=-1, out=self.next_ids)
-        self.input_ids.copy_(self.next_ids)
-        ops.advance_positions(self.positions)
+        if self.keep_logits:  # checking / debugging only: the greedy step needs no logits
+            torch.mm(self.x, self.lm_head.t(), out=self.logits)
+        # lm_head + greedy argmax in the linear's epilogue; also feeds the token back and
+        # advances the positions (src/run.py:585-588)
+        ops.lm_head_argmax(w=self.lm_head, x=self.x, keys=self.argmax_keys, next_ids=self.next_ids,
+                           family=self.family, input_ids=self.input_ids, positions=self.positions)
 
     # ------------------------------------------------------------------ state
     def set_state(self, positions: torch.Tensor, input_ids: torch.Tensor) -> None:

@@ -20,7 +20,7 @@ from ._lib import (
 __all__ = [
     "stream", "rmsnorm", "add_rmsnorm", "embed_rmsnorm", "residual_add", "silu_mul", "sum_partials",
     "prepare_decode_inputs", "copy_token_to_cache", "advance_positions", "linear",
-    "router", "softmax_topk", "moe_bucket", "gather_rows", "moe", "mla_prep", "mla_decode",
+    "router", "softmax_topk", "moe_bucket", "gather_rows", "moe", "mla_prep", "mla_decode", "lm_head_argmax",
     "EPI_STORE_BF16", "EPI_STORE_F32", "EPI_SWIGLU", "EPI_SCALE_F32", "FAMILY_SMALL", "FAMILY_BATCH",
 ]
 
@@ -221,6 +221,24 @@ def moe(*, gate_up: torch.Tensor, down: torch.Tensor, x_sorted: torch.Tensor, h:
     a.y, a.sync = y.data_ptr(), sync.data_ptr()
     a.tile_tokens = tile_tokens
     _lib.call("dsv2_moe", ctypes.byref(a), stream())
+
+
+def lm_head_argmax(*, w: torch.Tensor, x: torch.Tensor, keys: torch.Tensor, next_ids: torch.Tensor,
+                   family: int, input_ids: torch.Tensor | None = None,
+                   positions: torch.Tensor | None = None) -> None:
+    """next_ids[t] = argmax over the vocabulary of bf16(x[t] @ w^T) (lowest index on ties),
+    without materialising the logits; optionally input_ids = next_ids and positions += 1.
+    keys: uint64 (int64) work buffer of at least ceil(vocab / 16) * tokens entries."""
+    _cuda(x, "x")
+    if w.dtype != torch.bfloat16 or x.dtype != torch.bfloat16 or w.stride(1) != 1 or x.stride(1) != 1:
+        raise NotImplementedError("lm_head_argmax supports bf16 weights/activations with contiguous rows")
+    if next_ids.dtype != torch.int64 or keys.dtype not in (torch.int64, torch.uint64):
+        raise ValueError("next_ids must be int64 and keys 64-bit")
+    vocab, hidden = w.shape
+    n = x.shape[0]
+    _lib.call("dsv2_lm_head_argmax", w.data_ptr(), vocab, hidden, x.data_ptr(), x.stride(0), n, keys.data_ptr(),
+              keys.numel(), next_ids.data_ptr(), _ptr(input_ids), _ptr(positions),
+              positions.numel() if positions is not None else 0, family, stream())
 
 
 def router(*, x: torch.Tensor, w: torch.Tensor, scaling: float, logits: torch.Tensor,

@@ -42,6 +42,7 @@ extern "C" {
 #define DSV2_EPI_STORE_F32 1  /* y = acc                                             */
 #define DSV2_EPI_SWIGLU 2     /* y = bf16(silu(bf16(gate)) * bf16(up)), fp32 math    */
 #define DSV2_EPI_SCALE_F32 3  /* y = bf16(acc) * route_scale[route] (fp32 store)     */
+#define DSV2_EPI_ARGMAX 4     /* internal to dsv2_lm_head_argmax                     */
 
 /* ---- linear families ------------------------------------------------------ */
 #define DSV2_FAMILY_SMALL 0 /* mma.sync weight-streaming GEMV (<= 8 tokens per pass)  */
@@ -228,6 +229,21 @@ typedef struct dsv2_moe_args {
 } dsv2_moe_args;
 
 DSV2_API int dsv2_moe(const dsv2_moe_args* args, void* stream);
+
+/* ---- lm_head + greedy sampling ------------------------------------------------ */
+/* next_ids[t] = argmax_v bf16(sum_k w[v, k] * x[t, k]) for every token t (lowest index on
+ * ties, like torch.argmax over bf16 logits), without writing the logits: the linear's
+ * epilogue keeps one (value, index) key per row block and token in `keys`, a second
+ * launch reduces them.  When given, input_ids[t] = next_ids[t] and positions[t] += 1
+ * (pos_numel 1: positions[0] += 1), closing a decode step.  w: [vocab, hidden] bf16,
+ * x: [n_tokens, hidden] bf16 rows at x_row_stride; hidden % 64 == 0 (batch family) or
+ * % 32 == 0 (small).  keys: uint64 work buffer of at least ceil(vocab / 16) * n_tokens
+ * entries.  Reference: the greedy step of the decode loop, lm_head + argmax
+ * (src/run.py:585-586). */
+DSV2_API int dsv2_lm_head_argmax(const void* w, int vocab, int hidden, const void* x,
+                                 int64_t x_row_stride, int n_tokens, uint64_t* keys,
+                                 int64_t keys_capacity, int64_t* next_ids, int64_t* input_ids,
+                                 int64_t* positions, int pos_numel, int family, void* stream);
 
 /* ---- MoE routing ------------------------------------------------------------ */
 /* Gate GEMV (fp32 over bf16 activations) + softmax + top-6, then bucketing (two launches).

@@ -77,7 +77,7 @@ def test_engine_matches_hf(models, family):
     g = torch.Generator().manual_seed(2)
     lens = [20, 33, 7, 50]
     prompts = [torch.randint(0, model.config.vocab_size, (n,), generator=g) for n in lens]
-    eng = DecodeEngine(model, batch=len(lens), max_len=96, family=family, alias_hf=False)
+    eng = DecodeEngine(model, batch=len(lens), max_len=96, family=family, alias_hf=False, keep_logits=True)
     first = eng.prefill(prompts)
     steps = 3
     traces, fed = [], []
@@ -142,7 +142,7 @@ def test_programmatic_launch_matches_serialized(models, family, batch):
     g = torch.Generator().manual_seed(4)
     prompts = [torch.randint(0, model.config.vocab_size, (int(n),), generator=g)
                for n in torch.randint(5, 60, (batch,), generator=g)]
-    eng = DecodeEngine(model, batch=batch, max_len=96, family=family, alias_hf=False)
+    eng = DecodeEngine(model, batch=batch, max_len=96, family=family, alias_hf=False, keep_logits=True)
     eng.prefill(prompts)
     n0 = _lib.kernel_launches()
     eng.step()

@@ -27,7 +27,8 @@ def _prompts():
 def _run_engine(model, prompts, family, rank=0, world=1, group=None):
     from dsv2.engine import DecodeEngine
     B = len(prompts) // world
-    eng = DecodeEngine(model, B, 96, family, rank=rank, world=world, group=group, alias_hf=(world == 1))
+    eng = DecodeEngine(model, B, 96, family, rank=rank, world=world, group=group, alias_hf=(world == 1),
+                       keep_logits=True)
     eng.prefill(prompts[rank * B:(rank + 1) * B])
     eng.capture()
     logits, toks = [], []

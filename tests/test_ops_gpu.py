@@ -309,3 +309,33 @@ def test_sum_partials_fixed_order(D):
     out16 = torch.empty(6, 2048, dtype=torch.bfloat16, device=DEV)
     D.sum_partials(part.to(DEV)[:, :5], out16)
     assert torch.equal(out16.cpu(), ref.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("family", ["small", "batch"])
+@pytest.mark.parametrize("V,T", [(3001, 1), (5000, 5), (102400, 33)])
+def test_lm_head_argmax(D, family, V, T):
+    """Greedy token of bf16 logits without materialising them: the chosen index holds the
+    largest bf16 logit (oracle fp32 product rounded to bf16), lowest index among equals
+    whose value the oracle reproduces; input_ids / positions are updated in place."""
+    g = torch.Generator().manual_seed(V + T)
+    w = (torch.randn(V, 2048, generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.randn(T, 2048, generator=g).to(torch.bfloat16)
+    keys = torch.zeros(((V + 15) // 16) * T, dtype=torch.int64, device=DEV)
+    nxt = torch.full((T,), -1, dtype=torch.int64, device=DEV)
+    inp = torch.full((T,), -1, dtype=torch.int64, device=DEV)
+    pos = torch.arange(T, dtype=torch.int64, device=DEV) * 3
+    f = D.FAMILY_SMALL if family == "small" else D.FAMILY_BATCH
+    D.lm_head_argmax(w=w.to(DEV), x=x.to(DEV), keys=keys, next_ids=nxt, family=f, input_ids=inp, positions=pos)
+    logits = (x.float() @ w.float().t()).to(torch.bfloat16).float()
+    got = nxt.cpu()
+    best = logits.max(dim=1).values
+    picked = logits[torch.arange(T), got]
+    # the pick is a maximal bf16 logit up to one ulp of summation-order difference
+    assert bool(((best - picked) <= best.abs() * 2 ** -7).all())
+    ref = logits.argmax(dim=1)
+    # with a unique maximum (all rows here) the index is the reference's
+    uniq = (logits == best[:, None]).sum(1) == 1
+    agree = (got == ref) | ~uniq
+    assert float(agree.float().mean()) >= 0.95
+    assert torch.equal(inp.cpu(), got)
+    assert torch.equal(pos.cpu(), torch.arange(T) * 3 + 1)
