@@ -286,6 +286,7 @@ def run_ours(args, cfg_id: int):
         cpu = cpu_baseline(model, prompts_all, cfg, args)
     eng.release()
     barrier(world)
+    eng.close()
     out = None
     if rank == 0:
         out = {

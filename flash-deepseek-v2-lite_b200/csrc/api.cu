@@ -149,9 +149,61 @@ int mla_cache_map(const void* cache, int64_t cache_b_stride, int max_len, int ba
                        static_cast<uint64_t>(cache_b_stride) * 2, box_rows, out);
 }
 
+// dsv2_peer_table -> kernel-side PeerTable (world 0 when NULL or single GPU)
+int to_peers(const dsv2_peer_table* t, PeerTable* out) {
+  *out = PeerTable{};
+  if (!t || t->world <= 1) return DSV2_OK;
+  if (t->world > kMaxPeers || t->rank < 0 || t->rank >= t->world || !t->epoch || t->rows_per_rank <= 0 ||
+      t->n_moe_layers <= 0)
+    return fail(DSV2_ERR_INVALID, "peer table: world %d rank %d", t->world, t->rank);
+  for (int q = 0; q < t->world; ++q) {
+    if (!t->base[q]) return fail(DSV2_ERR_INVALID, "peer table: buffer of rank %d missing", q);
+    out->base[q] = static_cast<char*>(t->base[q]);
+  }
+  out->world = t->world;
+  out->rank = t->rank;
+  out->xg_off = t->xg_offset;
+  out->ids_off = t->ids_offset;
+  out->w_off = t->w_offset;
+  out->part_off = t->part_offset;
+  out->ctr_off = t->ctr_offset;
+  out->rows_per_rank = t->rows_per_rank;
+  out->n_moe = t->n_moe_layers;
+  out->epoch = reinterpret_cast<const long long*>(t->epoch);
+  return DSV2_OK;
+}
+
 }  // namespace
 
 extern "C" {
+
+int dsv2_peer_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return fail(DSV2_ERR_INVALID, "peer_alloc: bad arguments");
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess) return check_launch(e, "peer_alloc");
+  e = cudaMemset(*ptr, 0, bytes);
+  return check_launch(e, "peer_alloc: clear");
+}
+
+int dsv2_peer_free(void* ptr) { return check_launch(cudaFree(ptr), "peer_free"); }
+
+int dsv2_peer_export(const void* ptr, void* handle) {
+  if (!ptr || !handle) return fail(DSV2_ERR_INVALID, "peer_export: null pointer");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (e != cudaSuccess) return check_launch(e, "peer_export");
+  memcpy(handle, &h, sizeof(h));
+  return DSV2_OK;
+}
+
+int dsv2_peer_import(const void* handle, void** ptr) {
+  if (!ptr || !handle) return fail(DSV2_ERR_INVALID, "peer_import: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return check_launch(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "peer_import");
+}
+
+int dsv2_peer_close(void* ptr) { return check_launch(cudaIpcCloseMemHandle(ptr), "peer_close"); }
 
 int dsv2_version(void) { return 100; }
 
@@ -196,7 +248,10 @@ int dsv2_rmsnorm(const void* x, int64_t x_row_stride, const void* w, int w_dtype
 
 int dsv2_add_rmsnorm(void* h, void* h_out, const void* delta, int delta_dtype, int n_delta,
                      int64_t delta_part_stride, int64_t delta_row_stride, const void* w,
-                     int w_dtype, void* y, int rows, int cols, float eps, void* stream) {
+                     int w_dtype, void* y, int rows, int cols, float eps,
+                     const dsv2_peer_table* peers, int moe_layer, void* stream) {
+  PeerTable pt;
+  if (int rc = to_peers(peers, &pt)) return rc;
   if (!h || (n_delta > 0 && !delta) || (y && !w))
     return fail(DSV2_ERR_INVALID, "add_rmsnorm: null pointer");
   if (cols <= 0 || cols % 8 || cols > 4096)
@@ -209,7 +264,7 @@ int dsv2_add_rmsnorm(void* h, void* h_out, const void* delta, int delta_dtype, i
   if (rows <= 0) return DSV2_OK;
   return check_launch(launch_add_rmsnorm(h, h_out, delta, delta_dtype, n_delta, delta_part_stride,
                                          delta_row_stride, w, w_dtype, y, rows, cols, eps,
-                                         static_cast<cudaStream_t>(stream)),
+                                         static_cast<cudaStream_t>(stream), &pt, moe_layer),
                       "add_rmsnorm");
 }
 
@@ -321,7 +376,8 @@ int dsv2_linear(const dsv2_linear_args* a, int family, void* stream) {
 
 int dsv2_lm_head_argmax(const void* w, int vocab, int hidden, const void* x, int64_t x_row_stride,
                         int n_tokens, uint64_t* keys, int64_t keys_capacity, int64_t* next_ids,
-                        int64_t* input_ids, int64_t* positions, int pos_numel, int family, void* stream) {
+                        int64_t* input_ids, int64_t* positions, int pos_numel, int64_t* step_counter,
+                        int family, void* stream) {
   if (!w || !x || !keys || !next_ids) return fail(DSV2_ERR_INVALID, "lm_head_argmax: null pointer");
   if (vocab <= 0 || hidden <= 0 || n_tokens < 0)
     return fail(DSV2_ERR_INVALID, "lm_head_argmax: vocab %d hidden %d tokens %d", vocab, hidden, n_tokens);
@@ -354,6 +410,7 @@ int dsv2_lm_head_argmax(const void* w, int vocab, int hidden, const void* x, int
                                              reinterpret_cast<long long*>(next_ids),
                                              reinterpret_cast<long long*>(input_ids),
                                              reinterpret_cast<long long*>(positions), pos_numel,
+                                             reinterpret_cast<long long*>(step_counter),
                                              static_cast<cudaStream_t>(stream)),
                       "lm_head_argmax: finalize");
 }
@@ -478,6 +535,7 @@ int dsv2_moe(const dsv2_moe_args* a, void* stream) {
   if ((rc = tensor_map_3d(a->h, I, R, 1, I * 2, R * I * 2, 16, &hm))) return rc;
   if ((rc = tensor_map_3d(a->h, I, R, 1, I * 2, R * I * 2, shp.x_box, &hb))) return rc;
   MoeParams p = {};
+  if ((rc = to_peers(a->peers, &p.peers))) return rc;
   p.n_groups = a->n_groups;
   p.hidden = a->hidden;
   p.inter = a->inter;
@@ -516,7 +574,9 @@ int dsv2_router(const dsv2_router_args* a, void* stream) {
         a->shared_lo < 0 || a->shared_hi < a->shared_lo || a->shared_hi > a->rows)
       return fail(DSV2_ERR_INVALID, "router: bad expert/shared ranges");
   }
-  RouterParams p;
+  RouterParams p = {};
+  if (int rc = to_peers(a->peers, &p.peers)) return rc;
+  p.row_base = a->row_base;
   p.x = reinterpret_cast<const bf16*>(a->x);
   p.x_row_stride = a->x_row_stride;
   p.w = a->w;
@@ -530,8 +590,6 @@ int dsv2_router(const dsv2_router_args* a, void* stream) {
   p.topk_ids = reinterpret_cast<long long*>(a->topk_ids64);
   p.topk_ids32 = a->topk_ids32;
   p.topk_w = a->topk_weights;
-  p.ticket = nullptr;
-  p.experts_per_cta = a->n_experts;
   p.gather_x = a->gather_out ? 1 : 0;
   p.gather_out = a->gather_out;
   p.expert_lo = a->expert_lo;
@@ -562,9 +620,12 @@ int dsv2_moe_bucket(const int32_t* topk_ids32, const float* topk_weights, int ro
                     int expert_lo, int n_local, int shared_lo, int shared_hi,
                     int32_t* group_offsets, int32_t* route_token, int32_t* route_slot,
                     float* route_weight, const void* gather_src, int64_t gather_src_stride,
-                    void* gather_out, int cols, void* stream) {
+                    void* gather_out, int cols, const dsv2_peer_table* peers, int moe_layer,
+                    void* stream) {
   if (!topk_ids32 || !topk_weights || !group_offsets || !route_token || !route_slot || !route_weight)
     return fail(DSV2_ERR_INVALID, "moe_bucket: null pointer");
+  PeerTable pt;
+  if (int rc = to_peers(peers, &pt)) return rc;
   if (rows > 4096) return fail(DSV2_ERR_UNSUPPORTED, "moe_bucket: at most 4096 rows (got %d)", rows);
   if (n_local < 0 || n_local > 64 || shared_lo < 0 || shared_hi < shared_lo || shared_hi > rows)
     return fail(DSV2_ERR_INVALID, "moe_bucket: bad ranges");
@@ -575,7 +636,7 @@ int dsv2_moe_bucket(const int32_t* topk_ids32, const float* topk_weights, int ro
   return check_launch(launch_bucket(topk_ids32, topk_weights, rows, expert_lo, n_local, shared_lo,
                                     shared_hi, group_offsets, route_token, route_slot, route_weight,
                                     gather_out ? gather_src : nullptr, gather_src_stride, gather_out,
-                                    cols, static_cast<cudaStream_t>(stream)),
+                                    cols, static_cast<cudaStream_t>(stream), &pt, moe_layer),
                       "moe_bucket");
 }
 

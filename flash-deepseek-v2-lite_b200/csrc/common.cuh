@@ -66,6 +66,34 @@ __device__ __forceinline__ void pdl_enter() {
 }
 
 // ----------------------------------------------------------------------------
+// Cross-GPU signals (expert parallelism over NVLink peer memory)
+// ----------------------------------------------------------------------------
+// A writer stores its data into a peer's buffer, fences at system scope and adds to the
+// peer's counter with release semantics; the reader polls its own counter with acquire
+// semantics (bounded) and then reads the data with L1-bypassing loads.  Counters only
+// grow; the expected value of a wait is derived from the step counter.
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys_add_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Returns false (and records kErrMbarTimeout) when the counter does not reach target;
+// gives up at once when an earlier wait of any kernel already failed (so that a broken
+// exchange ends quickly instead of timing out at every layer).
+__device__ __forceinline__ bool wait_counter_sys(const unsigned long long* ctr, unsigned long long target) {
+  for (uint32_t i = 0; i < (1u << 24); ++i) {
+    if (ld_acquire_sys_u64(ctr) >= target) return true;
+    if ((i & 255) == 0 && *reinterpret_cast<volatile int*>(&g_device_error) != 0) return false;
+    __nanosleep(64);
+  }
+  set_device_error(kErrMbarTimeout);
+  return false;
+}
+
+// ----------------------------------------------------------------------------
 // bf16 <-> fp32
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ float bf16lo(uint32_t u) { return __uint_as_float(u << 16); }

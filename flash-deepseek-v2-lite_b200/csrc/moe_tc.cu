@@ -44,6 +44,7 @@ struct MoeParams {
   bf16* h;                    // [x_rows, inter] phase-1 output / phase-2 input
   float* y;                   // [*, hidden] fp32
   int* sync;                  // [n_groups + 1]: per-group phase-1 counters + exit ticket
+  PeerTable peers;            // world > 0: y rows (route slots) live in their owner rank's part
 };
 
 struct MoeShape {
@@ -365,8 +366,18 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
           for (int j = 0; j < 16; ++j) {
             const int yrow = __shfl_sync(0xffffffffu, my_row, j);
             const float sc = __shfl_sync(0xffffffffu, my_scale, j);
-            if (row_ok && c0 + j < ntok)
-              p.y[static_cast<long long>(yrow) * p.hidden + n] = bf16_round(acc[j]) * sc;
+            if (row_ok && c0 + j < ntok) {
+              float* dst;
+              if (p.peers.world > 0) {  // slot of a row owned by rank yrow / slots_per_rank
+                const int spr = 8 * p.peers.rows_per_rank;
+                const int owner = yrow / spr;
+                dst = reinterpret_cast<float*>(p.peers.base[owner] + p.peers.part_off) +
+                      static_cast<long long>(yrow - owner * spr) * p.hidden;
+              } else {
+                dst = p.y + static_cast<long long>(yrow) * p.hidden;
+              }
+              dst[n] = bf16_round(acc[j]) * sc;
+            }
           }
         }
       }
@@ -379,15 +390,20 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
     tc_fence_after();
     tmem_dealloc(tmem_base, static_cast<uint32_t>(shp.tmem_cols));
   }
-  // the last CTA out returns the group counters and the ticket to zero
+  // the last CTA out returns the group counters and the ticket to zero (and, expert
+  // parallel, tells every rank that this rank's slot outputs are in place)
   if (threadIdx.x == 0) {
-    __threadfence();
+    if (p.peers.world > 0) __threadfence_system(); else __threadfence();
     const int t = atomicAdd(&p.sync[G], 1);
     if (t == static_cast<int>(gridDim.x) - 1) {
       __threadfence();
       for (int g = 0; g < G; ++g) p.sync[g] = 0;
       p.sync[G] = 0;
       __threadfence();
+      if (p.peers.world > 0) {
+        __threadfence_system();
+        for (int q = 0; q < p.peers.world; ++q) red_release_sys_add_u64(peer_ctr(p.peers, q, 1), 1ull);
+      }
     }
   }
 }

@@ -98,8 +98,17 @@ __global__ __launch_bounds__(kNormThreads) void rmsnorm_kernel(const bf16* __res
 __global__ __launch_bounds__(kNormThreads) void add_rmsnorm_kernel(
     bf16* __restrict__ h, bf16* __restrict__ h_out, const void* __restrict__ delta, int delta_dtype,
     int n_delta, long long delta_part_stride, long long delta_row_stride,
-    const void* __restrict__ w, int w_dtype, bf16* __restrict__ y, int cols, float eps) {
+    const void* __restrict__ w, int w_dtype, bf16* __restrict__ y, int cols, float eps,
+    const PeerTable peers, int layer) {
   pdl_enter();
+  if (peers.world > 0) {
+    // expert parallel: every rank has written its MoE slot outputs for these rows
+    __shared__ int s_ok;
+    if (threadIdx.x == 0)
+      s_ok = wait_counter_sys(peer_ctr(peers, peers.rank, 1), peer_target(peers, layer, 1ull));
+    __syncthreads();
+    if (!s_ok) return;
+  }
   __shared__ float red[kNormThreads / 32];
   const int row = blockIdx.x;
   bf16* hr = h + static_cast<long long>(row) * cols;
@@ -126,8 +135,8 @@ __global__ __launch_bounds__(kNormThreads) void add_rmsnorm_kernel(
         if (delta_dtype == 2) {
           const float* dp = reinterpret_cast<const float*>(delta) + row * delta_row_stride + c * 8;
           for (int p = 0; p < n_delta; ++p) {
-            const float4 a = *reinterpret_cast<const float4*>(dp + p * delta_part_stride);
-            const float4 b = *reinterpret_cast<const float4*>(dp + p * delta_part_stride + 4);
+            const float4 a = __ldcg(reinterpret_cast<const float4*>(dp + p * delta_part_stride));
+            const float4 b = __ldcg(reinterpret_cast<const float4*>(dp + p * delta_part_stride + 4));
             d[0] += a.x; d[1] += a.y; d[2] += a.z; d[3] += a.w;
             d[4] += b.x; d[5] += b.y; d[6] += b.z; d[7] += b.w;
           }
@@ -266,8 +275,9 @@ __global__ __launch_bounds__(256) void argmax_finalize_kernel(const unsigned lon
                                                               long long* __restrict__ next_ids,
                                                               long long* __restrict__ input_ids,
                                                               long long* __restrict__ positions,
-                                                              int pos_numel) {
+                                                              int pos_numel, long long* step_counter) {
   pdl_enter();
+  if (step_counter && blockIdx.x == 0 && threadIdx.x == 0) *step_counter += 1;
   __shared__ unsigned long long s_best[8];
   const int t = blockIdx.x;
   unsigned long long best = 0;
@@ -363,8 +373,12 @@ cudaError_t launch_rmsnorm(const void* x, long long xs, const void* w, int wd, v
 
 cudaError_t launch_add_rmsnorm(void* h, void* h_out, const void* delta, int dd, int nd,
                                long long dps, long long drs, const void* w, int wd, void* y,
-                               int rows, int cols, float eps, cudaStream_t st) {
-  launch_kernel(add_rmsnorm_kernel, rows, kNormThreads, 0, st, reinterpret_cast<bf16*>(h), reinterpret_cast<bf16*>(h_out), delta, dd, nd, dps, drs, w, wd, reinterpret_cast<bf16*>(y), cols, eps);
+                               int rows, int cols, float eps, cudaStream_t st, const PeerTable* peers,
+                               int layer) {
+  PeerTable none = {};
+  launch_kernel(add_rmsnorm_kernel, rows, kNormThreads, 0, st, reinterpret_cast<bf16*>(h),
+                reinterpret_cast<bf16*>(h_out), delta, dd, nd, dps, drs, w, wd, reinterpret_cast<bf16*>(y),
+                cols, eps, peers ? *peers : none, layer);
   return cudaGetLastError();
 }
 
@@ -393,9 +407,10 @@ cudaError_t launch_sum_partials(const float* part, int n_parts, long long ps, lo
 
 cudaError_t launch_argmax_finalize(const unsigned long long* keys, int n_blocks, long long key_stride,
                                    int n_tokens, long long* next_ids, long long* input_ids,
-                                   long long* positions, int pos_numel, cudaStream_t st) {
+                                   long long* positions, int pos_numel, long long* step_counter,
+                                   cudaStream_t st) {
   launch_kernel(argmax_finalize_kernel, n_tokens, 256, 0, st, keys, n_blocks, key_stride, next_ids, input_ids,
-                positions, pos_numel);
+                positions, pos_numel, step_counter);
   return cudaGetLastError();
 }
 

@@ -5,6 +5,34 @@
 
 namespace dsv2 {
 
+// Expert-parallel peer table: every rank's peer-visible buffer as mapped in this process
+// (base[rank] is local), with the same layout in every buffer:
+//   xg   [world * rows_per_rank, hidden] bf16   normalised MoE inputs of all rows
+//   ids  [world * rows_per_rank, 6] int32, w [...] fp32   their top-6 routing
+//   part [rows_per_rank, 8, hidden] fp32         slot outputs of this rank's rows
+//   ctr  two uint64 counters (128 B apart): dispatch arrivals, combine arrivals
+// world == 0: single GPU (no peers).
+constexpr int kMaxPeers = 8;
+struct PeerTable {
+  int world;
+  int rank;
+  char* base[kMaxPeers];
+  long long xg_off, ids_off, w_off, part_off, ctr_off;
+  int rows_per_rank;
+  int n_moe;                  // MoE layers per step
+  const long long* epoch;     // completed steps of this rank
+};
+
+__device__ __forceinline__ unsigned long long* peer_ctr(const PeerTable& t, int rank, int which) {
+  return reinterpret_cast<unsigned long long*>(t.base[rank] + t.ctr_off + which * 128);
+}
+// value of a counter once every rank has signalled layer `layer` of the current step
+__device__ __forceinline__ unsigned long long peer_target(const PeerTable& t, int layer,
+                                                          unsigned long long per_rank) {
+  const unsigned long long e = static_cast<unsigned long long>(*t.epoch);
+  return (e * t.n_moe + layer + 1) * static_cast<unsigned long long>(t.world) * per_rank;
+}
+
 struct RouterParams {
   const bf16* x;           // [rows, hidden] normalised activations
   long long x_row_stride;
@@ -19,8 +47,6 @@ struct RouterParams {
   long long* topk_ids;     // [rows, 6] int64 (may be nullptr)
   int* topk_ids32;         // [rows, 6] int32 (bucketing input)
   float* topk_w;           // [rows, 6]
-  unsigned int* ticket;    // one zero-initialised counter, reset by the last CTA
-  int experts_per_cta;     // 8 (small batches, softmax in the last CTA) or n_experts
   // bucketing (skipped when group_offsets == nullptr)
   int expert_lo;           // first local expert
   int n_local;             // local routed experts
@@ -31,6 +57,8 @@ struct RouterParams {
   float* route_weight;
   int gather_x;            // copy each route's x row into gather_out (expert order)
   void* gather_out;
+  PeerTable peers;         // world > 0: write x / ids / weights of these rows to every rank
+  int row_base;            // global index of this rank's first row
 };
 
 struct MlaPrepParams {
@@ -76,7 +104,8 @@ struct MlaDecodeParams {
 cudaError_t launch_rmsnorm(const void*, long long, const void*, int, void*, long long, int, int,
                            float, cudaStream_t);
 cudaError_t launch_add_rmsnorm(void*, void*, const void*, int, int, long long, long long,
-                               const void*, int, void*, int, int, float, cudaStream_t);
+                               const void*, int, void*, int, int, float, cudaStream_t,
+                               const PeerTable* peers = nullptr, int layer = 0);
 cudaError_t launch_embed_rmsnorm(const long long*, const void*, long long, const void*, int, void*,
                                  void*, int, int, float, cudaStream_t);
 cudaError_t launch_residual_add(const void*, const void*, void*, long long, cudaStream_t);
@@ -91,11 +120,13 @@ cudaError_t launch_copy_token_to_cache(const void*, const long long*, void*, con
 cudaError_t launch_advance_positions(long long*, int, cudaStream_t);
 cudaError_t launch_argmax_finalize(const unsigned long long* keys, int n_blocks, long long key_stride,
                                    int n_tokens, long long* next_ids, long long* input_ids,
-                                   long long* positions, int pos_numel, cudaStream_t st);
+                                   long long* positions, int pos_numel, long long* step_counter,
+                                   cudaStream_t st);
 // router.cu
 cudaError_t launch_router(const RouterParams&, cudaStream_t);
 cudaError_t launch_bucket(const int*, const float*, int, int, int, int, int, int*, int*, int*,
-                          float*, const void*, long long, void*, int, cudaStream_t);
+                          float*, const void*, long long, void*, int, cudaStream_t,
+                          const PeerTable* peers, int layer);
 cudaError_t launch_softmax_topk(const float*, int, int, float, long long*, int*, float*,
                                 cudaStream_t);
 cudaError_t launch_gather_rows(const void*, long long, const int*, const int*, int, void*, int,

@@ -151,6 +151,32 @@ __global__ __launch_bounds__(kRtThreads) void router_topk_kernel(const RouterPar
   if (warp < nt)
     softmax_topk_warp(s_logits[warp], p.n_experts, p.scaling, row0 + warp, p.topk_ids, p.topk_ids32,
                       p.topk_w);
+  if (p.peers.world > 0) {
+    // expert-parallel dispatch: this CTA's rows (normalised x, top-6 ids and weights) go
+    // to every rank's buffer at their global row, then one arrival per rank
+    __syncthreads();
+    const PeerTable& pt = p.peers;
+    const long long g0 = static_cast<long long>(p.row_base) + row0;
+    for (int q = 0; q < pt.world; ++q) {
+      bf16* xg = reinterpret_cast<bf16*>(pt.base[q] + pt.xg_off) + g0 * p.hidden;
+      for (int i = tid; i < nt * nch; i += kRtThreads) {
+        const int t = i / nch, c = i % nch;
+        *reinterpret_cast<uint4*>(xg + static_cast<long long>(t) * p.hidden + c * 8) =
+            *reinterpret_cast<const uint4*>(&s_x[t][c * 8]);
+      }
+      int* ig = reinterpret_cast<int*>(pt.base[q] + pt.ids_off) + g0 * kTopK;
+      float* wg = reinterpret_cast<float*>(pt.base[q] + pt.w_off) + g0 * kTopK;
+      for (int i = tid; i < nt * kTopK; i += kRtThreads) {
+        ig[i] = p.topk_ids32[row0 * kTopK + i];
+        wg[i] = p.topk_w[row0 * kTopK + i];
+      }
+    }
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence_system();
+      for (int q = 0; q < pt.world; ++q) red_release_sys_add_u64(peer_ctr(pt, q, 0), 1ull);
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------------
@@ -171,10 +197,22 @@ struct RouteParams {
   bf16* gout;              // optional gather destination [routes, cols]
   int cols;
   int tok_per_cta;
+  PeerTable peers;         // world > 0: ids / weights / x were dispatched by every rank
+  int layer;               // MoE layer index (expected dispatch arrivals)
 };
 
 __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams p) {
   pdl_enter();
+  if (p.peers.world > 0) {
+    // every rank's router has written its rows into this rank's buffer
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+      const unsigned long long per_rank = (p.peers.rows_per_rank + kRtTok - 1) / kRtTok;
+      s_ok = wait_counter_sys(peer_ctr(p.peers, p.peers.rank, 0), peer_target(p.peers, p.layer, per_rank));
+    }
+    __syncthreads();
+    if (!s_ok) return;
+  }
   __shared__ int s_total[kMaxExperts];
   __shared__ int s_before[kMaxExperts];
   __shared__ int s_off[kMaxExperts + 3];
@@ -190,7 +228,7 @@ __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams 
   const int n_routes = p.rows * kTopK;
   const int r_first = tok0 * kTopK;
   for (int r = tid; r < n_routes; r += kRouteThreads) {
-    const int e = p.ids32[r] - p.expert_lo;
+    const int e = __ldcg(p.ids32 + r) - p.expert_lo;
     if (e >= 0 && e < p.n_local) {
       atomicAdd(&s_total[e], 1);
       if (r < r_first) atomicAdd(&s_before[e], 1);
@@ -221,7 +259,7 @@ __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams 
   // this CTA's routes, in (token, k) order
   const int my_routes = ntok * kTopK;
   for (int i = tid; i < my_routes; i += kRouteThreads) {
-    const int e = p.ids32[r_first + i] - p.expert_lo;
+    const int e = __ldcg(p.ids32 + r_first + i) - p.expert_lo;
     s_e[i] = (e >= 0 && e < p.n_local) ? e : -1;
   }
   __syncthreads();
@@ -238,7 +276,7 @@ __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams 
       const int b = r / kTopK, k = r % kTopK;
       p.route_token[pos] = b;
       p.route_slot[pos] = b * kSlots + k;
-      p.route_weight[pos] = p.tw[r];
+      p.route_weight[pos] = __ldcg(p.tw + r);
       s_tok[i] = b;
     }
     s_pos[i] = pos;
@@ -274,7 +312,7 @@ __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams 
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const int c = c0 + u * 32 + lane;
-        if (c < n16) v[u] = src[c];
+        if (c < n16) v[u] = __ldcg(src + c);
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
@@ -312,8 +350,11 @@ __global__ void gather_rows_kernel(const bf16* __restrict__ x, long long x_row_s
 static cudaError_t launch_route(const int* ids32, const float* tw, int rows, int expert_lo,
                                 int n_local, int shared_lo, int shared_hi, int* go, int* rt,
                                 int* rs, float* rw, const bf16* gx, long long gxs, bf16* gout,
-                                int cols, cudaStream_t st) {
-  RouteParams q;
+                                int cols, cudaStream_t st, const PeerTable* peers = nullptr,
+                                int layer = 0) {
+  RouteParams q = {};
+  if (peers) q.peers = *peers;
+  q.layer = layer;
   q.ids32 = ids32;
   q.tw = tw;
   q.rows = rows;
@@ -348,9 +389,11 @@ cudaError_t launch_router(const RouterParams& p, cudaStream_t st) {
 
 cudaError_t launch_bucket(const int* ids32, const float* tw, int rows, int expert_lo, int n_local,
                           int shared_lo, int shared_hi, int* go, int* rt, int* rs, float* rw,
-                          const void* gx, long long gxs, void* gout, int cols, cudaStream_t st) {
+                          const void* gx, long long gxs, void* gout, int cols, cudaStream_t st,
+                          const PeerTable* peers, int layer) {
   return launch_route(ids32, tw, rows, expert_lo, n_local, shared_lo, shared_hi, go, rt, rs, rw,
-                      reinterpret_cast<const bf16*>(gx), gxs, reinterpret_cast<bf16*>(gout), cols, st);
+                      reinterpret_cast<const bf16*>(gx), gxs, reinterpret_cast<bf16*>(gout), cols, st,
+                      peers, layer);
 }
 
 cudaError_t launch_softmax_topk(const float* logits, int rows, int n_experts, float scaling,

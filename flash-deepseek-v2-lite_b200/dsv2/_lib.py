@@ -50,12 +50,20 @@ class LinearArgs(ctypes.Structure):
     ]
 
 
+class PeerTable(ctypes.Structure):
+    _fields_ = [
+        ("world", c_i32), ("rank", c_i32), ("base", c_vp * 8),
+        ("xg_offset", c_i64), ("ids_offset", c_i64), ("w_offset", c_i64), ("part_offset", c_i64),
+        ("ctr_offset", c_i64), ("rows_per_rank", c_i32), ("n_moe_layers", c_i32), ("epoch", c_vp),
+    ]
+
+
 class MoeArgs(ctypes.Structure):
     _fields_ = [
         ("gate_up", c_vp), ("down", c_vp), ("n_groups", c_i32), ("hidden", c_i32), ("inter", c_i32),
         ("x_sorted", c_vp), ("h", c_vp), ("x_rows", c_i32), ("group_offsets", c_vp),
         ("max_routes_per_group", c_i32), ("route_slot", c_vp), ("route_weight", c_vp), ("y", c_vp),
-        ("sync", c_vp), ("tile_tokens", c_i32),
+        ("sync", c_vp), ("peers", ctypes.POINTER(PeerTable)), ("tile_tokens", c_i32),
     ]
 
 
@@ -68,6 +76,7 @@ class RouterArgs(ctypes.Structure):
         ("gather_out", c_vp),
         ("expert_lo", c_i32), ("n_local", c_i32), ("shared_lo", c_i32), ("shared_hi", c_i32),
         ("group_offsets", c_vp), ("route_token", c_vp), ("route_slot", c_vp), ("route_weight", c_vp),
+        ("peers", ctypes.POINTER(PeerTable)), ("row_base", c_i32),
     ]
 
 
@@ -100,7 +109,12 @@ _SIGNATURES = {
     "dsv2_get_device_error": ([ctypes.POINTER(c_i32), c_i32], c_i32),
     "dsv2_rmsnorm": ([c_vp, c_i64, c_vp, c_i32, c_vp, c_i64, c_i32, c_i32, c_f32, c_vp], c_i32),
     "dsv2_add_rmsnorm": ([c_vp, c_vp, c_vp, c_i32, c_i32, c_i64, c_i64, c_vp, c_i32, c_vp, c_i32, c_i32,
-                          c_f32, c_vp], c_i32),
+                          c_f32, ctypes.POINTER(PeerTable), c_i32, c_vp], c_i32),
+    "dsv2_peer_alloc": ([ctypes.c_size_t, ctypes.POINTER(c_vp)], c_i32),
+    "dsv2_peer_free": ([c_vp], c_i32),
+    "dsv2_peer_export": ([c_vp, c_vp], c_i32),
+    "dsv2_peer_import": ([c_vp, ctypes.POINTER(c_vp)], c_i32),
+    "dsv2_peer_close": ([c_vp], c_i32),
     "dsv2_embed_rmsnorm": ([c_vp, c_vp, c_i64, c_vp, c_i32, c_vp, c_vp, c_i32, c_i32, c_f32, c_vp], c_i32),
     "dsv2_residual_add": ([c_vp, c_vp, c_vp, c_i64, c_vp], c_i32),
     "dsv2_silu_mul": ([c_vp, c_vp, c_vp, c_i64, c_vp], c_i32),
@@ -111,12 +125,12 @@ _SIGNATURES = {
     "dsv2_advance_positions": ([c_vp, c_i32, c_vp], c_i32),
     "dsv2_linear": ([ctypes.POINTER(LinearArgs), c_i32, c_vp], c_i32),
     "dsv2_moe": ([ctypes.POINTER(MoeArgs), c_vp], c_i32),
-    "dsv2_lm_head_argmax": ([c_vp, c_i32, c_i32, c_vp, c_i64, c_i32, c_vp, c_i64, c_vp, c_vp, c_vp, c_i32, c_i32,
-                             c_vp], c_i32),
+    "dsv2_lm_head_argmax": ([c_vp, c_i32, c_i32, c_vp, c_i64, c_i32, c_vp, c_i64, c_vp, c_vp, c_vp, c_i32, c_vp,
+                             c_i32, c_vp], c_i32),
     "dsv2_router": ([ctypes.POINTER(RouterArgs), c_vp], c_i32),
     "dsv2_softmax_topk": ([c_vp, c_i32, c_i32, c_f32, c_vp, c_vp, c_vp, c_vp], c_i32),
     "dsv2_moe_bucket": ([c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp,
-                         c_vp, c_i64, c_vp, c_i32, c_vp], c_i32),
+                         c_vp, c_i64, c_vp, c_i32, ctypes.POINTER(PeerTable), c_i32, c_vp], c_i32),
     "dsv2_gather_rows": ([c_vp, c_i64, c_vp, c_vp, c_i32, c_vp, c_i32, c_i32, c_vp], c_i32),
     "dsv2_mla_prep": ([ctypes.POINTER(MlaPrepArgs), c_vp], c_i32),
     "dsv2_mla_decode": ([ctypes.POINTER(MlaDecodeArgs), c_vp], c_i32),
@@ -166,6 +180,34 @@ def check(rc: int, what: str) -> None:
 
 def call(name: str, *args) -> None:
     check(getattr(load(), name)(*args), name)
+
+
+def peer_alloc(nbytes: int) -> int:
+    """cudaMalloc'd, zeroed device buffer that other processes can map (expert parallel)."""
+    ptr = c_vp()
+    check(load().dsv2_peer_alloc(nbytes, ctypes.byref(ptr)), "dsv2_peer_alloc")
+    return int(ptr.value)
+
+
+def peer_export(ptr: int) -> bytes:
+    handle = ctypes.create_string_buffer(64)
+    check(load().dsv2_peer_export(ptr, handle), "dsv2_peer_export")
+    return handle.raw
+
+
+def peer_import(handle: bytes) -> int:
+    ptr = c_vp()
+    buf = ctypes.create_string_buffer(handle, 64)
+    check(load().dsv2_peer_import(buf, ctypes.byref(ptr)), "dsv2_peer_import")
+    return int(ptr.value)
+
+
+def peer_close(ptr: int) -> None:
+    check(load().dsv2_peer_close(ptr), "dsv2_peer_close")
+
+
+def peer_free(ptr: int) -> None:
+    check(load().dsv2_peer_free(ptr), "dsv2_peer_free")
 
 
 def kernel_launches() -> int:

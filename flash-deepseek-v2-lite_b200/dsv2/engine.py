@@ -57,6 +57,20 @@ class DecodeState:
     input_ids: torch.Tensor   # [B] int64: token fed to the next step
 
 
+class _CudaArray:
+    """__cuda_array_interface__ over a raw device pointer (zero-copy torch view)."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3}
+
+
+def _device_view(ptr: int, shape: tuple, dtype: torch.dtype, dev: torch.device) -> torch.Tensor:
+    typestr = {torch.int16: "<i2", torch.int32: "<i4", torch.float32: "<f4"}[dtype]
+    with torch.cuda.device(dev):
+        return torch.as_tensor(_CudaArray(ptr, shape, typestr), device=dev)
+
+
 class DecodeEngine:
     def __init__(self, model, batch: int, max_len: int, family: str = "batch", *,
                  rank: int = 0, world: int = 1, group=None, gate_bias: torch.Tensor | None = None,
@@ -162,6 +176,58 @@ class DecodeEngine:
                 self.moe_local = torch.zeros((B, 1, HIDDEN), device=dev, dtype=f32)
         self.logits = torch.zeros((B if self.keep_logits else 1, self.vocab), device=dev, dtype=bf)
         self.argmax_keys = torch.zeros(((self.vocab + 15) // 16) * B, device=dev, dtype=i64)
+        self.step_count = torch.zeros(1, device=dev, dtype=i64)   # steps completed (peer epoch)
+        self.peers = None
+        if moe and self.world > 1 and self.family == ops.FAMILY_BATCH:
+            self._setup_peers(len(moe))
+
+    def _setup_peers(self, n_moe: int) -> None:
+        """Expert parallel over NVLink peer memory (batch family): one buffer per rank holding
+        [xg | ids | w | part | counters] (see dsv2_peer_table in include/dsv2.h), mapped by
+        every rank.  The router dispatches into every rank's xg / ids / w, the fused MoE
+        combines each routed slot into its owner's part; no collective runs in the step."""
+        import torch.distributed as dist
+        from . import _lib
+        B, Ball, W = self.B, self.B_all, self.world
+
+        def up(n):
+            return (n + 255) // 256 * 256
+        off_xg = 0
+        off_ids = up(off_xg + Ball * HIDDEN * 2)
+        off_w = up(off_ids + Ball * TOPK * 4)
+        off_part = up(off_w + Ball * TOPK * 4)
+        off_ctr = up(off_part + B * SLOTS * HIDDEN * 4)
+        total = off_ctr + 256
+        torch.cuda.synchronize(self.dev)
+        local = _lib.peer_alloc(total)
+        handles = [None] * W
+        dist.all_gather_object(handles, _lib.peer_export(local), group=self.group)
+        bases = [local if q == self.rank else _lib.peer_import(handles[q]) for q in range(W)]
+        t = _lib.PeerTable()
+        t.world, t.rank = W, self.rank
+        for q in range(W):
+            t.base[q] = bases[q]
+        t.xg_offset, t.ids_offset, t.w_offset, t.part_offset, t.ctr_offset = off_xg, off_ids, off_w, off_part, off_ctr
+        t.rows_per_rank, t.n_moe_layers = B, n_moe
+        t.epoch = self.step_count.data_ptr()
+        self.peers = t
+        self._peer_local, self._peer_remote = local, [b for q, b in enumerate(bases) if q != self.rank]
+        self.x_g = _device_view(local + off_xg, (Ball, HIDDEN), torch.int16, self.dev).view(torch.bfloat16)
+        self.ids_g = _device_view(local + off_ids, (Ball, TOPK), torch.int32, self.dev)
+        self.w_g = _device_view(local + off_w, (Ball, TOPK), torch.float32, self.dev)
+        self.part_peer = _device_view(local + off_part, (B, SLOTS, HIDDEN), torch.float32, self.dev)
+        dist.barrier(group=self.group)
+
+    def close(self) -> None:
+        """Unmap the other ranks' peer buffers and free this rank's (expert parallel)."""
+        if self.peers is None:
+            return
+        from . import _lib
+        torch.cuda.synchronize(self.dev)
+        for b in self._peer_remote:
+            _lib.peer_close(b)
+        _lib.peer_free(self._peer_local)
+        self.peers = None
 
     # ------------------------------------------------------------------ layers
     def _linear(self, **kw):
@@ -224,6 +290,21 @@ class DecodeEngine:
         go = self.group_offsets_hist[self.moe_index[li]]
         # batch family: the routing kernel also copies x into expert order for the TMA loads
         gather = self.x_sorted if self.family == ops.FAMILY_BATCH else None
+        if self.peers is not None:
+            # expert parallel over peer memory: dispatch, bucket (waits for every rank's
+            # dispatch), fused MoE writing each slot into its owner's part (+ signal)
+            sh, mi = self.shard, self.moe_index[li]
+            ops.router(x=self.x, w=m.gate_w, scaling=m.scaling, bias=m.gate_bias, logits=self.logits_r,
+                       topk_ids32=self.ids_local, topk_weights=self.w_local, topk_ids64=self.topk_ids64,
+                       peers=self.peers, row_base=sh.row_lo)
+            ops.moe_bucket(self.ids_g, self.w_g, m.expert_lo, m.n_local, sh.row_lo, sh.row_hi, go,
+                           self.route_token, self.route_slot, self.route_weight, gather_src=self.x_g,
+                           gather_out=self.x_sorted, peers=self.peers, moe_layer=mi)
+            ops.moe(gate_up=m.gate_up, down=m.down, x_sorted=self.x_sorted, h=self.h_moe, group_offsets=go,
+                    max_routes_per_group=self.B_all, route_slot=self.route_slot, route_weight=self.route_weight,
+                    y=self.part_peer.view(-1, HIDDEN), sync=self.moe_sync, peers=self.peers)
+            self._moe_pending = mi
+            return self.part_peer
         if self.world == 1:
             ops.router(x=self.x, w=m.gate_w, scaling=m.scaling, bias=m.gate_bias, logits=self.logits_r,
                        topk_ids32=self.topk_ids32, topk_weights=self.topk_w, topk_ids64=self.topk_ids64,
@@ -253,6 +334,7 @@ class DecodeEngine:
         """gate_up + SwiGLU and down + route-weight scaling over local experts + shared halves
         (batch family: one fused persistent launch; small family: two GEMV launches)."""
         if self.family == ops.FAMILY_BATCH and self.fused_moe:
+            # (expert parallel: local slots only, no combine; used to time the GEMMs alone)
             ops.moe(gate_up=m.gate_up, down=m.down, x_sorted=self.x_sorted, h=self.h_moe, group_offsets=go,
                     max_routes_per_group=self.B_all, route_slot=self.route_slot,
                     route_weight=self.route_weight, y=self.partial.view(-1, HIDDEN), sync=self.moe_sync)
@@ -326,9 +408,10 @@ class DecodeEngine:
             trace.setdefault("hidden", []).append(self.h.float().clone())
             trace.setdefault("routes", [])
         delta = None
+        self._moe_pending = None
         for li, lp in enumerate(self.layers):
             if li > 0:
-                ops.add_rmsnorm(self.h, delta, lp.in_norm_w, lp.eps, self.x)
+                self._add_rmsnorm(delta, lp.in_norm_w, lp.eps)
             attn = self._attention(li, lp)
             ops.add_rmsnorm(self.h, attn, lp.post_norm_w, lp.eps, self.x)
             delta = self._dense_mlp(lp) if lp.dense is not None else self._moe(li, lp)
@@ -337,13 +420,23 @@ class DecodeEngine:
                 trace["hidden"].append(self.h.float() + d)
                 if lp.moe is not None:
                     trace["routes"].append(self.topk_ids64.clone())
-        ops.add_rmsnorm(self.h, delta, self.final_norm_w, self.final_eps, self.x)
+        self._add_rmsnorm(delta, self.final_norm_w, self.final_eps)
         if self.keep_logits:  # checking / debugging only: the greedy step needs no logits
             torch.mm(self.x, self.lm_head.t(), out=self.logits)
         # lm_head + greedy argmax in the linear's epilogue; also feeds the token back and
         # advances the positions (src/run.py:585-588)
         ops.lm_head_argmax(w=self.lm_head, x=self.x, keys=self.argmax_keys, next_ids=self.next_ids,
-                           family=self.family, input_ids=self.input_ids, positions=self.positions)
+                           family=self.family, input_ids=self.input_ids, positions=self.positions,
+                           step_counter=self.step_count)
+
+    def _add_rmsnorm(self, delta, w, eps) -> None:
+        """Residual add of the previous sublayer's output + the next RMSNorm; an expert-parallel
+        MoE output first waits for every rank's combine."""
+        if self._moe_pending is not None:
+            ops.add_rmsnorm(self.h, delta, w, eps, self.x, peers=self.peers, moe_layer=self._moe_pending)
+            self._moe_pending = None
+        else:
+            ops.add_rmsnorm(self.h, delta, w, eps, self.x)
 
     # ------------------------------------------------------------------ state
     def set_state(self, positions: torch.Tensor, input_ids: torch.Tensor) -> None:

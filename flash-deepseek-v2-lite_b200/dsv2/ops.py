@@ -14,7 +14,7 @@ import torch
 from . import _lib
 from ._lib import (
     DSV2_BF16, DSV2_F32, EPI_STORE_BF16, EPI_STORE_F32, EPI_SWIGLU, EPI_SCALE_F32,
-    FAMILY_SMALL, FAMILY_BATCH, LinearArgs, MlaDecodeArgs, MlaPrepArgs, MoeArgs, RouterArgs,
+    FAMILY_SMALL, FAMILY_BATCH, LinearArgs, MlaDecodeArgs, MlaPrepArgs, MoeArgs, PeerTable, RouterArgs,
 )
 
 __all__ = [
@@ -59,11 +59,18 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor) -> 
     return out
 
 
+def _peers_ref(peers: PeerTable | None):
+    return None if peers is None else ctypes.byref(peers)
+
+
 def add_rmsnorm(h: torch.Tensor, delta: torch.Tensor | None, w: torch.Tensor | None, eps: float,
-                y: torch.Tensor | None, h_out: torch.Tensor | None = None) -> None:
+                y: torch.Tensor | None, h_out: torch.Tensor | None = None, peers: PeerTable | None = None,
+                moe_layer: int = 0) -> None:
     """h(_out) = bf16(h + sum of delta parts); y = rmsnorm(h(_out)) * w.
 
     delta: None, bf16 [rows, cols], or fp32 [rows, parts, cols] (summed over parts).
+    peers / moe_layer: delta is the expert-parallel part buffer of MoE layer moe_layer
+    (waits for every rank's combine first).
     """
     _cuda(h, "h")
     rows, cols = h.shape
@@ -78,7 +85,8 @@ def add_rmsnorm(h: torch.Tensor, delta: torch.Tensor | None, w: torch.Tensor | N
             raise NotImplementedError("3-D delta (per-slot partials) must be fp32")
         dptr, ddt, nd, dps, drs = delta.data_ptr(), DSV2_F32, delta.shape[1], delta.stride(1), delta.stride(0)
     _lib.call("dsv2_add_rmsnorm", h.data_ptr(), _ptr(h_out), dptr, ddt, nd, dps, drs,
-              _ptr(w), _wdtype(w) if w is not None else DSV2_BF16, _ptr(y), rows, cols, float(eps), stream())
+              _ptr(w), _wdtype(w) if w is not None else DSV2_BF16, _ptr(y), rows, cols, float(eps),
+              _peers_ref(peers), moe_layer, stream())
 
 
 def embed_rmsnorm(ids: torch.Tensor, table: torch.Tensor, w: torch.Tensor, eps: float,
@@ -192,7 +200,8 @@ def linear(*, w: torch.Tensor, n_rows: int, k: int, x: torch.Tensor, y: torch.Te
 
 def moe(*, gate_up: torch.Tensor, down: torch.Tensor, x_sorted: torch.Tensor, h: torch.Tensor,
         group_offsets: torch.Tensor, max_routes_per_group: int, route_slot: torch.Tensor,
-        route_weight: torch.Tensor, y: torch.Tensor, sync: torch.Tensor, tile_tokens: int = 0) -> None:
+        route_weight: torch.Tensor, y: torch.Tensor, sync: torch.Tensor, tile_tokens: int = 0,
+        peers: PeerTable | None = None) -> None:
     """Fused grouped MoE of one layer (batch family): gate_up + SwiGLU -> h, then down scaled
     by the route weight into y[route_slot] (fp32 rows).  See dsv2_moe_args in include/dsv2.h.
     gate_up [G, 2I, H], down [G, H, I] bf16; x_sorted [R, H], h [R, I] bf16; sync int32 [G + 1]
@@ -220,12 +229,14 @@ def moe(*, gate_up: torch.Tensor, down: torch.Tensor, x_sorted: torch.Tensor, h:
     a.route_slot, a.route_weight = route_slot.data_ptr(), route_weight.data_ptr()
     a.y, a.sync = y.data_ptr(), sync.data_ptr()
     a.tile_tokens = tile_tokens
+    if peers is not None:
+        a.peers = ctypes.pointer(peers)
     _lib.call("dsv2_moe", ctypes.byref(a), stream())
 
 
 def lm_head_argmax(*, w: torch.Tensor, x: torch.Tensor, keys: torch.Tensor, next_ids: torch.Tensor,
                    family: int, input_ids: torch.Tensor | None = None,
-                   positions: torch.Tensor | None = None) -> None:
+                   positions: torch.Tensor | None = None, step_counter: torch.Tensor | None = None) -> None:
     """next_ids[t] = argmax over the vocabulary of bf16(x[t] @ w^T) (lowest index on ties),
     without materialising the logits; optionally input_ids = next_ids and positions += 1.
     keys: uint64 (int64) work buffer of at least ceil(vocab / 16) * tokens entries."""
@@ -238,7 +249,7 @@ def lm_head_argmax(*, w: torch.Tensor, x: torch.Tensor, keys: torch.Tensor, next
     n = x.shape[0]
     _lib.call("dsv2_lm_head_argmax", w.data_ptr(), vocab, hidden, x.data_ptr(), x.stride(0), n, keys.data_ptr(),
               keys.numel(), next_ids.data_ptr(), _ptr(input_ids), _ptr(positions),
-              positions.numel() if positions is not None else 0, family, stream())
+              positions.numel() if positions is not None else 0, _ptr(step_counter), family, stream())
 
 
 def router(*, x: torch.Tensor, w: torch.Tensor, scaling: float, logits: torch.Tensor,
@@ -246,9 +257,11 @@ def router(*, x: torch.Tensor, w: torch.Tensor, scaling: float, logits: torch.Te
            bias: torch.Tensor | None = None, gather_out: torch.Tensor | None = None,
            expert_lo: int = 0, n_local: int = 0, shared_lo: int = 0, shared_hi: int = 0,
            group_offsets: torch.Tensor | None = None, route_token: torch.Tensor | None = None,
-           route_slot: torch.Tensor | None = None, route_weight: torch.Tensor | None = None) -> None:
+           route_slot: torch.Tensor | None = None, route_weight: torch.Tensor | None = None,
+           peers: PeerTable | None = None, row_base: int = 0) -> None:
     """Gate logits + softmax + top-6 (+ bucketing when group_offsets is given, + the
-    expert-ordered copy of x into gather_out when given)."""
+    expert-ordered copy of x into gather_out when given; + expert-parallel dispatch of
+    x / ids / weights to every rank's peer buffer when peers is given)."""
     a = RouterArgs()
     a.x = x.data_ptr()
     a.x_row_stride = x.stride(0)
@@ -269,6 +282,9 @@ def router(*, x: torch.Tensor, w: torch.Tensor, scaling: float, logits: torch.Te
     a.route_token = _ptr(route_token)
     a.route_slot = _ptr(route_slot)
     a.route_weight = _ptr(route_weight)
+    if peers is not None:
+        a.peers = ctypes.pointer(peers)
+    a.row_base = row_base
     _lib.call("dsv2_router", ctypes.byref(a), stream())
 
 
@@ -281,12 +297,13 @@ def softmax_topk(logits: torch.Tensor, scaling: float, topk_ids64: torch.Tensor 
 def moe_bucket(topk_ids32: torch.Tensor, topk_weights: torch.Tensor, expert_lo: int, n_local: int,
                shared_lo: int, shared_hi: int, group_offsets: torch.Tensor, route_token: torch.Tensor,
                route_slot: torch.Tensor, route_weight: torch.Tensor, gather_src: torch.Tensor | None = None,
-               gather_out: torch.Tensor | None = None) -> None:
+               gather_out: torch.Tensor | None = None, peers: PeerTable | None = None,
+               moe_layer: int = 0) -> None:
     _lib.call("dsv2_moe_bucket", topk_ids32.data_ptr(), topk_weights.data_ptr(), topk_ids32.shape[0],
               expert_lo, n_local, shared_lo, shared_hi, group_offsets.data_ptr(), route_token.data_ptr(),
               route_slot.data_ptr(), route_weight.data_ptr(), _ptr(gather_src),
               gather_src.stride(0) if gather_src is not None else 0, _ptr(gather_out),
-              gather_src.shape[1] if gather_src is not None else 0, stream())
+              gather_src.shape[1] if gather_src is not None else 0, _peers_ref(peers), moe_layer, stream())
 
 
 def gather_rows(x: torch.Tensor, route_token: torch.Tensor, group_offsets: torch.Tensor,

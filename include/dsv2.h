@@ -14,6 +14,7 @@
 #ifndef DSV2_H
 #define DSV2_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -75,6 +76,40 @@ DSV2_API int64_t dsv2_kernel_launches(void);
  * Synchronous (cudaMemcpyFromSymbol); call outside the hot loop. */
 DSV2_API int dsv2_get_device_error(int* code, int clear);
 
+/* ---- expert parallelism over NVLink peer memory -------------------------------- */
+/* Every rank allocates one peer-visible buffer (dsv2_peer_alloc), exports it
+ * (dsv2_peer_export, a 64-byte handle), the handles are exchanged by the host (e.g.
+ * torch.distributed all_gather_object), and every rank maps the others' buffers
+ * (dsv2_peer_import).  The same layout is used in every buffer (byte offsets):
+ *   xg   [world * rows_per_rank, hidden] bf16   the router's inputs of every row
+ *   ids  [world * rows_per_rank, 6] int32, w [world * rows_per_rank, 6] fp32
+ *   part [rows_per_rank, 8, hidden] fp32         MoE slot outputs of this rank's rows
+ *   ctr  two uint64 arrival counters, 128 bytes apart (zeroed by dsv2_peer_alloc)
+ * With a table whose world > 1: the router writes its rows' inputs and routing into
+ * every rank's buffer and signals (dispatch); the bucketing waits for all ranks'
+ * dispatch of the MoE layer; the fused MoE writes each routed slot output into the
+ * owner rank's part and signals (combine); the add+RMSNorm that consumes a MoE layer's
+ * output waits for every rank's combine.  The expected counts come from *epoch (steps
+ * completed; advanced by dsv2_lm_head_argmax) and the MoE layer index, so every rank
+ * must run the same sequence of steps.  Waits are bounded (device error word).  The
+ * reference runs on one GPU (pack_routed_experts rejects ep_size != 1,
+ * moe_batch.py:325-326); no reference counterpart. */
+typedef struct dsv2_peer_table {
+  int32_t world; /* <= 8; 0 or 1 = single GPU */
+  int32_t rank;
+  void* base[8]; /* base[q] = rank q's buffer as mapped in this process */
+  int64_t xg_offset, ids_offset, w_offset, part_offset, ctr_offset;
+  int32_t rows_per_rank;
+  int32_t n_moe_layers;
+  const int64_t* epoch;
+} dsv2_peer_table;
+
+DSV2_API int dsv2_peer_alloc(size_t bytes, void** ptr);
+DSV2_API int dsv2_peer_free(void* ptr);
+DSV2_API int dsv2_peer_export(const void* ptr, void* handle /* 64 bytes */);
+DSV2_API int dsv2_peer_import(const void* handle, void** ptr);
+DSV2_API int dsv2_peer_close(void* ptr);
+
 /* RMSNorm: y[r] = bf16(x[r] * rsqrt(mean(x[r]^2) + eps) * w), fp32 math, one
  * rounding.  cols % 8 == 0, cols <= 4096.  w_dtype DSV2_BF16 or DSV2_F32.
  * Reference: rmsnorm_triton, triton_kernels/rmsnorm.py:60-95 (kernel :8-57). */
@@ -86,11 +121,14 @@ DSV2_API int dsv2_rmsnorm(const void* x, int64_t x_row_stride, const void* w, in
  * delta_dtype DSV2_BF16: delta rows at delta_row_stride, parts at delta_part_stride;
  * DSV2_F32: same, fp32 (MoE per-slot partials).  n_delta == 0 skips the add.
  * h_out == NULL updates h in place; y == NULL skips the norm.  h rows are contiguous.
+ * peers (may be NULL): delta is the expert-parallel part of MoE layer moe_layer; the
+ * kernel first waits until every rank has combined into it. 
  * Reference: residual_add_triton (attention_prepost.py:191-223) followed by
  * rmsnorm_triton, as applied per decoder layer in src/run.py:459-493. */
 DSV2_API int dsv2_add_rmsnorm(void* h, void* h_out, const void* delta, int delta_dtype, int n_delta,
                      int64_t delta_part_stride, int64_t delta_row_stride, const void* w,
-                     int w_dtype, void* y, int rows, int cols, float eps, void* stream);
+                     int w_dtype, void* y, int rows, int cols, float eps,
+                     const dsv2_peer_table* peers, int moe_layer, void* stream);
 
 /* Embedding gather + first input RMSNorm: h[r] = table[ids[r]]; y[r] = rmsnorm(h[r]) * w.
  * ids are int64; an id outside [0, vocab) sets the device error word and reads row 0.
@@ -223,6 +261,9 @@ typedef struct dsv2_moe_args {
   const float* route_weight;
   float* y;
   int32_t* sync;
+  /* world > 1: route slot s (token * 8 + k, global tokens) is written to rank
+   * s / (8 * rows_per_rank)'s part instead of y, then every rank is signalled */
+  const dsv2_peer_table* peers;
   /* tokens per work item (16..128, multiple of 16); 0 = the largest group's size capped
    * at 128 */
   int32_t tile_tokens;
@@ -239,11 +280,13 @@ DSV2_API int dsv2_moe(const dsv2_moe_args* args, void* stream);
  * x: [n_tokens, hidden] bf16 rows at x_row_stride; hidden % 64 == 0 (batch family) or
  * % 32 == 0 (small).  keys: uint64 work buffer of at least ceil(vocab / 16) * n_tokens
  * entries.  Reference: the greedy step of the decode loop, lm_head + argmax
- * (src/run.py:585-586). */
+ * (src/run.py:585-586).  step_counter (may be NULL) is incremented once: the epoch of
+ * an expert-parallel peer table. */
 DSV2_API int dsv2_lm_head_argmax(const void* w, int vocab, int hidden, const void* x,
                                  int64_t x_row_stride, int n_tokens, uint64_t* keys,
                                  int64_t keys_capacity, int64_t* next_ids, int64_t* input_ids,
-                                 int64_t* positions, int pos_numel, int family, void* stream);
+                                 int64_t* positions, int pos_numel, int64_t* step_counter,
+                                 int family, void* stream);
 
 /* ---- MoE routing ------------------------------------------------------------ */
 /* Gate GEMV (fp32 over bf16 activations) + softmax + top-6, then bucketing (two launches).
@@ -284,6 +327,10 @@ typedef struct dsv2_router_args {
   int32_t* route_token;
   int32_t* route_slot;
   float* route_weight;
+  /* world > 1: also write x / top-6 ids / weights of these rows (global rows
+   * row_base ..) into every rank's buffer and signal (no bucketing here then) */
+  const dsv2_peer_table* peers;
+  int32_t row_base;
 } dsv2_router_args;
 
 DSV2_API int dsv2_router(const dsv2_router_args* args, void* stream);
@@ -294,14 +341,17 @@ DSV2_API int dsv2_softmax_topk(const float* logits, int rows, int n_experts, flo
                       int64_t* topk_ids64, int32_t* topk_ids32, float* topk_weights,
                       void* stream);
 
-/* Bucketing alone (expert parallel: after the all-gather of the top-k results); same
- * outputs as dsv2_router.  gather_out (optional): row i = gather_src[route_token[i]]
- * (row stride gather_src_stride, cols columns).  Reference: moe_batch.py:101-148. */
+/* Bucketing alone (expert parallel: over every rank's rows); same outputs as
+ * dsv2_router.  gather_out (optional): row i = gather_src[route_token[i]] (row stride
+ * gather_src_stride, cols columns).  peers (may be NULL): the ids / weights / gather
+ * source are the peer buffer's, and the kernel first waits for every rank's dispatch of
+ * MoE layer moe_layer.  Reference: moe_batch.py:101-148. */
 DSV2_API int dsv2_moe_bucket(const int32_t* topk_ids32, const float* topk_weights, int rows,
                     int expert_lo, int n_local, int shared_lo, int shared_hi,
                     int32_t* group_offsets, int32_t* route_token, int32_t* route_slot,
                     float* route_weight, const void* gather_src, int64_t gather_src_stride,
-                    void* gather_out, int cols, void* stream);
+                    void* gather_out, int cols, const dsv2_peer_table* peers, int moe_layer,
+                    void* stream);
 
 /* out[r] = x[route_token[r]] for r < group_offsets[n_groups] (r < max_routes): gathers
  * activations into expert-contiguous rows for the batch family.  cols % 8 == 0. */

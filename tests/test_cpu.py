@@ -211,3 +211,24 @@ def test_oracle_restatement_matches_hf_decode_layer(hf2, golden_hf):
     for li in range(len(hidden)):
         err = float((hidden[li][0] - ref[li]).abs().max() / ref[li].abs().max())
         assert err < 2e-2, (li, err)
+
+
+def test_ctypes_structs_match_the_header():
+    """Field order of every args struct in dsv2._lib follows include/dsv2.h."""
+    import re
+    from dsv2 import _lib
+    text = (REPO / "include" / "dsv2.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    for cname, py in (("dsv2_linear_args", _lib.LinearArgs), ("dsv2_router_args", _lib.RouterArgs),
+                      ("dsv2_moe_args", _lib.MoeArgs), ("dsv2_mla_prep_args", _lib.MlaPrepArgs),
+                      ("dsv2_mla_decode_args", _lib.MlaDecodeArgs), ("dsv2_peer_table", _lib.PeerTable)):
+        body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), text, re.S).group(1)
+        names = []
+        for decl in body.split(";"):
+            decl = decl.strip()
+            if not decl:
+                continue
+            for part in decl.split(","):
+                m = re.search(r"(\w+)\s*(\[\d+\])?\s*$", part.strip())
+                names.append(m.group(1))
+        assert names == [f[0] for f in py._fields_], (cname, names, [f[0] for f in py._fields_])

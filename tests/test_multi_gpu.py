@@ -2,10 +2,11 @@
 
 Runs only where at least two GPUs are visible (skipped otherwise).  Each rank owns half
 of the routed experts and half of the rows; the MoE activations are all-gathered and
-the expert outputs reduce-scattered inside the captured decode graph.  The logits of
-every row must match the single-GPU engine's (cosine >= 0.999; the fp32 sums over
-experts are associated differently across ranks) and the greedy tokens of the first
-step must be identical.
+the expert outputs combined inside the captured decode graph: batch family over NVLink
+peer memory (the router writes every rank's inputs, the fused MoE writes each slot into
+its owner's buffer; logits and tokens must be bit-identical to one GPU's), small family
+with NCCL all-gather / reduce-scatter (logits cosine >= 0.999; the fp32 sums over
+experts are associated differently across ranks; first-step tokens identical).
 """
 import os
 import socket
@@ -38,6 +39,7 @@ def _run_engine(model, prompts, family, rank=0, world=1, group=None):
         toks.append(eng.next_ids.cpu())
     torch.cuda.synchronize()
     eng.release()
+    eng.close()
     return torch.stack(logits), torch.stack(toks)
 
 
@@ -81,6 +83,12 @@ def test_expert_parallel_matches_single_gpu(family, tmp_path):
     for r in range(2):
         got = torch.load(f"{out}.{r}")
         rows = slice(r * half, (r + 1) * half)
+        if family == "batch":
+            # peer-memory expert parallelism computes every slot exactly as one GPU does and
+            # sums the 8 slots in the same order: bit-identical logits and tokens
+            assert torch.equal(got["toks"], ref_toks[:, rows])
+            assert torch.equal(got["logits"], ref_logits[:, rows])
+            continue
         assert torch.equal(got["toks"][0], ref_toks[0, rows])
         for s in range(STEPS):
             a, b = got["logits"][s].double(), ref_logits[s, rows].double()
