@@ -149,6 +149,20 @@ int mla_cache_map(const void* cache, int64_t cache_b_stride, int max_len, int ba
                        static_cast<uint64_t>(cache_b_stride) * 2, box_rows, out);
 }
 
+// Balanced mma.sync latent attention: cache / query tensor maps, grid, launch.
+int mla_decode_balanced(const MlaDecodeParams& p, int sms, long long part_slots, cudaStream_t st,
+                        const char* what) {
+  CUtensorMap tm_kv, tm_qa, tm_qp;
+  int rc = mla_cache_map(p.cache, p.cache_b_stride, p.max_len, p.batch, 32, &tm_kv);
+  if (rc) return rc;
+  // q_abs [B][16][512] and q_pe [B][16][64] as {dims, heads, rows} maps with 64 x 16 boxes
+  if ((rc = tensor_map_3d(p.q_abs, 512, 16, static_cast<uint64_t>(p.batch), 1024, 16384, 16, &tm_qa))) return rc;
+  if ((rc = tensor_map_3d(p.q_pe, 64, 16, static_cast<uint64_t>(p.batch), 128, 2048, 16, &tm_qp))) return rc;
+  const int grid = mla_decode_grid(p, sms, part_slots);
+  if (grid <= 0) return fail(DSV2_ERR_INVALID, "%s: no partial slots", what);
+  return check_launch(launch_mla_decode(p, tm_kv, tm_qa, tm_qp, grid, st), what);
+}
+
 // dsv2_peer_table -> kernel-side PeerTable (world 0 when NULL or single GPU)
 int to_peers(const dsv2_peer_table* t, PeerTable* out) {
   *out = PeerTable{};
@@ -692,17 +706,26 @@ int dsv2_mla_prep(const dsv2_mla_prep_args* a, void* stream) {
 int dsv2_mla_decode(const dsv2_mla_decode_args* a, void* stream) {
   if (!a || !a->q_abs || !a->q_pe || !a->cache || !a->positions || !a->o_part || !a->ml_part || !a->o_lat)
     return fail(DSV2_ERR_INVALID, "mla_decode: null pointer");
-  if (a->split_len <= 0 || a->split_len % 64)
-    return fail(DSV2_ERR_INVALID, "mla_decode: split_len %d must be a positive multiple of 64", a->split_len);
-  if (static_cast<long long>(a->n_splits) * a->split_len < a->max_len)
-    return fail(DSV2_ERR_INVALID, "mla_decode: n_splits * split_len < max_len");
+  const bool tc = a->family == DSV2_FAMILY_BATCH;
+  if (!tc && a->family != DSV2_FAMILY_SMALL) return fail(DSV2_ERR_INVALID, "mla_decode: family %d", a->family);
+  if (a->split_len <= 0 || a->split_len % (tc ? 64 : 32))
+    return fail(DSV2_ERR_INVALID, "mla_decode: split_len %d must be a positive multiple of %d", a->split_len,
+                tc ? 64 : 32);
+  if (a->max_len <= 0 || a->n_splits <= 0) return fail(DSV2_ERR_INVALID, "mla_decode: max_len / n_splits");
+  if (tc && static_cast<long long>(a->n_splits) * a->split_len < a->max_len)
+    return fail(DSV2_ERR_INVALID, "mla_decode(batch): n_splits * split_len < max_len");
+  if (!tc && !a->row_sync) return fail(DSV2_ERR_INVALID, "mla_decode: row_sync (int32[batch], zeroed) is required");
+  if (tc && a->row_sync) return fail(DSV2_ERR_UNSUPPORTED, "mla_decode(batch): row_sync is not supported");
+  if (!tc && static_cast<long long>(a->batch) * a->n_splits < 2)
+    return fail(DSV2_ERR_INVALID, "mla_decode: batch * n_splits must give at least 2 partial slots");
   if (a->pos_numel != 1 && a->pos_numel != a->batch)
     return fail(DSV2_ERR_INVALID, "mla_decode: positions numel %d for batch %d", a->pos_numel, a->batch);
   if (!aligned16(a->q_abs) || !aligned16(a->q_pe) || !aligned16(a->cache) || a->cache_b_stride % 8 ||
       !aligned16(a->o_part))
     return fail(DSV2_ERR_INVALID, "mla_decode: operands must be 16-byte aligned");
   if (a->batch <= 0) return DSV2_OK;
-  int rc = ensure_init(nullptr);
+  int sms = 0;
+  int rc = ensure_init(&sms);
   if (rc) return rc;
   MlaDecodeParams p = {};
   p.q_abs = reinterpret_cast<const bf16*>(a->q_abs);
@@ -720,50 +743,44 @@ int dsv2_mla_decode(const dsv2_mla_decode_args* a, void* stream) {
   p.o_lat = reinterpret_cast<bf16*>(a->o_lat);
   p.inputs_prior = a->inputs_prior != 0;
   p.row_sync = a->row_sync;
+  p.batch = a->batch;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   CUtensorMap tm_kv;
-  if (a->family == DSV2_FAMILY_BATCH) {
-    if (a->row_sync) return fail(DSV2_ERR_UNSUPPORTED, "mla_decode(batch): row_sync is not supported");
+  if (tc) {
     if ((rc = mla_cache_map(a->cache, a->cache_b_stride, a->max_len, a->batch, 64, &tm_kv))) return rc;
     rc = check_launch(launch_mla_tc(p, tm_kv, a->batch, st), "mla_decode(batch)");
-  } else {
-    if (a->family != DSV2_FAMILY_SMALL) return fail(DSV2_ERR_INVALID, "mla_decode: family %d", a->family);
-    if ((rc = mla_cache_map(a->cache, a->cache_b_stride, a->max_len, a->batch, 32, &tm_kv))) return rc;
-    rc = check_launch(launch_mla_decode(p, tm_kv, a->batch, st), "mla_decode");
+    if (rc) return rc;
+    return check_launch(launch_mla_combine(p, a->batch, st), "mla_combine");
   }
-  if (rc) return rc;
-  return check_launch(launch_mla_combine(p, a->batch, st), "mla_combine");
+  return mla_decode_balanced(p, sms, static_cast<long long>(a->batch) * a->n_splits, st, "mla_decode");
 }
 
-// Same computation as dsv2_mla_decode, with the split partials kept in the library's
-// fixed device array instead of caller buffers (no allocation of any kind here).
+// Same computation as dsv2_mla_decode (mma.sync kernel), with the partials and the row
+// tickets kept in the library's fixed device array instead of caller buffers (no
+// allocation of any kind here).
 int dsv2_mla_decode_noalloc(const void* q_abs, const void* q_pe, const void* cache,
                             int64_t cache_b_stride, int max_len, const int64_t* positions,
                             int pos_numel, float softmax_scale, int split_len, void* o_lat,
                             int batch, void* stream) {
   if (!q_abs || !q_pe || !cache || !positions || !o_lat)
     return fail(DSV2_ERR_INVALID, "mla_decode_noalloc: null pointer");
-  if (split_len <= 0 || split_len % 64 || max_len <= 0)
-    return fail(DSV2_ERR_INVALID, "mla_decode_noalloc: split_len %d must be a positive multiple of 64",
+  if (split_len <= 0 || split_len % 32 || max_len <= 0)
+    return fail(DSV2_ERR_INVALID, "mla_decode_noalloc: split_len %d must be a positive multiple of 32",
                 split_len);
   if (pos_numel != 1 && pos_numel != batch)
     return fail(DSV2_ERR_INVALID, "mla_decode_noalloc: positions numel %d for batch %d", pos_numel, batch);
   if (!aligned16(q_abs) || !aligned16(q_pe) || !aligned16(cache) || cache_b_stride % 8)
     return fail(DSV2_ERR_INVALID, "mla_decode_noalloc: operands must be 16-byte aligned");
   if (batch <= 0) return DSV2_OK;
-  const long long n_splits = (static_cast<long long>(max_len) + split_len - 1) / split_len;
-  if (static_cast<long long>(batch) * n_splits > kNoAllocMaxParts)
-    return fail(DSV2_ERR_INVALID,
-                "mla_decode_noalloc: batch * ceil(max_len / split_len) = %lld exceeds the %d split "
-                "partials of the built-in scratch; raise split_len or use dsv2_mla_decode",
-                static_cast<long long>(batch) * n_splits, kNoAllocMaxParts);
-  int rc = ensure_init(nullptr);
+  if (batch > kNoAllocMaxRows)
+    return fail(DSV2_ERR_INVALID, "mla_decode_noalloc: batch %d exceeds the %d row tickets of the built-in "
+                "scratch; use dsv2_mla_decode", batch, kNoAllocMaxRows);
+  int sms = 0;
+  int rc = ensure_init(&sms);
   if (rc) return rc;
   float* scratch = nullptr;
   cudaError_t e = mla_noalloc_scratch(&scratch);
   if (e != cudaSuccess) return check_launch(e, "mla_decode_noalloc: scratch address");
-  float* o_part = scratch;
-  float* ml_part = scratch + static_cast<size_t>(kNoAllocMaxParts) * kHeads * kLatent;
   MlaDecodeParams p = {};
   p.q_abs = reinterpret_cast<const bf16*>(q_abs);
   p.q_pe = reinterpret_cast<const bf16*>(q_pe);
@@ -774,16 +791,13 @@ int dsv2_mla_decode_noalloc(const void* q_abs, const void* q_pe, const void* cac
   p.pos_numel = pos_numel;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.split_len = split_len;
-  p.n_splits = static_cast<int>(n_splits);
-  p.o_part = o_part;
-  p.ml_part = ml_part;
+  p.n_splits = 1;
+  p.o_part = scratch;
+  p.ml_part = scratch + static_cast<size_t>(kNoAllocMaxParts) * kHeads * kLatent;
+  p.row_sync = reinterpret_cast<int*>(scratch + static_cast<size_t>(kNoAllocMaxParts) * kHeads * (kLatent + 2));
   p.o_lat = reinterpret_cast<bf16*>(o_lat);
-  CUtensorMap tm_kv;
-  if ((rc = mla_cache_map(cache, cache_b_stride, max_len, batch, 32, &tm_kv))) return rc;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  rc = check_launch(launch_mla_decode(p, tm_kv, batch, st), "mla_decode_noalloc");
-  if (rc) return rc;
-  return check_launch(launch_mla_combine(p, batch, st), "mla_decode_noalloc: combine");
+  p.batch = batch;
+  return mla_decode_balanced(p, sms, kNoAllocMaxParts, static_cast<cudaStream_t>(stream), "mla_decode_noalloc");
 }
 
 }  // extern "C"

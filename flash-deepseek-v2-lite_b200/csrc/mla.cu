@@ -14,15 +14,19 @@
 // apply_rotary_emb; q and k use the same pairing, so q.k matches the reference's
 // half-split layout.
 //
-// mla_decode_kernel: split-KV flash-decode.  One CTA = (split, sequence), 4 warps.
-// 32-position tiles of the latent cache are staged through a 2-deep cp.async ring in
-// a 128-byte-swizzled layout (conflict-free ldmatrix).  Scores use mma.sync with
-// the 16 heads as M: each warp owns a 144-wide slice of the 576 dims and keeps its
-// query fragments in registers for the whole kernel; slices are summed through
-// shared memory.  P @ V (the latent part) uses mma.sync with each warp owning 128
-// latent dims.  A row that fits one split writes o_lat directly; otherwise the split
-// partials (o, m, l) are merged by the last split of the row to finish (row_sync
-// counters) or, without counters, by mla_combine_kernel.
+// mla_decode_kernel: balanced persistent flash-decode, one CTA per SM.  The 32-position
+// tiles of all rows form one stream cut into equal ranges (ragged batches keep every SM
+// busy); a TMA producer warp keeps 5 tiles of the latent cache (128-byte swizzle) and the
+// per-row query block in flight.  Warp-specialised: 4 score warps (mma.sync, 16 heads as
+// M, 8 positions each, the whole query block in registers) hand bf16 P to 4 P @ V warps
+// (128 latent dims each) through a double buffer, so the scores of one tile overlap the
+// P @ V of the previous one.  A row inside one CTA's range writes o_lat directly; a row
+// cut by a range boundary leaves (o, m, l) partials that the last of its CTAs merges
+// (row tickets), so no second launch follows.
+//
+// mla_combine_kernel merges the split partials of the tcgen05 kernel (mla_tc.cu).
+#include <algorithm>
+
 #include "params.cuh"
 
 namespace dsv2 {
@@ -33,14 +37,18 @@ constexpr int kRope = 64;
 constexpr int kRow = kLatent + kRope;           // 576
 constexpr int kRowBytes = kRow * 2;             // 1152
 constexpr int kChunks = kRow / 64;              // 9 swizzle chunks of 64 dims
-constexpr int kTile = 32;                       // positions per tile (two CTAs per SM)
-constexpr int kStages = 2;
+constexpr int kTile = 32;                       // positions per tile
+constexpr int kStages = 5;                      // cache tiles in flight per CTA (one CTA per SM)
 constexpr int kTileBytes = kTile * kRowBytes;   // 36864
 constexpr int kQBytes = kHeads * kRowBytes;     // 18432
-constexpr int kSRedStride = kTile + 4;          // fp32 row stride of the score-reduction buffer
 constexpr int kPStride = kTile + 8;             // bf16 row stride of P
-constexpr int kMlaPvWarps = 8;                 // warps doing P @ V (64 latent dims each)
-constexpr int kMlaThreads = (kChunks) * 32;     // 9 warps: one 64-dim chunk of the scores each
+constexpr int kScoreWarps = 4;                  // per half of the 576 dims: 8 positions of a tile each
+constexpr int kPvWarps = 4;                     // 128 latent dims each
+constexpr int kProducerWarp = 2 * kScoreWarps + kPvWarps;      // warp 12
+constexpr int kMergeThreads = kProducerWarp * 32;              // 384 compute threads
+constexpr int kMlaThreads = kMergeThreads + 32;                // + the TMA producer warp
+constexpr int kQSteps = kRow / 16 / 2;          // 18 mma k-steps of 16 dims per score half
+constexpr int kMlaMaxCtas = 160;                // merge scratch: 2 x 16 x CTAs floats
 
 // ----------------------------------------------------------------------------
 // mla_prep: latent RMSNorm + RoPE + cache write for the new token, RoPE of q_pe
@@ -134,7 +142,7 @@ __global__ __launch_bounds__(256) void mla_prep_kernel(const MlaPrepParams p) {
 }
 
 // ----------------------------------------------------------------------------
-// split-KV decode
+// balanced persistent decode
 // ----------------------------------------------------------------------------
 
 // byte offset of (row r, 16-byte column c16) inside one 64-dim swizzle chunk of R rows
@@ -142,284 +150,557 @@ __device__ __forceinline__ uint32_t swz(int r, int c16) {
   return static_cast<uint32_t>(r * 128 + ((c16 ^ (r & 7)) << 4));
 }
 
-__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, bool valid) {
-  const int n = valid ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n));
+__device__ __forceinline__ void bar_half0() {   // the 4 softmax (first-half score) warps
+  asm volatile("bar.sync 1, %0;" ::"n"(kScoreWarps * 32) : "memory");
+}
+__device__ __forceinline__ void bar_score() {   // all 8 score warps
+  asm volatile("bar.sync 2, %0;" ::"n"(2 * kScoreWarps * 32) : "memory");
+}
+__device__ __forceinline__ void bar_all() {     // score + P @ V warps
+  asm volatile("bar.sync 3, %0;" ::"n"(kMergeThreads) : "memory");
 }
 
-// o_lat[b] = merge of the first n_active split partials of row b (the splits of a row are
-// contiguous from 0): o = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s, per head.
-// Partials written by other CTAs are read with L1-bypassing loads.
-__device__ __forceinline__ void mla_merge_row(const float* o_part, const float* ml_part, int n_splits,
-                                              int n_active, bf16* o_lat, int b, int tid, int nthreads) {
-  const float* ml = ml_part + (static_cast<long long>(b) * n_splits) * kHeads * 2;
-  for (int i = tid; i < kHeads * kLatent / 4; i += nthreads) {
-    const int h = i / (kLatent / 4), d = (i % (kLatent / 4)) * 4;
-    float M = -INFINITY;
-    for (int s = 0; s < n_active; ++s) {
-      const float l = __ldcg(ml + (s * kHeads + h) * 2 + 1);
-      if (l > 0.f) M = fmaxf(M, __ldcg(ml + (s * kHeads + h) * 2));
-    }
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, den = 0.f;
-    for (int s = 0; s < n_active; ++s) {
-      const float l = __ldcg(ml + (s * kHeads + h) * 2 + 1);
-      if (!(l > 0.f)) continue;
-      const float w = exp2f(__ldcg(ml + (s * kHeads + h) * 2) - M);
-      den += w * l;
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(
-          o_part + ((static_cast<long long>(b) * n_splits + s) * kHeads + h) * kLatent + d));
-      a0 += w * v.x; a1 += w * v.y; a2 += w * v.z; a3 += w * v.w;
-    }
-    const float inv = den > 0.f ? 1.f / den : 0.f;
-    uint2 o;
-    o.x = pack_bf16x2(a0 * inv, a1 * inv);
-    o.y = pack_bf16x2(a2 * inv, a3 * inv);
-    *reinterpret_cast<uint2*>(o_lat + (static_cast<long long>(b) * kHeads + h) * kLatent + d) = o;
+// Attended length of row b (0 .. max_len) and its number of 32-position tiles; a row
+// with nothing to attend still owns one fully masked tile (its output is zero).
+__device__ __forceinline__ int mla_row_len(const MlaDecodeParams& p, int b) {
+  const long long pos = p.positions[p.pos_numel == 1 ? 0 : b];
+  return static_cast<int>(max(0LL, min(static_cast<long long>(p.max_len), pos + 1)));
+}
+__device__ __forceinline__ int mla_tiles_of(int len) { return len > 0 ? (len + kTile - 1) / kTile : 1; }
+
+// Bounded mbarrier wait that gives up at once when this CTA (or any kernel) has already
+// recorded a failure, so that one lost wait cannot turn into a long chain of timeouts.
+__device__ __forceinline__ bool mla_wait(uint64_t* bar, uint32_t parity, volatile int* s_abort) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023) == 1023 &&
+        (*s_abort != 0 || *reinterpret_cast<volatile int*>(&g_device_error) != 0))
+      break;
   }
+  *s_abort = 1;
+  set_device_error(kErrMbarTimeout);
+  return false;
 }
 
-__global__ __launch_bounds__(kMlaThreads, 2) void mla_decode_kernel(const MlaDecodeParams p,
-                                                                   const __grid_constant__ CUtensorMap tm_kv) {
-  // inputs_prior: positions, q_pe and the cache are older than the previous launch, so
-  // the first cache tiles are requested before waiting for it (it writes q_abs)
-  const bool early = p.inputs_prior != 0;
-  if (!early) pdl_enter();
+// Slot of the partial that CTA c holds for a row starting at tile S_b of the stream:
+// 0 when the row is the CTA's first segment, 1 when it is its last one.
+__device__ __forceinline__ int mla_slot(long long S_b, long long cta_start) { return S_b <= cta_start ? 0 : 1; }
+
+// First tile of CTA c's range when T tiles are spread over n CTAs, and the CTA that owns tile t.
+__device__ __forceinline__ long long mla_range_start(long long c, long long T, long long n) { return c * T / n; }
+__device__ __forceinline__ long long mla_owner(long long t, long long T, long long n) {
+  return ((t + 1) * n - 1) / T;
+}
+
+// The whole decode in one launch: the 32-position tiles of all rows form one stream of
+// T = sum_b ceil(len_b / 32) tiles, cut into equal contiguous ranges, one per CTA (one
+// CTA per SM, so ragged batches keep every SM busy to the end).  Each CTA walks its
+// range row by row ("segments"): a row that lies wholly inside the range is normalised
+// and written to o_lat; a row cut by a range boundary leaves (o, m, l) partials in the
+// CTA's slot 0 (first segment) or 1 (last segment), and the last of the row's CTAs to
+// finish merges them (row_sync ticket) — no second launch.
+//
+// Warp roles (warp-specialised, the scores of tile t + 1 overlap P @ V of tile t):
+//  - warps 0-3, scores: warp w owns positions [8w, 8w + 8) of a tile and keeps the whole
+//    16 x 576 query block in registers (36 mma k-steps, 4 accumulator chains), so no
+//    cross-warp reduction of scores is needed; the tile max per head is exchanged
+//    through shared memory (one 128-thread barrier per tile); P (bf16) and the rescale
+//    factor go to a double buffer handed over with mbarriers;
+//  - warps 4-7, P @ V: warp v owns latent dims [128v, 128v + 128);
+//  - warp 8, producer: TMA ring of 5 cache tiles and the per-segment query block.
+__global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDecodeParams p,
+                                                                   const __grid_constant__ CUtensorMap tm_kv,
+                                                                   const __grid_constant__ CUtensorMap tm_qa,
+                                                                   const __grid_constant__ CUtensorMap tm_qp) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* s_kv = smem;                                    // stages x 9 chunks x 32 rows x 128 B
   unsigned char* s_q = smem + kStages * kTileBytes;              // 9 chunks x 16 rows x 128 B
-  float* s_red = reinterpret_cast<float*>(s_q + kQBytes);        // [9][16][kSRedStride]
-  bf16* s_p = reinterpret_cast<bf16*>(s_red + kChunks * kHeads * kSRedStride);  // [16][kPStride]
-  float* s_alpha = reinterpret_cast<float*>(s_p + kHeads * kPStride);           // [16]
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(s_alpha + kHeads);           // [kStages]
-  uint64_t* empty_bar = full_bar + kStages;                                      // [kStages]
+  bf16* s_p = reinterpret_cast<bf16*>(s_q + kQBytes);            // [2][16][kPStride]
+  float* s_max = reinterpret_cast<float*>(s_p + 2 * kHeads * kPStride);  // [2][4][16]
+  float* s_alpha = s_max + 2 * kScoreWarps * kHeads;             // [2][16]
+  float* s_lsum = s_alpha + 2 * kHeads;                          // [4][16]
+  float* s_fin = s_lsum + kScoreWarps * kHeads;                  // [2][16] 1/l of a finished segment
+  float* s_mrg = s_fin + 2 * kHeads;                             // [2][16][kMlaMaxCtas] merge scratch
+  float* s_part = s_mrg + 2 * kHeads * kMlaMaxCtas;              // [2][4][32 lanes][4] second-half scores
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(s_part + 2 * kScoreWarps * 32 * 4);  // [kStages]
+  uint64_t* empty_bar = full_bar + kStages;                      // [kStages]
+  uint64_t* p_full = empty_bar + kStages;                        // [2]
+  uint64_t* p_empty = p_full + 2;                                // [2]
+  uint64_t* q_full = p_empty + 2;
+  uint64_t* q_empty = q_full + 1;
+  int* s_misc = reinterpret_cast<int*>(q_empty + 1);             // [16]
+  long long* s_ll = reinterpret_cast<long long*>(s_misc + 16);   // [2]
+  volatile int* s_abort = s_misc + 12;
 
-  const int split = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int gq = lane >> 2, tq = lane & 3;
-  const long long pos = p.positions[p.pos_numel == 1 ? 0 : b];
-  const int len = static_cast<int>(min(static_cast<long long>(p.max_len), pos + 1));
-  const int s_beg = split * p.split_len;
-  const int s_end = min(len, s_beg + p.split_len);
-  float* mlp = p.ml_part + ((static_cast<long long>(b) * p.n_splits + split) * kHeads) * 2;
-  if (s_beg >= s_end) {
-    if (early) pdl_enter();
-    if (tid < kHeads) {
-      mlp[tid * 2] = -INFINITY;
-      mlp[tid * 2 + 1] = 0.f;
-    }
-    return;
-  }
-  const int n_tiles = (s_end - s_beg + kTile - 1) / kTile;
-  const bool producer = (warp == kMlaPvWarps && lane == 0);
-  // tile ti -> stage ti % 2: 9 TMA boxes of 64 dims x 32 positions (128-byte swizzle);
-  // positions past the split are masked below, past the cache they read as zeros
-  auto load_tile = [&](int ti) {
-    const int st = ti % kStages;
-    mbar_arrive_expect_tx(&full_bar[st], kTileBytes);
-    for (int c = 0; c < kChunks; ++c)
-      tma_load_3d(smem_u32(s_kv + st * kTileBytes + c * (kTile * 128)), &tm_kv, &full_bar[st], c * 64,
-                  s_beg + ti * kTile, b);
-  };
-  if (producer) {
+  const int B = p.batch;
+  const bool early = p.inputs_prior != 0;
+
+  // positions may come from the previous launch unless inputs_prior
+  if (!early) pdl_enter();
+  if (tid == 0) {
     for (int st = 0; st < kStages; ++st) {
       mbar_init(&full_bar[st], 1);
-      mbar_init(&empty_bar[st], kMlaPvWarps);
+      mbar_init(&empty_bar[st], 2 * kScoreWarps + kPvWarps);
     }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&p_full[i], kScoreWarps);
+      mbar_init(&p_empty[i], kPvWarps);
+    }
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 2 * kScoreWarps);
+    *s_abort = 0;
     fence_mbar_init();
-    prefetch_tmap(&tm_kv);
-    load_tile(0);
-    if (n_tiles > 1) load_tile(1);
-  }
-  if (early) pdl_enter();
-
-  // --- stage Q = [q_abs | q_pe] (16 x 576) into swizzled smem
-  for (int i = tid; i < kHeads * kChunks * 8; i += kMlaThreads) {
-    const int h = i / (kChunks * 8), rem = i % (kChunks * 8);
-    const int ch = rem / 8, c16 = rem % 8;
-    const int d = ch * 64 + c16 * 8;
-    const bf16* src = (d < kLatent)
-                          ? p.q_abs + (static_cast<long long>(b) * kHeads + h) * kLatent + d
-                          : p.q_pe + (static_cast<long long>(b) * kHeads + h) * kRope + (d - kLatent);
-    *reinterpret_cast<uint4*>(s_q + ch * (kHeads * 128) + swz(h, c16)) = *reinterpret_cast<const uint4*>(src);
-  }
-  __syncthreads();  // Q and the barriers visible
-
-  // --- query fragments of this warp's 64-dim chunk (warp w scores dims [64w, 64w + 64))
-  uint32_t qa[4][4];
-#pragma unroll
-  for (int ks = 0; ks < 4; ++ks) {
-    const int mi = lane >> 3, ri = lane & 7;
-    const int row = (mi & 1) * 8 + ri;
-    const int c16 = ks * 2 + (mi >> 1);
-    ldmatrix_x4(smem_u32(s_q + warp * (kHeads * 128) + swz(row, c16)), qa[ks][0], qa[ks][1], qa[ks][2],
-                qa[ks][3]);
   }
 
-  // softmax state: threads 0..255, head hs = tid / 16, positions 2*js, 2*js + 1 of a tile
-  const int hs = (tid >> 4) & 15, js = tid & 15;
-  float m_run = -INFINITY, l_run = 0.f;
-  // P @ V accumulators: warps 0..7 own latent dims [64w, 64w + 64)
-  float o_acc[8][4];
+  // --- tile prefix over the rows (every CTA computes the same one): T = all tiles, then
+  // this CTA's range [start, end) and its first row b0 (S_b0 <= start < S_b0 + nt_b0).
+  // One pass when the batch fits the block (the usual case), else two.
+  long long T = 0, start = 0, end = 0, c = blockIdx.x, n_cta = 0;
+  const long long min_tpc = max(1, p.split_len / kTile);
+  int nt_mine = 0, incl = 0;
+  for (int base = 0; base < B; base += kMlaThreads) {
+    const int b = base + tid;
+    const int nt = b < B ? mla_tiles_of(mla_row_len(p, b)) : 0;
+    int v = nt;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) o_acc[j][0] = o_acc[j][1] = o_acc[j][2] = o_acc[j][3] = 0.f;
-  bool ok = true;
-
-  for (int ti = 0; ti < n_tiles; ++ti) {
-    const int stage = ti % kStages;
-    const uint32_t par = static_cast<uint32_t>((ti / kStages) & 1);
-    if (!mbar_wait(&full_bar[stage], par)) ok = false;
-    const unsigned char* kv = s_kv + stage * kTileBytes;
-
-    // --- partial scores over this warp's 64 dims for the 32 positions of the tile
-    {
-      float sc[kTile / 8][4];
-#pragma unroll
-      for (int j = 0; j < kTile / 8; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
-      const unsigned char* kc = kv + warp * (kTile * 128);
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-#pragma unroll
-        for (int np = 0; np < kTile / 16; ++np) {  // pairs of n8 tiles (16 positions)
-          const int mi = lane >> 3, ri = lane & 7;
-          const int r = np * 16 + (mi >> 1) * 8 + ri;
-          const int c16 = ks * 2 + (mi & 1);
-          uint32_t b0, b1, b2, b3;
-          ldmatrix_x4(smem_u32(kc + swz(r, c16)), b0, b1, b2, b3);
-          mma_bf16_16816(sc[2 * np], qa[ks], b0, b1);
-          mma_bf16_16816(sc[2 * np + 1], qa[ks], b2, b3);
-        }
-      }
-      float* red_w = s_red + warp * kHeads * kSRedStride;
-#pragma unroll
-      for (int j = 0; j < kTile / 8; ++j) {
-        const int c = j * 8 + 2 * tq;
-        *reinterpret_cast<float2*>(red_w + gq * kSRedStride + c) = make_float2(sc[j][0], sc[j][1]);
-        *reinterpret_cast<float2*>(red_w + (gq + 8) * kSRedStride + c) = make_float2(sc[j][2], sc[j][3]);
-      }
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += u;
+    }
+    if (lane == 31) s_misc[warp] = v;
+    if (base == 0) {
+      nt_mine = nt;
+      incl = v;
     }
     __syncthreads();
-
-    // --- online softmax (log2 domain) for head hs, positions 2*js, 2*js + 1
-    if (tid < 256) {
-      const int t0 = s_beg + ti * kTile;
-      const int c = 2 * js;
-      float v0 = 0.f, v1 = 0.f;
 #pragma unroll
-      for (int w = 0; w < kChunks; ++w) {
-        const float2 r2 = *reinterpret_cast<const float2*>(s_red + (w * kHeads + hs) * kSRedStride + c);
-        v0 += r2.x;
-        v1 += r2.y;
-      }
-      v0 = (t0 + c < s_end) ? v0 * p.scale_log2 : -INFINITY;
-      v1 = (t0 + c + 1 < s_end) ? v1 * p.scale_log2 : -INFINITY;
-      float mx = fmaxf(v0, v1);
-#pragma unroll
-      for (int o = 1; o < 16; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float m_new = fmaxf(m_run, mx);
-      const float alpha = exp2f(m_run - m_new);
-      const float p0 = exp2f(v0 - m_new), p1 = exp2f(v1 - m_new);
-      float sum = p0 + p1;
-#pragma unroll
-      for (int o = 1; o < 16; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      l_run = l_run * alpha + sum;
-      m_run = m_new;
-      *reinterpret_cast<uint32_t*>(s_p + hs * kPStride + c) = pack_bf16x2(p0, p1);
-      if (js == 0) s_alpha[hs] = alpha;
-    }
+    for (int w = 0; w < kMlaThreads / 32; ++w) T += s_misc[w];
     __syncthreads();
-
-    if (warp < kMlaPvWarps) {
-      // --- O[:, 64*warp .. +64] = alpha * O + P @ V
-      const float a0 = s_alpha[gq], a1 = s_alpha[gq + 8];
+  }
+  n_cta = min(static_cast<long long>(gridDim.x), (T + min_tpc - 1) / min_tpc);
+  if (c >= n_cta) {
+    if (early) pdl_enter();
+    return;
+  }
+  start = mla_range_start(c, T, n_cta);
+  end = mla_range_start(c + 1, T, n_cta);
+  if (B <= kMlaThreads) {
+    // s_misc[0..9] still hold the warp totals of the only chunk
+    long long off = 0;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        o_acc[j][0] *= a0; o_acc[j][1] *= a0;
-        o_acc[j][2] *= a1; o_acc[j][3] *= a1;
+    for (int w = 0; w < kMlaThreads / 32; ++w)
+      if (w < warp) off += s_misc[w];
+    const long long S = off + incl - nt_mine;
+    if (tid < B && S <= start && start < S + nt_mine) {
+      s_ll[0] = S;
+      s_misc[10] = tid;
+    }
+  } else {
+    long long run = 0;
+    for (int base = 0; base < B; base += kMlaThreads) {
+      const int b = base + tid;
+      const int nt = b < B ? mla_tiles_of(mla_row_len(p, b)) : 0;
+      int v = nt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
       }
-      const unsigned char* vc = kv + warp * (kTile * 128);
+      if (lane == 31) s_misc[warp] = v;
+      __syncthreads();
+      long long off = run, total = 0;
 #pragma unroll
-      for (int kk = 0; kk < kTile / 16; ++kk) {
-        uint32_t pa[4];
-        {
-          const int mi = lane >> 3, ri = lane & 7;
-          const int row = (mi & 1) * 8 + ri;
-          const int col = kk * 16 + (mi >> 1) * 8;
-          ldmatrix_x4(smem_u32(s_p + row * kPStride + col), pa[0], pa[1], pa[2], pa[3]);
-        }
-#pragma unroll
-        for (int np = 0; np < 4; ++np) {
-          const int mi = lane >> 3, ri = lane & 7;
-          const int r = kk * 16 + (mi & 1) * 8 + ri;
-          const int c16 = np * 2 + (mi >> 1);
-          uint32_t b0, b1, b2, b3;
-          ldmatrix_x4_trans(smem_u32(vc + swz(r, c16)), b0, b1, b2, b3);
-          mma_bf16_16816(o_acc[2 * np], pa, b0, b1);
-          mma_bf16_16816(o_acc[2 * np + 1], pa, b2, b3);
-        }
+      for (int w = 0; w < kMlaThreads / 32; ++w) {
+        if (w < warp) off += s_misc[w];
+        total += s_misc[w];
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty_bar[stage]);  // this warp is done with the tile
-    } else if (producer && ti + kStages < n_tiles) {
-      // refill this stage once the P @ V warps have released it
-      if (!mbar_wait(&empty_bar[stage], par)) ok = false;
-      else load_tile(ti + kStages);
+      const long long S = off + v - nt;
+      if (b < B && S <= start && start < S + nt) {
+        s_ll[0] = S;
+        s_misc[10] = b;
+      }
+      __syncthreads();
+      run += total;
+      if (run > start) break;  // uniform across the block
     }
   }
-  if (!ok) set_device_error(kErrMbarTimeout);
+  __syncthreads();
+  const long long S0 = s_ll[0];
+  const int b0 = s_misc[10];
 
-  if (len <= p.split_len) {
-    // the whole row fitted in this one split: normalise and write o_lat directly
-    // (no partials, and the merge skips the row)
-    if (tid < 256 && js == 0) s_alpha[hs] = 1.f / l_run;
-    __syncthreads();
-    if (warp < kMlaPvWarps) {
-      const float i0 = s_alpha[gq], i1 = s_alpha[gq + 8];
-      bf16* ob = p.o_lat + static_cast<long long>(b) * kHeads * kLatent;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int d = warp * 64 + j * 8 + 2 * tq;
-        *reinterpret_cast<uint32_t*>(ob + gq * kLatent + d) = pack_bf16x2(o_acc[j][0] * i0, o_acc[j][1] * i0);
-        *reinterpret_cast<uint32_t*>(ob + (gq + 8) * kLatent + d) =
-            pack_bf16x2(o_acc[j][2] * i1, o_acc[j][3] * i1);
+  if (warp == kProducerWarp) {
+    // ================= producer warp: cache tiles and query blocks
+    if (lane == 0) {
+      prefetch_tmap(&tm_kv);
+      prefetch_tmap(&tm_qa);
+      prefetch_tmap(&tm_qp);
+      bool waited = !early, ok = true;
+      int early_rows[kStages];
+      int q_issued = 0, seg = 0;
+      long long g = 0;
+      auto issue_q = [&](int k, int row) {
+        if (k > 0 && ok) ok = mla_wait(q_empty, static_cast<uint32_t>((k - 1) & 1), s_abort);
+        if (!ok) return;
+        mbar_arrive_expect_tx(q_full, kQBytes);
+        for (int ch = 0; ch < kLatent / 64; ++ch)
+          tma_load_3d(smem_u32(s_q + ch * (kHeads * 128)), &tm_qa, q_full, ch * 64, 0, row);
+        tma_load_3d(smem_u32(s_q + (kLatent / 64) * (kHeads * 128)), &tm_qp, q_full, 0, 0, row);
+      };
+      long long S = S0;
+      for (int b = b0; S < end && b < B; ++b, ++seg) {
+        const int len = mla_row_len(p, b), nt = mla_tiles_of(len);
+        const int j0 = static_cast<int>(max(0LL, start - S)), j1 = static_cast<int>(min(static_cast<long long>(nt), end - S));
+        if (seg < kStages) early_rows[seg] = b;
+        for (int j = j0; j < j1; ++j, ++g) {
+          if (!waited && g >= kStages) {
+            pdl_enter();
+            waited = true;
+          }
+          if (waited) {
+            for (; q_issued <= seg; ++q_issued) issue_q(q_issued, q_issued < kStages ? early_rows[q_issued] : b);
+          }
+          const int st = static_cast<int>(g % kStages);
+          if (g >= kStages && ok) ok = mla_wait(&empty_bar[st], static_cast<uint32_t>(((g / kStages) - 1) & 1), s_abort);
+          if (!ok) continue;
+          mbar_arrive_expect_tx(&full_bar[st], kTileBytes);
+          for (int ch = 0; ch < kChunks; ++ch)
+            tma_load_3d(smem_u32(s_kv + st * kTileBytes + ch * (kTile * 128)), &tm_kv, &full_bar[st], ch * 64,
+                        j * kTile, b);
+        }
+        S += nt;
       }
+      if (!waited) pdl_enter();
+      for (; q_issued < seg; ++q_issued) issue_q(q_issued, early_rows[q_issued]);
+      // every issued copy has landed before the CTA may exit (consumed ones at once; after
+      // a failed wait, the ones nobody consumed)
+      for (int st = 0; st < kStages && st < g; ++st) {
+        const long long last = g - 1 - ((g - 1 - st) % kStages);
+        for (uint32_t i = 0; i < (1u << 20) && !mbar_try_wait(&full_bar[st], static_cast<uint32_t>((last / kStages) & 1)); ++i) {
+        }
+      }
+      if (seg > 0)
+        for (uint32_t i = 0; i < (1u << 20) && !mbar_try_wait(q_full, static_cast<uint32_t>((seg - 1) & 1)); ++i) {
+        }
+    } else if (early) {
+      pdl_enter();
     }
     return;
   }
-  // --- write partial results
-  if (warp < kMlaPvWarps) {
-    float* op = p.o_part + ((static_cast<long long>(b) * p.n_splits + split) * kHeads) * kLatent;
+
+  // ================= compute warps (scores: warps 0-3, P @ V: warps 4-7)
+  if (early) pdl_enter();
+  const int gq = lane >> 2, tq = lane & 3;
+  const int mi = lane >> 3, ri = lane & 7;
+  const bool score_role = warp < 2 * kScoreWarps;
+  long long g = 0;   // tiles of this CTA so far (ring slot, P buffer)
+  int seg = 0;
+  long long S = S0;
+
+  // merge of row b (all 384 compute threads; the row's partials are published)
+  auto merge_row = [&](int b, long long Sb, int nt) {
+    const long long c_first = mla_owner(Sb, T, n_cta), c_last = mla_owner(Sb + nt - 1, T, n_cta);
+    const int n_seg = static_cast<int>(c_last - c_first + 1);
+    float* s_m = s_mrg;
+    float* s_l = s_mrg + kHeads * n_seg;
+    auto part_index = [&](int k) -> long long {
+      const long long cc = c_first + k;
+      return cc * 2 + ((k == 0) ? mla_slot(Sb, mla_range_start(cc, T, n_cta)) : 0);
+    };
+    for (int i = tid; i < kHeads * n_seg; i += kMergeThreads) {
+      const int h = i / n_seg, k = i % n_seg;
+      const long long pk = part_index(k);
+      s_m[i] = __ldcg(p.ml_part + (pk * kHeads + h) * 2);
+      s_l[i] = __ldcg(p.ml_part + (pk * kHeads + h) * 2 + 1);
+    }
+    bar_all();
+    if (tid < kHeads) {
+      // w_k = 2^(m_k - M) / sum_k 2^(m_k - M) l_k
+      float M = -INFINITY;
+      for (int k = 0; k < n_seg; ++k)
+        if (s_l[tid * n_seg + k] > 0.f) M = fmaxf(M, s_m[tid * n_seg + k]);
+      float den = 0.f;
+      for (int k = 0; k < n_seg; ++k) {
+        const float l = s_l[tid * n_seg + k];
+        const float w = l > 0.f ? exp2f(s_m[tid * n_seg + k] - M) : 0.f;
+        s_m[tid * n_seg + k] = w;
+        den += w * l;
+      }
+      const float inv = den > 0.f ? 1.f / den : 0.f;
+      for (int k = 0; k < n_seg; ++k) s_m[tid * n_seg + k] *= inv;
+    }
+    bar_all();
+    constexpr int kItems = kHeads * kLatent / 4;
+    constexpr int kPer = 3;   // float4 outputs per thread and pass (two passes cover 384 x 6 >= 2048)
+    static_assert(2 * kPer * kMergeThreads >= kItems, "merge passes do not cover the row");
+    bf16* ob = p.o_lat + static_cast<long long>(b) * kHeads * kLatent;
+#pragma unroll 1
+    for (int pass = 0; pass < 2; ++pass) {
+      float4 acc[kPer];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int d = warp * 64 + j * 8 + 2 * tq;
-      *reinterpret_cast<float2*>(op + gq * kLatent + d) = make_float2(o_acc[j][0], o_acc[j][1]);
-      *reinterpret_cast<float2*>(op + (gq + 8) * kLatent + d) = make_float2(o_acc[j][2], o_acc[j][3]);
+      for (int r = 0; r < kPer; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+      for (int k = 0; k < n_seg; ++k) {
+        const float4* o0 = reinterpret_cast<const float4*>(p.o_part + part_index(k) * kHeads * kLatent);
+        float4 v0[kPer];
+#pragma unroll
+        for (int r = 0; r < kPer; ++r) {
+          const int i = tid + (pass * kPer + r) * kMergeThreads;
+          v0[r] = i < kItems ? __ldcg(o0 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int r = 0; r < kPer; ++r) {
+          const int i = tid + (pass * kPer + r) * kMergeThreads;
+          const float w0 = i < kItems ? s_m[(i / (kLatent / 4)) * n_seg + k] : 0.f;
+          acc[r].x += w0 * v0[r].x;
+          acc[r].y += w0 * v0[r].y;
+          acc[r].z += w0 * v0[r].z;
+          acc[r].w += w0 * v0[r].w;
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kPer; ++r) {
+        const int i = tid + (pass * kPer + r) * kMergeThreads;
+        if (i < kItems) {
+          uint2 o;
+          o.x = pack_bf16x2(acc[r].x, acc[r].y);
+          o.y = pack_bf16x2(acc[r].z, acc[r].w);
+          *reinterpret_cast<uint2*>(ob + 4 * i) = o;
+        }
+      }
     }
-  }
-  if (tid < 256 && js == 0) {
-    mlp[hs * 2] = m_run;
-    mlp[hs * 2 + 1] = l_run;
-  }
-  if (!p.row_sync) return;  // mla_combine_kernel merges the splits
-  // The last split of the row to finish merges all of them (no separate launch): the
-  // partial stores above are published by a fence + counter increment, the last
-  // arriver reads the others' partials through L2 and returns the counter to zero.
-  __syncthreads();
-  int* s_flag = reinterpret_cast<int*>(s_alpha);
-  if (tid == 0) {
-    const int n_active = (len + p.split_len - 1) / p.split_len;
-    __threadfence();
-    const int t = atomicAdd(&p.row_sync[b], 1);
-    const bool last = (t == n_active - 1);
-    if (last) {
-      p.row_sync[b] = 0;
+    bar_all();  // s_mrg is free again
+  };
+
+  // ticket of a partial row (after both roles wrote their part); the last of the row's
+  // CTAs merges it after its own range is done (a CTA holds at most two cut rows)
+  int pend_b[2] = {0, 0}, pend_nt[2] = {0, 0}, n_pend = 0;
+  long long pend_S[2] = {0, 0};
+  auto finish_partial = [&](int b, long long Sb, int nt) {
+    bar_all();
+    if (tid == 0) {
+      const int n_seg = static_cast<int>(mla_owner(Sb + nt - 1, T, n_cta) - mla_owner(Sb, T, n_cta) + 1);
       __threadfence();
+      const int t = atomicAdd(&p.row_sync[b], 1);
+      const bool last = (t == n_seg - 1);
+      if (last) {
+        p.row_sync[b] = 0;
+        __threadfence();
+      }
+      s_misc[11] = last ? 1 : 0;
     }
-    *s_flag = last ? n_active : 0;
+    bar_all();
+    if (s_misc[11] && n_pend < 2) {
+      pend_b[n_pend] = b;
+      pend_S[n_pend] = Sb;
+      pend_nt[n_pend] = nt;
+      ++n_pend;
+    }
+  };
+
+  if (score_role) {
+    // ============ score warps: half 0 (warps 0-3) k-steps 0-17 and the softmax,
+    // half 1 (warps 4-7) k-steps 18-35; warp w of a half owns positions [8w, 8w + 8)
+    const int half = warp / kScoreWarps, sw = warp % kScoreWarps;
+    for (int b = b0; S < end && b < B; ++b, ++seg) {
+      const int len = mla_row_len(p, b), nt = mla_tiles_of(len);
+      const int j0 = static_cast<int>(max(0LL, start - S)), j1 = static_cast<int>(min(static_cast<long long>(nt), end - S));
+      const bool complete = (S >= start) && (S + nt <= end);
+      // this half's 16 x 288 query slice as 18 A fragments (k-steps of 16 dims)
+      mla_wait(q_full, static_cast<uint32_t>(seg & 1), s_abort);
+      uint32_t qa[kQSteps][4];
+#pragma unroll
+      for (int i = 0; i < kQSteps; ++i) {
+        const int ks = half * kQSteps + i;
+        const int row = (mi & 1) * 8 + ri;
+        const int c16 = (ks & 3) * 2 + (mi >> 1);
+        ldmatrix_x4(smem_u32(s_q + (ks >> 2) * (kHeads * 128) + swz(row, c16)), qa[i][0], qa[i][1], qa[i][2],
+                    qa[i][3]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_empty);
+      float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;   // heads gq, gq + 8 (half 0)
+
+      for (int j = j0; j < j1; ++j, ++g) {
+        const int st = static_cast<int>(g % kStages);
+        const int buf = static_cast<int>(g & 1);
+        mla_wait(&full_bar[st], static_cast<uint32_t>((g / kStages) & 1), s_abort);
+        const unsigned char* kv = s_kv + st * kTileBytes;
+        // S[16 heads, 8 positions] over this half's dims; B fragments of two k-steps per ldmatrix
+        float acc[2][4];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+#pragma unroll
+        for (int kp = 0; kp < kQSteps / 2; ++kp) {
+          const int i = 2 * kp, ks = half * kQSteps + i;
+          uint32_t b0r, b1r, b2r, b3r;
+          ldmatrix_x4(smem_u32(kv + (ks >> 2) * (kTile * 128) + swz(8 * sw + ri, (ks & 3) * 2 + mi)), b0r, b1r,
+                      b2r, b3r);
+          mma_bf16_16816(acc[0], qa[i], b0r, b1r);
+          mma_bf16_16816(acc[1], qa[i + 1], b2r, b3r);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[st]);  // this warp is done with K
+        float s00 = acc[0][0] + acc[1][0];
+        float s01 = acc[0][1] + acc[1][1];
+        float s10 = acc[0][2] + acc[1][2];
+        float s11 = acc[0][3] + acc[1][3];
+        float4* sp = reinterpret_cast<float4*>(s_part) + (buf * kScoreWarps + sw) * 32 + lane;
+        if (half == 1) *sp = make_float4(s00, s01, s10, s11);
+        bar_score();
+        if (half == 1) continue;
+        {
+          const float4 o = *sp;
+          s00 += o.x; s01 += o.y; s10 += o.z; s11 += o.w;
+        }
+        const int t0 = j * kTile + 8 * sw + 2 * tq;
+        const bool v0 = t0 < len, v1 = t0 + 1 < len;
+        s00 = v0 ? s00 * p.scale_log2 : -INFINITY;
+        s01 = v1 ? s01 * p.scale_log2 : -INFINITY;
+        s10 = v0 ? s10 * p.scale_log2 : -INFINITY;
+        s11 = v1 ? s11 * p.scale_log2 : -INFINITY;
+        float x0 = fmaxf(s00, s01), x1 = fmaxf(s10, s11);
+        x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, 1));
+        x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, 1));
+        x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, 2));
+        x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, 2));
+        float* smx = s_max + buf * (kScoreWarps * kHeads);
+        if (tq == 0) {
+          smx[sw * kHeads + gq] = x0;
+          smx[sw * kHeads + gq + 8] = x1;
+        }
+        bar_half0();
+#pragma unroll
+        for (int w = 0; w < kScoreWarps; ++w) {
+          x0 = fmaxf(x0, smx[w * kHeads + gq]);
+          x1 = fmaxf(x1, smx[w * kHeads + gq + 8]);
+        }
+        const float n0 = fmaxf(m0, x0), n1 = fmaxf(m1, x1);
+        const float u0 = (n0 == -INFINITY) ? 0.f : n0, u1 = (n1 == -INFINITY) ? 0.f : n1;
+        const float a0 = exp2f(m0 - u0), a1 = exp2f(m1 - u1);
+        const float p00 = exp2f(s00 - u0), p01 = exp2f(s01 - u0);
+        const float p10 = exp2f(s10 - u1), p11 = exp2f(s11 - u1);
+        l0 = l0 * a0 + p00 + p01;
+        l1 = l1 * a1 + p10 + p11;
+        m0 = n0;
+        m1 = n1;
+        // hand P (bf16) and the rescale factors to the P @ V warps
+        if (g >= 2) mla_wait(&p_empty[buf], static_cast<uint32_t>(((g >> 1) - 1) & 1), s_abort);
+        bf16* pb = s_p + buf * (kHeads * kPStride);
+        *reinterpret_cast<uint32_t*>(pb + gq * kPStride + 8 * sw + 2 * tq) = pack_bf16x2(p00, p01);
+        *reinterpret_cast<uint32_t*>(pb + (gq + 8) * kPStride + 8 * sw + 2 * tq) = pack_bf16x2(p10, p11);
+        if (sw == 0 && tq == 0) {
+          s_alpha[buf * kHeads + gq] = a0;
+          s_alpha[buf * kHeads + gq + 8] = a1;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[buf]);
+      }
+
+      if (half == 0) {
+        // --- segment end: l per head (sum over this thread's quad, then the 4 warps)
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+        if (tq == 0) {
+          s_lsum[sw * kHeads + gq] = l0;
+          s_lsum[sw * kHeads + gq + 8] = l1;
+        }
+        bar_half0();
+        if (sw == 0 && tq == 0) {
+          float L0 = 0.f, L1 = 0.f;
+#pragma unroll
+          for (int w = 0; w < kScoreWarps; ++w) {
+            L0 += s_lsum[w * kHeads + gq];
+            L1 += s_lsum[w * kHeads + gq + 8];
+          }
+          s_fin[(seg & 1) * kHeads + gq] = L0 > 0.f ? 1.f / L0 : 0.f;
+          s_fin[(seg & 1) * kHeads + gq + 8] = L1 > 0.f ? 1.f / L1 : 0.f;
+          if (!complete) {
+            const long long part = c * 2 + mla_slot(S, start);
+            float* ml = p.ml_part + part * kHeads * 2;
+            ml[gq * 2] = m0;
+            ml[gq * 2 + 1] = L0;
+            ml[(gq + 8) * 2] = m1;
+            ml[(gq + 8) * 2 + 1] = L1;
+          }
+        }
+      }
+      bar_all();
+      if (!complete) finish_partial(b, S, nt);
+      S += nt;
+    }
+  } else {
+    // ============ P @ V warps
+    const int pv = warp - 2 * kScoreWarps;   // latent dims [128 pv, 128 pv + 128)
+    for (int b = b0; S < end && b < B; ++b, ++seg) {
+      const int len = mla_row_len(p, b), nt = mla_tiles_of(len);
+      const int j0 = static_cast<int>(max(0LL, start - S)), j1 = static_cast<int>(min(static_cast<long long>(nt), end - S));
+      const bool complete = (S >= start) && (S + nt <= end);
+      float o_acc[16][4];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) o_acc[i][0] = o_acc[i][1] = o_acc[i][2] = o_acc[i][3] = 0.f;
+      for (int j = j0; j < j1; ++j, ++g) {
+        const int st = static_cast<int>(g % kStages);
+        const int buf = static_cast<int>(g & 1);
+        mla_wait(&p_full[buf], static_cast<uint32_t>((g >> 1) & 1), s_abort);
+        mla_wait(&full_bar[st], static_cast<uint32_t>((g / kStages) & 1), s_abort);
+        const unsigned char* kv = s_kv + st * kTileBytes;
+        const float a0 = s_alpha[buf * kHeads + gq], a1 = s_alpha[buf * kHeads + gq + 8];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          o_acc[i][0] *= a0; o_acc[i][1] *= a0;
+          o_acc[i][2] *= a1; o_acc[i][3] *= a1;
+        }
+        const bf16* pb = s_p + buf * (kHeads * kPStride);
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk) {
+          uint32_t pa[4];
+          ldmatrix_x4(smem_u32(pb + ((mi & 1) * 8 + ri) * kPStride + kk * 16 + (mi >> 1) * 8), pa[0], pa[1], pa[2],
+                      pa[3]);
+#pragma unroll
+          for (int np = 0; np < 8; ++np) {
+            const int r = kk * 16 + (mi & 1) * 8 + ri;
+            const int c16 = (np & 3) * 2 + (mi >> 1);
+            uint32_t b0r, b1r, b2r, b3r;
+            ldmatrix_x4_trans(smem_u32(kv + (2 * pv + (np >> 2)) * (kTile * 128) + swz(r, c16)), b0r, b1r, b2r,
+                              b3r);
+            mma_bf16_16816(o_acc[2 * np], pa, b0r, b1r);
+            mma_bf16_16816(o_acc[2 * np + 1], pa, b2r, b3r);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&empty_bar[st]);
+          mbar_arrive(&p_empty[buf]);
+        }
+      }
+      bar_all();   // the score warps have published 1/l (and m, l of a partial row)
+      if (complete) {
+        const float i0 = s_fin[(seg & 1) * kHeads + gq], i1 = s_fin[(seg & 1) * kHeads + gq + 8];
+        bf16* ob = p.o_lat + static_cast<long long>(b) * kHeads * kLatent;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int d = pv * 128 + i * 8 + 2 * tq;
+          *reinterpret_cast<uint32_t*>(ob + gq * kLatent + d) = pack_bf16x2(o_acc[i][0] * i0, o_acc[i][1] * i0);
+          *reinterpret_cast<uint32_t*>(ob + (gq + 8) * kLatent + d) =
+              pack_bf16x2(o_acc[i][2] * i1, o_acc[i][3] * i1);
+        }
+      } else {
+        float* op = p.o_part + (c * 2 + mla_slot(S, start)) * kHeads * kLatent;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int d = pv * 128 + i * 8 + 2 * tq;
+          *reinterpret_cast<float2*>(op + gq * kLatent + d) = make_float2(o_acc[i][0], o_acc[i][1]);
+          *reinterpret_cast<float2*>(op + (gq + 8) * kLatent + d) = make_float2(o_acc[i][2], o_acc[i][3]);
+        }
+        finish_partial(b, S, nt);
+      }
+      S += nt;
+    }
   }
-  __syncthreads();
-  const int n_active = *s_flag;
-  if (n_active == 0) return;
-  mla_merge_row(p.o_part, p.ml_part, p.n_splits, n_active, p.o_lat, b, tid, kMlaThreads);
+  for (int i = 0; i < n_pend; ++i) merge_row(pend_b[i], pend_S[i], pend_nt[i]);
 }
 
 // o_lat[b, h, :] = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s   (bf16 out)
@@ -459,16 +740,18 @@ __global__ __launch_bounds__(128) void mla_combine_kernel(const float* __restric
 }
 
 // ----------------------------------------------------------------------------
-// Scratch for dsv2_mla_decode_noalloc: the split partials (o: [parts, 16, 512] then
-// (m, l): [parts, 16, 2], parts = batch * n_splits <= kNoAllocMaxParts) in one
-// fixed file-scope device array, so that entry point allocates nothing.  Every GPU
-// that loads the library holds these 8.4 MB until the process exits.  Host code
+// Scratch for dsv2_mla_decode_noalloc: the partials (o: [parts, 16, 512] then
+// (m, l): [parts, 16, 2], two parts per CTA, kNoAllocMaxParts parts) and the row
+// tickets (int32[kNoAllocMaxRows], zero from load time; every call leaves them zero)
+// in one fixed file-scope device array, so that entry point allocates nothing.  Every
+// GPU that loads the library holds these 8.4 MB until the process exits.  Host code
 // must not use the symbol as a pointer: its device address is looked up once per
 // device with cudaGetSymbolAddress (below) and passed to the kernels.
 // ----------------------------------------------------------------------------
 constexpr int kNoAllocMaxParts = 256;
+constexpr int kNoAllocMaxRows = 4096;
 constexpr size_t kNoAllocFloats =
-    static_cast<size_t>(kNoAllocMaxParts) * kHeads * (kLatent + 2);
+    static_cast<size_t>(kNoAllocMaxParts) * kHeads * (kLatent + 2) + kNoAllocMaxRows;
 static __device__ __align__(256) float g_mla_noalloc_scratch[kNoAllocFloats];
 static float* g_mla_noalloc_ptr[128];
 
@@ -489,9 +772,13 @@ cudaError_t mla_noalloc_scratch(float** out) {
 }
 
 constexpr size_t mla_decode_smem_bytes() {
-  return kStages * kTileBytes + kQBytes + kChunks * kHeads * kSRedStride * sizeof(float) +
-         kHeads * kPStride * sizeof(bf16) + kHeads * sizeof(float) + 2 * kStages * sizeof(uint64_t);
+  return kStages * kTileBytes + kQBytes + 2 * kHeads * kPStride * sizeof(bf16) +
+         (2 * kScoreWarps * kHeads + 2 * kHeads + kScoreWarps * kHeads + 2 * kHeads + 2 * kHeads * kMlaMaxCtas +
+          2 * kScoreWarps * 32 * 4) *
+             sizeof(float) +
+         (2 * kStages + 6) * sizeof(uint64_t) + 16 * sizeof(int) + 2 * sizeof(long long);
 }
+static_assert(mla_decode_smem_bytes() <= 232448, "latent-attention shared memory exceeds 227 KB");
 
 cudaError_t launch_mla_prep(const MlaPrepParams& p, int batch, cudaStream_t st) {
   launch_kernel(mla_prep_kernel, batch, 256, 0, st, p);
@@ -503,17 +790,28 @@ cudaError_t mla_decode_init() {
                               static_cast<int>(mla_decode_smem_bytes()));
 }
 
-cudaError_t launch_mla_decode(const MlaDecodeParams& p, const CUtensorMap& tm_kv, int batch,
-                              cudaStream_t st) {
-  launch_kernel(mla_decode_kernel, dim3(p.n_splits, batch), kMlaThreads, mla_decode_smem_bytes(), st, p,
-                tm_kv);
+// CTAs of the balanced decode: one per SM, at most one per tile of the largest possible
+// stream, and two partial slots each within the caller's batch * n_splits slots.
+int mla_decode_grid(const MlaDecodeParams& p, int num_sms, long long part_slots) {
+  const long long tiles = static_cast<long long>(p.batch) * ((p.max_len + kTile - 1) / kTile);
+  const long long slots = part_slots / 2;
+  long long g = num_sms;
+  g = std::min<long long>(g, kMlaMaxCtas);
+  g = std::min<long long>(g, tiles);
+  g = std::min<long long>(g, slots);
+  return static_cast<int>(std::max<long long>(g, 0));
+}
+
+cudaError_t launch_mla_decode(const MlaDecodeParams& p, const CUtensorMap& tm_kv, const CUtensorMap& tm_qa,
+                              const CUtensorMap& tm_qp, int grid, cudaStream_t st) {
+  launch_kernel(mla_decode_kernel, grid, kMlaThreads, mla_decode_smem_bytes(), st, p, tm_kv, tm_qa, tm_qp);
   return cudaGetLastError();
 }
 
 cudaError_t launch_mla_combine(const MlaDecodeParams& p, int batch, cudaStream_t st) {
   // one split covers the whole cache: every row wrote its output directly; with
   // row_sync the decode kernel merged the splits itself
-  if (static_cast<long long>(p.split_len) >= p.max_len || p.row_sync) return cudaSuccess;
+  if (static_cast<long long>(p.split_len) >= p.max_len) return cudaSuccess;
   launch_kernel(mla_combine_kernel, dim3(batch, kHeads), 128, 0, st, p.o_part, p.ml_part, p.n_splits, p.o_lat, p.positions, p.pos_numel, p.max_len, p.split_len);
   return cudaGetLastError();
 }

@@ -91,13 +91,17 @@ struct MlaDecodeParams {
   const long long* positions;  // [1] or [B]; attended length = position + 1
   int pos_numel;
   float scale_log2;            // softmax_scale * log2(e)
-  int split_len;               // positions per split, multiple of the tile
+  // mma.sync kernel: split_len = fewest positions per CTA, o_part / ml_part hold
+  // batch * n_splits partial slots (two per CTA), row_sync = per-row merge tickets.
+  // tcgen05 kernel: split_len = positions per split, o_part [B, n_splits, 16, 512].
+  int split_len;
   int n_splits;
-  float* o_part;               // [B, n_splits, 16, 512]
-  float* ml_part;              // [B, n_splits, 16, 2]  (m in log2 domain, l)
+  float* o_part;
+  float* ml_part;              // (m in log2 domain, l) per head and partial
   bf16* o_lat;                 // [B, 16, 512] output
   int inputs_prior;            // q_pe / positions / cache written >= 2 launches earlier
-  int* row_sync;               // [B] split counters (merge in the decode kernel), or nullptr
+  int* row_sync;               // [B] zero-initialised, left zero
+  int batch;
 };
 
 // norm.cu
@@ -134,7 +138,9 @@ cudaError_t launch_gather_rows(const void*, long long, const int*, const int*, i
 // mla.cu
 cudaError_t launch_mla_prep(const MlaPrepParams&, int, cudaStream_t);
 cudaError_t mla_decode_init();
-cudaError_t launch_mla_decode(const MlaDecodeParams&, const CUtensorMap&, int, cudaStream_t);
+int mla_decode_grid(const MlaDecodeParams&, int num_sms, long long part_slots);
+cudaError_t launch_mla_decode(const MlaDecodeParams&, const CUtensorMap& tm_kv, const CUtensorMap& tm_qa,
+                              const CUtensorMap& tm_qp, int grid, cudaStream_t);
 cudaError_t launch_mla_combine(const MlaDecodeParams&, int, cudaStream_t);
 // linear_tc.cu (TcShape, tc_launch_shape and launch_linear_tc_impl are defined there; the
 // unity build includes it before api.cu)

@@ -31,10 +31,12 @@ FAMILIES = {"small": ops.FAMILY_SMALL, "batch": ops.FAMILY_BATCH}
 
 
 def choose_split_len(batch: int, max_len: int, num_sms: int, family: int = ops.FAMILY_SMALL) -> int:
-    """Positions per split-KV CTA.  Large batches use 256-position splits, so that rows of
-    very different lengths (ragged batches) spread over the SMs and a row of up to 256
-    positions writes its output directly; smaller batches are split so that they yield
-    about four CTAs per SM.  Splits are multiples of 64 positions."""
+    """split_len of mla_decode.  FAMILY_SMALL (balanced kernel): the fewest positions a CTA
+    takes, 64 (two tiles), so that short contexts use fewer CTAs and merge fewer partials.
+    FAMILY_BATCH (tcgen05 split grid): large batches use 256-position splits, smaller
+    batches about four CTAs per SM; multiples of 64 positions."""
+    if family == ops.FAMILY_SMALL:
+        return 64
     unit = 64
     if batch * 2 >= 3 * num_sms:
         return int(min(256, (max_len + unit - 1) // unit * unit))
@@ -108,7 +110,7 @@ class DecodeEngine:
         props = torch.cuda.get_device_properties(self.dev)
         self.num_sms = props.multi_processor_count
         self.split_len = choose_split_len(self.B, self.max_len, self.num_sms)
-        self.n_splits = math.ceil(self.max_len / self.split_len)
+        self.n_splits = ops.mla_splits(self.B, self.max_len, self.split_len, self.num_sms)
         self._alloc()
         self.graph = None
         self._saved = None
@@ -142,6 +144,7 @@ class DecodeEngine:
         self.attn_out = torch.zeros((B, HIDDEN), device=dev, dtype=bf)
         self.o_part = torch.zeros((B, self.n_splits, N_HEADS, KV_LORA), device=dev, dtype=f32)
         self.ml_part = torch.zeros((B, self.n_splits, N_HEADS, 2), device=dev, dtype=f32)
+        self.mla_sync = torch.zeros(B, device=dev, dtype=i32)
         dense = [lp.dense for lp in self.layers if lp.dense is not None]
         inter_d = max([d.inter for d in dense], default=8)
         self.mlp_h = torch.zeros((B, inter_d), device=dev, dtype=bf)
@@ -262,7 +265,7 @@ class DecodeEngine:
                      x_group_rows=B)
         ops.mla_decode(q_abs=self.q_abs, q_pe=self.q_pe, cache=self.cache[li], positions=self.positions,
                        softmax_scale=self.scale, split_len=self.split_len, o_part=self.o_part,
-                       ml_part=self.ml_part, o_lat=self.o_lat, inputs_prior=True)
+                       ml_part=self.ml_part, o_lat=self.o_lat, inputs_prior=True, row_sync=self.mla_sync)
         # o[b, h] = o_lat[b, h] @ W_UV[h]^T,  W_UV[h] = kv_b[h*256 + 128 : h*256 + 256]
         self._linear(w=a.kv_b[QK_NOPE:], n_rows=V_DIM, k=KV_LORA, w_row_stride=KV_LORA,
                      w_group_stride=(QK_NOPE + V_DIM) * KV_LORA, x=self.o_lat, x_row_stride=N_HEADS * KV_LORA,

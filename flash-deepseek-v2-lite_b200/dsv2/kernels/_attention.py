@@ -36,8 +36,9 @@ class AttentionDecodeWorkspace:
     q_pe: torch.Tensor      # [B, 16, 64] roped q_pe
     q_nope: torch.Tensor    # [B, 16, 128]
     q_abs: torch.Tensor     # [B, 16, 512]
-    o_part: torch.Tensor    # [B, n_splits, 16, 512] fp32 split-KV partials
-    ml_part: torch.Tensor   # [B, n_splits, 16, 2] fp32 (max, sum) per split
+    o_part: torch.Tensor    # [B, n_splits, 16, 512] fp32 attention partials
+    ml_part: torch.Tensor   # [B, n_splits, 16, 2] fp32 (max, sum) per partial
+    row_sync: torch.Tensor  # [B] int32 merge tickets (zero between calls)
     o_lat: torch.Tensor     # [B, 16, 512]
     attn_o: torch.Tensor    # [B, 2048] (16 heads x 128)
     o_out: torch.Tensor     # [B, 2048] returned as [B, 1, 2048]
@@ -97,8 +98,8 @@ def _workspace(packed: AttentionPackedWeights, dev: torch.device, B: int, max_le
         return ws
     from ..engine import choose_split_len
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    split_len = choose_split_len(B, max_len, sms, family)
-    n_splits = math.ceil(max_len / split_len)
+    split_len = choose_split_len(B, max_len, sms)
+    n_splits = ops.mla_splits(B, max_len, split_len, sms)
     bf, f32 = torch.bfloat16, torch.float32
     ws = AttentionDecodeWorkspace(
         qkva=torch.empty((B, QKVA_ROWS), device=dev, dtype=bf),
@@ -107,6 +108,7 @@ def _workspace(packed: AttentionPackedWeights, dev: torch.device, B: int, max_le
         q_abs=torch.empty((B, HEADS, KV_LORA), device=dev, dtype=bf),
         o_part=torch.empty((B, n_splits, HEADS, KV_LORA), device=dev, dtype=f32),
         ml_part=torch.empty((B, n_splits, HEADS, 2), device=dev, dtype=f32),
+        row_sync=torch.zeros(B, device=dev, dtype=torch.int32),
         o_lat=torch.empty((B, HEADS, KV_LORA), device=dev, dtype=bf),
         attn_o=torch.empty((B, HEADS * V_DIM), device=dev, dtype=bf),
         o_out=torch.empty((B, HIDDEN), device=dev, dtype=bf),
@@ -173,7 +175,7 @@ def mla_decode_layer(name: str, hidden_states, cos, sin, position_ids, cache_pos
                n_groups=HEADS, n_tokens=B, family=family, w_group_rows=KV_LORA, x_group_rows=B)
     ops.mla_decode(q_abs=ws.q_abs, q_pe=ws.q_pe, cache=key_cache, positions=pos, softmax_scale=softmax_scale,
                    split_len=ws.split_len, o_part=ws.o_part, ml_part=ws.ml_part, o_lat=ws.o_lat,
-                   inputs_prior=True)
+                   inputs_prior=True, row_sync=ws.row_sync)
     kv_b = packed.kv_b_weight
     ops.linear(w=kv_b[QK_NOPE:], n_rows=V_DIM, k=KV_LORA, w_row_stride=KV_LORA,
                w_group_stride=(QK_NOPE + V_DIM) * KV_LORA, x=ws.o_lat, x_row_stride=HEADS * KV_LORA,

@@ -32,8 +32,7 @@ def _routing(B, n_exp, g, dev):
 
 
 def build_case(kernel: str, B: int, family: int, ctx: int, split_len: int | None, dev="cuda",
-               k_splits: int = 1, tile_tokens: int = 0, ragged: tuple[int, int] | None = None,
-               merge_in_kernel: bool = True):
+               k_splits: int = 1, tile_tokens: int = 0, ragged: tuple[int, int] | None = None):
     g = torch.Generator(device=dev).manual_seed(0)
     H, I, E = 2048, 1408, 64
     calls = []
@@ -142,15 +141,10 @@ def build_case(kernel: str, B: int, family: int, ctx: int, split_len: int | None
         from .engine import choose_split_len
         sl = split_len or choose_split_len(B, S, torch.cuda.get_device_properties(dev).multi_processor_count,
                                            family)
-        ns = math.ceil(S / sl)
-        o_part = torch.zeros(B, ns, 16, 512, device=dev)
-        ml = torch.zeros(B, ns, 16, 2, device=dev)
+        ws = ops.mla_workspace(B, S, sl, dev, family)
         o_lat = torch.zeros(B, 16, 512, dtype=torch.bfloat16, device=dev)
-        sync = (torch.zeros(B, dtype=torch.int32, device=dev)
-                if merge_in_kernel and family == ops.FAMILY_SMALL else None)
         calls.append(lambda: ops.mla_decode(q_abs=q_abs, q_pe=q_pe, cache=cache, positions=pos, softmax_scale=0.07,
-                                            split_len=sl, o_part=o_part, ml_part=ml, o_lat=o_lat, row_sync=sync,
-                                            family=family))
+                                            split_len=sl, o_lat=o_lat, family=family, **ws))
         nbytes = int((pos + 1).sum()) * 576 * 2
     else:
         raise ValueError(kernel)
@@ -167,7 +161,6 @@ def main():
     ap.add_argument("--k-splits", type=int, default=1)
     ap.add_argument("--tile-tokens", type=int, default=0, help="moe: tokens per work item (0 = auto)")
     ap.add_argument("--ragged", default=None, help="mla_decode: lo,hi row lengths uniform in [lo, hi)")
-    ap.add_argument("--merge-launch", action="store_true", help="mla_decode: merge splits in a second launch")
     ap.add_argument("--no-graph", action="store_true", help="issue launches from Python (host-bound)")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -175,7 +168,7 @@ def main():
     fam = ops.FAMILY_BATCH if a.family == "batch" else ops.FAMILY_SMALL
     ragged = tuple(int(v) for v in a.ragged.split(",")) if a.ragged else None
     calls, nbytes = build_case(a.kernel, a.batch, fam, a.ctx, a.split_len, k_splits=a.k_splits,
-                               tile_tokens=a.tile_tokens, ragged=ragged, merge_in_kernel=not a.merge_launch)
+                               tile_tokens=a.tile_tokens, ragged=ragged)
     for _ in range(a.warmup):
         for c in calls:
             c()

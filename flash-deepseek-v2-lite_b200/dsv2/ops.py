@@ -8,6 +8,7 @@ contiguity) and raises the same exception classes.
 from __future__ import annotations
 
 import ctypes
+import math
 
 import torch
 
@@ -20,7 +21,7 @@ from ._lib import (
 __all__ = [
     "stream", "rmsnorm", "add_rmsnorm", "embed_rmsnorm", "residual_add", "silu_mul", "sum_partials",
     "prepare_decode_inputs", "copy_token_to_cache", "advance_positions", "linear",
-    "router", "softmax_topk", "moe_bucket", "gather_rows", "moe", "mla_prep", "mla_decode", "lm_head_argmax",
+    "router", "softmax_topk", "moe_bucket", "gather_rows", "moe", "mla_prep", "mla_decode", "mla_splits", "mla_workspace", "lm_head_argmax",
     "EPI_STORE_BF16", "EPI_STORE_F32", "EPI_SWIGLU", "EPI_SCALE_F32", "FAMILY_SMALL", "FAMILY_BATCH",
 ]
 
@@ -365,15 +366,40 @@ def mla_prep(*, qkva: torch.Tensor, kv_norm_w: torch.Tensor, eps: float, cos: to
     _lib.call("dsv2_mla_prep", ctypes.byref(a), stream())
 
 
+MLA_MAX_CTAS = 160   # CTAs of the balanced latent-attention kernel (at most one per SM)
+
+
+def mla_splits(batch: int, max_len: int, split_len: int, num_sms: int, family: int = FAMILY_SMALL) -> int:
+    """n_splits of the [B, n_splits, 16, 512] / [B, n_splits, 16, 2] partial buffers:
+    FAMILY_SMALL (balanced kernel) needs two slots per CTA, FAMILY_BATCH (split grid) one
+    per split of the longest row."""
+    if family == FAMILY_SMALL:
+        return max(1, math.ceil(2 * min(num_sms, MLA_MAX_CTAS) / batch))
+    return math.ceil(max_len / split_len)
+
+
+def mla_workspace(batch: int, max_len: int, split_len: int, device, family: int = FAMILY_SMALL) -> dict:
+    """Work buffers of mla_decode: o_part, ml_part and (FAMILY_SMALL) the zeroed row tickets."""
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    n = mla_splits(batch, max_len, split_len, sms, family)
+    ws = {"o_part": torch.zeros((batch, n, 16, 512), device=device, dtype=torch.float32),
+          "ml_part": torch.zeros((batch, n, 16, 2), device=device, dtype=torch.float32)}
+    if family == FAMILY_SMALL:
+        ws["row_sync"] = torch.zeros(batch, device=device, dtype=torch.int32)
+    return ws
+
+
 def mla_decode(*, q_abs: torch.Tensor, q_pe: torch.Tensor, cache: torch.Tensor, positions: torch.Tensor,
                softmax_scale: float, split_len: int, o_part: torch.Tensor, ml_part: torch.Tensor,
                o_lat: torch.Tensor, inputs_prior: bool = False, row_sync: torch.Tensor | None = None,
                family: int = FAMILY_SMALL) -> None:
     """Latent attention for every row (see dsv2_mla_decode_args in include/dsv2.h).
     inputs_prior: q_pe, positions and the cache were written at least two launches earlier
-    on this stream (only q_abs by the previous one).  row_sync: int32 [B] zero-initialised
-    counters; when given, the splits of a row are merged inside the decode launch.
-    family: FAMILY_SMALL (mma.sync kernel) or FAMILY_BATCH (tcgen05 kernel)."""
+    on this stream (only q_abs by the previous one).
+    family FAMILY_SMALL: balanced mma.sync kernel, one launch; split_len = fewest positions
+    per CTA (multiple of 32); row_sync (int32 [B], zero-initialised, left zero) required.
+    family FAMILY_BATCH: tcgen05 kernel over split_len-position splits + merge launch.
+    Buffers: see mla_workspace."""
     for name, t in (("q_abs", q_abs), ("q_pe", q_pe), ("o_part", o_part), ("ml_part", ml_part), ("o_lat", o_lat)):
         _cuda(t, name)
         if not t.is_contiguous():
@@ -400,7 +426,10 @@ def mla_decode(*, q_abs: torch.Tensor, q_pe: torch.Tensor, cache: torch.Tensor, 
     a.batch = q_abs.shape[0]
     a.inputs_prior = 1 if inputs_prior else 0
     a.family = family
+    if family == FAMILY_SMALL and row_sync is None:
+        raise ValueError("mla_decode: row_sync (int32 [B], zeroed) is required; see mla_workspace")
     if row_sync is not None:
+        _cuda(row_sync, "row_sync")
         if row_sync.dtype != torch.int32 or row_sync.numel() < q_abs.shape[0]:
             raise ValueError("row_sync must be int32 with one entry per row")
         a.row_sync = row_sync.data_ptr()

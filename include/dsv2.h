@@ -394,12 +394,17 @@ typedef struct dsv2_mla_prep_args {
 
 DSV2_API int dsv2_mla_prep(const dsv2_mla_prep_args* args, void* stream);
 
-/* Split-KV latent attention for q_len = 1:
+/* Latent attention for q_len = 1:
  *   score[h, s] = softmax_scale * (q_abs[b, h] . cache[b, s, :512] + q_pe[b, h] . cache[b, s, 512:])
  *   o_lat[b, h] = sum_{s <= pos_b} softmax(score)[h, s] * cache[b, s, :512]   (bf16 out)
- * for 16 heads.  split_len (multiple of 64) positions per CTA; o_part [batch, n_splits,
- * 16, 512] and ml_part [batch, n_splits, 16, 2] fp32 are caller work buffers with
- * n_splits >= ceil(max_len / split_len).  Runs the split kernel and the merge kernel.
+ * for 16 heads.  o_part (batch * n_splits * 16 * 512 fp32) and ml_part (batch * n_splits *
+ * 16 * 2 fp32) are caller work buffers.
+ * DSV2_FAMILY_SMALL (one launch): the cache tiles of all rows are spread evenly over at
+ * most one CTA per SM; split_len (multiple of 32) = fewest positions per CTA; the buffers
+ * hold batch * n_splits partial slots, two per CTA (so at most batch * n_splits / 2
+ * CTAs); row_sync is required.
+ * DSV2_FAMILY_BATCH (two launches, split + merge): split_len (multiple of 64) positions
+ * per CTA, o_part [batch, n_splits, 16, 512] with n_splits >= ceil(max_len / split_len).
  * Reference: _decode_attention_q1_kernel / _batched_decode_attention_q1_kernel
  * (attention_decode_small.py:342-423, attention_decode_batch.py:240-342) over the
  * expanded cache; here over the latent cache. */
@@ -423,12 +428,12 @@ typedef struct dsv2_mla_decode_args {
    * decode): the kernel then starts loading cache tiles while the previous kernel is still
    * running.  0 = no such guarantee. */
   int32_t inputs_prior;
-  /* optional int32[batch], zero before the first call and left zero by every call: the
-   * last split of each row to finish merges the row's partials, so no merge launch
-   * follows.  NULL = merge in a second launch. */
+  /* int32[batch], zero before the first call and left zero by every call: the last CTA
+   * of a row cut between CTAs merges the row's partials (DSV2_FAMILY_SMALL: required;
+   * DSV2_FAMILY_BATCH: must be NULL). */
   int32_t* row_sync;
-  /* DSV2_FAMILY_SMALL: mma.sync kernel (32-position tiles);
-   * DSV2_FAMILY_BATCH: tcgen05/TMEM kernel (64-position tiles; row_sync must be NULL). */
+  /* DSV2_FAMILY_SMALL: mma.sync kernel (32-position tiles, balanced persistent grid);
+   * DSV2_FAMILY_BATCH: tcgen05/TMEM kernel (64-position tiles, split grid + merge). */
   int32_t family;
 } dsv2_mla_decode_args;
 
@@ -440,10 +445,10 @@ DSV2_API int dsv2_mla_decode(const dsv2_mla_decode_args* args, void* stream);
  * latency-critical decode thread where cudaMalloc's implicit device synchronisation
  * is not acceptable.  No counterpart in the reference (its attention wrappers
  * allocate their outputs and workspaces with torch).
- * The split-KV partials live in a fixed device array inside libdsv2.so (8.4 MB,
- * held by every GPU that loads the library until the process exits): at most 256
- * split partials, i.e. batch * ceil(max_len / split_len) <= 256; larger requests
- * return DSV2_ERR_INVALID with a message.  The caller still passes every input and
+ * Runs the DSV2_FAMILY_SMALL kernel; its partials (256 slots, so at most 128 CTAs) and
+ * row tickets (batch <= 4096, else DSV2_ERR_INVALID with a message) live in a fixed
+ * device array inside libdsv2.so (8.4 MB, held by every GPU that loads the library
+ * until the process exits).  The caller still passes every input and
  * the o_lat output, laid out as for dsv2_mla_decode.
  * The first call on each device looks up that array's device address
  * (cudaGetSymbolAddress) and the kernels' shared-memory attributes; make that first

@@ -190,31 +190,51 @@ def _mla_inputs(B, S, lengths, seed):
     return cache, q_abs, q_pe, pos
 
 
+def _short_rows(n, hi, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(1, hi + 1, (n,), generator=g).tolist()
+
+
 @pytest.mark.parametrize("B,S,lengths,split", [
-    (1, 128, [1], 64), (1, 700, [613], 64), (3, 300, [5, 300, 129], 128), (4, 1100, [1100, 64, 65, 700], 256),
-    (2, 8300, [8292, 4000], 1024)])
+    (1, 128, [1], 32), (1, 700, [613], 64), (3, 300, [5, 300, 129], 128), (4, 1100, [1100, 64, 65, 700], 32),
+    (2, 8300, [8292, 4000], 64),
+    (1, 9000, [8999], 32),                  # one row cut into ~150 CTA ranges, one merge of all of them
+    (200, 64, _short_rows(200, 64, 1), 32),  # many whole rows per CTA, boundaries inside rows
+    (5, 100, [0, 37, 100, 1, 64], 32),      # a row with nothing to attend gives zeros
+    (64, 1200, _short_rows(64, 1200, 2), 64)])
 def test_mla_decode_vs_oracle(D, B, S, lengths, split):
+    """Balanced latent attention (tile stream spread over the SMs, in-launch merge of rows
+    cut between CTAs) against the float64 oracle."""
     cache, q_abs, q_pe, pos = _mla_inputs(B, S, lengths, seed=S + B)
     scale = 192 ** -0.5
-    n_splits = math.ceil(S / split)
-    o_part = torch.zeros(B, n_splits, 16, 512, device=DEV)
-    ml = torch.zeros(B, n_splits, 16, 2, device=DEV)
-    o_lat = torch.zeros(B, 16, 512, dtype=torch.bfloat16, device=DEV)
-    D.mla_decode(q_abs=q_abs.to(DEV), q_pe=q_pe.to(DEV), cache=cache.to(DEV), positions=pos.to(DEV),
-                 softmax_scale=scale, split_len=split, o_part=o_part, ml_part=ml, o_lat=o_lat)
+    ws = D.mla_workspace(B, S, split, DEV)
+    o_lat = torch.full((B, 16, 512), float("nan"), dtype=torch.bfloat16, device=DEV)
+    args = dict(q_abs=q_abs.to(DEV), q_pe=q_pe.to(DEV), cache=cache.to(DEV), positions=pos.to(DEV),
+                softmax_scale=scale, split_len=split)
+    D.mla_decode(o_lat=o_lat, **args, **ws)
     ref = O.mla_decode(q_abs, q_pe, cache, pos + 1, scale)
     # bf16 P (as the reference's P.V) and bf16 output: 1e-2 relative bound
+    assert not torch.isnan(o_lat.float()).any()
     assert relerr(o_lat.cpu(), ref) < 1e-2
-    # merging the splits inside the decode launch (row counters) gives the same bits as
-    # the separate merge launch, and leaves the counters at zero (run twice)
-    sync = torch.zeros(B, dtype=torch.int32, device=DEV)
-    for _ in range(2):
-        o2 = torch.zeros_like(o_lat)
-        D.mla_decode(q_abs=q_abs.to(DEV), q_pe=q_pe.to(DEV), cache=cache.to(DEV), positions=pos.to(DEV),
-                     softmax_scale=scale, split_len=split, o_part=o_part, ml_part=ml, o_lat=o2, row_sync=sync)
-        torch.cuda.synchronize()
-        assert torch.equal(o2, o_lat)
-        assert int(sync.abs().sum()) == 0
+    # the row tickets are left at zero, and a second call gives the same bits
+    assert int(ws["row_sync"].abs().sum()) == 0
+    o2 = torch.zeros_like(o_lat)
+    D.mla_decode(o_lat=o2, **args, **ws)
+    torch.cuda.synchronize()
+    assert torch.equal(o2, o_lat)
+    assert int(ws["row_sync"].abs().sum()) == 0
+
+
+def test_mla_decode_requires_row_tickets(D):
+    B, S = 2, 64
+    z = torch.zeros(B, 16, 512, dtype=torch.bfloat16, device=DEV)
+    ws = D.mla_workspace(B, S, 32, DEV)
+    ws.pop("row_sync")
+    with pytest.raises(ValueError):
+        D.mla_decode(q_abs=z, q_pe=torch.zeros(B, 16, 64, dtype=torch.bfloat16, device=DEV),
+                     cache=torch.zeros(B, S, 576, dtype=torch.bfloat16, device=DEV),
+                     positions=torch.zeros(B, dtype=torch.int64, device=DEV), softmax_scale=0.1, split_len=32,
+                     o_lat=z, **ws)
 
 
 @pytest.mark.parametrize("B,S,lengths,split", [
@@ -253,12 +273,10 @@ def test_mla_decode_matches_reference_expanded_attention(D, golden_ref):
     scale = 192 ** -0.5
     ref = O.expanded_attention_decode(q, k, v, [L] * B, scale)
     q_abs = torch.einsum("bhd,hdc->bhc", q_nope, w_uk).to(torch.bfloat16).contiguous()
-    o_part = torch.zeros(B, 2, 16, 512, device=DEV)
-    ml = torch.zeros(B, 2, 16, 2, device=DEV)
     o_lat = torch.zeros(B, 16, 512, dtype=torch.bfloat16, device=DEV)
     D.mla_decode(q_abs=q_abs.to(DEV), q_pe=q_pe.to(DEV), cache=cache.to(DEV),
                  positions=torch.tensor([L - 1], device=DEV), softmax_scale=scale, split_len=64,
-                 o_part=o_part, ml_part=ml, o_lat=o_lat)
+                 o_lat=o_lat, **D.mla_workspace(B, S, 64, DEV))
     out = torch.einsum("bhc,hvc->bhv", o_lat.cpu().float(), w_uv)
     assert relerr(out, ref) < 2e-2
     # and the oracle's expanded attention agrees with the reference kernel's golden output

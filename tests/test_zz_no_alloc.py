@@ -4,7 +4,7 @@ Some callers of this library cannot allocate device memory: a serving runtime th
 has reserved all GPU memory for its own pool, a host program driving the kernels
 through a foreign-function interface without a CUDA allocator, or a decode thread
 that must not pay cudaMalloc's implicit device synchronisation.  For them the
-library keeps the split-KV partials in a fixed array of its own.  This test calls
+library keeps the attention partials and row tickets in a fixed array of its own.  This test calls
 that entry point through the C ABI twice in a row, on different shapes, and checks
 each result against the allocating entry point (dsv2_mla_decode with caller
 buffers) to the same 1e-2 relative bound the other attention tests use; it also
@@ -14,7 +14,6 @@ The file name sorts last so that a run stopping at the first failure has already
 run every other test.
 """
 import ctypes
-import math
 
 import pytest
 import torch
@@ -46,12 +45,9 @@ def test_noalloc_mla_decode_matches_allocating_entry_point():
     # two calls in a row: the second must not see anything left over from the first
     for B, S, lengths, split in ((3, 700, [613, 5, 700], 64), (4, 300, [300, 64, 65, 1], 128)):
         cache, q_abs, q_pe, pos = _case(B, S, lengths, seed=S + B)
-        n_splits = math.ceil(S / split)
-        o_part = torch.zeros(B, n_splits, 16, 512, device=DEV)
-        ml = torch.zeros(B, n_splits, 16, 2, device=DEV)
         want = torch.zeros(B, 16, 512, dtype=torch.bfloat16, device=DEV)
         ops.mla_decode(q_abs=q_abs, q_pe=q_pe, cache=cache, positions=pos, softmax_scale=scale,
-                       split_len=split, o_part=o_part, ml_part=ml, o_lat=want)
+                       split_len=split, o_lat=want, **ops.mla_workspace(B, S, split, DEV))
         got = torch.full((B, 16, 512), float("nan"), dtype=torch.bfloat16, device=DEV)
         rc = lib.dsv2_mla_decode_noalloc(q_abs.data_ptr(), q_pe.data_ptr(), cache.data_ptr(), cache.stride(0),
                                          S, pos.data_ptr(), pos.numel(), ctypes.c_float(scale), split,
@@ -67,8 +63,8 @@ def test_noalloc_rejects_requests_larger_than_its_scratch():
     lib = _lib.load()
     t = torch.zeros(16, dtype=torch.bfloat16, device=DEV)
     p = torch.zeros(1, dtype=torch.int64, device=DEV)
-    # 300 rows x 1 split > 256 partials
+    # 5000 rows > the 4096 row tickets of the fixed array
     rc = lib.dsv2_mla_decode_noalloc(t.data_ptr(), t.data_ptr(), t.data_ptr(), 64 * 576, 64, p.data_ptr(), 1,
-                                     ctypes.c_float(0.07), 64, t.data_ptr(), 300, None)
+                                     ctypes.c_float(0.07), 64, t.data_ptr(), 5000, None)
     assert rc == _lib.DSV2_ERR_INVALID
     assert "exceeds" in lib.dsv2_last_error().decode()
