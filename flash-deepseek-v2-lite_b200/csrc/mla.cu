@@ -45,10 +45,12 @@ constexpr int kPStride = kTile + 8;             // bf16 row stride of P
 constexpr int kScoreWarps = 4;                  // per half of the 576 dims: 8 positions of a tile each
 constexpr int kPvWarps = 4;                     // 128 latent dims each
 constexpr int kProducerWarp = 2 * kScoreWarps + kPvWarps;      // warp 12
+constexpr int kTicketWarp = kProducerWarp + 1;                 // warp 13
 constexpr int kMergeThreads = kProducerWarp * 32;              // 384 compute threads
-constexpr int kMlaThreads = kMergeThreads + 32;                // + the TMA producer warp
+constexpr int kMlaThreads = kMergeThreads + 64;                // + the TMA producer and ticket warps
 constexpr int kQSteps = kRow / 16 / 2;          // 18 mma k-steps of 16 dims per score half
-constexpr int kMlaMaxCtas = 160;                // merge scratch: 2 x 16 x CTAs floats
+static_assert(kMlaThreads / 32 <= 16, "per-warp prefix sums hold 16 warps");
+constexpr int kMlaMaxCtas = 160;                // merge scratch: 2 x 16 x CTAs floats (in the drained ring)
 
 // ----------------------------------------------------------------------------
 // mla_prep: latent RMSNorm + RoPE + cache write for the new token, RoPE of q_pe
@@ -198,44 +200,58 @@ __device__ __forceinline__ long long mla_owner(long long t, long long T, long lo
 // range row by row ("segments"): a row that lies wholly inside the range is normalised
 // and written to o_lat; a row cut by a range boundary leaves (o, m, l) partials in the
 // CTA's slot 0 (first segment) or 1 (last segment), and the last of the row's CTAs to
-// finish merges them (row_sync ticket) — no second launch.
+// publish merges them (row_sync ticket) after its own range — no second launch.
 //
-// Warp roles (warp-specialised, the scores of tile t + 1 overlap P @ V of tile t):
-//  - warps 0-3, scores: warp w owns positions [8w, 8w + 8) of a tile and keeps the whole
-//    16 x 576 query block in registers (36 mma k-steps, 4 accumulator chains), so no
-//    cross-warp reduction of scores is needed; the tile max per head is exchanged
-//    through shared memory (one 128-thread barrier per tile); P (bf16) and the rescale
-//    factor go to a double buffer handed over with mbarriers;
-//  - warps 4-7, P @ V: warp v owns latent dims [128v, 128v + 128);
-//  - warp 8, producer: TMA ring of 5 cache tiles and the per-segment query block.
+// Warp roles (warp-specialised; the scores of tile t + 1 overlap P @ V of tile t):
+//  - warps 0-7, scores: half h = warp / 4 covers k-steps [18h, 18h + 18) of the 36
+//    (16 dims each) with its query slice in registers; warp w = warp % 4 owns positions
+//    [8w, 8w + 8) of a tile.  Half 1 hands its partial scores to half 0 through shared
+//    memory; half 0 exchanges the tile max per head (one 128-thread barrier), runs the
+//    online softmax and hands bf16 P and the rescale factors to the P @ V warps through a
+//    double buffer (mbarriers);
+//  - warps 8-11, P @ V: warp v owns latent dims [128v, 128v + 128);
+//  - warp 12, producer: TMA ring of 5 cache tiles and the per-segment query block;
+//  - warp 13, tickets: publishes the CTA's (at most two) partial rows and records which
+//    of them this CTA has to merge, off the compute warps' path.
 __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDecodeParams p,
                                                                    const __grid_constant__ CUtensorMap tm_kv,
                                                                    const __grid_constant__ CUtensorMap tm_qa,
                                                                    const __grid_constant__ CUtensorMap tm_qp) {
   extern __shared__ __align__(1024) unsigned char smem[];
-  unsigned char* s_kv = smem;                                    // stages x 9 chunks x 32 rows x 128 B
-  unsigned char* s_q = smem + kStages * kTileBytes;              // 9 chunks x 16 rows x 128 B
-  bf16* s_p = reinterpret_cast<bf16*>(s_q + kQBytes);            // [2][16][kPStride]
+  unsigned char* s_kv = smem;                                    // stages x 32 positions x 9 chunks x 128 B
+  unsigned char* s_q = smem + kStages * kTileBytes;              // [2] x 9 chunks x 16 rows x 128 B
+  bf16* s_p = reinterpret_cast<bf16*>(s_q + 2 * kQBytes);        // [2][16][kPStride]
   float* s_max = reinterpret_cast<float*>(s_p + 2 * kHeads * kPStride);  // [2][4][16]
   float* s_alpha = s_max + 2 * kScoreWarps * kHeads;             // [2][16]
   float* s_lsum = s_alpha + 2 * kHeads;                          // [4][16]
   float* s_fin = s_lsum + kScoreWarps * kHeads;                  // [2][16] 1/l of a finished segment
-  float* s_mrg = s_fin + 2 * kHeads;                             // [2][16][kMlaMaxCtas] merge scratch
-  float* s_part = s_mrg + 2 * kHeads * kMlaMaxCtas;              // [2][4][32 lanes][4] second-half scores
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(s_part + 2 * kScoreWarps * 32 * 4);  // [kStages]
-  uint64_t* empty_bar = full_bar + kStages;                      // [kStages]
-  uint64_t* p_full = empty_bar + kStages;                        // [2]
-  uint64_t* p_empty = p_full + 2;                                // [2]
-  uint64_t* q_full = p_empty + 2;
-  uint64_t* q_empty = q_full + 1;
-  int* s_misc = reinterpret_cast<int*>(q_empty + 1);             // [16]
-  long long* s_ll = reinterpret_cast<long long*>(s_misc + 16);   // [2]
+  float* s_part = s_fin + 2 * kHeads;                            // [2][4][32 lanes][4] second-half scores
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_part + 2 * kScoreWarps * 32 * 4);
+  uint64_t* full_bar = bars;                                     // [kStages] cache tile landed
+  uint64_t* empty_bar = full_bar + kStages;                      // [kStages] tile consumed
+  uint64_t* p_full = empty_bar + kStages;                        // [2] P handed over
+  uint64_t* p_empty = p_full + 2;                                // [2] P consumed
+  uint64_t* q_full = p_empty + 2;                                // [2] query block landed
+  uint64_t* q_empty = q_full + 2;                                // [2] query block in registers
+  uint64_t* fin_full = q_empty + 2;                              // [2] 1/l of a segment published
+  uint64_t* fin_empty = fin_full + 2;                            // [2] 1/l read
+  uint64_t* tk_full = fin_empty + 2;                             // [2] partial of slot 0 / 1 written
+  uint64_t* tk_done = tk_full + 2;                               // tickets taken, merge list final
+  int* s_misc = reinterpret_cast<int*>(tk_done + 1);             // [16] named slots (below)
+  int* s_wsum = s_misc + 16;                                     // [16] per-warp tile sums of the prefix
+  long long* s_ll = reinterpret_cast<long long*>(s_misc + 32);   // [4]: S of the first row, pending S
   volatile int* s_abort = s_misc + 12;
+  float* s_mrg = reinterpret_cast<float*>(s_kv);                 // merge scratch, once the ring is drained
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int B = p.batch;
   const bool early = p.inputs_prior != 0;
 
+  if (warp == kProducerWarp && lane == 0) {
+    prefetch_tmap(&tm_kv);
+    prefetch_tmap(&tm_qa);
+    prefetch_tmap(&tm_qp);
+  }
   // positions may come from the previous launch unless inputs_prior
   if (!early) pdl_enter();
   if (tid == 0) {
@@ -246,9 +262,13 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
     for (int i = 0; i < 2; ++i) {
       mbar_init(&p_full[i], kScoreWarps);
       mbar_init(&p_empty[i], kPvWarps);
+      mbar_init(&fin_full[i], 1);
+      mbar_init(&fin_empty[i], kPvWarps);
+      mbar_init(&tk_full[i], 1 + kPvWarps);
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 2 * kScoreWarps);
     }
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 2 * kScoreWarps);
+    mbar_init(tk_done, 1);
     *s_abort = 0;
     fence_mbar_init();
   }
@@ -268,14 +288,14 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
       const int u = __shfl_up_sync(0xffffffffu, v, o);
       if (lane >= o) v += u;
     }
-    if (lane == 31) s_misc[warp] = v;
+    if (lane == 31) s_wsum[warp] = v;
     if (base == 0) {
       nt_mine = nt;
       incl = v;
     }
     __syncthreads();
 #pragma unroll
-    for (int w = 0; w < kMlaThreads / 32; ++w) T += s_misc[w];
+    for (int w = 0; w < kMlaThreads / 32; ++w) T += s_wsum[w];
     __syncthreads();
   }
   n_cta = min(static_cast<long long>(gridDim.x), (T + min_tpc - 1) / min_tpc);
@@ -286,11 +306,11 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
   start = mla_range_start(c, T, n_cta);
   end = mla_range_start(c + 1, T, n_cta);
   if (B <= kMlaThreads) {
-    // s_misc[0..9] still hold the warp totals of the only chunk
+    // s_wsum still holds the warp totals of the only chunk
     long long off = 0;
 #pragma unroll
     for (int w = 0; w < kMlaThreads / 32; ++w)
-      if (w < warp) off += s_misc[w];
+      if (w < warp) off += s_wsum[w];
     const long long S = off + incl - nt_mine;
     if (tid < B && S <= start && start < S + nt_mine) {
       s_ll[0] = S;
@@ -307,13 +327,13 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
         const int u = __shfl_up_sync(0xffffffffu, v, o);
         if (lane >= o) v += u;
       }
-      if (lane == 31) s_misc[warp] = v;
+      if (lane == 31) s_wsum[warp] = v;
       __syncthreads();
       long long off = run, total = 0;
 #pragma unroll
       for (int w = 0; w < kMlaThreads / 32; ++w) {
-        if (w < warp) off += s_misc[w];
-        total += s_misc[w];
+        if (w < warp) off += s_wsum[w];
+        total += s_wsum[w];
       }
       const long long S = off + v - nt;
       if (b < B && S <= start && start < S + nt) {
@@ -332,20 +352,20 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
   if (warp == kProducerWarp) {
     // ================= producer warp: cache tiles and query blocks
     if (lane == 0) {
-      prefetch_tmap(&tm_kv);
-      prefetch_tmap(&tm_qa);
-      prefetch_tmap(&tm_qp);
       bool waited = !early, ok = true;
       int early_rows[kStages];
       int q_issued = 0, seg = 0;
       long long g = 0;
       auto issue_q = [&](int k, int row) {
-        if (k > 0 && ok) ok = mla_wait(q_empty, static_cast<uint32_t>((k - 1) & 1), s_abort);
+        // query buffer k & 1 (two segments in flight)
+        const int qb = k & 1;
+        if (k >= 2 && ok) ok = mla_wait(&q_empty[qb], static_cast<uint32_t>(((k >> 1) - 1) & 1), s_abort);
         if (!ok) return;
-        mbar_arrive_expect_tx(q_full, kQBytes);
+        unsigned char* dq = s_q + qb * kQBytes;
+        mbar_arrive_expect_tx(&q_full[qb], kQBytes);
         for (int ch = 0; ch < kLatent / 64; ++ch)
-          tma_load_3d(smem_u32(s_q + ch * (kHeads * 128)), &tm_qa, q_full, ch * 64, 0, row);
-        tma_load_3d(smem_u32(s_q + (kLatent / 64) * (kHeads * 128)), &tm_qp, q_full, 0, 0, row);
+          tma_load_3d(smem_u32(dq + ch * (kHeads * 128)), &tm_qa, &q_full[qb], ch * 64, 0, row);
+        tma_load_3d(smem_u32(dq + (kLatent / 64) * (kHeads * 128)), &tm_qp, &q_full[qb], 0, 0, row);
       };
       long long S = S0;
       for (int b = b0; S < end && b < B; ++b, ++seg) {
@@ -379,8 +399,8 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
         for (uint32_t i = 0; i < (1u << 20) && !mbar_try_wait(&full_bar[st], static_cast<uint32_t>((last / kStages) & 1)); ++i) {
         }
       }
-      if (seg > 0)
-        for (uint32_t i = 0; i < (1u << 20) && !mbar_try_wait(q_full, static_cast<uint32_t>((seg - 1) & 1)); ++i) {
+      for (int k = max(0, seg - 2); k < seg; ++k)
+        for (uint32_t i = 0; i < (1u << 20) && !mbar_try_wait(&q_full[k & 1], static_cast<uint32_t>((k >> 1) & 1)); ++i) {
         }
     } else if (early) {
       pdl_enter();
@@ -388,137 +408,68 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
     return;
   }
 
-  // ================= compute warps (scores: warps 0-3, P @ V: warps 4-7)
+  if (warp == kTicketWarp) {
+    // ================= ticket warp: publish the CTA's partial rows (slot 0: a row that
+    // began before this range, slot 1: a row that ends after it)
+    if (early) pdl_enter();
+    if (lane == 0) {
+      int n_pend = 0;
+      long long S = S0;
+      for (int b = b0; S < end && b < B; ++b) {
+        const int nt = mla_tiles_of(mla_row_len(p, b));
+        if (!((S >= start) && (S + nt <= end))) {
+          const int slot = mla_slot(S, start);
+          if (mla_wait(&tk_full[slot], 0, s_abort)) {
+            const int n_seg = static_cast<int>(mla_owner(S + nt - 1, T, n_cta) - mla_owner(S, T, n_cta) + 1);
+            __threadfence();   // the partial (written by other warps, ordered by the mbarrier) first
+            const int t = atomicAdd(&p.row_sync[b], 1);
+            if (t == n_seg - 1) {
+              p.row_sync[b] = 0;
+              __threadfence();
+              s_misc[13 + n_pend] = b;
+              s_misc[5 + n_pend] = nt;
+              s_ll[2 + n_pend] = S;
+              ++n_pend;
+            }
+          }
+        }
+        S += nt;
+      }
+      s_misc[15] = n_pend;
+      mbar_arrive(tk_done);
+    }
+    return;
+  }
+
+  // ================= compute warps
   if (early) pdl_enter();
   const int gq = lane >> 2, tq = lane & 3;
   const int mi = lane >> 3, ri = lane & 7;
-  const bool score_role = warp < 2 * kScoreWarps;
   long long g = 0;   // tiles of this CTA so far (ring slot, P buffer)
   int seg = 0;
   long long S = S0;
 
-  // merge of row b (all 384 compute threads; the row's partials are published)
-  auto merge_row = [&](int b, long long Sb, int nt) {
-    const long long c_first = mla_owner(Sb, T, n_cta), c_last = mla_owner(Sb + nt - 1, T, n_cta);
-    const int n_seg = static_cast<int>(c_last - c_first + 1);
-    float* s_m = s_mrg;
-    float* s_l = s_mrg + kHeads * n_seg;
-    auto part_index = [&](int k) -> long long {
-      const long long cc = c_first + k;
-      return cc * 2 + ((k == 0) ? mla_slot(Sb, mla_range_start(cc, T, n_cta)) : 0);
-    };
-    for (int i = tid; i < kHeads * n_seg; i += kMergeThreads) {
-      const int h = i / n_seg, k = i % n_seg;
-      const long long pk = part_index(k);
-      s_m[i] = __ldcg(p.ml_part + (pk * kHeads + h) * 2);
-      s_l[i] = __ldcg(p.ml_part + (pk * kHeads + h) * 2 + 1);
-    }
-    bar_all();
-    if (tid < kHeads) {
-      // w_k = 2^(m_k - M) / sum_k 2^(m_k - M) l_k
-      float M = -INFINITY;
-      for (int k = 0; k < n_seg; ++k)
-        if (s_l[tid * n_seg + k] > 0.f) M = fmaxf(M, s_m[tid * n_seg + k]);
-      float den = 0.f;
-      for (int k = 0; k < n_seg; ++k) {
-        const float l = s_l[tid * n_seg + k];
-        const float w = l > 0.f ? exp2f(s_m[tid * n_seg + k] - M) : 0.f;
-        s_m[tid * n_seg + k] = w;
-        den += w * l;
-      }
-      const float inv = den > 0.f ? 1.f / den : 0.f;
-      for (int k = 0; k < n_seg; ++k) s_m[tid * n_seg + k] *= inv;
-    }
-    bar_all();
-    constexpr int kItems = kHeads * kLatent / 4;
-    constexpr int kPer = 3;   // float4 outputs per thread and pass (two passes cover 384 x 6 >= 2048)
-    static_assert(2 * kPer * kMergeThreads >= kItems, "merge passes do not cover the row");
-    bf16* ob = p.o_lat + static_cast<long long>(b) * kHeads * kLatent;
-#pragma unroll 1
-    for (int pass = 0; pass < 2; ++pass) {
-      float4 acc[kPer];
-#pragma unroll
-      for (int r = 0; r < kPer; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 1
-      for (int k = 0; k < n_seg; ++k) {
-        const float4* o0 = reinterpret_cast<const float4*>(p.o_part + part_index(k) * kHeads * kLatent);
-        float4 v0[kPer];
-#pragma unroll
-        for (int r = 0; r < kPer; ++r) {
-          const int i = tid + (pass * kPer + r) * kMergeThreads;
-          v0[r] = i < kItems ? __ldcg(o0 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int r = 0; r < kPer; ++r) {
-          const int i = tid + (pass * kPer + r) * kMergeThreads;
-          const float w0 = i < kItems ? s_m[(i / (kLatent / 4)) * n_seg + k] : 0.f;
-          acc[r].x += w0 * v0[r].x;
-          acc[r].y += w0 * v0[r].y;
-          acc[r].z += w0 * v0[r].z;
-          acc[r].w += w0 * v0[r].w;
-        }
-      }
-#pragma unroll
-      for (int r = 0; r < kPer; ++r) {
-        const int i = tid + (pass * kPer + r) * kMergeThreads;
-        if (i < kItems) {
-          uint2 o;
-          o.x = pack_bf16x2(acc[r].x, acc[r].y);
-          o.y = pack_bf16x2(acc[r].z, acc[r].w);
-          *reinterpret_cast<uint2*>(ob + 4 * i) = o;
-        }
-      }
-    }
-    bar_all();  // s_mrg is free again
-  };
-
-  // ticket of a partial row (after both roles wrote their part); the last of the row's
-  // CTAs merges it after its own range is done (a CTA holds at most two cut rows)
-  int pend_b[2] = {0, 0}, pend_nt[2] = {0, 0}, n_pend = 0;
-  long long pend_S[2] = {0, 0};
-  auto finish_partial = [&](int b, long long Sb, int nt) {
-    bar_all();
-    if (tid == 0) {
-      const int n_seg = static_cast<int>(mla_owner(Sb + nt - 1, T, n_cta) - mla_owner(Sb, T, n_cta) + 1);
-      __threadfence();
-      const int t = atomicAdd(&p.row_sync[b], 1);
-      const bool last = (t == n_seg - 1);
-      if (last) {
-        p.row_sync[b] = 0;
-        __threadfence();
-      }
-      s_misc[11] = last ? 1 : 0;
-    }
-    bar_all();
-    if (s_misc[11] && n_pend < 2) {
-      pend_b[n_pend] = b;
-      pend_S[n_pend] = Sb;
-      pend_nt[n_pend] = nt;
-      ++n_pend;
-    }
-  };
-
-  if (score_role) {
-    // ============ score warps: half 0 (warps 0-3) k-steps 0-17 and the softmax,
-    // half 1 (warps 4-7) k-steps 18-35; warp w of a half owns positions [8w, 8w + 8)
+  if (warp < 2 * kScoreWarps) {
+    // ============ score warps
     const int half = warp / kScoreWarps, sw = warp % kScoreWarps;
     for (int b = b0; S < end && b < B; ++b, ++seg) {
       const int len = mla_row_len(p, b), nt = mla_tiles_of(len);
       const int j0 = static_cast<int>(max(0LL, start - S)), j1 = static_cast<int>(min(static_cast<long long>(nt), end - S));
       const bool complete = (S >= start) && (S + nt <= end);
       // this half's 16 x 288 query slice as 18 A fragments (k-steps of 16 dims)
-      mla_wait(q_full, static_cast<uint32_t>(seg & 1), s_abort);
+      const int qb = seg & 1;
+      mla_wait(&q_full[qb], static_cast<uint32_t>((seg >> 1) & 1), s_abort);
       uint32_t qa[kQSteps][4];
 #pragma unroll
       for (int i = 0; i < kQSteps; ++i) {
         const int ks = half * kQSteps + i;
         const int row = (mi & 1) * 8 + ri;
         const int c16 = (ks & 3) * 2 + (mi >> 1);
-        ldmatrix_x4(smem_u32(s_q + (ks >> 2) * (kHeads * 128) + swz(row, c16)), qa[i][0], qa[i][1], qa[i][2],
-                    qa[i][3]);
+        ldmatrix_x4(smem_u32(s_q + qb * kQBytes + (ks >> 2) * (kHeads * 128) + swz(row, c16)), qa[i][0], qa[i][1],
+                    qa[i][2], qa[i][3]);
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(q_empty);
+      if (lane == 0) mbar_arrive(&q_empty[qb]);
       float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;   // heads gq, gq + 8 (half 0)
 
       for (int j = j0; j < j1; ++j, ++g) {
@@ -598,7 +549,8 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
       }
 
       if (half == 0) {
-        // --- segment end: l per head (sum over this thread's quad, then the 4 warps)
+        // --- segment end: l per head (this thread's quad, then the 4 warps); warp 0
+        // publishes 1/l (and m, l of a partial row) without waiting for the other roles
         l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
         l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
         l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
@@ -608,27 +560,34 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
           s_lsum[sw * kHeads + gq + 8] = l1;
         }
         bar_half0();
-        if (sw == 0 && tq == 0) {
-          float L0 = 0.f, L1 = 0.f;
+        if (sw == 0) {
+          const int fb = seg & 1;
+          if (tq == 0) {
+            float L0 = 0.f, L1 = 0.f;
 #pragma unroll
-          for (int w = 0; w < kScoreWarps; ++w) {
-            L0 += s_lsum[w * kHeads + gq];
-            L1 += s_lsum[w * kHeads + gq + 8];
+            for (int w = 0; w < kScoreWarps; ++w) {
+              L0 += s_lsum[w * kHeads + gq];
+              L1 += s_lsum[w * kHeads + gq + 8];
+            }
+            if (seg >= 2) mla_wait(&fin_empty[fb], static_cast<uint32_t>(((seg >> 1) - 1) & 1), s_abort);
+            s_fin[fb * kHeads + gq] = L0 > 0.f ? 1.f / L0 : 0.f;
+            s_fin[fb * kHeads + gq + 8] = L1 > 0.f ? 1.f / L1 : 0.f;
+            if (!complete) {
+              float* ml = p.ml_part + (c * 2 + mla_slot(S, start)) * kHeads * 2;
+              ml[gq * 2] = m0;
+              ml[gq * 2 + 1] = L0;
+              ml[(gq + 8) * 2] = m1;
+              ml[(gq + 8) * 2 + 1] = L1;
+            }
           }
-          s_fin[(seg & 1) * kHeads + gq] = L0 > 0.f ? 1.f / L0 : 0.f;
-          s_fin[(seg & 1) * kHeads + gq + 8] = L1 > 0.f ? 1.f / L1 : 0.f;
-          if (!complete) {
-            const long long part = c * 2 + mla_slot(S, start);
-            float* ml = p.ml_part + part * kHeads * 2;
-            ml[gq * 2] = m0;
-            ml[gq * 2 + 1] = L0;
-            ml[(gq + 8) * 2] = m1;
-            ml[(gq + 8) * 2 + 1] = L1;
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&fin_full[fb]);
+            if (!complete) mbar_arrive(&tk_full[mla_slot(S, start)]);
           }
         }
+        // s_lsum is rewritten at the next segment end, after that segment's tile barriers
       }
-      bar_all();
-      if (!complete) finish_partial(b, S, nt);
       S += nt;
     }
   } else {
@@ -676,9 +635,10 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
           mbar_arrive(&p_empty[buf]);
         }
       }
-      bar_all();   // the score warps have published 1/l (and m, l of a partial row)
+      const int fb = seg & 1;
+      mla_wait(&fin_full[fb], static_cast<uint32_t>((seg >> 1) & 1), s_abort);
       if (complete) {
-        const float i0 = s_fin[(seg & 1) * kHeads + gq], i1 = s_fin[(seg & 1) * kHeads + gq + 8];
+        const float i0 = s_fin[fb * kHeads + gq], i1 = s_fin[fb * kHeads + gq + 8];
         bf16* ob = p.o_lat + static_cast<long long>(b) * kHeads * kLatent;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -695,12 +655,96 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
           *reinterpret_cast<float2*>(op + gq * kLatent + d) = make_float2(o_acc[i][0], o_acc[i][1]);
           *reinterpret_cast<float2*>(op + (gq + 8) * kLatent + d) = make_float2(o_acc[i][2], o_acc[i][3]);
         }
-        finish_partial(b, S, nt);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&fin_empty[fb]);
+        if (!complete) mbar_arrive(&tk_full[mla_slot(S, start)]);
       }
       S += nt;
     }
   }
-  for (int i = 0; i < n_pend; ++i) merge_row(pend_b[i], pend_S[i], pend_nt[i]);
+
+  // ================= merges of the rows this CTA published last (all compute warps)
+  mla_wait(tk_done, 0, s_abort);
+  const int n_pend = min(s_misc[15], 2);
+  for (int pi = 0; pi < n_pend; ++pi) {
+    const int b = s_misc[13 + pi], nt = s_misc[5 + pi];
+    const long long Sb = s_ll[2 + pi];
+    const long long c_first = mla_owner(Sb, T, n_cta), c_last = mla_owner(Sb + nt - 1, T, n_cta);
+    const int n_seg = static_cast<int>(c_last - c_first + 1);
+    float* s_m = s_mrg;
+    float* s_l = s_mrg + kHeads * n_seg;
+    auto part_index = [&](int k) -> long long {
+      const long long cc = c_first + k;
+      return cc * 2 + ((k == 0) ? mla_slot(Sb, mla_range_start(cc, T, n_cta)) : 0);
+    };
+    bar_all();   // s_mrg (the drained ring) is free; the previous merge is done with it
+    for (int i = tid; i < kHeads * n_seg; i += kMergeThreads) {
+      const int h = i / n_seg, k = i % n_seg;
+      const long long pk = part_index(k);
+      s_m[i] = __ldcg(p.ml_part + (pk * kHeads + h) * 2);
+      s_l[i] = __ldcg(p.ml_part + (pk * kHeads + h) * 2 + 1);
+    }
+    bar_all();
+    if (tid < kHeads) {
+      // w_k = 2^(m_k - M) / sum_k 2^(m_k - M) l_k
+      float M = -INFINITY;
+      for (int k = 0; k < n_seg; ++k)
+        if (s_l[tid * n_seg + k] > 0.f) M = fmaxf(M, s_m[tid * n_seg + k]);
+      float den = 0.f;
+      for (int k = 0; k < n_seg; ++k) {
+        const float l = s_l[tid * n_seg + k];
+        const float w = l > 0.f ? exp2f(s_m[tid * n_seg + k] - M) : 0.f;
+        s_m[tid * n_seg + k] = w;
+        den += w * l;
+      }
+      const float inv = den > 0.f ? 1.f / den : 0.f;
+      for (int k = 0; k < n_seg; ++k) s_m[tid * n_seg + k] *= inv;
+    }
+    bar_all();
+    constexpr int kItems = kHeads * kLatent / 4;
+    constexpr int kPer = (kItems + kMergeThreads - 1) / kMergeThreads;   // 6
+    float4 acc[kPer];
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+    // two partials per round: 2 x 6 independent 16-byte loads in flight per thread
+    for (int k = 0; k < n_seg; k += 2) {
+      const bool two = k + 1 < n_seg;
+      const float4* o0 = reinterpret_cast<const float4*>(p.o_part + part_index(k) * kHeads * kLatent);
+      const float4* o1 = two ? reinterpret_cast<const float4*>(p.o_part + part_index(k + 1) * kHeads * kLatent) : o0;
+      float4 v0[kPer], v1[kPer];
+#pragma unroll
+      for (int r = 0; r < kPer; ++r) {
+        const int i = tid + r * kMergeThreads;
+        const bool in = i < kItems;
+        v0[r] = in ? __ldcg(o0 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        v1[r] = (in && two) ? __ldcg(o1 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int r = 0; r < kPer; ++r) {
+        const int i = tid + r * kMergeThreads;
+        const int h = (i < kItems ? i : 0) / (kLatent / 4);
+        const float w0 = i < kItems ? s_m[h * n_seg + k] : 0.f;
+        const float w1 = (i < kItems && two) ? s_m[h * n_seg + k + 1] : 0.f;
+        acc[r].x += w0 * v0[r].x + w1 * v1[r].x;
+        acc[r].y += w0 * v0[r].y + w1 * v1[r].y;
+        acc[r].z += w0 * v0[r].z + w1 * v1[r].z;
+        acc[r].w += w0 * v0[r].w + w1 * v1[r].w;
+      }
+    }
+    bf16* ob = p.o_lat + static_cast<long long>(b) * kHeads * kLatent;
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) {
+      const int i = tid + r * kMergeThreads;
+      if (i < kItems) {
+        uint2 o;
+        o.x = pack_bf16x2(acc[r].x, acc[r].y);
+        o.y = pack_bf16x2(acc[r].z, acc[r].w);
+        *reinterpret_cast<uint2*>(ob + 4 * i) = o;
+      }
+    }
+  }
 }
 
 // o_lat[b, h, :] = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s   (bf16 out)
@@ -772,13 +816,13 @@ cudaError_t mla_noalloc_scratch(float** out) {
 }
 
 constexpr size_t mla_decode_smem_bytes() {
-  return kStages * kTileBytes + kQBytes + 2 * kHeads * kPStride * sizeof(bf16) +
-         (2 * kScoreWarps * kHeads + 2 * kHeads + kScoreWarps * kHeads + 2 * kHeads + 2 * kHeads * kMlaMaxCtas +
-          2 * kScoreWarps * 32 * 4) *
+  return kStages * kTileBytes + 2 * kQBytes + 2 * kHeads * kPStride * sizeof(bf16) +
+         (2 * kScoreWarps * kHeads + 2 * kHeads + kScoreWarps * kHeads + 2 * kHeads + 2 * kScoreWarps * 32 * 4) *
              sizeof(float) +
-         (2 * kStages + 6) * sizeof(uint64_t) + 16 * sizeof(int) + 2 * sizeof(long long);
+         (2 * kStages + 15) * sizeof(uint64_t) + 32 * sizeof(int) + 4 * sizeof(long long);
 }
 static_assert(mla_decode_smem_bytes() <= 232448, "latent-attention shared memory exceeds 227 KB");
+static_assert(2 * kHeads * kMlaMaxCtas * sizeof(float) <= kStages * kTileBytes, "merge scratch exceeds the ring");
 
 cudaError_t launch_mla_prep(const MlaPrepParams& p, int batch, cudaStream_t st) {
   launch_kernel(mla_prep_kernel, batch, 256, 0, st, p);
