@@ -63,17 +63,43 @@ __global__ __launch_bounds__(256) void mla_prep_kernel(const MlaPrepParams p) {
   const int b = blockIdx.x;
   // stage the row (summing fp32 split-K partials and rounding to bf16, like a bf16 linear)
   if (p.qkva_f32) {
+    // 912 float4 per row over 256 threads: each thread sums its (up to 4) float4 columns,
+    // four partials at a time with all their loads in flight, in order of the partial
     const float* src = reinterpret_cast<const float*>(p.qkva) + b * p.qkva_row_stride;
-    for (int i = threadIdx.x; i < (kHeads * 192 + kRow) / 4; i += blockDim.x) {
-      float4 acc = *reinterpret_cast<const float4*>(src + 4 * i);
-      for (int s = 1; s < p.qkva_parts; ++s) {
-        const float4 v = *reinterpret_cast<const float4*>(src + s * p.qkva_part_stride + 4 * i);
-        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    constexpr int kN4 = (kHeads * 192 + kRow) / 4;
+    constexpr int kPer = (kN4 + 255) / 256;
+    float4 acc[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < p.qkva_parts; s0 += 4) {
+      float4 v[4][kPer];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+          const int i = threadIdx.x + k * 256;
+          if (s0 + q < p.qkva_parts && i < kN4)
+            v[q][k] = __ldcg(reinterpret_cast<const float4*>(src + (s0 + q) * p.qkva_part_stride + 4 * i));
+        }
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+          const int i = threadIdx.x + k * 256;
+          if (s0 + q < p.qkva_parts && i < kN4) {
+            acc[k].x += v[q][k].x; acc[k].y += v[q][k].y; acc[k].z += v[q][k].z; acc[k].w += v[q][k].w;
+          }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int i = threadIdx.x + k * 256;
+      if (i < kN4) {
+        uint2 o;
+        o.x = pack_bf16x2(acc[k].x, acc[k].y);
+        o.y = pack_bf16x2(acc[k].z, acc[k].w);
+        *reinterpret_cast<uint2*>(s_row + 4 * i) = o;
       }
-      uint2 o;
-      o.x = pack_bf16x2(acc.x, acc.y);
-      o.y = pack_bf16x2(acc.z, acc.w);
-      *reinterpret_cast<uint2*>(s_row + 4 * i) = o;
     }
   } else {
     const bf16* src = reinterpret_cast<const bf16*>(p.qkva) + b * p.qkva_row_stride;

@@ -95,6 +95,32 @@ __global__ __launch_bounds__(kNormThreads) void rmsnorm_kernel(const bf16* __res
 // delta_dtype: 0 bf16 (row stride delta_row_stride), 2 fp32 partials laid out
 // [rows][n_delta][cols] (part stride delta_part_stride).  n_delta == 0 means no add.
 // When h_out != nullptr the sum is written there instead of in place.
+// acc[0..7] += sum over p < n of src[p * stride + 0..7] (fp32), added in order of p.  The
+// loads of four partials are issued before their adds, so a thread keeps 8 independent
+// 16-byte loads in flight instead of one round trip per partial.  l2_only: read through
+// L2 only (partials written by another CTA of the previous launch).
+__device__ __forceinline__ void sum_parts8(const float* src, long long stride, int n, float (&acc)[8],
+                                           bool l2_only) {
+  for (int p0 = 0; p0 < n; p0 += 4) {
+    float4 a[4], b[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (p0 + q < n) {
+        const float4* s = reinterpret_cast<const float4*>(src + (p0 + q) * stride);
+        a[q] = l2_only ? __ldcg(s) : s[0];
+        b[q] = l2_only ? __ldcg(s + 1) : s[1];
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (p0 + q < n) {
+        acc[0] += a[q].x; acc[1] += a[q].y; acc[2] += a[q].z; acc[3] += a[q].w;
+        acc[4] += b[q].x; acc[5] += b[q].y; acc[6] += b[q].z; acc[7] += b[q].w;
+      }
+    }
+  }
+}
+
 __global__ __launch_bounds__(kNormThreads) void add_rmsnorm_kernel(
     bf16* __restrict__ h, bf16* __restrict__ h_out, const void* __restrict__ delta, int delta_dtype,
     int n_delta, long long delta_part_stride, long long delta_row_stride,
@@ -134,12 +160,7 @@ __global__ __launch_bounds__(kNormThreads) void add_rmsnorm_kernel(
         for (int j = 0; j < 8; ++j) d[j] = 0.f;
         if (delta_dtype == 2) {
           const float* dp = reinterpret_cast<const float*>(delta) + row * delta_row_stride + c * 8;
-          for (int p = 0; p < n_delta; ++p) {
-            const float4 a = __ldcg(reinterpret_cast<const float4*>(dp + p * delta_part_stride));
-            const float4 b = __ldcg(reinterpret_cast<const float4*>(dp + p * delta_part_stride + 4));
-            d[0] += a.x; d[1] += a.y; d[2] += a.z; d[3] += a.w;
-            d[4] += b.x; d[5] += b.y; d[6] += b.z; d[7] += b.w;
-          }
+          sum_parts8(dp, delta_part_stride, n_delta, d, true);
         } else {
           const bf16* dp = reinterpret_cast<const bf16*>(delta) + row * delta_row_stride + c * 8;
           for (int p = 0; p < n_delta; ++p) {
@@ -247,12 +268,7 @@ __global__ void sum_partials_kernel(const float* __restrict__ part, int n_parts,
   float acc[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-  for (int p = 0; p < n_parts; ++p) {
-    const float4 a = *reinterpret_cast<const float4*>(src + p * ps);
-    const float4 b = *reinterpret_cast<const float4*>(src + p * ps + 4);
-    acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
-    acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
-  }
+  sum_parts8(src, ps, n_parts, acc, false);
   if (out_f32) {
     float* o = reinterpret_cast<float*>(out) + r * ors + c;
     *reinterpret_cast<float4*>(o) = make_float4(acc[0], acc[1], acc[2], acc[3]);

@@ -227,11 +227,22 @@ __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams 
   __syncthreads();
   const int n_routes = p.rows * kTopK;
   const int r_first = tok0 * kTopK;
-  for (int r = tid; r < n_routes; r += kRouteThreads) {
-    const int e = __ldcg(p.ids32 + r) - p.expert_lo;
-    if (e >= 0 && e < p.n_local) {
-      atomicAdd(&s_total[e], 1);
-      if (r < r_first) atomicAdd(&s_before[e], 1);
+  // all routes' expert ids, eight loads in flight per thread
+  for (int r0 = 0; r0 < n_routes; r0 += 8 * kRouteThreads) {
+    int ev[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int r = r0 + u * kRouteThreads + tid;
+      ev[u] = r < n_routes ? __ldcg(p.ids32 + r) - p.expert_lo : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int r = r0 + u * kRouteThreads + tid;
+      const int e = ev[u];
+      if (r < n_routes && e >= 0 && e < p.n_local) {
+        atomicAdd(&s_total[e], 1);
+        if (r < r_first) atomicAdd(&s_before[e], 1);
+      }
     }
   }
   __syncthreads();
