@@ -524,8 +524,8 @@ int dsv2_moe(const dsv2_moe_args* a, void* stream) {
   if (!a || !a->gate_up || !a->down || !a->x_sorted || !a->h || !a->group_offsets || !a->route_slot ||
       !a->route_weight || !a->y || !a->sync)
     return fail(DSV2_ERR_INVALID, "moe: null pointer");
-  if (a->n_groups <= 0 || a->n_groups + 1 > kTcMaxGroups)
-    return fail(DSV2_ERR_UNSUPPORTED, "moe: n_groups=%d (max %d)", a->n_groups, kTcMaxGroups - 1);
+  if (a->n_groups <= 0 || a->n_groups + 2 > kTcMaxGroups)
+    return fail(DSV2_ERR_UNSUPPORTED, "moe: n_groups=%d (max %d)", a->n_groups, kTcMaxGroups - 2);
   if (a->hidden <= 0 || a->inter <= 0 || a->hidden % 64 || a->inter % 64)
     return fail(DSV2_ERR_UNSUPPORTED, "moe: hidden %d / inter %d must be multiples of 64", a->hidden,
                 a->inter);

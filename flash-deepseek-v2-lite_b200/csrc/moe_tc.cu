@@ -11,10 +11,11 @@
 // Phase 2 item (group g, 128-row tile of the hidden dimension, token tile):
 //   y[route_slot[route], n] = bf16(W_down[g] h[route]) * route_weight[route]
 // A group is a routed expert or one half of the shared MLP (see the router's bucketing).
-// Every CTA walks one list holding all phase-1 items followed by all phase-2 items
-// (items blockIdx.x, blockIdx.x + gridDim.x, ...), so the two GEMMs share one
-// balanced stream of weight tiles instead of two launches that each end on a partial
-// wave.  A phase-2 item of group g starts once every phase-1 item of g has stored
+// All phase-1 items followed by all phase-2 items form one list, groups that need
+// several token tiles first (the shared-expert halves at large batches, whose wide
+// epilogues are the longest, start early).  The first rounds are dealt round-robin;
+// the rest of the list is taken from a global counter, so the two GEMMs share one
+// balanced stream of weight tiles and no CTA is left with a whole extra item at the end.  A phase-2 item of group g starts once every phase-1 item of g has stored
 // its h rows: the phase-1 epilogue publishes a per-group counter (release), the
 // phase-2 producer polls it (acquire, bounded) before its TMA loads of h.  Each CTA
 // finishes its phase-1 items before its phase-2 items, and all CTAs are resident
@@ -31,6 +32,7 @@
 namespace dsv2 {
 
 constexpr int kMoeThreads = 192;
+constexpr int kMoeQueue = 4;   // item ids the producer may run ahead of the epilogue
 
 struct MoeParams {
   int n_groups;
@@ -43,7 +45,7 @@ struct MoeParams {
   const float* route_weight;  // [routes]
   bf16* h;                    // [x_rows, inter] phase-1 output / phase-2 input
   float* y;                   // [*, hidden] fp32
-  int* sync;                  // [n_groups + 1]: per-group phase-1 counters + exit ticket
+  int* sync;                  // [n_groups + 2]: per-group phase-1 counters, exit ticket, item counter
   PeerTable peers;            // world > 0: y rows (route slots) live in their owner rank's part
 };
 
@@ -87,10 +89,14 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
   uint64_t* empty_bar = full_bar + shp.stages;
   uint64_t* tfull_bar = empty_bar + shp.stages;   // [2]
   uint64_t* tempty_bar = tfull_bar + 2;            // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  uint64_t* wq_full = tempty_bar + 2;              // [kMoeQueue] item id published
+  uint64_t* wq_empty = wq_full + kMoeQueue;         // [kMoeQueue] item id read by MMA + 4 epilogue warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wq_empty + kMoeQueue);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   __shared__ int s_r0[kTcMaxGroups], s_cnt[kTcMaxGroups], s_nts[kTcMaxGroups];
   __shared__ int s_first1[kTcMaxGroups + 1], s_first2[kTcMaxGroups + 1];
+  __shared__ int s_order[kTcMaxGroups];   // list position -> group (multi-tile groups first)
+  __shared__ int s_item[kMoeQueue];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -101,6 +107,10 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
       mbar_init(&tempty_bar[b], 128);
+    }
+    for (int q = 0; q < kMoeQueue; ++q) {
+      mbar_init(&wq_full[q], 1);
+      mbar_init(&wq_empty[q], 5);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -138,13 +148,31 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
     s_nts[g] = nts;
   }
   __syncthreads();
+  // groups that need more than one token tile (the shared-expert halves at large
+  // batches) go first, the rest keep their order
+  {
+    __shared__ int s_nwide;
+    if (threadIdx.x == 0) s_nwide = 0;
+    __syncthreads();
+    int mine = 0;
+    for (int g = threadIdx.x; g < G; g += kMoeThreads) mine += s_nts[g] > 1;
+    if (mine) atomicAdd(&s_nwide, mine);
+    __syncthreads();
+    for (int g = threadIdx.x; g < G; g += kMoeThreads) {
+      const bool wide = s_nts[g] > 1;
+      int before = 0;   // groups of the same class with a lower index
+      for (int h = 0; h < g; ++h) before += ((s_nts[h] > 1) == wide);
+      s_order[wide ? before : s_nwide + before] = g;
+    }
+  }
+  __syncthreads();
   if (threadIdx.x == 0) {
     int a1 = 0, a2 = 0;
-    for (int g = 0; g < G; ++g) {
-      s_first1[g] = a1;
-      s_first2[g] = a2;
-      a1 += s_nts[g] * mt1;
-      a2 += s_nts[g] * mt2;
+    for (int i = 0; i < G; ++i) {
+      s_first1[i] = a1;
+      s_first2[i] = a2;
+      a1 += s_nts[s_order[i]] * mt1;
+      a2 += s_nts[s_order[i]] * mt2;
     }
     s_first1[G] = a1;
     s_first2[G] = a2;
@@ -164,12 +192,12 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
       ph = 2;
     }
     int lo = 0, hi = G - 1;
-    while (lo < hi) {  // last group with first[g] <= local
+    while (lo < hi) {  // last list position with first[pos] <= local
       const int mid = (lo + hi + 1) >> 1;
       if (first[mid] <= local) lo = mid; else hi = mid - 1;
     }
-    g = lo;
-    local -= first[g];
+    local -= first[lo];
+    g = s_order[lo];
     const int nts = s_nts[g];
     mt = local / nts;
     nt = local - mt * nts;
@@ -183,7 +211,32 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int it = blockIdx.x; it < total_items && !*abort_flag; it += gridDim.x) {
+      // items of the first rounds are dealt round-robin (no atomics); the rest of the
+      // list is taken from a global counter, one grab ahead so its latency overlaps
+      // the current item's loads
+      const int n_static = max(0, total_items / static_cast<int>(gridDim.x) - 1);
+      const int dyn_base = n_static * static_cast<int>(gridDim.x);
+      int next_dyn = -1;
+      if (n_static == 0) next_dyn = dyn_base + atomicAdd(&p.sync[G + 1], 1);
+      for (int k = 0;; ++k) {
+        // next item of the list (or the end marker) into the CTA's queue
+        int it;
+        if (k < n_static) {
+          it = blockIdx.x + k * static_cast<int>(gridDim.x);
+          if (k == n_static - 1) next_dyn = dyn_base + atomicAdd(&p.sync[G + 1], 1);
+        } else {
+          it = next_dyn;
+          if (it < total_items) next_dyn = dyn_base + atomicAdd(&p.sync[G + 1], 1);
+        }
+        if (it >= total_items || *abort_flag) it = -1;
+        const int qs = k % kMoeQueue;
+        if (k >= kMoeQueue && !mbar_wait(&wq_empty[qs], ((k / kMoeQueue) - 1) & 1)) {
+          *abort_flag = 1;
+          it = -1;
+        }
+        s_item[qs] = it;
+        mbar_arrive(&wq_full[qs]);
+        if (it < 0) break;
         int ph, g, mt, nt, r0, ntok;
         if (!decode(it, ph, g, mt, nt, r0, ntok)) continue;
         if (ph == 2) {
@@ -251,7 +304,12 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
       int stage = 0;
       uint32_t phase = 0;
       uint32_t local = 0;
-      for (int it = blockIdx.x; it < total_items && !*abort_flag; it += gridDim.x) {
+      for (int k = 0;; ++k) {
+        const int qs = k % kMoeQueue;
+        if (!mbar_wait(&wq_full[qs], (k / kMoeQueue) & 1)) { *abort_flag = 1; break; }
+        const int it = s_item[qs];
+        mbar_arrive(&wq_empty[qs]);
+        if (it < 0 || *abort_flag) break;
         int ph, g, mt, nt, r0, ntok;
         if (!decode(it, ph, g, mt, nt, r0, ntok)) continue;
         const int npad = round_up(ntok, 16);
@@ -304,7 +362,13 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
     const int quad = warp & 3;
     const int row_in_tile = quad * 32 + lane;
     uint32_t local = 0;
-    for (int it = blockIdx.x; it < total_items; it += gridDim.x) {
+    for (int k = 0;; ++k) {
+      const int qs = k % kMoeQueue;
+      if (!mbar_wait(&wq_full[qs], (k / kMoeQueue) & 1)) { *abort_flag = 1; break; }
+      const int it = s_item[qs];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&wq_empty[qs]);
+      if (it < 0) break;
       int ph, g, mt, nt, r0, ntok;
       if (!decode(it, ph, g, mt, nt, r0, ntok)) continue;
       const int npad = round_up(ntok, 16);
@@ -399,6 +463,7 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
       __threadfence();
       for (int g = 0; g < G; ++g) p.sync[g] = 0;
       p.sync[G] = 0;
+      p.sync[G + 1] = 0;
       __threadfence();
       if (p.peers.world > 0) {
         __threadfence_system();
@@ -427,8 +492,8 @@ MoeShape moe_shape(int max_routes_per_group, int tile_tokens) {
 }
 
 size_t moe_smem_bytes(const MoeShape& s) {
-  return 1024 + static_cast<size_t>(s.stages) * s.stage_bytes + (2 * s.stages + 4) * sizeof(uint64_t) +
-         16;
+  return 1024 + static_cast<size_t>(s.stages) * s.stage_bytes +
+         (2 * s.stages + 4 + 2 * kMoeQueue) * sizeof(uint64_t) + 16;
 }
 
 cudaError_t moe_tc_init() {
@@ -439,7 +504,7 @@ cudaError_t moe_tc_init() {
 cudaError_t launch_moe_tc(const MoeParams& p, const CUtensorMap& w1, const CUtensorMap& x1,
                           const CUtensorMap& x1b, const CUtensorMap& w2, const CUtensorMap& h,
                           const CUtensorMap& hb, const MoeShape& shp, int num_sms, cudaStream_t st) {
-  if (p.n_groups + 1 > kTcMaxGroups) return cudaErrorInvalidValue;
+  if (p.n_groups + 2 > kTcMaxGroups) return cudaErrorInvalidValue;
   launch_kernel(moe_tc_kernel, num_sms, kMoeThreads, moe_smem_bytes(shp), st, p, w1, x1, x1b, w2, h,
                 hb, shp);
   return cudaGetLastError();

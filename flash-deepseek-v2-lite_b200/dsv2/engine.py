@@ -171,7 +171,7 @@ class DecodeEngine:
             self.route_weight = torch.zeros(self.r_max, device=dev, dtype=f32)
             self.x_sorted = torch.zeros((self.r_max, HIDDEN), device=dev, dtype=bf)
             self.h_moe = torch.zeros((self.r_max, m0.inter), device=dev, dtype=bf)
-            self.moe_sync = torch.zeros(self.n_groups + 1, device=dev, dtype=i32)
+            self.moe_sync = torch.zeros(self.n_groups + 2, device=dev, dtype=i32)
             self.partial = torch.zeros((Ball, SLOTS, HIDDEN), device=dev, dtype=f32)
             if self.world > 1:
                 self.x_all = torch.zeros((Ball, HIDDEN), device=dev, dtype=bf)

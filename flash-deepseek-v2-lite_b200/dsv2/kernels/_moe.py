@@ -128,7 +128,7 @@ def routed_moe(name: str, x: torch.Tensor, topk_ids: torch.Tensor, topk_weight: 
     xs = torch.empty((R, H), device=dev, dtype=torch.bfloat16) if batch else None
     ops.moe_bucket(ids32, tw, 0, E, 0, 0, go, rt, rs, rw, gather_src=x if batch else None, gather_out=xs)
     if batch:
-        sync = torch.zeros(E + 1, device=dev, dtype=torch.int32)
+        sync = torch.zeros(E + 2, device=dev, dtype=torch.int32)
         ops.moe(gate_up=packed.gate_up_weights, down=packed.down_weights, x_sorted=xs, h=h, group_offsets=go,
                 max_routes_per_group=B, route_slot=rs, route_weight=rw, y=partial.view(-1, H), sync=sync)
         ops.sum_partials(partial[:, :K], out)

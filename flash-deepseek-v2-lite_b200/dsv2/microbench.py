@@ -57,7 +57,7 @@ def build_case(kernel: str, B: int, family: int, ctx: int, split_len: int | None
         distinct = int((torch.bincount(ids.view(-1).long(), minlength=E) > 0).sum())
         batch = family == ops.FAMILY_BATCH
         if kernel == "moe":
-            sync = torch.zeros(G + 1, dtype=torch.int32, device=dev)
+            sync = torch.zeros(G + 2, dtype=torch.int32, device=dev)
             calls.append(lambda: ops.moe(gate_up=gate_up, down=down, x_sorted=xs, h=h, group_offsets=go,
                                          max_routes_per_group=B, route_slot=rs, route_weight=rw,
                                          y=part.view(-1, H), sync=sync, tile_tokens=tile_tokens))

@@ -205,7 +205,7 @@ def moe(*, gate_up: torch.Tensor, down: torch.Tensor, x_sorted: torch.Tensor, h:
         peers: PeerTable | None = None) -> None:
     """Fused grouped MoE of one layer (batch family): gate_up + SwiGLU -> h, then down scaled
     by the route weight into y[route_slot] (fp32 rows).  See dsv2_moe_args in include/dsv2.h.
-    gate_up [G, 2I, H], down [G, H, I] bf16; x_sorted [R, H], h [R, I] bf16; sync int32 [G + 1]
+    gate_up [G, 2I, H], down [G, H, I] bf16; x_sorted [R, H], h [R, I] bf16; sync int32 [G + 2]
     (zero-initialised once, left zero by every call)."""
     for name, t in (("gate_up", gate_up), ("down", down), ("x_sorted", x_sorted), ("h", h), ("y", y)):
         _cuda(t, name)
@@ -219,8 +219,8 @@ def moe(*, gate_up: torch.Tensor, down: torch.Tensor, x_sorted: torch.Tensor, h:
     inter = two_i // 2
     if tuple(down.shape) != (G, H, inter) or x_sorted.shape[1] != H or tuple(h.shape) != (x_sorted.shape[0], inter):
         raise ValueError("moe: inconsistent shapes")
-    if sync.numel() < G + 1 or group_offsets.numel() < G + 1:
-        raise ValueError("moe: sync and group_offsets need n_groups + 1 entries")
+    if sync.numel() < G + 2 or group_offsets.numel() < G + 1:
+        raise ValueError("moe: sync needs n_groups + 2 entries and group_offsets n_groups + 1")
     a = MoeArgs()
     a.gate_up, a.down = gate_up.data_ptr(), down.data_ptr()
     a.n_groups, a.hidden, a.inter = G, H, inter

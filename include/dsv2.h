@@ -240,9 +240,10 @@ DSV2_API int dsv2_linear(const dsv2_linear_args* args, int family, void* stream)
  * as the router's bucketing lays them out).  gate_up: [n_groups, 2*inter, hidden] (gate
  * rows then up rows), down: [n_groups, hidden, inter], bf16.  x_sorted / h: [x_rows,
  * hidden] / [x_rows, inter] bf16; y rows are hidden wide, fp32 (the per-slot partials the
- * next fused add+RMSNorm sums).  sync: int32[n_groups + 1], zero before the first call
- * and left zero by every call (per-group progress counters between the two GEMMs).
- * hidden % 64 == 0, inter % 64 == 0, n_groups <= 255.  Calls that share `sync` must not
+ * next fused add+RMSNorm sums).  sync: int32[n_groups + 2], zero before the first call
+ * and left zero by every call (per-group progress counters between the two GEMMs, the
+ * exit ticket and the shared item counter).
+ * hidden % 64 == 0, inter % 64 == 0, n_groups <= 254.  Calls that share `sync` must not
  * overlap on the GPU.
  * Reference: the grouped gate/up + SwiGLU and down kernels of packed_routed_moe
  * (moe_batch.py:151-307, launched at :425-557). */

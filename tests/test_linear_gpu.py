@@ -149,7 +149,7 @@ def test_grouped_moe(D, family, B):
     if family == "batch":
         # the fused single-launch MoE computes the same values bit for bit, and leaves its
         # progress counters at zero (checked by running it twice)
-        sync = torch.zeros(G + 1, dtype=torch.int32, device=DEV)
+        sync = torch.zeros(G + 2, dtype=torch.int32, device=DEV)
         for tt in (0, 0, 32):   # auto token tile (twice), and a fixed 32-token tile
             h2 = torch.full((R, I), float("nan"), dtype=torch.bfloat16, device=DEV)
             p2 = torch.zeros(B, 8, H, device=DEV)
