@@ -46,10 +46,12 @@ def choose_split_len(batch: int, max_len: int, num_sms: int, family: int = ops.F
 
 
 def split_count(n_rows: int, k: int, num_sms: int) -> int:
-    """K splits for a dense batch-family linear: about one 128-row tile per SM, at least
-    two 64-wide K blocks per split."""
+    """K splits for a dense batch-family linear: about one 128-row tile per two SMs (the
+    token dimension splits too), at least two 64-wide K blocks per split.  Fewer splits
+    also mean fewer fp32 partials for the consumer to read (measured on B200 at B=256:
+    qkva 3 splits 13.4 us vs 5 splits 13.2 us, o_proj 5 splits 11.7 us vs 9 splits 12.1 us)."""
     m_tiles = (n_rows + 127) // 128
-    s = max(1, round(num_sms / m_tiles))
+    s = max(1, round(num_sms / (2 * m_tiles)))
     return int(min(s, max(1, (k // 64) // 2), 16))
 
 
