@@ -51,9 +51,9 @@ GATE_BYTES = 2 * 131_072
 LMHEAD_BYTES = 2 * 209_715_200
 EXPERT_BYTES = 2 * 8_650_752
 KV_ROW_BYTES = 576 * 2
-# DRAM traffic / algorithmic bytes of the grouped MoE GEMMs, from one ncu capture of the
-# gate_up and down launches at B=256: (770.6 + 7.8 + 386.5 + 13.3) MB / (761.3 + 380.6) MB
-MOE_TRAFFIC_RATIO = 1.032
+# DRAM traffic / algorithmic bytes of the fused MoE launch, from one ncu capture at B=256
+# (all 64 experts hit): (1157.2 + 22.2) MB / 1141.9 MB
+MOE_TRAFFIC_RATIO = 1.033
 
 
 def prompt_lengths(cfg: dict, batch: int) -> list[int]:
@@ -323,9 +323,9 @@ def run_ours(args, cfg_id: int):
                 "frac": round(dk_gbs / peak, 4) if dk_gbs else None,
                 "peak_kind": peak_kind,
                 "traffic": round(moe_bytes / max(moe_launches, 1) * MOE_TRAFFIC_RATIO),
-                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the same two launches "
-                                  "(dsv2.microbench moe_gate_up / moe_down, B=256, all 64 experts hit), "
-                                  "scaled to this launch by its algorithmic bytes",
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one fused MoE launch "
+                                  "(dsv2.microbench moe, B=256, all 64 experts hit), scaled to this launch "
+                                  "by its algorithmic bytes",
                 "algorithmic_bytes_per_launch": round(moe_bytes / max(moe_launches, 1)),
                 "launch_ms": round(moe_ms / max(moe_launches, 1), 5),
             },
