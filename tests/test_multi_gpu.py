@@ -86,7 +86,12 @@ def test_expert_parallel_matches_single_gpu(family, tmp_path):
         got = torch.load(f"{out}.{r}")
         rows = slice(r * half, (r + 1) * half)
         assert torch.equal(got["toks"][0], ref_toks[0, rows])
+        # a row is compared while its inputs agree: up to and including the first step
+        # whose greedy token differs (a near-tie can flip under the different summation
+        # order; from then on the row decodes a different sequence)
+        live = torch.ones(half, dtype=torch.bool)
         for s in range(STEPS):
             a, b = got["logits"][s].double(), ref_logits[s, rows].double()
             cos = (a * b).sum(-1) / (a.norm(dim=-1) * b.norm(dim=-1))
-            assert float(cos.min()) >= 0.999, (r, s, cos)
+            assert float(cos[live].min()) >= 0.999, (r, s, cos)
+            live &= got["toks"][s] == ref_toks[s, rows]
