@@ -222,7 +222,7 @@ def run_ours(args, cfg_id: int):
     eng = DecodeEngine(model, B, max_len, family, rank=rank, world=world, group=group, gate_bias=bias)
     t_build = time.time() - t0
     t0 = time.time()
-    eng.prefill(prompts, max_tokens_per_chunk=args.prefill_chunk)
+    eng.prefill(prompts, max_tokens_per_chunk=args.prefill_chunk, method=args.prefill)
     torch.cuda.synchronize()
     t_prefill = time.time() - t0
     launches_per_step = count_launches(lambda: (eng.step(), eng.restore()))
@@ -343,7 +343,8 @@ def run_ours(args, cfg_id: int):
             "launches_per_step": launches_per_step,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
-            "setup_s": {"build": round(t_build, 1), "prefill": round(t_prefill, 1)},
+            "setup_s": {"build": round(t_build, 1), "prefill": round(t_prefill, 1),
+                        "prefill_method": args.prefill, "prefill_tokens": sum(len(p) for p in prompts)},
         }
     if world > 1:
         import torch.distributed as dist
@@ -446,7 +447,9 @@ def main():
     ap.add_argument("--family", default=None, choices=["small", "batch"])
     ap.add_argument("--layers", type=int, default=27)
     ap.add_argument("--e2e-steps", type=int, default=20)
-    ap.add_argument("--prefill-chunk", type=int, default=16384)
+    ap.add_argument("--prefill-chunk", type=int, default=4096)
+    ap.add_argument("--prefill", default="kernels", choices=["kernels", "eager"],
+                    help="prompt prefill: the decode kernels over token batches, or the HF forward")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":

@@ -153,7 +153,7 @@ int mla_cache_map(const void* cache, int64_t cache_b_stride, int max_len, int ba
 int mla_decode_balanced(const MlaDecodeParams& p, int sms, long long part_slots, cudaStream_t st,
                         const char* what) {
   CUtensorMap tm_kv, tm_qa, tm_qp;
-  int rc = mla_cache_map(p.cache, p.cache_b_stride, p.max_len, p.batch, 32, &tm_kv);
+  int rc = mla_cache_map(p.cache, p.cache_b_stride, p.max_len, p.cache_batch, 32, &tm_kv);
   if (rc) return rc;
   // q_abs [B][16][512] and q_pe [B][16][64] as {dims, heads, rows} maps with 64 x 16 boxes
   if ((rc = tensor_map_3d(p.q_abs, 512, 16, static_cast<uint64_t>(p.batch), 1024, 16384, 16, &tm_qa))) return rc;
@@ -675,7 +675,10 @@ int dsv2_mla_prep(const dsv2_mla_prep_args* a, void* stream) {
     return fail(DSV2_ERR_INVALID, "mla_prep: operands must be 16-byte aligned");
   if (a->rope_stride < 32) return fail(DSV2_ERR_INVALID, "mla_prep: rope table stride %lld < 32", (long long)a->rope_stride);
   if (a->batch <= 0) return DSV2_OK;
-  MlaPrepParams p;
+  if (a->cache_batch < 0) return fail(DSV2_ERR_INVALID, "mla_prep: cache_batch %d", a->cache_batch);
+  MlaPrepParams p = {};
+  p.cache_rows = a->cache_rows;
+  p.cache_batch = a->cache_batch > 0 ? a->cache_batch : a->batch;
   if (a->qkva_dtype != DSV2_BF16 && a->qkva_dtype != DSV2_F32)
     return fail(DSV2_ERR_UNSUPPORTED, "mla_prep: qkva dtype %d", a->qkva_dtype);
   if (a->qkva_dtype == DSV2_F32 && (a->qkva_parts < 1 || a->qkva_part_stride % 4))
@@ -716,6 +719,8 @@ int dsv2_mla_decode(const dsv2_mla_decode_args* a, void* stream) {
     return fail(DSV2_ERR_INVALID, "mla_decode(batch): n_splits * split_len < max_len");
   if (!tc && !a->row_sync) return fail(DSV2_ERR_INVALID, "mla_decode: row_sync (int32[batch], zeroed) is required");
   if (tc && a->row_sync) return fail(DSV2_ERR_UNSUPPORTED, "mla_decode(batch): row_sync is not supported");
+  if (tc && a->cache_rows) return fail(DSV2_ERR_UNSUPPORTED, "mla_decode(batch): cache_rows is not supported");
+  if (a->cache_batch < 0) return fail(DSV2_ERR_INVALID, "mla_decode: cache_batch %d", a->cache_batch);
   if (!tc && static_cast<long long>(a->batch) * a->n_splits < 2)
     return fail(DSV2_ERR_INVALID, "mla_decode: batch * n_splits must give at least 2 partial slots");
   if (a->pos_numel != 1 && a->pos_numel != a->batch)
@@ -744,6 +749,8 @@ int dsv2_mla_decode(const dsv2_mla_decode_args* a, void* stream) {
   p.inputs_prior = a->inputs_prior != 0;
   p.row_sync = a->row_sync;
   p.batch = a->batch;
+  p.cache_rows = a->cache_rows;
+  p.cache_batch = a->cache_batch > 0 ? a->cache_batch : a->batch;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   CUtensorMap tm_kv;
   if (tc) {
@@ -797,6 +804,7 @@ int dsv2_mla_decode_noalloc(const void* q_abs, const void* q_pe, const void* cac
   p.row_sync = reinterpret_cast<int*>(scratch + static_cast<size_t>(kNoAllocMaxParts) * kHeads * (kLatent + 2));
   p.o_lat = reinterpret_cast<bf16*>(o_lat);
   p.batch = batch;
+  p.cache_batch = batch;
   return mla_decode_balanced(p, sms, kNoAllocMaxParts, static_cast<cudaStream_t>(stream), "mla_decode_noalloc");
 }
 

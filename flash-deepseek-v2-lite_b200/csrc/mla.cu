@@ -121,7 +121,12 @@ __global__ __launch_bounds__(256) void mla_prep_kernel(const MlaPrepParams p) {
     if (threadIdx.x == 0) set_device_error(kErrIndex);
     return;
   }
-  bf16* crow = p.cache + b * p.cache_b_stride + pos * kRow;
+  const int cr = p.cache_rows ? p.cache_rows[b] : b;
+  if (cr < 0 || cr >= p.cache_batch) {
+    if (threadIdx.x == 0) set_device_error(kErrIndex);
+    return;
+  }
+  bf16* crow = p.cache + static_cast<long long>(cr) * p.cache_b_stride + pos * kRow;
   const float* cs = p.cos_tab + pos * p.rope_stride;
   const float* sn = p.sin_tab + pos * p.rope_stride;
   // latent RMSNorm: threads 0..63 own 8 elements each
@@ -397,6 +402,12 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
       for (int b = b0; S < end && b < B; ++b, ++seg) {
         const int len = mla_row_len(p, b), nt = mla_tiles_of(len);
         const int j0 = static_cast<int>(max(0LL, start - S)), j1 = static_cast<int>(min(static_cast<long long>(nt), end - S));
+        // cache row read by query row b (prefill: many query rows share one sequence)
+        int crow_b = p.cache_rows ? p.cache_rows[b] : b;
+        if (crow_b < 0 || crow_b >= p.cache_batch) {
+          set_device_error(kErrIndex);
+          crow_b = 0;
+        }
         if (seg < kStages) early_rows[seg] = b;
         for (int j = j0; j < j1; ++j, ++g) {
           if (!waited && g >= kStages) {
@@ -412,7 +423,7 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
           mbar_arrive_expect_tx(&full_bar[st], kTileBytes);
           for (int ch = 0; ch < kChunks; ++ch)
             tma_load_3d(smem_u32(s_kv + st * kTileBytes + ch * (kTile * 128)), &tm_kv, &full_bar[st], ch * 64,
-                        j * kTile, b);
+                        j * kTile, crow_b);
         }
         S += nt;
       }

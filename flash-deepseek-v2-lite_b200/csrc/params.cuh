@@ -80,6 +80,8 @@ struct MlaPrepParams {
   long long cache_b_stride;    // elements
   int max_len;
   bf16* q_pe_out;              // [B, 16, 64]
+  const int* cache_rows;       // optional [B]: cache row of input row b (else b)
+  int cache_batch;             // rows of the cache
 };
 
 struct MlaDecodeParams {
@@ -102,6 +104,8 @@ struct MlaDecodeParams {
   int inputs_prior;            // q_pe / positions / cache written >= 2 launches earlier
   int* row_sync;               // [B] zero-initialised, left zero
   int batch;
+  const int* cache_rows;       // optional [B]: cache row read by query row b (else b)
+  int cache_batch;             // rows of the cache
 };
 
 // norm.cu

@@ -88,6 +88,7 @@ class MlaPrepArgs(ctypes.Structure):
         ("cache", c_vp), ("cache_b_stride", c_i64), ("max_len", c_i32),
         ("q_pe_out", c_vp), ("batch", c_i32),
         ("qkva_dtype", c_i32), ("qkva_parts", c_i32), ("qkva_part_stride", c_i64), ("q_nope_out", c_vp),
+        ("cache_rows", c_vp), ("cache_batch", c_i32),
     ]
 
 
@@ -97,6 +98,7 @@ class MlaDecodeArgs(ctypes.Structure):
         ("positions", c_vp), ("pos_numel", c_i32), ("softmax_scale", c_f32),
         ("split_len", c_i32), ("n_splits", c_i32), ("o_part", c_vp), ("ml_part", c_vp),
         ("o_lat", c_vp), ("batch", c_i32), ("inputs_prior", c_i32), ("row_sync", c_vp), ("family", c_i32),
+        ("cache_rows", c_vp), ("cache_batch", c_i32),
     ]
 
 

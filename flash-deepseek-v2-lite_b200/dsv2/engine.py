@@ -78,7 +78,8 @@ def _device_view(ptr: int, shape: tuple, dtype: torch.dtype, dev: torch.device) 
 class DecodeEngine:
     def __init__(self, model, batch: int, max_len: int, family: str = "batch", *,
                  rank: int = 0, world: int = 1, group=None, gate_bias: torch.Tensor | None = None,
-                 alias_hf: bool = True, fused_moe: bool = True, keep_logits: bool = False):
+                 alias_hf: bool = True, fused_moe: bool = True, keep_logits: bool = False,
+                 cache: torch.Tensor | None = None):
         cfg = model.config
         check_config(cfg)
         if family not in FAMILIES:
@@ -92,7 +93,11 @@ class DecodeEngine:
         self.max_len = int(max_len)
         self.rank, self.world, self.group = rank, world, group
         self.fused_moe = fused_moe
+        self._gate_bias = gate_bias
         self.keep_logits = keep_logits   # also materialise the bf16 logits every step
+        # cache given: rows of this engine are tokens of the cache's sequences (kernel
+        # prefill); cache_rows[b] names the sequence of row b
+        self._external_cache = cache
         self.B_all = self.B * world
         self.shard = ep_shard(int(cfg.n_routed_experts), self.B_all, rank, world)
         self.n_local = self.shard.n_local
@@ -121,7 +126,12 @@ class DecodeEngine:
     def _alloc(self):
         B, dev, bf = self.B, self.dev, torch.bfloat16
         f32, i32, i64 = torch.float32, torch.int32, torch.int64
-        self.cache = torch.zeros((self.L, B, self.max_len, LATENT_ROW), device=dev, dtype=bf)
+        if self._external_cache is not None:
+            self.cache = self._external_cache
+            self.cache_rows = torch.zeros(B, device=dev, dtype=i32)
+        else:
+            self.cache = torch.zeros((self.L, B, self.max_len, LATENT_ROW), device=dev, dtype=bf)
+            self.cache_rows = None
         self.positions = torch.zeros(B, device=dev, dtype=i64)
         self.input_ids = torch.zeros(B, device=dev, dtype=i64)
         self.next_ids = torch.zeros(B, device=dev, dtype=i64)
@@ -258,7 +268,8 @@ class DecodeEngine:
                          x_group_rows=B)
             qkva = self.qkva
         ops.mla_prep(qkva=qkva, kv_norm_w=a.kv_norm_w, eps=a.kv_norm_eps, cos=self.cos, sin=self.sin,
-                     positions=self.positions, cache=self.cache[li], q_pe_out=self.q_pe, q_nope_out=self.q_nope)
+                     positions=self.positions, cache=self.cache[li], q_pe_out=self.q_pe, q_nope_out=self.q_nope,
+                     cache_rows=self.cache_rows)
         # q_abs[b, h] = q_nope[b, h] @ W_UK[h]
         self._linear(w=a.w_uk_t, n_rows=KV_LORA, k=QK_NOPE, w_row_stride=QK_NOPE,
                      w_group_stride=KV_LORA * QK_NOPE, x=self.q_nope, x_row_stride=N_HEADS * QK_NOPE,
@@ -267,7 +278,8 @@ class DecodeEngine:
                      x_group_rows=B)
         ops.mla_decode(q_abs=self.q_abs, q_pe=self.q_pe, cache=self.cache[li], positions=self.positions,
                        softmax_scale=self.scale, split_len=self.split_len, o_part=self.o_part,
-                       ml_part=self.ml_part, o_lat=self.o_lat, inputs_prior=True, row_sync=self.mla_sync)
+                       ml_part=self.ml_part, o_lat=self.o_lat, inputs_prior=True, row_sync=self.mla_sync,
+                       cache_rows=self.cache_rows)
         # o[b, h] = o_lat[b, h] @ W_UV[h]^T,  W_UV[h] = kv_b[h*256 + 128 : h*256 + 256]
         self._linear(w=a.kv_b[QK_NOPE:], n_rows=V_DIM, k=KV_LORA, w_row_stride=KV_LORA,
                      w_group_stride=(QK_NOPE + V_DIM) * KV_LORA, x=self.o_lat, x_row_stride=N_HEADS * KV_LORA,
@@ -482,7 +494,71 @@ class DecodeEngine:
 
     # ------------------------------------------------------------------ prefill
     @torch.no_grad()
-    def prefill(self, prompts: list[torch.Tensor], max_tokens_per_chunk: int = 16384) -> torch.Tensor:
+    def prefill(self, prompts: list[torch.Tensor], max_tokens_per_chunk: int = 16384,
+                method: str = "kernels") -> torch.Tensor:
+        """Prefill this rank's rows and return the first generated token of every row.
+        method "kernels": the decode kernels run over all prompt tokens at once
+        (prefill_kernels); "eager": the HF model's own forward (prefill_eager)."""
+        if method == "kernels":
+            return self.prefill_kernels(prompts, max_tokens_per_chunk=min(max_tokens_per_chunk, 4096))
+        if method != "eager":
+            raise ValueError(f"unknown prefill method {method!r}")
+        return self.prefill_eager(prompts, max_tokens_per_chunk)
+
+    @torch.no_grad()
+    def prefill_kernels(self, prompts: list[torch.Tensor], max_tokens_per_chunk: int = 4096) -> torch.Tensor:
+        """Prefill through the same kernels as the decode step: every prompt token is a row
+        of a token batch (up to max_tokens_per_chunk tokens, across prompts); its latent
+        row goes straight into this engine's cache at (sequence, position), and its
+        attention reads the positions <= its own of its sequence (cache_rows), so the
+        chunk's tokens attend causally in one launch.  Chunks run in prompt order, all
+        layers each, so later chunks see every earlier token.  The token batch uses the
+        batch (tcgen05) kernels whatever this engine's family.  Returns the greedy next
+        token after each prompt (src/run.py:526-544 runs the HF forward instead)."""
+        if len(prompts) != self.B:
+            raise ValueError(f"expected {self.B} prompts, got {len(prompts)}")
+        if not 1 <= max_tokens_per_chunk <= 4096:
+            raise ValueError("max_tokens_per_chunk must be in [1, 4096] (router bucketing bound)")
+        lens = [int(p.numel()) for p in prompts]
+        if min(lens) < 1 or max(lens) >= self.max_len:
+            raise ValueError("prompts must hold 1 .. max_len - 1 tokens")
+        dev = self.dev
+        tokens = torch.cat([p.view(-1).to(device=dev, dtype=torch.int64) for p in prompts])
+        lens_t = torch.tensor(lens, device=dev, dtype=torch.int64)
+        seq = torch.repeat_interleave(torch.arange(self.B, device=dev, dtype=torch.int32), lens_t)
+        starts = torch.cumsum(lens_t, 0) - lens_t
+        pos = torch.arange(tokens.numel(), device=dev, dtype=torch.int64) - torch.repeat_interleave(starts, lens_t)
+        last = (torch.cumsum(lens_t, 0) - 1).cpu()
+        first = torch.zeros(self.B, dtype=torch.int64, device=dev)
+        n = tokens.numel()
+        subs: dict[int, DecodeEngine] = {}
+        try:
+            for c0 in range(0, n, max_tokens_per_chunk):
+                c1 = min(n, c0 + max_tokens_per_chunk)
+                t = c1 - c0
+                sub = subs.get(t)
+                if sub is None:
+                    sub = DecodeEngine(self.model, t, self.max_len, "batch", cache=self.cache,
+                                       gate_bias=self._gate_bias)
+                    subs[t] = sub
+                sub.cache_rows.copy_(seq[c0:c1])
+                sub.positions.copy_(pos[c0:c1])
+                sub.input_ids.copy_(tokens[c0:c1])
+                sub.step()
+                rows = [(b, int(last[b]) - c0) for b in range(self.B) if c0 <= int(last[b]) < c1]
+                if rows:
+                    bi = torch.tensor([r[0] for r in rows], device=dev)
+                    ti = torch.tensor([r[1] for r in rows], device=dev)
+                    first[bi] = sub.next_ids[ti]
+        finally:
+            for s in subs.values():
+                s.close()
+            subs.clear()
+        self.set_state(lens_t, first)
+        return first
+
+    @torch.no_grad()
+    def prefill_eager(self, prompts: list[torch.Tensor], max_tokens_per_chunk: int = 16384) -> torch.Tensor:
         """Eager HF prefill of this rank's rows (ragged prompts, right-padded in chunks).
 
         The latent cache rows are rebuilt from the kv_a_proj_with_mqa outputs that the HF

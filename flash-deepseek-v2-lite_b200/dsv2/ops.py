@@ -321,12 +321,14 @@ def _check_cache(cache: torch.Tensor) -> None:
 
 def mla_prep(*, qkva: torch.Tensor, kv_norm_w: torch.Tensor, eps: float, cos: torch.Tensor,
              sin: torch.Tensor, positions: torch.Tensor, cache: torch.Tensor,
-             q_pe_out: torch.Tensor, q_nope_out: torch.Tensor | None = None) -> None:
+             q_pe_out: torch.Tensor, q_nope_out: torch.Tensor | None = None,
+             cache_rows: torch.Tensor | None = None) -> None:
     """New-token preparation for one layer.
 
     qkva: bf16 [B, 3648], or fp32 split-K partial sums [S, B, 3648] (summed here);
-    cache: [B, max_len, 576] (one layer); positions int64 [1] or [B];
-    q_nope_out (optional): bf16 [B, 16, 128] copy of the (summed) q_nope."""
+    cache: [rows, max_len, 576] (one layer); positions int64 [1] or [B];
+    q_nope_out (optional): bf16 [B, 16, 128] copy of the (summed) q_nope;
+    cache_rows (optional): int32 [B], the cache row of each input row (default: row b)."""
     _cuda(qkva, "qkva")
     if qkva.dim() == 2 and qkva.dtype == torch.bfloat16:
         dt, parts, pstride, rstride, batch = DSV2_BF16, 1, 0, qkva.stride(0), qkva.shape[0]
@@ -363,6 +365,14 @@ def mla_prep(*, qkva: torch.Tensor, kv_norm_w: torch.Tensor, eps: float, cos: to
     a.qkva_parts = parts
     a.qkva_part_stride = pstride
     a.q_nope_out = _ptr(q_nope_out)
+    a.cache_batch = cache.shape[0]
+    if cache_rows is not None:
+        _cuda(cache_rows, "cache_rows")
+        if cache_rows.dtype != torch.int32 or cache_rows.numel() < batch:
+            raise ValueError("cache_rows must be int32 with one entry per input row")
+        a.cache_rows = cache_rows.data_ptr()
+    elif cache.shape[0] < batch:
+        raise ValueError("the cache has fewer rows than the batch (pass cache_rows)")
     _lib.call("dsv2_mla_prep", ctypes.byref(a), stream())
 
 
@@ -392,13 +402,15 @@ def mla_workspace(batch: int, max_len: int, split_len: int, device, family: int 
 def mla_decode(*, q_abs: torch.Tensor, q_pe: torch.Tensor, cache: torch.Tensor, positions: torch.Tensor,
                softmax_scale: float, split_len: int, o_part: torch.Tensor, ml_part: torch.Tensor,
                o_lat: torch.Tensor, inputs_prior: bool = False, row_sync: torch.Tensor | None = None,
-               family: int = FAMILY_SMALL) -> None:
+               family: int = FAMILY_SMALL, cache_rows: torch.Tensor | None = None) -> None:
     """Latent attention for every row (see dsv2_mla_decode_args in include/dsv2.h).
     inputs_prior: q_pe, positions and the cache were written at least two launches earlier
     on this stream (only q_abs by the previous one).
     family FAMILY_SMALL: balanced mma.sync kernel, one launch; split_len = fewest positions
     per CTA (multiple of 32); row_sync (int32 [B], zero-initialised, left zero) required.
     family FAMILY_BATCH: tcgen05 kernel over split_len-position splits + merge launch.
+    cache_rows (FAMILY_SMALL, optional): int32 [B], the cache row each query row reads
+    (kernel prefill: the tokens of one sequence attend causally through their positions).
     Buffers: see mla_workspace."""
     for name, t in (("q_abs", q_abs), ("q_pe", q_pe), ("o_part", o_part), ("ml_part", ml_part), ("o_lat", o_lat)):
         _cuda(t, name)
@@ -426,6 +438,14 @@ def mla_decode(*, q_abs: torch.Tensor, q_pe: torch.Tensor, cache: torch.Tensor, 
     a.batch = q_abs.shape[0]
     a.inputs_prior = 1 if inputs_prior else 0
     a.family = family
+    a.cache_batch = cache.shape[0]
+    if cache_rows is not None:
+        _cuda(cache_rows, "cache_rows")
+        if cache_rows.dtype != torch.int32 or cache_rows.numel() < q_abs.shape[0]:
+            raise ValueError("cache_rows must be int32 with one entry per query row")
+        a.cache_rows = cache_rows.data_ptr()
+    elif cache.shape[0] < q_abs.shape[0]:
+        raise ValueError("the cache has fewer rows than the batch (pass cache_rows)")
     if family == FAMILY_SMALL and row_sync is None:
         raise ValueError("mla_decode: row_sync (int32 [B], zeroed) is required; see mla_workspace")
     if row_sync is not None:

@@ -391,6 +391,11 @@ typedef struct dsv2_mla_prep_args {
   int64_t qkva_part_stride;
   /* optional [B, 16, 128] bf16 copy of q_nope (the input of the absorbed projection) */
   void* q_nope_out;
+  /* optional int32[batch]: the cache row (sequence) of each input row, so that several
+   * tokens of one sequence are prepared at once (kernel prefill); NULL = row b is cache
+   * row b.  cache_batch = rows of the cache (0 = batch). */
+  const int32_t* cache_rows;
+  int32_t cache_batch;
 } dsv2_mla_prep_args;
 
 DSV2_API int dsv2_mla_prep(const dsv2_mla_prep_args* args, void* stream);
@@ -436,6 +441,12 @@ typedef struct dsv2_mla_decode_args {
   /* DSV2_FAMILY_SMALL: mma.sync kernel (32-position tiles, balanced persistent grid);
    * DSV2_FAMILY_BATCH: tcgen05/TMEM kernel (64-position tiles, split grid + merge). */
   int32_t family;
+  /* optional int32[batch] (DSV2_FAMILY_SMALL only): the cache row (sequence) each query
+   * row attends to, so that many query tokens of one sequence attend at once (kernel
+   * prefill, causal through their positions); NULL = query row b reads cache row b.
+   * cache_batch = rows of the cache (0 = batch). */
+  const int32_t* cache_rows;
+  int32_t cache_batch;
 } dsv2_mla_decode_args;
 
 DSV2_API int dsv2_mla_decode(const dsv2_mla_decode_args* args, void* stream);
