@@ -12,7 +12,8 @@
 // router_topk_kernel: one CTA per 8 tokens computes all 64 logits on the tensor cores
 // (mma.sync m16n8k16, experts as M, tokens as N; bf16 products are exact in fp32, so
 // this is the fp32 linear up to summation order), warps split K and meet in shared
-// memory, then one warp per token does the softmax and the six argmax rounds
+// memory (16 warps: 4 expert blocks x 4 K quarters), then one warp per token does the
+// softmax and the six argmax rounds
 // (lowest index first on ties).
 //
 // route_kernel: stable counting sort of the routes by local expert.  Every CTA counts
@@ -30,7 +31,8 @@ constexpr int kTopK = 6;
 constexpr int kMaxExperts = 64;
 constexpr int kSlots = 8;              // 6 routed + 2 shared-expert halves per token
 constexpr int kRtTok = 8;              // tokens per CTA (the mma N dimension)
-constexpr int kRtThreads = 256;        // 8 warps: 4 expert blocks of 16 x 2 K halves
+constexpr int kRtKParts = 4;           // K quarters per expert block
+constexpr int kRtThreads = 128 * kRtKParts;  // 16 warps: 4 expert blocks of 16 x 4 K quarters
 constexpr int kRtMaxHidden = 2048;
 constexpr int kRouteTokMax = 32;       // tokens per route_kernel CTA (upper bound)
 constexpr int kRouteThreads = 256;
@@ -76,7 +78,7 @@ __global__ __launch_bounds__(kRtThreads) void router_topk_kernel(const RouterPar
   pdl_enter();
   constexpr int XS = kRtMaxHidden + 8;  // padded row (bank spread for the 16-byte reads)
   __shared__ __align__(16) bf16 s_x[kRtTok][XS];
-  __shared__ float s_part[2][kMaxExperts][kRtTok];
+  __shared__ float s_part[kRtKParts][kMaxExperts][kRtTok];
   __shared__ float s_logits[kRtTok][kMaxExperts];
   const int row0 = blockIdx.x * kRtTok;
   const int nt = min(kRtTok, p.rows - row0);
@@ -89,14 +91,14 @@ __global__ __launch_bounds__(kRtThreads) void router_topk_kernel(const RouterPar
     *reinterpret_cast<uint4*>(&s_x[t][c * 8]) = v;
   }
   __syncthreads();
-  // warp -> experts [16*eb, 16*eb + 16), K half kh
+  // warp -> experts [16*eb, 16*eb + 16), K part kh
   const int eb = warp & 3, kh = warp >> 2;
   const int gq = lane >> 2, tq = lane & 3;
   const int eA = eb * 16 + gq, eB = eA + 8;
   const bool okA = eA < p.n_experts, okB = eB < p.n_experts;
   float c[4] = {0.f, 0.f, 0.f, 0.f};
   const int nkb = p.hidden / 32;              // 32-wide K blocks
-  const int kb_beg = kh * (nkb / 2), kb_end = kh ? nkb : nkb / 2;
+  const int kb_beg = kh * nkb / kRtKParts, kb_end = (kh + 1) * nkb / kRtKParts;
   const bf16* xr = &s_x[gq][tq * 8];
   if (p.w_dtype == 0) {
     const bf16* wA = reinterpret_cast<const bf16*>(p.w) + static_cast<long long>(okA ? eA : 0) * p.hidden + tq * 8;
@@ -141,7 +143,9 @@ __global__ __launch_bounds__(kRtThreads) void router_topk_kernel(const RouterPar
   for (int i = tid; i < kRtTok * kMaxExperts; i += kRtThreads) {
     const int t = i / kMaxExperts, e = i % kMaxExperts;
     if (e < p.n_experts && t < nt) {
-      float v = s_part[0][e][t] + s_part[1][e][t];
+      float v = s_part[0][e][t];
+#pragma unroll
+      for (int q = 1; q < kRtKParts; ++q) v += s_part[q][e][t];
       if (p.bias) v += p.bias[e];
       s_logits[t][e] = v;
       p.logits[(row0 + t) * p.n_experts + e] = v;
