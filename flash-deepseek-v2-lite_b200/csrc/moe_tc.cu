@@ -11,9 +11,9 @@
 // Phase 2 item (group g, 128-row tile of the hidden dimension, token tile):
 //   y[route_slot[route], n] = bf16(W_down[g] h[route]) * route_weight[route]
 // A group is a routed expert or one half of the shared MLP (see the router's bucketing).
-// All phase-1 items followed by all phase-2 items form one list, groups that need
-// several token tiles first (the shared-expert halves at large batches, whose wide
-// epilogues are the longest, start early).  The first rounds are dealt round-robin;
+// All phase-1 items followed by all phase-2 items form one list, groups in order of token
+// count (largest first: the shared-expert halves at large batches, whose wide epilogues
+// are the longest, start early, and the list ends on the shortest items).  The first rounds are dealt round-robin;
 // the rest of the list is taken from a global counter, so the two GEMMs share one
 // balanced stream of weight tiles and no CTA is left with a whole extra item at the end.  A phase-2 item of group g starts once every phase-1 item of g has stored
 // its h rows: the phase-1 epilogue publishes a per-group counter (release), the
@@ -148,21 +148,18 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
     s_nts[g] = nts;
   }
   __syncthreads();
-  // groups that need more than one token tile (the shared-expert halves at large
-  // batches) go first, the rest keep their order
+  // groups in order of token count, largest first (ties by index): the multi-tile groups
+  // (the shared-expert halves at large batches) start early and the list ends on the
+  // items with the shortest epilogues
   {
-    __shared__ int s_nwide;
-    if (threadIdx.x == 0) s_nwide = 0;
-    __syncthreads();
-    int mine = 0;
-    for (int g = threadIdx.x; g < G; g += kMoeThreads) mine += s_nts[g] > 1;
-    if (mine) atomicAdd(&s_nwide, mine);
-    __syncthreads();
     for (int g = threadIdx.x; g < G; g += kMoeThreads) {
-      const bool wide = s_nts[g] > 1;
-      int before = 0;   // groups of the same class with a lower index
-      for (int h = 0; h < g; ++h) before += ((s_nts[h] > 1) == wide);
-      s_order[wide ? before : s_nwide + before] = g;
+      const int cg = s_cnt[g];
+      int rank = 0;   // groups with more tokens, or as many and a lower index
+      for (int h = 0; h < G; ++h) {
+        const int ch = s_cnt[h];
+        rank += (ch > cg) || (ch == cg && h < g);
+      }
+      s_order[rank] = g;
     }
   }
   __syncthreads();
