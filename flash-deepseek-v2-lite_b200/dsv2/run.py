@@ -41,6 +41,8 @@ def _parse_args(argv=None):
     ap.add_argument("--kernel-family", choices=sorted(FAMILIES), default=None,
                     help="small (GEMV) or batch (tcgen05); default: small for B <= 4, else batch")
     ap.add_argument("--device", type=str, default="cuda:0")
+    ap.add_argument("--prefill", choices=["kernels", "eager"], default="kernels",
+                    help="prompt prefill through the decode kernels or the HF forward")
     ap.add_argument("--dump-token-ids", action="store_true")
     ap.add_argument("--dump-step-trace", action="store_true")
     return ap.parse_args(argv)
@@ -95,7 +97,8 @@ def hardware_info(dev: torch.device) -> dict:
 
 
 def run_graph_decode(model, prompt: torch.Tensor, batch: int, max_new_tokens: int, family: str,
-                     dump_token_ids: bool = False, dump_step_trace: bool = False) -> dict:
+                     dump_token_ids: bool = False, dump_step_trace: bool = False,
+                     prefill: str = "kernels") -> dict:
     """Prefill + graph decode of `prompt` replicated over `batch` rows; returns the
     reference runner's per-batch result fields."""
     dev = prompt.device
@@ -104,7 +107,7 @@ def run_graph_decode(model, prompt: torch.Tensor, batch: int, max_new_tokens: in
     eng = DecodeEngine(model, batch, max_len, family)
     torch.cuda.synchronize(dev)
     t0 = time.perf_counter()
-    first = eng.prefill([prompt] * batch)
+    first = eng.prefill([prompt] * batch, method=prefill)
     torch.cuda.synchronize(dev)
     prefill_s = time.perf_counter() - t0
     collect = dump_token_ids or dump_step_trace
@@ -156,7 +159,7 @@ def main(argv=None) -> None:
     for b in _batch_sizes(args):
         family = args.kernel_family or ("small" if b <= 4 else "batch")
         results.append(run_graph_decode(model, prompt, b, args.max_new_tokens, family,
-                                        args.dump_token_ids, args.dump_step_trace))
+                                        args.dump_token_ids, args.dump_step_trace, prefill=args.prefill))
     hw = hardware_info(dev)
     doc = dict(results[0], hardware=hw) if len(results) == 1 else {"results": results, "hardware": hw}
     print(json.dumps(doc, ensure_ascii=False, indent=2))
