@@ -81,7 +81,6 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
     const __grid_constant__ CUtensorMap tm_x1, const __grid_constant__ CUtensorMap tm_x1b,
     const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_h,
     const __grid_constant__ CUtensorMap tm_hb, const MoeShape shp) {
-  pdl_enter();  // the group offsets and x come from the bucketing launch just before
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -129,6 +128,9 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // barriers, TMEM and tensor maps are set up while the previous launch finishes; the
+  // group offsets and x come from the bucketing launch just before
+  pdl_enter();
 
   const int n_tile = shp.n_tile;
   const int G = p.n_groups;
