@@ -525,10 +525,8 @@ class DecodeEngine:
         dev = self.dev
         tokens = torch.cat([p.view(-1).to(device=dev, dtype=torch.int64) for p in prompts])
         lens_t = torch.tensor(lens, device=dev, dtype=torch.int64)
-        seq = torch.repeat_interleave(torch.arange(self.B, device=dev, dtype=torch.int32), lens_t)
-        starts = torch.cumsum(lens_t, 0) - lens_t
-        pos = torch.arange(tokens.numel(), device=dev, dtype=torch.int64) - torch.repeat_interleave(starts, lens_t)
-        last = (torch.cumsum(lens_t, 0) - 1).cpu()
+        seq, pos, last = prefill_token_plan(lens_t)
+        last = last.cpu()
         first = torch.zeros(self.B, dtype=torch.int64, device=dev)
         n = tokens.numel()
         subs: dict[int, DecodeEngine] = {}
@@ -608,6 +606,17 @@ class DecodeEngine:
         pos = torch.tensor(lens, dtype=torch.int64, device=self.dev)
         self.set_state(pos, first)
         return first
+
+
+def prefill_token_plan(lens: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Token rows of a kernel prefill: prompts of lens [B] laid end to end.  Returns the
+    sequence of every token (int32, the cache row it writes and reads), its position in
+    its prompt (int64) and the index of each prompt's last token (int64 [B])."""
+    lens = lens.to(torch.int64)
+    seq = torch.repeat_interleave(torch.arange(lens.numel(), device=lens.device, dtype=torch.int32), lens)
+    starts = torch.cumsum(lens, 0) - lens
+    pos = torch.arange(int(lens.sum()), device=lens.device, dtype=torch.int64) - torch.repeat_interleave(starts, lens)
+    return seq, pos, torch.cumsum(lens, 0) - 1
 
 
 def latent_rows(kva: torch.Tensor, norm_w: torch.Tensor, eps: float, cos: torch.Tensor,

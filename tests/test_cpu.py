@@ -232,3 +232,15 @@ def test_ctypes_structs_match_the_header():
                 m = re.search(r"(\w+)\s*(\[\d+\])?\s*$", part.strip())
                 names.append(m.group(1))
         assert names == [f[0] for f in py._fields_], (cname, names, [f[0] for f in py._fields_])
+
+
+def test_prefill_token_plan():
+    """Kernel prefill rows: prompts end to end, positions restart per prompt, each
+    prompt's last token found (the greedy first token is read there)."""
+    from dsv2.engine import prefill_token_plan
+    lens = torch.tensor([3, 1, 4])
+    seq, pos, last = prefill_token_plan(lens)
+    assert seq.tolist() == [0, 0, 0, 1, 2, 2, 2, 2]
+    assert seq.dtype == torch.int32
+    assert pos.tolist() == [0, 1, 2, 0, 0, 1, 2, 3]
+    assert last.tolist() == [2, 3, 7]
