@@ -43,7 +43,8 @@ CONFIGS = {
 }
 WEIGHT_SEED = 1
 
-# algorithmic bytes (bf16 weights + latent KV), SURVEY section 8(d)
+# algorithmic bytes per step: bf16 weights read once (attention, dense MLP, shared experts,
+# gate, lm_head, distinct routed experts) + the latent KV rows attended
 ATTN_BYTES = 2 * 13_767_168
 DENSE_BYTES = 2 * 67_239_936
 SHARED_BYTES = 2 * 17_301_504

@@ -1,8 +1,9 @@
 """Generate the golden fixtures that pin the oracle (oracle/ops.py) to the reference.
 
-Run in the build container (needs /root/reference and the Triton CPU interpreter):
+Run where the reference checkout is available (its directory in DSV2_REFERENCE) with the
+Triton CPU interpreter:
 
-    TRITON_INTERPRET=1 python tests/golden/make_golden.py
+    DSV2_REFERENCE=<reference checkout> TRITON_INTERPRET=1 python tests/golden/make_golden.py
 
 Outputs (committed):
   tests/golden/ref_kernels.pt  inputs and outputs of the reference's own Triton kernels
@@ -28,7 +29,7 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REF = Path(os.environ.get("DSV2_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("DSV2_REFERENCE", str(REPO.parent / "reference")))
 
 
 def ref_kernels() -> dict:
