@@ -14,7 +14,9 @@
 // this is the fp32 linear up to summation order), warps split K and meet in shared
 // memory (16 warps: 4 expert blocks x 4 K quarters), then one warp per token does the
 // softmax and the six argmax rounds
-// (lowest index first on ties).
+// (lowest index first on ties).  It serves fp32 gates and the expert-parallel dispatch;
+// a bf16 gate on one rank takes router_topk_cluster_kernel (experts split over a 4-CTA
+// cluster, logits met in CTA 0's shared memory).
 //
 // route_kernel: stable counting sort of the routes by local expert.  Every CTA counts
 // all routes per expert (the top-k ids are a few KB) and the routes of earlier tokens,
@@ -181,6 +183,120 @@ __global__ __launch_bounds__(kRtThreads) void router_topk_kernel(const RouterPar
       for (int q = 0; q < pt.world; ++q) red_release_sys_add_u64(peer_ctr(pt, q, 0), 1ull);
     }
   }
+}
+
+// ---------------------------------------------------------------------------------
+// logits + softmax + top-6, experts split over a 4-CTA cluster (bf16 gate, one rank)
+// ---------------------------------------------------------------------------------
+// The single-CTA kernel above reads the whole gate (64 x 2048 bf16 = 256 KB) into every
+// CTA and fills only rows/8 SMs.  Here the four CTAs of a cluster share 8 tokens: CTA r
+// computes experts [16r, 16r + 16) (one mma M block) with its 16 warps each taking a
+// sixteenth of K, so a CTA reads 64 KB of gate and its weight fragments are loaded
+// before the programmatic-launch wait (weights are never written by earlier kernels).
+// Every CTA stores its 16 x 8 logits into CTA 0's shared memory (distributed shared
+// memory), and CTA 0 runs the softmax / top-6 after the cluster barrier.
+constexpr int kRcCtas = 4;                           // CTAs per cluster
+constexpr int kRcExperts = kMaxExperts / kRcCtas;    // experts per CTA (16)
+constexpr int kRcKParts = 16;                        // warps per CTA, one K part each
+constexpr int kRcThreads = 32 * kRcKParts;
+constexpr int kRcKb = kRtMaxHidden / 32 / kRcKParts;  // 32-wide K blocks per warp (4)
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+// store v at the address of `local` in the shared memory of cluster CTA `rank`
+__device__ __forceinline__ void st_cluster_f32(const float* local, uint32_t rank, float v) {
+  const uint32_t la = static_cast<uint32_t>(__cvta_generic_to_shared(local));
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+}
+
+__global__ __cluster_dims__(kRcCtas, 1, 1) __launch_bounds__(kRcThreads) void router_topk_cluster_kernel(
+    const RouterParams p) {
+  // first phase of the cluster barrier: every CTA has started (its shared memory exists)
+  // before any CTA stores into it; the matching wait comes after the GEMV
+  cluster_arrive_relaxed();
+  constexpr int XS = kRtMaxHidden + 8;
+  __shared__ __align__(16) bf16 s_x[kRtTok][XS];
+  __shared__ float s_part[kRcKParts][kRcExperts][kRtTok];
+  __shared__ float s_logits[kRtTok][kMaxExperts];
+  const uint32_t crank = cluster_ctarank();
+  const int row0 = static_cast<int>(blockIdx.x / kRcCtas) * kRtTok;
+  const int nt = min(kRtTok, p.rows - row0);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int eA = static_cast<int>(crank) * kRcExperts + gq, eB = eA + 8;
+  const bool okA = eA < p.n_experts, okB = eB < p.n_experts;
+  const int nkb = p.hidden / 32;
+  const int kb_beg = warp * nkb / kRcKParts, kb_end = (warp + 1) * nkb / kRcKParts;
+  const bf16* w = reinterpret_cast<const bf16*>(p.w);
+  const bf16* wA = w + static_cast<long long>(okA ? eA : 0) * p.hidden + tq * 8;
+  const bf16* wB = w + static_cast<long long>(okB ? eB : 0) * p.hidden + tq * 8;
+  uint4 a[kRcKb], b[kRcKb];
+#pragma unroll
+  for (int u = 0; u < kRcKb; ++u) {
+    const int kb = kb_beg + u;
+    a[u] = (kb < kb_end && okA) ? *reinterpret_cast<const uint4*>(wA + kb * 32) : make_uint4(0, 0, 0, 0);
+    b[u] = (kb < kb_end && okB) ? *reinterpret_cast<const uint4*>(wB + kb * 32) : make_uint4(0, 0, 0, 0);
+  }
+  pdl_enter();
+  const int nch = p.hidden / 8;
+  for (int i = tid; i < kRtTok * nch; i += kRcThreads) {
+    const int t = i / nch, c = i % nch;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (t < nt) v = *reinterpret_cast<const uint4*>(p.x + (row0 + t) * p.x_row_stride + c * 8);
+    *reinterpret_cast<uint4*>(&s_x[t][c * 8]) = v;
+  }
+  __syncthreads();
+  float c[4] = {0.f, 0.f, 0.f, 0.f};
+  const bf16* xr = &s_x[gq][tq * 8];
+#pragma unroll
+  for (int u = 0; u < kRcKb; ++u) {
+    const int kb = kb_beg + u;
+    if (kb >= kb_end) break;
+    const uint4 xv = *reinterpret_cast<const uint4*>(xr + kb * 32);
+    const uint32_t a0[4] = {a[u].x, b[u].x, a[u].y, b[u].y};
+    mma_bf16_16816(c, a0, xv.x, xv.y);
+    const uint32_t a1[4] = {a[u].z, b[u].z, a[u].w, b[u].w};
+    mma_bf16_16816(c, a1, xv.z, xv.w);
+  }
+  s_part[warp][gq][2 * tq] = c[0];
+  s_part[warp][gq][2 * tq + 1] = c[1];
+  s_part[warp][gq + 8][2 * tq] = c[2];
+  s_part[warp][gq + 8][2 * tq + 1] = c[3];
+  __syncthreads();
+  cluster_wait_acquire();
+  if (tid < kRcExperts * kRtTok) {
+    const int el = tid / kRtTok, t = tid % kRtTok;
+    const int e = static_cast<int>(crank) * kRcExperts + el;
+    if (e < p.n_experts && t < nt) {
+      float v = s_part[0][el][t];
+#pragma unroll
+      for (int q = 1; q < kRcKParts; ++q) v += s_part[q][el][t];
+      if (p.bias) v += p.bias[e];
+      p.logits[(row0 + t) * p.n_experts + e] = v;
+      st_cluster_f32(&s_logits[t][e], 0, v);
+    }
+  }
+  // second phase: CTA 0 sees every CTA's logits; the others leave after it
+  cluster_arrive_release();
+  cluster_wait_acquire();
+  if (crank != 0) return;
+  if (warp < nt)
+    softmax_topk_warp(s_logits[warp], p.n_experts, p.scaling, row0 + warp, p.topk_ids, p.topk_ids32,
+                      p.topk_w);
 }
 
 // ---------------------------------------------------------------------------------
@@ -393,7 +509,11 @@ static cudaError_t launch_route(const int* ids32, const float* tw, int rows, int
 }
 
 cudaError_t launch_router(const RouterParams& p, cudaStream_t st) {
-  launch_kernel(router_topk_kernel, (p.rows + kRtTok - 1) / kRtTok, kRtThreads, 0, st, p);
+  const int blocks = (p.rows + kRtTok - 1) / kRtTok;
+  if (p.w_dtype == 0 && p.peers.world == 0)
+    launch_kernel(router_topk_cluster_kernel, blocks * kRcCtas, kRcThreads, 0, st, p);
+  else
+    launch_kernel(router_topk_kernel, blocks, kRtThreads, 0, st, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || !p.group_offsets) return e;
   return launch_route(p.topk_ids32, p.topk_w, p.rows, p.expert_lo, p.n_local, p.shared_lo,
