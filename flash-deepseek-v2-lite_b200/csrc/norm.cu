@@ -96,15 +96,16 @@ __global__ __launch_bounds__(kNormThreads) void rmsnorm_kernel(const bf16* __res
 // [rows][n_delta][cols] (part stride delta_part_stride).  n_delta == 0 means no add.
 // When h_out != nullptr the sum is written there instead of in place.
 // acc[0..7] += sum over p < n of src[p * stride + 0..7] (fp32), added in order of p.  The
-// loads of four partials are issued before their adds, so a thread keeps 8 independent
-// 16-byte loads in flight instead of one round trip per partial.  l2_only: read through
+// loads of eight partials are issued before their adds, so a thread keeps 16 independent
+// 16-byte loads in flight instead of one round trip per partial (the MoE's eight slots
+// and the split-K partials of the dense linears take one round).  l2_only: read through
 // L2 only (partials written by another CTA of the previous launch).
 __device__ __forceinline__ void sum_parts8(const float* src, long long stride, int n, float (&acc)[8],
                                            bool l2_only) {
-  for (int p0 = 0; p0 < n; p0 += 4) {
-    float4 a[4], b[4];
+  for (int p0 = 0; p0 < n; p0 += 8) {
+    float4 a[8], b[8];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < 8; ++q) {
       if (p0 + q < n) {
         const float4* s = reinterpret_cast<const float4*>(src + (p0 + q) * stride);
         a[q] = l2_only ? __ldcg(s) : s[0];
@@ -112,7 +113,7 @@ __device__ __forceinline__ void sum_parts8(const float* src, long long stride, i
       }
     }
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < 8; ++q) {
       if (p0 + q < n) {
         acc[0] += a[q].x; acc[1] += a[q].y; acc[2] += a[q].z; acc[3] += a[q].w;
         acc[4] += b[q].x; acc[5] += b[q].y; acc[6] += b[q].z; acc[7] += b[q].w;
