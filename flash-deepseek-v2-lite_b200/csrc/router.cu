@@ -24,7 +24,10 @@
 // inside a CTA, routes are ranked in (token, k) order.  Two extra "shared" groups
 // carry the local tokens with weight 1 (slots 6 and 7), so the MoE kernels run the two
 // shared experts in the same launch as the routed ones.  Optionally the same kernel
-// copies each route's activation row into expert-contiguous order for the TMA path.
+// copies each route's activation row into expert-contiguous order for the TMA path: with
+// at most one token per warp, each warp loads its piece of its token's row together with
+// the routing ids and stores it to all of the token's placed slots; larger CTAs copy one
+// placed row per warp.
 #include "params.cuh"
 
 namespace dsv2 {
@@ -333,20 +336,47 @@ __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams 
     __syncthreads();
     if (!s_ok) return;
   }
+  static_assert(kRouteTokMax * kTopK <= kRouteThreads, "one thread per route of the CTA");
+  constexpr int kRouteWarps = kRouteThreads / 32;
   __shared__ int s_total[kMaxExperts];
   __shared__ int s_before[kMaxExperts];
   __shared__ int s_off[kMaxExperts + 3];
   __shared__ int s_e[kRouteTokMax * kTopK];
   __shared__ int s_pos[kRouteTokMax * kSlots];
   __shared__ int s_tok[kRouteTokMax * kSlots];
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tpc = p.tok_per_cta;
   const int tok0 = blockIdx.x * tpc;
   const int ntok = min(tpc, p.rows - tok0);
-  for (int i = tid; i < kMaxExperts; i += kRouteThreads) { s_total[i] = 0; s_before[i] = 0; }
-  __syncthreads();
   const int n_routes = p.rows * kTopK;
   const int r_first = tok0 * kTopK;
+  const int my_routes = ntok * kTopK;
+  // Issued together with the counting loads below: this thread's own route (route tid of
+  // the CTA) and, when the CTA has at most one token per warp-group, its share of its
+  // token's activation row, which every placed slot of that token receives.
+  int e_mine = -1;
+  float w_mine = 0.f;
+  if (tid < my_routes) {
+    e_mine = __ldcg(p.ids32 + r_first + tid) - p.expert_lo;
+    w_mine = __ldcg(p.tw + r_first + tid);
+  }
+  const int n16 = p.cols / 8;
+  const bool reg_gather = p.gout && ntok > 0 && ntok <= kRouteWarps && n16 <= 8 * 32 * (kRouteWarps / ntok);
+  const int gw_per_tok = reg_gather ? kRouteWarps / ntok : 1;
+  const int g_tok = warp / gw_per_tok, g_part = warp % gw_per_tok;
+  const bool g_warp = reg_gather && g_tok < ntok;
+  const int c_beg = g_part * n16 / gw_per_tok, c_end = (g_part + 1) * n16 / gw_per_tok;
+  uint4 xv[8];
+  if (g_warp) {
+    const uint4* src = reinterpret_cast<const uint4*>(p.gx + static_cast<long long>(tok0 + g_tok) * p.gx_stride);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int c = c_beg + u * 32 + lane;
+      if (c < c_end) xv[u] = __ldcg(src + c);
+    }
+  }
+  for (int i = tid; i < kMaxExperts; i += kRouteThreads) { s_total[i] = 0; s_before[i] = 0; }
+  __syncthreads();
   // all routes' expert ids, eight loads in flight per thread
   for (int r0 = 0; r0 < n_routes; r0 += 8 * kRouteThreads) {
     int ev[8];
@@ -388,15 +418,12 @@ __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams 
     }
   }
   // this CTA's routes, in (token, k) order
-  const int my_routes = ntok * kTopK;
-  for (int i = tid; i < my_routes; i += kRouteThreads) {
-    const int e = __ldcg(p.ids32 + r_first + i) - p.expert_lo;
-    s_e[i] = (e >= 0 && e < p.n_local) ? e : -1;
-  }
+  if (tid < my_routes) s_e[tid] = (e_mine >= 0 && e_mine < p.n_local) ? e_mine : -1;
   __syncthreads();
   if (blockIdx.x == 0)
     for (int g = tid; g <= p.n_local + 2; g += kRouteThreads) p.group_offsets[g] = s_off[g];
-  for (int i = tid; i < my_routes; i += kRouteThreads) {
+  if (tid < my_routes) {
+    const int i = tid;
     const int e = s_e[i];
     int pos = -1;
     if (e >= 0) {
@@ -407,7 +434,7 @@ __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams 
       const int b = r / kTopK, k = r % kTopK;
       p.route_token[pos] = b;
       p.route_slot[pos] = b * kSlots + k;
-      p.route_weight[pos] = __ldcg(p.tw + r);
+      p.route_weight[pos] = w_mine;
       s_tok[i] = b;
     }
     s_pos[i] = pos;
@@ -428,11 +455,24 @@ __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams 
   }
   if (!p.gout) return;
   __syncthreads();
+  if (reg_gather) {
+    // the staged row pieces go to every placed slot of their token (6 routed, 2 shared)
+    if (!g_warp) return;
+    for (int sl = 0; sl < kSlots; ++sl) {
+      const int pos = sl < kTopK ? s_pos[g_tok * kTopK + sl] : s_pos[tpc * kTopK + (sl - kTopK) * tpc + g_tok];
+      if (pos < 0) continue;
+      uint4* dst = reinterpret_cast<uint4*>(p.gout + static_cast<long long>(pos) * p.cols);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c_beg + u * 32 + lane;
+        if (c < c_end) dst[c] = xv[u];
+      }
+    }
+    return;
+  }
   // gather: one warp per placed row; each lane holds up to 8 16-byte chunks in flight
-  const int warp = tid >> 5, lane = tid & 31;
   const int nslots = tpc * kSlots;
-  const int n16 = p.cols / 8;
-  for (int i = warp; i < nslots; i += kRouteThreads / 32) {
+  for (int i = warp; i < nslots; i += kRouteWarps) {
     if (i < tpc * kTopK && i >= my_routes) continue;
     const int pos = s_pos[i];
     if (pos < 0) continue;

@@ -116,7 +116,9 @@ def _router_case(B, seed, bias=False):
     return x, w, b
 
 
-@pytest.mark.parametrize("B", [1, 3, 16, 17, 64, 256])
+# B up to 148 places one token per bucketing CTA, 300 three (two warps per token), 700 five
+# (one warp per token), 1300 nine (the row-per-warp gather of larger CTAs)
+@pytest.mark.parametrize("B", [1, 3, 16, 17, 64, 256, 300, 700, 1300])
 def test_router_topk_and_bucketing(D, B):
     x, w, bias = _router_case(B, 10 + B, bias=(B == 17))
     lg, ids, wts = O.router(x, w, 1.0, bias)
