@@ -57,10 +57,27 @@ constexpr int kMlaMaxCtas = 160;                // merge scratch: 2 x 16 x CTAs 
 // ----------------------------------------------------------------------------
 
 __global__ __launch_bounds__(256) void mla_prep_kernel(const MlaPrepParams p) {
+  const int t = threadIdx.x;
+  // the latent norm weights are never written by earlier kernels: load them before the wait
+  float kw[8];
+  if (t < 64) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) kw[j] = __bfloat162float(p.kv_norm_w[t * 8 + j]);
+  }
   pdl_enter();
   __shared__ float red[8];
   __shared__ __align__(16) bf16 s_row[kHeads * 192 + kRow];  // this row of qkva, bf16
   const int b = blockIdx.x;
+  // position, cache row and this thread's RoPE coefficients (every RoPE pair of thread t
+  // has pair index t % 32) are fetched while the split-K partials are in flight
+  const long long pos = p.positions[p.pos_numel == 1 ? 0 : b];
+  const bool pos_ok = (pos >= 0 && pos < p.max_len && pos < p.rope_rows);
+  const int cr = p.cache_rows ? p.cache_rows[b] : b;
+  float rc = 0.f, rs = 0.f;
+  if (pos_ok) {
+    rc = p.cos_tab[pos * p.rope_stride + (t & 31)];
+    rs = p.sin_tab[pos * p.rope_stride + (t & 31)];
+  }
   // stage the row (summing fp32 split-K partials and rounding to bf16, like a bf16 linear)
   if (p.qkva_f32) {
     // 912 float4 per row over 256 threads: each thread sums its (up to 4) float4 columns,
@@ -115,22 +132,16 @@ __global__ __launch_bounds__(256) void mla_prep_kernel(const MlaPrepParams p) {
           *reinterpret_cast<const uint4*>(row + h * 192 + c * 8);
     }
   }
-  long long pos = p.positions[p.pos_numel == 1 ? 0 : b];
-  const bool pos_ok = (pos >= 0 && pos < p.max_len && pos < p.rope_rows);
   if (!pos_ok) {
     if (threadIdx.x == 0) set_device_error(kErrIndex);
     return;
   }
-  const int cr = p.cache_rows ? p.cache_rows[b] : b;
   if (cr < 0 || cr >= p.cache_batch) {
     if (threadIdx.x == 0) set_device_error(kErrIndex);
     return;
   }
   bf16* crow = p.cache + static_cast<long long>(cr) * p.cache_b_stride + pos * kRow;
-  const float* cs = p.cos_tab + pos * p.rope_stride;
-  const float* sn = p.sin_tab + pos * p.rope_stride;
   // latent RMSNorm: threads 0..63 own 8 elements each
-  const int t = threadIdx.x;
   float v[8];
   float ss = 0.f;
   if (t < 64) {
@@ -152,11 +163,7 @@ __global__ __launch_bounds__(256) void mla_prep_kernel(const MlaPrepParams p) {
     uint4 o;
     uint32_t* op = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float w0 = __bfloat162float(p.kv_norm_w[t * 8 + 2 * j]);
-      const float w1 = __bfloat162float(p.kv_norm_w[t * 8 + 2 * j + 1]);
-      op[j] = pack_bf16x2(v[2 * j] * inv * w0, v[2 * j + 1] * inv * w1);
-    }
+    for (int j = 0; j < 4; ++j) op[j] = pack_bf16x2(v[2 * j] * inv * kw[2 * j], v[2 * j + 1] * inv * kw[2 * j + 1]);
     *reinterpret_cast<uint4*>(crow + t * 8) = o;
   }
   // RoPE pairs: 16 heads x 32 pairs of q_pe, plus 32 pairs of k_pe
@@ -164,8 +171,7 @@ __global__ __launch_bounds__(256) void mla_prep_kernel(const MlaPrepParams p) {
     const int h = i >> 5, j = i & 31;
     const bf16* src = (h < kHeads) ? (row + h * 192 + 128 + 2 * j) : (row + kHeads * 192 + kLatent + 2 * j);
     const float e = __bfloat162float(src[0]), o = __bfloat162float(src[1]);
-    const float c = cs[j], s = sn[j];
-    const float re = e * c - o * s, im = o * c + e * s;
+    const float re = e * rc - o * rs, im = o * rc + e * rs;
     const uint32_t packed = pack_bf16x2(re, im);
     if (h < kHeads)
       *reinterpret_cast<uint32_t*>(p.q_pe_out + (static_cast<long long>(b) * kHeads + h) * kRope + 2 * j) = packed;
