@@ -26,6 +26,7 @@ thread_local std::string g_last_error;
 std::mutex g_mu;
 bool g_dev_init[128];
 int g_dev_sms[128];
+float* g_noalloc_scratch[128];  // device address of the allocation-free entry point's array
 
 int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char* fmt, ...) {
@@ -73,6 +74,8 @@ int ensure_init(int* sms_out) {
       return fail(DSV2_ERR_LAUNCH, "moe_tc_init: %s", cudaGetErrorString(e));
     if ((e = mla_tc_init()) != cudaSuccess)
       return fail(DSV2_ERR_LAUNCH, "mla_tc_init: %s", cudaGetErrorString(e));
+    if ((e = mla_noalloc_lookup(&g_noalloc_scratch[dev])) != cudaSuccess)
+      return fail(DSV2_ERR_LAUNCH, "scratch address of the allocation-free entry point: %s", cudaGetErrorString(e));
     g_dev_sms[dev] = sms;
     g_dev_init[dev] = true;
   }
@@ -184,6 +187,8 @@ int to_peers(const dsv2_peer_table* t, PeerTable* out) {
   out->rows_per_rank = t->rows_per_rank;
   out->n_moe = t->n_moe_layers;
   out->epoch = reinterpret_cast<const long long*>(t->epoch);
+  if (t->wait_polls < 0) return fail(DSV2_ERR_INVALID, "peer table: wait_polls %d", t->wait_polls);
+  out->wait_polls = static_cast<unsigned int>(t->wait_polls);
   return DSV2_OK;
 }
 
@@ -237,12 +242,46 @@ int dsv2_get_device_error(int* code, int clear) {
   if (!code) return fail(DSV2_ERR_INVALID, "code is NULL");
   cudaError_t e = cudaMemcpyFromSymbol(code, g_device_error, sizeof(int));
   if (e != cudaSuccess) return check_launch(e, "read device error");
-  if (clear) {
+  if (clear && *code != 0) {
+    // a launch that gave up may have left row tickets of the allocation-free attention
+    // entry point's array nonzero: wait for the device, then zero them with the word
+    if ((e = cudaDeviceSynchronize()) != cudaSuccess) return check_launch(e, "clear device error: sync");
+    int dev = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return check_launch(e, "clear device error: device");
+    float* scratch = nullptr;
+    if (dev >= 0 && dev < 128) {
+      std::lock_guard<std::mutex> lk(g_mu);
+      scratch = g_noalloc_scratch[dev];
+    }
+    if (scratch && (e = cudaMemset(scratch + kNoAllocTicketOffset, 0, kNoAllocMaxRows * sizeof(int))) != cudaSuccess)
+      return check_launch(e, "clear device error: row tickets");
     const int zero = 0;
     e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
     if (e != cudaSuccess) return check_launch(e, "clear device error");
+    if ((e = cudaDeviceSynchronize()) != cudaSuccess) return check_launch(e, "clear device error: sync");
   }
   return DSV2_OK;
+}
+
+int dsv2_stream_check(void* stream) {
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return check_launch(e, "stream_check: synchronize");
+  int code = 0;
+  if ((e = cudaMemcpyFromSymbol(&code, g_device_error, sizeof(int))) != cudaSuccess)
+    return check_launch(e, "stream_check: read device error");
+  if (code == 0) return DSV2_OK;
+  static const char* what[] = {"none", "a bounded wait gave up", "an index was out of range",
+                               "tensor memory allocation failed"};
+  return fail(DSV2_ERR_DEVICE, "device error word %d (%s); read and clear it with dsv2_get_device_error",
+              code, code >= 0 && code <= 3 ? what[code] : "unknown");
+}
+
+int dsv2_reset_progress(void* counters, int64_t count, void* stream) {
+  if (count < 0 || (count > 0 && !counters)) return fail(DSV2_ERR_INVALID, "reset_progress: bad arguments");
+  if (count == 0) return DSV2_OK;
+  return check_launch(cudaMemsetAsync(counters, 0, static_cast<size_t>(count) * sizeof(int32_t),
+                                      static_cast<cudaStream_t>(stream)),
+                      "reset_progress");
 }
 
 int dsv2_rmsnorm(const void* x, int64_t x_row_stride, const void* w, int w_dtype, void* y,
@@ -785,9 +824,13 @@ int dsv2_mla_decode_noalloc(const void* q_abs, const void* q_pe, const void* cac
   int sms = 0;
   int rc = ensure_init(&sms);
   if (rc) return rc;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(DSV2_ERR_LAUNCH, "mla_decode_noalloc: cudaGetDevice");
   float* scratch = nullptr;
-  cudaError_t e = mla_noalloc_scratch(&scratch);
-  if (e != cudaSuccess) return check_launch(e, "mla_decode_noalloc: scratch address");
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    scratch = g_noalloc_scratch[dev];
+  }
   MlaDecodeParams p = {};
   p.q_abs = reinterpret_cast<const bf16*>(q_abs);
   p.q_pe = reinterpret_cast<const bf16*>(q_pe);
@@ -801,7 +844,7 @@ int dsv2_mla_decode_noalloc(const void* q_abs, const void* q_pe, const void* cac
   p.n_splits = 1;
   p.o_part = scratch;
   p.ml_part = scratch + static_cast<size_t>(kNoAllocMaxParts) * kHeads * kLatent;
-  p.row_sync = reinterpret_cast<int*>(scratch + static_cast<size_t>(kNoAllocMaxParts) * kHeads * (kLatent + 2));
+  p.row_sync = reinterpret_cast<int*>(scratch + kNoAllocTicketOffset);
   p.o_lat = reinterpret_cast<bf16*>(o_lat);
   p.batch = batch;
   p.cache_batch = batch;

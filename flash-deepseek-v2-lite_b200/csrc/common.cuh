@@ -80,11 +80,15 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned 
 __device__ __forceinline__ void red_release_sys_add_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-// Returns false (and records kErrMbarTimeout) when the counter does not reach target;
-// gives up at once when an earlier wait of any kernel already failed (so that a broken
-// exchange ends quickly instead of timing out at every layer).
-__device__ __forceinline__ bool wait_counter_sys(const unsigned long long* ctr, unsigned long long target) {
-  for (uint32_t i = 0; i < (1u << 24); ++i) {
+// Returns false (and records kErrMbarTimeout) when the counter does not reach target
+// within `polls` polls (0: 2^24, several seconds); gives up at once when an earlier wait
+// of any kernel already failed (so that a broken exchange ends quickly instead of timing
+// out at every layer).
+constexpr uint32_t kPeerWaitPolls = 1u << 24;
+__device__ __forceinline__ bool wait_counter_sys(const unsigned long long* ctr, unsigned long long target,
+                                                 uint32_t polls) {
+  const uint32_t limit = polls ? polls : kPeerWaitPolls;
+  for (uint32_t i = 0; i < limit; ++i) {
     if (ld_acquire_sys_u64(ctr) >= target) return true;
     if ((i & 255) == 0 && *reinterpret_cast<volatile int*>(&g_device_error) != 0) return false;
     __nanosleep(64);

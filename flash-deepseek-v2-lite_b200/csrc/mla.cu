@@ -829,7 +829,8 @@ __global__ __launch_bounds__(128) void mla_combine_kernel(const float* __restric
 // ----------------------------------------------------------------------------
 // Scratch for dsv2_mla_decode_noalloc: the partials (o: [parts, 16, 512] then
 // (m, l): [parts, 16, 2], two parts per CTA, kNoAllocMaxParts parts) and the row
-// tickets (int32[kNoAllocMaxRows], zero from load time; every call leaves them zero)
+// tickets (int32[kNoAllocMaxRows], zero from load time; every call that completes leaves
+// them zero, and clearing a nonzero device error word zeroes them after one that gave up)
 // in one fixed file-scope device array, so that entry point allocates nothing.  Every
 // GPU that loads the library holds these 8.4 MB until the process exits.  Host code
 // must not use the symbol as a pointer: its device address is looked up once per
@@ -839,22 +840,16 @@ constexpr int kNoAllocMaxParts = 256;
 constexpr int kNoAllocMaxRows = 4096;
 constexpr size_t kNoAllocFloats =
     static_cast<size_t>(kNoAllocMaxParts) * kHeads * (kLatent + 2) + kNoAllocMaxRows;
+constexpr size_t kNoAllocTicketOffset = static_cast<size_t>(kNoAllocMaxParts) * kHeads * (kLatent + 2);
 static __device__ __align__(256) float g_mla_noalloc_scratch[kNoAllocFloats];
-static float* g_mla_noalloc_ptr[128];
 
-// Device address of the scratch array on the current device (looked up on first use).
-cudaError_t mla_noalloc_scratch(float** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+// Device address of the scratch array on the current device.  Called once per device by
+// the library's per-device set-up (under its lock); the result is cached there.
+cudaError_t mla_noalloc_lookup(float** out) {
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_mla_noalloc_scratch);
   if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
-  if (!g_mla_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_mla_noalloc_scratch);
-    if (e != cudaSuccess) return e;
-    g_mla_noalloc_ptr[dev] = static_cast<float*>(p);
-  }
-  *out = g_mla_noalloc_ptr[dev];
+  *out = static_cast<float*>(p);
   return cudaSuccess;
 }
 

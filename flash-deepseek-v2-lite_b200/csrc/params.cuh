@@ -21,6 +21,7 @@ struct PeerTable {
   int rows_per_rank;
   int n_moe;                  // MoE layers per step
   const long long* epoch;     // completed steps of this rank
+  unsigned int wait_polls;    // poll limit of the cross-GPU waits (0 = kPeerWaitPolls)
 };
 
 __device__ __forceinline__ unsigned long long* peer_ctr(const PeerTable& t, int rank, int which) {

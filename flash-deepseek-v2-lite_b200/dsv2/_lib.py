@@ -55,6 +55,7 @@ class PeerTable(ctypes.Structure):
         ("world", c_i32), ("rank", c_i32), ("base", c_vp * 8),
         ("xg_offset", c_i64), ("ids_offset", c_i64), ("w_offset", c_i64), ("part_offset", c_i64),
         ("ctr_offset", c_i64), ("rows_per_rank", c_i32), ("n_moe_layers", c_i32), ("epoch", c_vp),
+        ("wait_polls", c_i32),
     ]
 
 
@@ -109,6 +110,8 @@ _SIGNATURES = {
     "dsv2_set_programmatic_launch": ([c_i32], c_i32),
     "dsv2_kernel_launches": ([], c_i64),
     "dsv2_get_device_error": ([ctypes.POINTER(c_i32), c_i32], c_i32),
+    "dsv2_stream_check": ([c_vp], c_i32),
+    "dsv2_reset_progress": ([c_vp, c_i64, c_vp], c_i32),
     "dsv2_rmsnorm": ([c_vp, c_i64, c_vp, c_i32, c_vp, c_i64, c_i32, c_i32, c_f32, c_vp], c_i32),
     "dsv2_add_rmsnorm": ([c_vp, c_vp, c_vp, c_i32, c_i32, c_i64, c_i64, c_vp, c_i32, c_vp, c_i32, c_i32,
                           c_f32, ctypes.POINTER(PeerTable), c_i32, c_vp], c_i32),
@@ -227,3 +230,13 @@ def device_error(clear: bool = True) -> int:
     code = c_i32(0)
     check(load().dsv2_get_device_error(ctypes.byref(code), 1 if clear else 0), "dsv2_get_device_error")
     return int(code.value)
+
+
+def stream_check(stream: int | None) -> None:
+    """Wait for `stream` and raise Dsv2Error if the device error word is set (not cleared)."""
+    check(load().dsv2_stream_check(stream), "dsv2_stream_check")
+
+
+def reset_progress(counters, count: int, stream: int | None) -> None:
+    """Zero `count` int32 progress counters (MoE group counters, attention row tickets) on `stream`."""
+    check(load().dsv2_reset_progress(counters, count, stream), "dsv2_reset_progress")

@@ -418,12 +418,14 @@ class DecodeEngine:
 
         trace (eager debugging/tests only): collects the residual stream after every layer
         ("hidden", fp32 [B, 2048] each, HF output_hidden_states order starting with the
-        embeddings) and the router's top-6 ids of every MoE layer ("routes")."""
+        embeddings), the router's top-6 ids of every MoE layer ("routes") and the
+        normalised activations that router read ("moe_x", bf16 [B, 2048])."""
         lp0 = self.layers[0]
         ops.embed_rmsnorm(self.input_ids, self.embed, lp0.in_norm_w, lp0.eps, self.h, self.x)
         if trace is not None:
             trace.setdefault("hidden", []).append(self.h.float().clone())
             trace.setdefault("routes", [])
+            trace.setdefault("moe_x", [])
         delta = None
         self._moe_pending = None
         for li, lp in enumerate(self.layers):
@@ -437,6 +439,7 @@ class DecodeEngine:
                 trace["hidden"].append(self.h.float() + d)
                 if lp.moe is not None:
                     trace["routes"].append(self.topk_ids64.clone())
+                    trace["moe_x"].append(self.x.clone())
         self._add_rmsnorm(delta, self.final_norm_w, self.final_eps)
         if self.keep_logits:  # checking / debugging only: the greedy step needs no logits
             torch.mm(self.x, self.lm_head.t(), out=self.logits)
@@ -491,6 +494,30 @@ class DecodeEngine:
 
     def release(self) -> None:
         self.graph = None
+
+    def recover(self) -> int:
+        """Check the device after a step: returns the device error word (0 = every bounded
+        wait and index check passed).  A nonzero word is cleared, and the progress counters
+        that a launch which gave up may have left behind (the fused MoE's group counters,
+        the latent attention's row tickets) are zeroed, so later steps compute correct
+        results again.  Expert-parallel engines cannot recover in place (their peer
+        counters follow the step count on every rank): they raise, and every rank
+        rebuilds its engine."""
+        from . import _lib
+        torch.cuda.synchronize(self.dev)
+        with torch.cuda.device(self.dev):
+            code = _lib.device_error(clear=True)
+            if code == 0:
+                return 0
+            if self.peers is not None:
+                raise _lib.Dsv2Error(f"device error {code} in an expert-parallel step: rebuild the engine "
+                                     "on every rank")
+            s = ops.stream()
+            for t in (getattr(self, "moe_sync", None), self.mla_sync):
+                if t is not None:
+                    _lib.reset_progress(t.data_ptr(), t.numel(), s)
+            torch.cuda.synchronize(self.dev)
+        return code
 
     # ------------------------------------------------------------------ prefill
     @torch.no_grad()

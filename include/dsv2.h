@@ -72,9 +72,36 @@ DSV2_API int dsv2_set_programmatic_launch(int enable);
  * streams), for launch accounting.  No reference counterpart. */
 DSV2_API int64_t dsv2_kernel_launches(void);
 
+/* ---- device error word ------------------------------------------------------
+ * Kernels never trap: a bounded wait that runs out, or an index check that fails,
+ * records a code in the current device's error word (first code wins) and the kernel
+ * skips the offending work.  Codes: */
+#define DSV2_DEVERR_TIMEOUT 1 /* a bounded wait (mbarrier, progress counter, peer) gave up */
+#define DSV2_DEVERR_INDEX 2   /* token id >= vocab, position >= max_len, cache row, tile bound */
+#define DSV2_DEVERR_TMEM 3    /* tensor-memory allocation failed */
+
 /* Reads (and optionally clears) the device error word of the current device.
- * Synchronous (cudaMemcpyFromSymbol); call outside the hot loop. */
+ * Synchronous (cudaMemcpyFromSymbol); call outside the hot loop.  Clearing a nonzero
+ * word first waits for the device and also zeroes the row tickets of the array that
+ * dsv2_mla_decode_noalloc uses (a launch that gave up can leave them nonzero).
+ * Progress counters owned by the caller (dsv2_moe sync, dsv2_mla_decode row_sync)
+ * must be zeroed by the caller after a nonzero word: dsv2_reset_progress.
+ * Expert-parallel state (peer counters derived from the step count) is not
+ * recoverable this way: every rank rebuilds its peer buffers. */
 DSV2_API int dsv2_get_device_error(int* code, int clear);
+
+/* Waits for `stream` (cudaStreamSynchronize) and returns DSV2_ERR_DEVICE, with the code
+ * in dsv2_last_error(), when the device error word is set; DSV2_OK otherwise.  Does not
+ * clear the word.  For hosts that check each step's status through the C ABI.  No
+ * reference counterpart (the reference's Triton kernels have no device-side checks). */
+DSV2_API int dsv2_stream_check(void* stream);
+
+/* Zeroes `count` int32 progress counters on `stream` (cudaMemsetAsync, capturable): the
+ * fused MoE's sync array and the latent attention's row_sync tickets, which every
+ * successful launch leaves at zero but a launch that gave up may not.  Call after
+ * reading a nonzero device error word, before the next launch that uses them.  No
+ * reference counterpart. */
+DSV2_API int dsv2_reset_progress(void* counters, int64_t count, void* stream);
 
 /* ---- expert parallelism over NVLink peer memory -------------------------------- */
 /* Every rank allocates one peer-visible buffer (dsv2_peer_alloc), exports it
@@ -102,6 +129,9 @@ typedef struct dsv2_peer_table {
   int32_t rows_per_rank;
   int32_t n_moe_layers;
   const int64_t* epoch;
+  /* polls before a cross-GPU wait gives up and sets the device error word
+   * (DSV2_DEVERR_TIMEOUT); 0 = the default 2^24 (several seconds) */
+  int32_t wait_polls;
 } dsv2_peer_table;
 
 DSV2_API int dsv2_peer_alloc(size_t bytes, void** ptr);
@@ -462,12 +492,17 @@ DSV2_API int dsv2_mla_decode(const dsv2_mla_decode_args* args, void* stream);
  * device array inside libdsv2.so (8.4 MB, held by every GPU that loads the library
  * until the process exits).  The caller still passes every input and
  * the o_lat output, laid out as for dsv2_mla_decode.
- * The first call on each device looks up that array's device address
- * (cudaGetSymbolAddress) and the kernels' shared-memory attributes; make that first
- * call before any stream capture.  Nothing needs clearing between calls (every
- * partial the merge reads is written earlier in the same call), but all calls share
- * the one array, so calls that overlap on the GPU (different streams, or several
- * host threads) race and corrupt each other's results: serialise them. */
+ * The first call of any libdsv2 entry point on a device (or dsv2_init) looks up that
+ * array's device address (cudaGetSymbolAddress) together with the kernels'
+ * shared-memory attributes, under the library's lock; make that first call before any
+ * stream capture.  The address is cached per device index for the life of the
+ * process: after cudaDeviceReset, reload the library.  Between successful calls
+ * nothing needs clearing (every partial the merge reads is written earlier in the same
+ * call, and every call leaves the row tickets at zero).  A call that gives up on a
+ * bounded wait sets the device error word and may leave tickets nonzero; clearing the
+ * word with dsv2_get_device_error(&code, 1) zeroes them.  All calls share the one
+ * array, so calls that overlap on the GPU (different streams, or several host threads)
+ * race and corrupt each other's results: serialise them. */
 DSV2_API int dsv2_mla_decode_noalloc(const void* q_abs, const void* q_pe, const void* cache,
                                      int64_t cache_b_stride, int max_len, const int64_t* positions,
                                      int pos_numel, float softmax_scale, int split_len, void* o_lat,

@@ -131,13 +131,18 @@ def moe(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, gate_up: torc
         down: torch.Tensor, shared_gate: torch.Tensor, shared_up: torch.Tensor,
         shared_down: torch.Tensor) -> torch.Tensor:
     """HF DeepseekV2Moe.forward (:121-128) + DeepseekV2Experts.forward (:58-80) in fp32 sums:
-    out = sum_k w_k * expert_{id_k}(x) + shared_mlp(x)  (returned in fp32)."""
-    out = torch.zeros(x.shape[0], x.shape[1], dtype=torch.float32)
-    for b in range(x.shape[0]):
-        for k in range(ids.shape[1]):
-            e = int(ids[b, k])
-            y = expert_mlp(x[b:b + 1], gate_up[e], down[e])
-            out[b] += y[0].float() * float(weights[b, k])
+    out = sum_k w_k * expert_{id_k}(x) + shared_mlp(x)  (returned in fp32).  Like HF's eager
+    experts loop, each expert hit runs once over all of its routed rows, and its weighted
+    outputs are added to their rows in fp32.  Runs on the tensors' device."""
+    out = torch.zeros(x.shape[0], x.shape[1], dtype=torch.float32, device=x.device)
+    ids = ids.to(x.device)
+    weights = weights.to(x.device)
+    flat = ids.reshape(-1)
+    for e in torch.unique(flat).tolist():
+        r = torch.nonzero(flat == e).flatten()
+        b = r // ids.shape[1]
+        y = expert_mlp(x[b], gate_up[e], down[e]).float()
+        out.index_add_(0, b, y * weights.reshape(-1)[r].float().view(-1, 1))
     sh = expert_mlp(x, torch.cat([shared_gate, shared_up], 0), shared_down)
     return out + sh.float()
 

@@ -244,3 +244,32 @@ def test_prefill_token_plan():
     assert seq.dtype == torch.int32
     assert pos.tolist() == [0, 1, 2, 0, 0, 1, 2, 3]
     assert last.tolist() == [2, 3, 7]
+
+
+def test_synthetic_model_matches_the_oracle_configuration():
+    """The package's synthetic model builder (used by bench.py and the runner) produces the
+    architecture written out independently in oracle/hf_model.py (shapes, routing, eps,
+    YaRN RoPE) and, for a given seed, the same weights."""
+    from dsv2 import synthetic as S
+    from oracle import hf_model as H
+    ours, ref = S.dsv2_lite_config(num_layers=27), H.dsv2_lite_config(num_layers=27)
+    for k, v in H.ARCH.items():
+        assert getattr(ours, k) == v, k
+    assert ours.num_hidden_layers == ref.num_hidden_layers == 27
+    assert dict(ours.rope_parameters) == dict(ref.rope_parameters) == H.YARN
+    assert ours._attn_implementation == ref._attn_implementation == "eager"
+    assert ours._experts_implementation == ref._experts_implementation == "eager"
+    assert torch.equal(S.router_bias_zipf(64, 1.1, 4), H.router_bias_zipf(64, 1.1, 4))
+    # weight fill: the same draws from the same seed (on a reduced vocabulary and the dense
+    # layer only, so that the CPU test stays fast)
+    small = H.dsv2_lite_config(num_layers=1)
+    small.vocab_size = 1024
+    a = S.build_model(small, seed=5)
+    b = H.build_model(small, seed=5)
+    pa, pb = dict(a.named_parameters()), dict(b.named_parameters())
+    assert pa.keys() == pb.keys()
+    for k in pa:
+        assert torch.equal(pa[k], pb[k]), k
+    # and the oracle's attention scale / rotary scaling follow the HF modules built from it
+    attn = b.model.layers[0].self_attn
+    assert abs(attn.scaling - 192 ** -0.5) < 1e-12

