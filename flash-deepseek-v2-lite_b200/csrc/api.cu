@@ -27,6 +27,7 @@ std::mutex g_mu;
 bool g_dev_init[128];
 int g_dev_sms[128];
 float* g_noalloc_scratch[128];  // device address of the allocation-free entry point's array
+int g_router_clusters[128];     // router_fused_kernel clusters resident at once
 
 int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char* fmt, ...) {
@@ -76,11 +77,21 @@ int ensure_init(int* sms_out) {
       return fail(DSV2_ERR_LAUNCH, "mla_tc_init: %s", cudaGetErrorString(e));
     if ((e = mla_noalloc_lookup(&g_noalloc_scratch[dev])) != cudaSuccess)
       return fail(DSV2_ERR_LAUNCH, "scratch address of the allocation-free entry point: %s", cudaGetErrorString(e));
+    if ((e = router_fused_max_clusters(&g_router_clusters[dev])) != cudaSuccess)
+      return fail(DSV2_ERR_LAUNCH, "router occupancy: %s", cudaGetErrorString(e));
     g_dev_sms[dev] = sms;
     g_dev_init[dev] = true;
   }
   if (sms_out) *sms_out = g_dev_sms[dev];
   return DSV2_OK;
+}
+
+// router_fused_kernel clusters resident at once on the current device (after ensure_init)
+int router_clusters() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 0;
+  std::lock_guard<std::mutex> lk(g_mu);
+  return g_router_clusters[dev];
 }
 
 // ---- TMA tensor maps ---------------------------------------------------------
@@ -619,6 +630,19 @@ int dsv2_router(const dsv2_router_args* a, void* stream) {
     return fail(DSV2_ERR_UNSUPPORTED, "router: gate dtype %d", a->w_dtype);
   if (a->gather_out && (!a->group_offsets || !aligned16(a->gather_out)))
     return fail(DSV2_ERR_INVALID, "router: gather_out needs bucketing and 16-byte alignment");
+  if (a->h) {
+    if (a->w_dtype != DSV2_BF16 || (a->peers && a->peers->world > 1))
+      return fail(DSV2_ERR_UNSUPPORTED, "router: the fused residual add + RMSNorm needs a bf16 gate on one rank");
+    if (!a->norm_w || (a->n_delta > 0 && !a->delta) || a->n_delta < 0)
+      return fail(DSV2_ERR_INVALID, "router: fused RMSNorm needs norm_w (and delta when n_delta > 0)");
+    if (a->delta_dtype != DSV2_BF16 && a->delta_dtype != DSV2_F32)
+      return fail(DSV2_ERR_UNSUPPORTED, "router: delta dtype %d", a->delta_dtype);
+    if (a->norm_w_dtype != DSV2_BF16 && a->norm_w_dtype != DSV2_F32)
+      return fail(DSV2_ERR_UNSUPPORTED, "router: norm weight dtype %d", a->norm_w_dtype);
+    if (!aligned16(a->h) || (a->delta && !aligned16(a->delta)) || a->delta_row_stride % 8 ||
+        a->delta_part_stride % 8)
+      return fail(DSV2_ERR_INVALID, "router: h / delta must be 16-byte aligned rows");
+  }
   if (a->rows <= 0) return DSV2_OK;
   if (a->group_offsets) {
     if (!a->route_token || !a->route_slot || !a->route_weight)
@@ -653,7 +677,20 @@ int dsv2_router(const dsv2_router_args* a, void* stream) {
   p.route_token = a->route_token;
   p.route_slot = a->route_slot;
   p.route_weight = a->route_weight;
-  return check_launch(launch_router(p, static_cast<cudaStream_t>(stream)), "router");
+  p.h = reinterpret_cast<bf16*>(a->h);
+  p.delta = a->delta;
+  p.delta_dtype = a->delta_dtype;
+  p.n_delta = a->delta ? a->n_delta : 0;
+  p.delta_part_stride = a->delta_part_stride;
+  p.delta_row_stride = a->delta_row_stride;
+  p.norm_w = a->norm_w;
+  p.norm_w_dtype = a->norm_w_dtype;
+  p.eps = a->eps;
+  p.x_out = a->h ? reinterpret_cast<bf16*>(const_cast<void*>(a->x)) : nullptr;
+  p.grid_sync = a->sync;
+  int sms = 0;
+  if (int rc = ensure_init(&sms)) return rc;
+  return check_launch(launch_router(p, router_clusters(), sms, static_cast<cudaStream_t>(stream)), "router");
 }
 
 int dsv2_softmax_topk(const float* logits, int rows, int n_experts, float scaling,
@@ -686,10 +723,12 @@ int dsv2_moe_bucket(const int32_t* topk_ids32, const float* topk_weights, int ro
                      !aligned16(gather_out)))
     return fail(DSV2_ERR_INVALID, "moe_bucket: gather rows must be 16-byte aligned");
   if (rows <= 0) return DSV2_OK;
+  int sms = 0;
+  if (int rc = ensure_init(&sms)) return rc;
   return check_launch(launch_bucket(topk_ids32, topk_weights, rows, expert_lo, n_local, shared_lo,
                                     shared_hi, group_offsets, route_token, route_slot, route_weight,
                                     gather_out ? gather_src : nullptr, gather_src_stride, gather_out,
-                                    cols, static_cast<cudaStream_t>(stream), &pt, moe_layer),
+                                    cols, sms, static_cast<cudaStream_t>(stream), &pt, moe_layer),
                       "moe_bucket");
 }
 

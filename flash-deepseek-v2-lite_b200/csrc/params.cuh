@@ -60,6 +60,18 @@ struct RouterParams {
   void* gather_out;
   PeerTable peers;         // world > 0: write x / ids / weights of these rows to every rank
   int row_base;            // global index of this rank's first row
+  // fused residual add + RMSNorm ahead of the gate (h != nullptr; router_fused_kernel):
+  // h[r] = bf16(h[r] + sum_p delta[r, p]), x_out[r] = rmsnorm(h[r]) * norm_w
+  bf16* h;
+  const void* delta;
+  int delta_dtype;         // 0 bf16, 2 fp32 partials
+  int n_delta;
+  long long delta_part_stride, delta_row_stride;
+  const void* norm_w;
+  int norm_w_dtype;
+  float eps;
+  bf16* x_out;             // normalised rows (row stride x_row_stride); x == x_out then
+  int* grid_sync;          // [2] grid barrier of the single-launch bucketing (nullptr: two launches)
 };
 
 struct MlaPrepParams {
@@ -132,9 +144,10 @@ cudaError_t launch_argmax_finalize(const unsigned long long* keys, int n_blocks,
                                    long long* positions, int pos_numel, long long* step_counter,
                                    cudaStream_t st);
 // router.cu
-cudaError_t launch_router(const RouterParams&, cudaStream_t);
+cudaError_t launch_router(const RouterParams&, int max_clusters, int num_sms, cudaStream_t);
+cudaError_t router_fused_max_clusters(int* n);
 cudaError_t launch_bucket(const int*, const float*, int, int, int, int, int, int*, int*, int*,
-                          float*, const void*, long long, void*, int, cudaStream_t,
+                          float*, const void*, long long, void*, int, int, cudaStream_t,
                           const PeerTable* peers, int layer);
 cudaError_t launch_softmax_topk(const float*, int, int, float, long long*, int*, float*,
                                 cudaStream_t);

@@ -15,8 +15,9 @@
 // memory (16 warps: 4 expert blocks x 4 K quarters), then one warp per token does the
 // softmax and the six argmax rounds
 // (lowest index first on ties).  It serves fp32 gates and the expert-parallel dispatch;
-// a bf16 gate on one rank takes router_topk_cluster_kernel (experts split over a 4-CTA
-// cluster, logits met in CTA 0's shared memory).
+// a bf16 gate on one rank takes router_fused_kernel (experts split over a 4-CTA cluster,
+// logits met in CTA 0's shared memory), which can also form its inputs (residual add +
+// RMSNorm) and bucket the routes in the same launch.
 //
 // route_kernel: stable counting sort of the routes by local expert.  Every CTA counts
 // all routes per expert (the top-k ids are a few KB) and the routes of earlier tokens,
@@ -189,120 +190,6 @@ __global__ __launch_bounds__(kRtThreads) void router_topk_kernel(const RouterPar
 }
 
 // ---------------------------------------------------------------------------------
-// logits + softmax + top-6, experts split over a 4-CTA cluster (bf16 gate, one rank)
-// ---------------------------------------------------------------------------------
-// The single-CTA kernel above reads the whole gate (64 x 2048 bf16 = 256 KB) into every
-// CTA and fills only rows/8 SMs.  Here the four CTAs of a cluster share 8 tokens: CTA r
-// computes experts [16r, 16r + 16) (one mma M block) with its 16 warps each taking a
-// sixteenth of K, so a CTA reads 64 KB of gate and its weight fragments are loaded
-// before the programmatic-launch wait (weights are never written by earlier kernels).
-// Every CTA stores its 16 x 8 logits into CTA 0's shared memory (distributed shared
-// memory), and CTA 0 runs the softmax / top-6 after the cluster barrier.
-constexpr int kRcCtas = 4;                           // CTAs per cluster
-constexpr int kRcExperts = kMaxExperts / kRcCtas;    // experts per CTA (16)
-constexpr int kRcKParts = 16;                        // warps per CTA, one K part each
-constexpr int kRcThreads = 32 * kRcKParts;
-constexpr int kRcKb = kRtMaxHidden / 32 / kRcKParts;  // 32-wide K blocks per warp (4)
-
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void cluster_arrive_relaxed() {
-  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_arrive_release() {
-  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait_acquire() {
-  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
-}
-// store v at the address of `local` in the shared memory of cluster CTA `rank`
-__device__ __forceinline__ void st_cluster_f32(const float* local, uint32_t rank, float v) {
-  const uint32_t la = static_cast<uint32_t>(__cvta_generic_to_shared(local));
-  uint32_t ra;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(rank));
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
-}
-
-__global__ __cluster_dims__(kRcCtas, 1, 1) __launch_bounds__(kRcThreads) void router_topk_cluster_kernel(
-    const RouterParams p) {
-  // first phase of the cluster barrier: every CTA has started (its shared memory exists)
-  // before any CTA stores into it; the matching wait comes after the GEMV
-  cluster_arrive_relaxed();
-  constexpr int XS = kRtMaxHidden + 8;
-  __shared__ __align__(16) bf16 s_x[kRtTok][XS];
-  __shared__ float s_part[kRcKParts][kRcExperts][kRtTok];
-  __shared__ float s_logits[kRtTok][kMaxExperts];
-  const uint32_t crank = cluster_ctarank();
-  const int row0 = static_cast<int>(blockIdx.x / kRcCtas) * kRtTok;
-  const int nt = min(kRtTok, p.rows - row0);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int gq = lane >> 2, tq = lane & 3;
-  const int eA = static_cast<int>(crank) * kRcExperts + gq, eB = eA + 8;
-  const bool okA = eA < p.n_experts, okB = eB < p.n_experts;
-  const int nkb = p.hidden / 32;
-  const int kb_beg = warp * nkb / kRcKParts, kb_end = (warp + 1) * nkb / kRcKParts;
-  const bf16* w = reinterpret_cast<const bf16*>(p.w);
-  const bf16* wA = w + static_cast<long long>(okA ? eA : 0) * p.hidden + tq * 8;
-  const bf16* wB = w + static_cast<long long>(okB ? eB : 0) * p.hidden + tq * 8;
-  uint4 a[kRcKb], b[kRcKb];
-#pragma unroll
-  for (int u = 0; u < kRcKb; ++u) {
-    const int kb = kb_beg + u;
-    a[u] = (kb < kb_end && okA) ? *reinterpret_cast<const uint4*>(wA + kb * 32) : make_uint4(0, 0, 0, 0);
-    b[u] = (kb < kb_end && okB) ? *reinterpret_cast<const uint4*>(wB + kb * 32) : make_uint4(0, 0, 0, 0);
-  }
-  pdl_enter();
-  const int nch = p.hidden / 8;
-  for (int i = tid; i < kRtTok * nch; i += kRcThreads) {
-    const int t = i / nch, c = i % nch;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (t < nt) v = *reinterpret_cast<const uint4*>(p.x + (row0 + t) * p.x_row_stride + c * 8);
-    *reinterpret_cast<uint4*>(&s_x[t][c * 8]) = v;
-  }
-  __syncthreads();
-  float c[4] = {0.f, 0.f, 0.f, 0.f};
-  const bf16* xr = &s_x[gq][tq * 8];
-#pragma unroll
-  for (int u = 0; u < kRcKb; ++u) {
-    const int kb = kb_beg + u;
-    if (kb >= kb_end) break;
-    const uint4 xv = *reinterpret_cast<const uint4*>(xr + kb * 32);
-    const uint32_t a0[4] = {a[u].x, b[u].x, a[u].y, b[u].y};
-    mma_bf16_16816(c, a0, xv.x, xv.y);
-    const uint32_t a1[4] = {a[u].z, b[u].z, a[u].w, b[u].w};
-    mma_bf16_16816(c, a1, xv.z, xv.w);
-  }
-  s_part[warp][gq][2 * tq] = c[0];
-  s_part[warp][gq][2 * tq + 1] = c[1];
-  s_part[warp][gq + 8][2 * tq] = c[2];
-  s_part[warp][gq + 8][2 * tq + 1] = c[3];
-  __syncthreads();
-  cluster_wait_acquire();
-  if (tid < kRcExperts * kRtTok) {
-    const int el = tid / kRtTok, t = tid % kRtTok;
-    const int e = static_cast<int>(crank) * kRcExperts + el;
-    if (e < p.n_experts && t < nt) {
-      float v = s_part[0][el][t];
-#pragma unroll
-      for (int q = 1; q < kRcKParts; ++q) v += s_part[q][el][t];
-      if (p.bias) v += p.bias[e];
-      p.logits[(row0 + t) * p.n_experts + e] = v;
-      st_cluster_f32(&s_logits[t][e], 0, v);
-    }
-  }
-  // second phase: CTA 0 sees every CTA's logits; the others leave after it
-  cluster_arrive_release();
-  cluster_wait_acquire();
-  if (crank != 0) return;
-  if (warp < nt)
-    softmax_topk_warp(s_logits[warp], p.n_experts, p.scaling, row0 + warp, p.topk_ids, p.topk_ids32,
-                      p.topk_w);
-}
-
-// ---------------------------------------------------------------------------------
 // bucketing (+ optional gather of activation rows)
 // ---------------------------------------------------------------------------------
 struct RouteParams {
@@ -324,21 +211,12 @@ struct RouteParams {
   int layer;               // MoE layer index (expected dispatch arrivals)
 };
 
-__global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams p) {
-  pdl_enter();
-  if (p.peers.world > 0) {
-    // every rank's router has written its rows into this rank's buffer
-    __shared__ int s_ok;
-    if (threadIdx.x == 0) {
-      const unsigned long long per_rank = (p.peers.rows_per_rank + kRtTok - 1) / kRtTok;
-      s_ok = wait_counter_sys(peer_ctr(p.peers, p.peers.rank, 0), peer_target(p.peers, p.layer, per_rank),
-                              p.peers.wait_polls);
-    }
-    __syncthreads();
-    if (!s_ok) return;
-  }
-  static_assert(kRouteTokMax * kTopK <= kRouteThreads, "one thread per route of the CTA");
-  constexpr int kRouteWarps = kRouteThreads / 32;
+// Bucketing of the tokens [cta * tok_per_cta, +tok_per_cta) by one CTA of THREADS threads
+// (shared by the separate bucketing launch and the fused router).
+template <int THREADS>
+__device__ void route_cta(const RouteParams& p, int cta) {
+  static_assert(kRouteTokMax * kTopK <= THREADS, "one thread per route of the CTA");
+  constexpr int kRouteWarps = THREADS / 32;
   __shared__ int s_total[kMaxExperts];
   __shared__ int s_before[kMaxExperts];
   __shared__ int s_off[kMaxExperts + 3];
@@ -347,7 +225,7 @@ __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams 
   __shared__ int s_tok[kRouteTokMax * kSlots];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tpc = p.tok_per_cta;
-  const int tok0 = blockIdx.x * tpc;
+  const int tok0 = cta * tpc;
   const int ntok = min(tpc, p.rows - tok0);
   const int n_routes = p.rows * kTopK;
   const int r_first = tok0 * kTopK;
@@ -376,19 +254,19 @@ __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams 
       if (c < c_end) xv[u] = __ldcg(src + c);
     }
   }
-  for (int i = tid; i < kMaxExperts; i += kRouteThreads) { s_total[i] = 0; s_before[i] = 0; }
+  for (int i = tid; i < kMaxExperts; i += THREADS) { s_total[i] = 0; s_before[i] = 0; }
   __syncthreads();
   // all routes' expert ids, eight loads in flight per thread
-  for (int r0 = 0; r0 < n_routes; r0 += 8 * kRouteThreads) {
+  for (int r0 = 0; r0 < n_routes; r0 += 8 * THREADS) {
     int ev[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
-      const int r = r0 + u * kRouteThreads + tid;
+      const int r = r0 + u * THREADS + tid;
       ev[u] = r < n_routes ? __ldcg(p.ids32 + r) - p.expert_lo : -1;
     }
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
-      const int r = r0 + u * kRouteThreads + tid;
+      const int r = r0 + u * THREADS + tid;
       const int e = ev[u];
       if (r < n_routes && e >= 0 && e < p.n_local) {
         atomicAdd(&s_total[e], 1);
@@ -421,8 +299,8 @@ __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams 
   // this CTA's routes, in (token, k) order
   if (tid < my_routes) s_e[tid] = (e_mine >= 0 && e_mine < p.n_local) ? e_mine : -1;
   __syncthreads();
-  if (blockIdx.x == 0)
-    for (int g = tid; g <= p.n_local + 2; g += kRouteThreads) p.group_offsets[g] = s_off[g];
+  if (cta == 0)
+    for (int g = tid; g <= p.n_local + 2; g += THREADS) p.group_offsets[g] = s_off[g];
   if (tid < my_routes) {
     const int i = tid;
     const int e = s_e[i];
@@ -441,7 +319,7 @@ __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams 
     s_pos[i] = pos;
   }
   // shared-expert routes of this CTA's tokens (slots 6 and 7)
-  for (int i = tid; i < 2 * tpc; i += kRouteThreads) {
+  for (int i = tid; i < 2 * tpc; i += THREADS) {
     const int sh = i / tpc, t = i % tpc;
     const int b = tok0 + t;
     int pos = -1;
@@ -495,6 +373,314 @@ __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams 
   }
 }
 
+__global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams p) {
+  pdl_enter();
+  if (p.peers.world > 0) {
+    // every rank's router has written its rows into this rank's buffer
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+      const unsigned long long per_rank = (p.peers.rows_per_rank + kRtTok - 1) / kRtTok;
+      s_ok = wait_counter_sys(peer_ctr(p.peers, p.peers.rank, 0), peer_target(p.peers, p.layer, per_rank),
+                              p.peers.wait_polls);
+    }
+    __syncthreads();
+    if (!s_ok) return;
+  }
+  route_cta<kRouteThreads>(p, blockIdx.x);
+}
+
+// ---------------------------------------------------------------------------------
+// Fused router (bf16 gate, one rank): [residual add + RMSNorm] + gate logits + softmax +
+// top-6 [+ bucketing + gather of the expert-ordered activations], one launch
+// ---------------------------------------------------------------------------------
+// Clusters of four CTAs share a group of 8 tokens: CTA r computes experts [16r, 16r + 16)
+// (one mma M block) with its 16 warps each taking a sixteenth of K, so a CTA reads 64 KB of
+// gate, and those weight fragments are loaded before the programmatic-launch wait (weights
+// are never written by earlier kernels).  Every CTA stores its 16 x 8 logits into CTA 0's
+// shared memory (distributed shared memory), and CTA 0 runs the softmax / top-6.  A cluster
+// loops over token groups when there are more groups than clusters.
+//
+// With p.h set, the group's inputs are first formed here: CTA r adds the previous
+// sublayer's output to the residual stream of tokens 2r and 2r + 1 and normalises them,
+// one 256-thread half per token with the same per-thread chunks and reduction order as
+// add_rmsnorm_kernel (so the results are bit-identical to that launch followed by the
+// router), writes h and x to global memory and x into all four CTAs' shared memory.
+//
+// With bucketing (p.group_offsets) the CTAs then meet at a grid-wide barrier (arrival
+// count + generation in p.grid_sync, bounded wait; the grid never exceeds the clusters
+// that fit on the GPU at once, so every CTA is resident) and each CTA buckets a slice of
+// the tokens and copies their activation rows into expert order (route_cta).  The
+// kernel triggers its dependents only after that barrier, so the next launch cannot take
+// the SMs that CTAs still waiting to start would need.
+constexpr int kRcCtas = 4;                           // CTAs per cluster
+constexpr int kRcExperts = kMaxExperts / kRcCtas;    // experts per CTA (16)
+constexpr int kRcKParts = 16;                        // warps per CTA, one K part each
+constexpr int kRcThreads = 32 * kRcKParts;
+constexpr int kRcKb = kRtMaxHidden / 32 / kRcKParts;  // 32-wide K blocks per warp (4)
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t n_clusters_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_addr(const void* local, uint32_t rank) {
+  const uint32_t la = static_cast<uint32_t>(__cvta_generic_to_shared(local));
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(rank));
+  return ra;
+}
+// store v at the address of `local` in the shared memory of cluster CTA `rank`
+__device__ __forceinline__ void st_cluster_f32(const float* local, uint32_t rank, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr(local, rank)), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_v4(const void* local, uint32_t rank, uint4 v) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr(local, rank)),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ int ld_acquire_gpu_s32(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_gpu_add_s32(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Grid-wide barrier of one launch: sync[0] counts arrivals, sync[1] is a generation that
+// the last arrival advances (after returning the count to zero), so the pair needs no
+// clearing between launches.  Bounded: returns false (device error set) if the grid does
+// not gather.
+__device__ bool grid_barrier(int* sync) {
+  __shared__ int s_ok;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int gen = ld_acquire_gpu_s32(&sync[1]);   // read before arriving
+    __threadfence();
+    bool ok = true;
+    if (atomicAdd(&sync[0], 1) == static_cast<int>(gridDim.x) - 1) {
+      sync[0] = 0;
+      red_release_gpu_add_s32(&sync[1], 1);
+    } else {
+      ok = false;
+      for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        if (ld_acquire_gpu_s32(&sync[1]) != gen) { ok = true; break; }
+        if ((i & 255) == 0 && *reinterpret_cast<volatile int*>(&g_device_error) != 0) break;
+        __nanosleep(32);
+      }
+      if (!ok) set_device_error(kErrMbarTimeout);
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+// Half of a 512-thread CTA (threads [256 * half, +256)): sum of v over the half, in the
+// order of block_sum<256> (warp tree, then the half's eight warps in order).
+__device__ __forceinline__ float half_sum(float v, float* red, int half) {
+  v = warp_sum(v);
+  const int warp = (threadIdx.x >> 5) & 7, lane = threadIdx.x & 31;
+  if (lane == 0) red[half * 8 + warp] = v;
+  asm volatile("bar.sync %0, 256;" ::"r"(1 + half) : "memory");
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s += red[half * 8 + i];
+  return s;
+}
+
+__global__ __cluster_dims__(kRcCtas, 1, 1) __launch_bounds__(kRcThreads) void router_fused_kernel(
+    const RouterParams p) {
+  // B0 of the first group: every CTA of the cluster has started (its shared memory
+  // exists) before any CTA stores into it
+  cluster_arrive_relaxed();
+  constexpr int XS = kRtMaxHidden + 8;
+  __shared__ __align__(16) bf16 s_x[kRtTok][XS];
+  __shared__ float s_part[kRcKParts][kRcExperts][kRtTok];
+  __shared__ float s_logits[kRtTok][kMaxExperts];
+  __shared__ float s_red[16];
+  const uint32_t crank = cluster_ctarank();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int eA = static_cast<int>(crank) * kRcExperts + gq, eB = eA + 8;
+  const bool okA = eA < p.n_experts, okB = eB < p.n_experts;
+  const int nkb = p.hidden / 32;
+  const int kb_beg = warp * nkb / kRcKParts, kb_end = (warp + 1) * nkb / kRcKParts;
+  const bf16* w = reinterpret_cast<const bf16*>(p.w);
+  const bf16* wA = w + static_cast<long long>(okA ? eA : 0) * p.hidden + tq * 8;
+  const bf16* wB = w + static_cast<long long>(okB ? eB : 0) * p.hidden + tq * 8;
+  uint4 a[kRcKb], b[kRcKb];
+#pragma unroll
+  for (int u = 0; u < kRcKb; ++u) {
+    const int kb = kb_beg + u;
+    a[u] = (kb < kb_end && okA) ? *reinterpret_cast<const uint4*>(wA + kb * 32) : make_uint4(0, 0, 0, 0);
+    b[u] = (kb < kb_end && okB) ? *reinterpret_cast<const uint4*>(wB + kb * 32) : make_uint4(0, 0, 0, 0);
+  }
+  pdl_wait();
+  const bool bucket = p.group_offsets != nullptr;
+  if (!bucket) pdl_launch_dependents();
+  const int nch = p.hidden / 8;
+  const int n_groups_tok = (p.rows + kRtTok - 1) / kRtTok;
+  for (int grp = static_cast<int>(cluster_id_x()); grp < n_groups_tok; grp += static_cast<int>(n_clusters_x())) {
+    const int row0 = grp * kRtTok;
+    const int nt = min(kRtTok, p.rows - row0);
+    cluster_wait_acquire();   // B0: the cluster is done with the previous group's s_x / s_logits
+    if (p.h) {
+      // residual add + RMSNorm of tokens 2r, 2r + 1 (one half each); x to all four CTAs
+      const int half = tid >> 8, ht = tid & 255;
+      const int t = 2 * static_cast<int>(crank) + half;
+      if (t < nt) {
+        const int row = row0 + t;
+        bf16* hr = p.h + static_cast<long long>(row) * p.hidden;
+        float v[8];
+        float ss = 0.f;
+        const int c = ht;
+        if (c < nch) {
+          const uint4 u = *reinterpret_cast<const uint4*>(hr + c * 8);
+          const uint32_t* up = reinterpret_cast<const uint32_t*>(&u);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            v[2 * j] = bf16lo(up[j]);
+            v[2 * j + 1] = bf16hi(up[j]);
+          }
+          if (p.n_delta > 0) {
+            float d[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) d[j] = 0.f;
+            if (p.delta_dtype == 2) {
+              const float* dp = reinterpret_cast<const float*>(p.delta) + row * p.delta_row_stride + c * 8;
+              sum_parts8(dp, p.delta_part_stride, p.n_delta, d, true);
+            } else {
+              const bf16* dp = reinterpret_cast<const bf16*>(p.delta) + row * p.delta_row_stride + c * 8;
+              for (int q = 0; q < p.n_delta; ++q) {
+                const uint4 dv = *reinterpret_cast<const uint4*>(dp + q * p.delta_part_stride);
+                const uint32_t* ap = reinterpret_cast<const uint32_t*>(&dv);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  d[2 * j] += bf16lo(ap[j]);
+                  d[2 * j + 1] += bf16hi(ap[j]);
+                }
+              }
+            }
+            uint4 o;
+            uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              op[j] = pack_bf16x2(v[2 * j] + d[2 * j], v[2 * j + 1] + d[2 * j + 1]);
+              v[2 * j] = bf16lo(op[j]);
+              v[2 * j + 1] = bf16hi(op[j]);
+            }
+            *reinterpret_cast<uint4*>(hr + c * 8) = o;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+        }
+        ss = half_sum(ss, s_red, half);
+        const float inv = rsqrtf(ss / static_cast<float>(p.hidden) + p.eps);
+        if (c < nch) {
+          uint4 o;
+          uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float x0 = v[2 * j] * inv * load_w(p.norm_w, p.norm_w_dtype, c * 8 + 2 * j);
+            const float x1 = v[2 * j + 1] * inv * load_w(p.norm_w, p.norm_w_dtype, c * 8 + 2 * j + 1);
+            op[j] = pack_bf16x2(x0, x1);
+          }
+          *reinterpret_cast<uint4*>(p.x_out + static_cast<long long>(row) * p.x_row_stride + c * 8) = o;
+#pragma unroll
+          for (uint32_t r = 0; r < kRcCtas; ++r) st_cluster_v4(&s_x[t][c * 8], r, o);
+        }
+      }
+    } else {
+      for (int i = tid; i < kRtTok * nch; i += kRcThreads) {
+        const int t = i / nch, c = i % nch;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (t < nt) v = *reinterpret_cast<const uint4*>(p.x + (row0 + t) * p.x_row_stride + c * 8);
+        *reinterpret_cast<uint4*>(&s_x[t][c * 8]) = v;
+      }
+    }
+    cluster_arrive_release();  // B1: s_x complete in every CTA
+    cluster_wait_acquire();
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    const bf16* xr = &s_x[gq][tq * 8];
+#pragma unroll
+    for (int u = 0; u < kRcKb; ++u) {
+      const int kb = kb_beg + u;
+      if (kb >= kb_end) break;
+      const uint4 xv = *reinterpret_cast<const uint4*>(xr + kb * 32);
+      const uint32_t a0[4] = {a[u].x, b[u].x, a[u].y, b[u].y};
+      mma_bf16_16816(c, a0, xv.x, xv.y);
+      const uint32_t a1[4] = {a[u].z, b[u].z, a[u].w, b[u].w};
+      mma_bf16_16816(c, a1, xv.z, xv.w);
+    }
+    s_part[warp][gq][2 * tq] = c[0];
+    s_part[warp][gq][2 * tq + 1] = c[1];
+    s_part[warp][gq + 8][2 * tq] = c[2];
+    s_part[warp][gq + 8][2 * tq + 1] = c[3];
+    __syncthreads();
+    if (tid < kRcExperts * kRtTok) {
+      const int el = tid / kRtTok, t = tid % kRtTok;
+      const int e = static_cast<int>(crank) * kRcExperts + el;
+      if (e < p.n_experts && t < nt) {
+        float v = s_part[0][el][t];
+#pragma unroll
+        for (int q = 1; q < kRcKParts; ++q) v += s_part[q][el][t];
+        if (p.bias) v += p.bias[e];
+        p.logits[(row0 + t) * p.n_experts + e] = v;
+        st_cluster_f32(&s_logits[t][e], 0, v);
+      }
+    }
+    cluster_arrive_release();  // B2: CTA 0 sees every CTA's logits
+    cluster_wait_acquire();
+    if (crank == 0 && warp < nt)
+      softmax_topk_warp(s_logits[warp], p.n_experts, p.scaling, row0 + warp, p.topk_ids, p.topk_ids32,
+                        p.topk_w);
+    cluster_arrive_release();  // B0 of the next group (or of the exit)
+  }
+  cluster_wait_acquire();      // no CTA leaves while another may still store into it
+  if (!bucket) return;
+  const bool ok = grid_barrier(p.grid_sync);
+  pdl_launch_dependents();
+  if (!ok) return;
+  RouteParams q = {};
+  q.ids32 = p.topk_ids32;
+  q.tw = p.topk_w;
+  q.rows = p.rows;
+  q.expert_lo = p.expert_lo;
+  q.n_local = p.n_local;
+  q.shared_lo = p.shared_lo;
+  q.shared_hi = p.shared_hi;
+  q.group_offsets = p.group_offsets;
+  q.route_token = p.route_token;
+  q.route_slot = p.route_slot;
+  q.route_weight = p.route_weight;
+  q.gx = p.gather_x ? (p.h ? p.x_out : p.x) : nullptr;
+  q.gx_stride = p.x_row_stride;
+  q.gout = p.gather_x ? reinterpret_cast<bf16*>(p.gather_out) : nullptr;
+  q.cols = p.hidden;
+  q.tok_per_cta = (p.rows + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
+  route_cta<kRcThreads>(q, blockIdx.x);
+}
+
 // Softmax/top-6 over precomputed logits (the reference's router_softmax_topk6_triton).
 __global__ void softmax_topk_kernel(const float* logits, int rows, int n_experts, float scaling,
                                     long long* ids64, int* ids32, float* tw) {
@@ -522,7 +708,7 @@ __global__ void gather_rows_kernel(const bf16* __restrict__ x, long long x_row_s
 static cudaError_t launch_route(const int* ids32, const float* tw, int rows, int expert_lo,
                                 int n_local, int shared_lo, int shared_hi, int* go, int* rt,
                                 int* rs, float* rw, const bf16* gx, long long gxs, bf16* gout,
-                                int cols, cudaStream_t st, const PeerTable* peers = nullptr,
+                                int cols, int num_sms, cudaStream_t st, const PeerTable* peers = nullptr,
                                 int layer = 0) {
   RouteParams q = {};
   if (peers) q.peers = *peers;
@@ -544,32 +730,62 @@ static cudaError_t launch_route(const int* ids32, const float* tw, int rows, int
   q.cols = cols;
   // about one CTA per SM (the counting pass is repeated by every CTA; the placement and
   // the row copies are split between them)
-  q.tok_per_cta = min(kRouteTokMax, max(1, (rows + 147) / 148));
+  q.tok_per_cta = min(kRouteTokMax, max(1, (rows + num_sms - 1) / max(num_sms, 1)));
   launch_kernel(route_kernel, (rows + q.tok_per_cta - 1) / q.tok_per_cta, kRouteThreads, 0, st, q);
   return cudaGetLastError();
 }
 
-cudaError_t launch_router(const RouterParams& p, cudaStream_t st) {
-  const int blocks = (p.rows + kRtTok - 1) / kRtTok;
-  if (p.w_dtype == 0 && p.peers.world == 0)
-    launch_kernel(router_topk_cluster_kernel, blocks * kRcCtas, kRcThreads, 0, st, p);
-  else
-    launch_kernel(router_topk_kernel, blocks, kRtThreads, 0, st, p);
+// Clusters of router_fused_kernel that can be resident at once on the current device
+// (the grid bound of its single-launch bucketing).
+cudaError_t router_fused_max_clusters(int* n) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kRcCtas * 64);
+  cfg.blockDim = dim3(kRcThreads);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kRcCtas;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaOccupancyMaxActiveClusters(n, router_fused_kernel, &cfg);
+}
+
+// One rank, bf16 gate: router_fused_kernel, with the bucketing inside when a grid-barrier
+// buffer is given and the whole grid fits (else a second launch, route_kernel).  fp32 gate
+// or expert-parallel dispatch: router_topk_kernel (+ route_kernel).
+cudaError_t launch_router(const RouterParams& p, int max_clusters, int num_sms, cudaStream_t st) {
+  const int groups = (p.rows + kRtTok - 1) / kRtTok;
+  bool second_route = p.group_offsets != nullptr;
+  if (p.w_dtype == 0 && p.peers.world == 0) {
+    RouterParams q = p;
+    int clusters = groups;
+    const int need = (p.rows + kRcCtas * kRouteTokMax - 1) / (kRcCtas * kRouteTokMax);
+    if (p.group_offsets && p.grid_sync && max_clusters >= need) {
+      clusters = std::min(groups, max_clusters);
+      second_route = false;
+    } else {
+      q.group_offsets = nullptr;
+    }
+    launch_kernel(router_fused_kernel, clusters * kRcCtas, kRcThreads, 0, st, q);
+  } else {
+    launch_kernel(router_topk_kernel, groups, kRtThreads, 0, st, p);
+  }
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess || !p.group_offsets) return e;
+  if (e != cudaSuccess || !second_route) return e;
   return launch_route(p.topk_ids32, p.topk_w, p.rows, p.expert_lo, p.n_local, p.shared_lo,
                       p.shared_hi, p.group_offsets, p.route_token, p.route_slot, p.route_weight,
-                      p.gather_x ? p.x : nullptr, p.x_row_stride, reinterpret_cast<bf16*>(p.gather_out),
-                      p.hidden, st);
+                      p.gather_x ? (p.h ? p.x_out : p.x) : nullptr, p.x_row_stride,
+                      reinterpret_cast<bf16*>(p.gather_out), p.hidden, num_sms, st);
 }
 
 cudaError_t launch_bucket(const int* ids32, const float* tw, int rows, int expert_lo, int n_local,
                           int shared_lo, int shared_hi, int* go, int* rt, int* rs, float* rw,
-                          const void* gx, long long gxs, void* gout, int cols, cudaStream_t st,
+                          const void* gx, long long gxs, void* gout, int cols, int num_sms, cudaStream_t st,
                           const PeerTable* peers, int layer) {
   return launch_route(ids32, tw, rows, expert_lo, n_local, shared_lo, shared_hi, go, rt, rs, rw,
-                      reinterpret_cast<const bf16*>(gx), gxs, reinterpret_cast<bf16*>(gout), cols, st,
-                      peers, layer);
+                      reinterpret_cast<const bf16*>(gx), gxs, reinterpret_cast<bf16*>(gout), cols, num_sms,
+                      st, peers, layer);
 }
 
 cudaError_t launch_softmax_topk(const float* logits, int rows, int n_experts, float scaling,

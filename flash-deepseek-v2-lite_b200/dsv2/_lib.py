@@ -78,6 +78,9 @@ class RouterArgs(ctypes.Structure):
         ("expert_lo", c_i32), ("n_local", c_i32), ("shared_lo", c_i32), ("shared_hi", c_i32),
         ("group_offsets", c_vp), ("route_token", c_vp), ("route_slot", c_vp), ("route_weight", c_vp),
         ("peers", ctypes.POINTER(PeerTable)), ("row_base", c_i32),
+        ("h", c_vp), ("delta", c_vp), ("delta_dtype", c_i32), ("n_delta", c_i32),
+        ("delta_part_stride", c_i64), ("delta_row_stride", c_i64), ("norm_w", c_vp), ("norm_w_dtype", c_i32),
+        ("eps", c_f32), ("sync", c_vp),
     ]
 
 

@@ -184,6 +184,8 @@ class DecodeEngine:
             self.x_sorted = torch.zeros((self.r_max, HIDDEN), device=dev, dtype=bf)
             self.h_moe = torch.zeros((self.r_max, m0.inter), device=dev, dtype=bf)
             self.moe_sync = torch.zeros(self.n_groups + 2, device=dev, dtype=i32)
+            # grid barrier of the single-launch router (add + RMSNorm, gate, top-6, bucketing)
+            self.router_sync = torch.zeros(2, device=dev, dtype=i32)
             self.partial = torch.zeros((Ball, SLOTS, HIDDEN), device=dev, dtype=f32)
             if self.world > 1:
                 self.x_all = torch.zeros((Ball, HIDDEN), device=dev, dtype=bf)
@@ -302,7 +304,10 @@ class DecodeEngine:
         self._linear(w=d.down, n_rows=HIDDEN, k=d.inter, x=h, y=self.mlp_out, n_tokens=B, x_group_rows=B)
         return self.mlp_out
 
-    def _moe(self, li: int, lp: LayerPack) -> torch.Tensor:
+    def _moe(self, li: int, lp: LayerPack, attn: torch.Tensor | None = None) -> torch.Tensor:
+        """MoE sublayer.  attn (one rank): the attention output still to be added to the
+        residual stream; the router launch adds it and applies the post-attention RMSNorm
+        itself (otherwise self.x already holds the normalised input)."""
         m, B = lp.moe, self.B
         go = self.group_offsets_hist[self.moe_index[li]]
         # batch family: the routing kernel also copies x into expert order for the TMA loads
@@ -323,11 +328,13 @@ class DecodeEngine:
             self._moe_pending = mi
             return self.part_peer
         if self.world == 1:
+            fused = {} if attn is None else dict(residual=self.h, delta=attn, norm_w=lp.post_norm_w, eps=lp.eps)
             ops.router(x=self.x, w=m.gate_w, scaling=m.scaling, bias=m.gate_bias, logits=self.logits_r,
                        topk_ids32=self.topk_ids32, topk_weights=self.topk_w, topk_ids64=self.topk_ids64,
                        gather_out=gather, expert_lo=m.expert_lo, n_local=m.n_local, shared_lo=0,
                        shared_hi=B, group_offsets=go, route_token=self.route_token,
-                       route_slot=self.route_slot, route_weight=self.route_weight)
+                       route_slot=self.route_slot, route_weight=self.route_weight, sync=self.router_sync,
+                       **fused)
             x_src = self.x
         else:
             sh = self.shard
@@ -432,8 +439,12 @@ class DecodeEngine:
             if li > 0:
                 self._add_rmsnorm(delta, lp.in_norm_w, lp.eps)
             attn = self._attention(li, lp)
-            ops.add_rmsnorm(self.h, attn, lp.post_norm_w, lp.eps, self.x)
-            delta = self._dense_mlp(lp) if lp.dense is not None else self._moe(li, lp)
+            if lp.moe is not None and self.world == 1 and m_bf16_gate(lp):
+                # one launch: residual add + RMSNorm, gate, top-6, bucketing, gather
+                delta = self._moe(li, lp, attn=attn)
+            else:
+                ops.add_rmsnorm(self.h, attn, lp.post_norm_w, lp.eps, self.x)
+                delta = self._dense_mlp(lp) if lp.dense is not None else self._moe(li, lp)
             if trace is not None:
                 d = delta.float().sum(1) if delta.dim() == 3 else delta.float()
                 trace["hidden"].append(self.h.float() + d)
@@ -633,6 +644,11 @@ class DecodeEngine:
         pos = torch.tensor(lens, dtype=torch.int64, device=self.dev)
         self.set_state(pos, first)
         return first
+
+
+def m_bf16_gate(lp: LayerPack) -> bool:
+    """The MoE router of this layer runs the single-launch kernel (bf16 gate weights)."""
+    return lp.moe is not None and lp.moe.gate_w.dtype == torch.bfloat16
 
 
 def prefill_token_plan(lens: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:

@@ -259,10 +259,17 @@ def router(*, x: torch.Tensor, w: torch.Tensor, scaling: float, logits: torch.Te
            expert_lo: int = 0, n_local: int = 0, shared_lo: int = 0, shared_hi: int = 0,
            group_offsets: torch.Tensor | None = None, route_token: torch.Tensor | None = None,
            route_slot: torch.Tensor | None = None, route_weight: torch.Tensor | None = None,
-           peers: PeerTable | None = None, row_base: int = 0) -> None:
+           peers: PeerTable | None = None, row_base: int = 0, residual: torch.Tensor | None = None,
+           delta: torch.Tensor | None = None, norm_w: torch.Tensor | None = None, eps: float = 0.0,
+           sync: torch.Tensor | None = None) -> None:
     """Gate logits + softmax + top-6 (+ bucketing when group_offsets is given, + the
     expert-ordered copy of x into gather_out when given; + expert-parallel dispatch of
-    x / ids / weights to every rank's peer buffer when peers is given)."""
+    x / ids / weights to every rank's peer buffer when peers is given).
+
+    residual / delta / norm_w / eps (bf16 gate, one rank): the router's input is formed in
+    the same launch, residual = bf16(residual + delta) in place and x = rmsnorm(residual) *
+    norm_w written into x (delta: bf16 [rows, cols] or fp32 partials [rows, parts, cols],
+    as add_rmsnorm).  sync (int32 [2], zeroed once): the bucketing runs in the same launch."""
     a = RouterArgs()
     a.x = x.data_ptr()
     a.x_row_stride = x.stride(0)
@@ -286,6 +293,29 @@ def router(*, x: torch.Tensor, w: torch.Tensor, scaling: float, logits: torch.Te
     if peers is not None:
         a.peers = ctypes.pointer(peers)
     a.row_base = row_base
+    if residual is not None:
+        _cuda(residual, "residual")
+        if residual.dtype != torch.bfloat16 or not residual.is_contiguous() or residual.shape != x.shape:
+            raise NotImplementedError("residual must be a contiguous bf16 tensor shaped like x")
+        a.h = residual.data_ptr()
+        a.norm_w = norm_w.data_ptr()
+        a.norm_w_dtype = _wdtype(norm_w)
+        a.eps = float(eps)
+        if delta is not None:
+            if delta.dim() == 2:
+                if delta.dtype != torch.bfloat16:
+                    raise NotImplementedError("2-D delta must be bf16")
+                a.delta, a.delta_dtype, a.n_delta = delta.data_ptr(), DSV2_BF16, 1
+                a.delta_part_stride, a.delta_row_stride = 0, delta.stride(0)
+            else:
+                if delta.dtype != torch.float32:
+                    raise NotImplementedError("3-D delta (per-part partials) must be fp32")
+                a.delta, a.delta_dtype, a.n_delta = delta.data_ptr(), DSV2_F32, delta.shape[1]
+                a.delta_part_stride, a.delta_row_stride = delta.stride(1), delta.stride(0)
+    if sync is not None:
+        if sync.dtype != torch.int32 or sync.numel() < 2:
+            raise ValueError("sync must be int32 with 2 entries")
+        a.sync = sync.data_ptr()
     _lib.call("dsv2_router", ctypes.byref(a), stream())
 
 

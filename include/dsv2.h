@@ -320,7 +320,7 @@ DSV2_API int dsv2_lm_head_argmax(const void* w, int vocab, int hidden, const voi
                                  int family, void* stream);
 
 /* ---- MoE routing ------------------------------------------------------------ */
-/* Gate GEMV (fp32 over bf16 activations) + softmax + top-6, then bucketing (two launches).
+/* Gate GEMV (fp32 over bf16 activations) + softmax + top-6, then bucketing.
  *   logits[r, e] = sum_k x[r, k] * w[e, k] (+ bias[e]);  p = softmax(logits[r]);
  *   topk_ids / topk_weights = 6 largest p (descending, lowest index first on ties),
  *   weights multiplied by `scaling` (routed_scaling_factor).
@@ -362,6 +362,24 @@ typedef struct dsv2_router_args {
    * row_base ..) into every rank's buffer and signal (no bucketing here then) */
   const dsv2_peer_table* peers;
   int32_t row_base;
+  /* optional residual add + RMSNorm that forms the router's input in the same launch
+   * (bf16 gate, one rank): h[r] = bf16(h[r] + sum_p delta[r, p]) and
+   * x[r] = rmsnorm(h[r]) * norm_w, bit for bit what dsv2_add_rmsnorm(h, NULL, delta, ...,
+   * norm_w, ..., y = x) computes; x is then an output (rows at x_row_stride).  delta as in
+   * dsv2_add_rmsnorm (DSV2_BF16 rows or DSV2_F32 per-part partials); h == NULL: none. */
+  void* h;
+  const void* delta;
+  int32_t delta_dtype;
+  int32_t n_delta;
+  int64_t delta_part_stride;
+  int64_t delta_row_stride;
+  const void* norm_w;
+  int32_t norm_w_dtype;
+  float eps;
+  /* optional int32[2], zeroed once before first use and never by the caller again: the
+   * grid barrier that lets the bucketing (and gather) run in the same launch as the gate
+   * (bf16 gate, one rank).  NULL: the bucketing is a second launch. */
+  int32_t* sync;
 } dsv2_router_args;
 
 DSV2_API int dsv2_router(const dsv2_router_args* args, void* stream);

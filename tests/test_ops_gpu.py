@@ -152,6 +152,66 @@ def test_router_topk_and_bucketing(D, B):
     assert torch.equal(dev["xs"].cpu()[:n], x[rt.long()])  # expert-ordered activation copy
 
 
+# B up to 256 takes one token group per cluster; 1300 and 4096 loop over groups and need the
+# grid barrier with every cluster resident
+@pytest.mark.parametrize("B,parts", [(1, 3), (5, 1), (64, 0), (256, 5), (256, -1), (1300, 8), (4096, 3)])
+def test_fused_router_equals_add_rmsnorm_then_router(D, B, parts):
+    """The single-launch router (residual add + RMSNorm, gate, top-6, bucketing, gather)
+    against add_rmsnorm followed by the router and the bucketing launch: the same bits in
+    every output.  parts > 0: fp32 split-K partials as delta; -1: a bf16 delta; 0: none."""
+    g = torch.Generator().manual_seed(40 + B)
+    h0 = torch.randn(B, 2048, generator=g).to(torch.bfloat16).to(DEV)
+    if parts > 0:
+        delta = (0.3 * torch.randn(B, parts, 2048, generator=g)).to(DEV)
+    elif parts < 0:
+        delta = (0.3 * torch.randn(B, 2048, generator=g)).to(torch.bfloat16).to(DEV)
+    else:
+        delta = None
+    nw = (1 + 0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16).to(DEV)
+    w = (0.02 * torch.randn(64, 2048, generator=g)).to(torch.bfloat16).to(DEV)
+    bias = (0.5 * torch.randn(64, generator=g)).to(DEV) if B == 256 else None
+
+    def bufs():
+        return {k: torch.full(sh, -7, dtype=t, device=DEV) for k, sh, t in (
+            ("logits", (B, 64), torch.float32), ("ids32", (B, 6), torch.int32), ("ids64", (B, 6), torch.int64),
+            ("tw", (B, 6), torch.float32), ("go", (67,), torch.int32), ("xs", (8 * B, 2048), torch.bfloat16),
+            ("rt", (8 * B,), torch.int32), ("rs", (8 * B,), torch.int32), ("rw", (8 * B,), torch.float32),
+            ("x", (B, 2048), torch.bfloat16))}
+    # reference: two launches of add_rmsnorm + router with bucketing in its own launch
+    ha, ra = h0.clone(), bufs()
+    D.add_rmsnorm(ha, delta, nw, 1e-6, ra["x"])
+    D.router(x=ra["x"], w=w, scaling=1.5, bias=bias, logits=ra["logits"], topk_ids32=ra["ids32"],
+             topk_weights=ra["tw"], topk_ids64=ra["ids64"], gather_out=ra["xs"], expert_lo=0, n_local=64,
+             shared_lo=0, shared_hi=B, group_offsets=ra["go"], route_token=ra["rt"], route_slot=ra["rs"],
+             route_weight=ra["rw"])
+    # one launch, twice (the grid barrier's counters carry over between launches)
+    sync = torch.zeros(2, dtype=torch.int32, device=DEV)
+    from dsv2 import _lib
+    for _ in range(2):
+        hb, rb = h0.clone(), bufs()
+        n0 = _lib.kernel_launches()
+        D.router(x=rb["x"], w=w, scaling=1.5, bias=bias, logits=rb["logits"], topk_ids32=rb["ids32"],
+                 topk_weights=rb["tw"], topk_ids64=rb["ids64"], gather_out=rb["xs"], expert_lo=0, n_local=64,
+                 shared_lo=0, shared_hi=B, group_offsets=rb["go"], route_token=rb["rt"], route_slot=rb["rs"],
+                 route_weight=rb["rw"], residual=hb, delta=delta, norm_w=nw, eps=1e-6, sync=sync)
+        if B <= 1300:
+            assert _lib.kernel_launches() - n0 == 1
+        torch.cuda.synchronize()
+        assert torch.equal(hb, ha)
+        for k in ra:
+            assert torch.equal(rb[k], ra[k]), k
+        assert int(sync[0]) == 0
+    assert _lib.device_error(clear=True) == 0
+    # and the routing itself against the oracle on that input
+    lg, ids, _ = O.router(ra["x"].cpu(), w.cpu(), 1.5, None if bias is None else bias.cpu())
+    p = torch.softmax(lg, -1)
+    got = rb["ids64"].cpu()
+    for r in range(B):
+        if set(got[r].tolist()) != set(ids[r].tolist()):
+            vals = p[r, sorted(set(got[r].tolist()) ^ set(ids[r].tolist()))]
+            assert float(vals.max() - vals.min()) <= 1e-3 * float(vals.max())
+
+
 def test_router_golden_topk6(D, golden_ref):
     g = golden_ref["router_topk6"]
     lg = g["logits"].to(DEV)
