@@ -14,7 +14,10 @@ layers, lm_head and greedy argmax).  `value` = decoded tokens / s over all ranks
 with CUDA events over K replays (max over ranks); the per-step working set (~31 GB of
 weights) is far larger than L2, so no flush is needed between steps.  `e2e` repeats the
 decode through the public engine API with the token ids crossing host<->device every
-step (pinned buffers, copies inside the timed region).
+step (pinned buffers, copies inside the timed region).  The default single-GPU run also
+summarises configs 3 and 2 (B=32, B=1) under "other_configs".  `cpu_baseline` and the
+`--impl reference` arm run the same routine: the reference's CPU path (HF eager bf16) on
+the host cores for the whole workload batch, per-layer times measured on a 2-layer slice.
 """
 from __future__ import annotations
 
@@ -52,9 +55,13 @@ GATE_BYTES = 2 * 131_072
 LMHEAD_BYTES = 2 * 209_715_200
 EXPERT_BYTES = 2 * 8_650_752
 KV_ROW_BYTES = 576 * 2
-# DRAM traffic / algorithmic bytes of the fused MoE launch, from one ncu capture at B=256
-# (all 64 experts hit): (1157.2 + 22.2) MB / 1141.9 MB
-MOE_TRAFFIC_RATIO = 1.033
+# DRAM traffic / algorithmic bytes of the fused MoE launch, from one ncu capture of the
+# current kernel at B=256 (all 64 experts hit; profiles/moe_tc_b256.md):
+# (1159.34 + 23.19) MB / 1141.90 MB
+MOE_TRAFFIC_RATIO = 1.0356
+MOE_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one fused MoE launch "
+                      "(dsv2.microbench moe, B=256, all 64 experts hit; profiles/moe_tc_b256.md), "
+                      "scaled to this launch by its algorithmic bytes")
 
 
 def prompt_lengths(cfg: dict, batch: int) -> list[int]:
@@ -198,29 +205,30 @@ def distinct_experts(eng) -> list[int]:
     return [int((c > 0).sum()) for c in counts]
 
 
-def run_ours(args, cfg_id: int):
+def build_engine_for(model, cfg_id: int, B_all: int, family: str, rank: int, world: int, group, args,
+                     steps_total: int, bias):
     from dsv2.engine import DecodeEngine
-    from dsv2.synthetic import add_router_bias, build_model, dsv2_lite_config, router_bias_zipf
-
-    rank, world, local, group = init_dist(args)
-    dev = torch.device("cuda", local)
     cfg = CONFIGS[cfg_id]
-    B_all = args.batch or cfg["batch"]
+    B = B_all // world
+    prompts_all = make_prompts(cfg, B_all, model.config.vocab_size)
+    prompts = prompts_all[rank * B:(rank + 1) * B]
+    max_len = max(len(p) for p in prompts_all) + steps_total + 8
+    eng = DecodeEngine(model, B, max_len, family, rank=rank, world=world, group=group, gate_bias=bias)
+    return eng, prompts
+
+
+def measure(model, cfg_id: int, args, rank: int, world: int, group, local: int, bias, steps: int, warmup: int,
+            e2e_steps: int, family: str | None = None, batch: int | None = None, clocks_out: dict | None = None):
+    """Prefill, capture and time one configuration on this rank's GPU (max over ranks).
+    Returns the measured figures (whole-job tok/s, ms/step, step roofline, e2e, launches)."""
+    cfg = CONFIGS[cfg_id]
+    B_all = batch or cfg["batch"]
     if B_all % world:
         raise SystemExit(f"batch {B_all} not divisible by {world} ranks")
-    B = B_all // world
-    family = args.family or cfg["family"]
+    family = family or cfg["family"]
     t0 = time.time()
-    mcfg = dsv2_lite_config(num_layers=args.layers)
-    model = build_model(mcfg, seed=WEIGHT_SEED, device=dev, dtype=torch.bfloat16)
-    bias = router_bias_zipf(mcfg.n_routed_experts, 1.1, seed=4).to(dev) if cfg["skew"] else None
-    if bias is not None:
-        add_router_bias(model, bias)
-    prompts_all = make_prompts(cfg, B_all, mcfg.vocab_size)
-    prompts = prompts_all[rank * B:(rank + 1) * B]
-    total_steps = args.warmup + args.steps + args.e2e_steps + 8
-    max_len = max(len(p) for p in prompts_all) + total_steps + 8
-    eng = DecodeEngine(model, B, max_len, family, rank=rank, world=world, group=group, gate_bias=bias)
+    eng, prompts = build_engine_for(model, cfg_id, B_all, family, rank, world, group, args,
+                                    warmup + steps + e2e_steps + 8, bias)
     t_build = time.time() - t0
     t0 = time.time()
     eng.prefill(prompts, max_tokens_per_chunk=args.prefill_chunk, method=args.prefill)
@@ -229,7 +237,7 @@ def run_ours(args, cfg_id: int):
     launches_per_step = count_launches(lambda: (eng.step(), eng.restore()))
     eng.capture()
     barrier(world)
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         eng.replay()
     lens_before = [int(x) for x in eng.positions.cpu()]
     barrier(world)
@@ -238,31 +246,25 @@ def run_ours(args, cfg_id: int):
     with ClockSampler(local) as clocks:
         torch.cuda.nvtx.range_push("dsv2_timed")  # lets ncu --nvtx-include select the timed steps
         start.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             eng.replay()
         end.record(stream)
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_pop()
     barrier(world)
-    ms = start.elapsed_time(end)
-    ms = max_over_ranks(ms, world)
-    ms_step = ms / args.steps
-    tokens = B_all * args.steps
-    value = tokens / (ms / 1000.0)
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    ms_step = ms / steps
+    value = B_all * steps / (ms / 1000.0)
     distinct = distinct_experts(eng)
-    lens_mid = [l + args.steps // 2 for l in lens_before]
-    bytes_rank = step_bytes(eng, lens_mid, distinct)
-    bytes_rank = max_over_ranks(bytes_rank, world)
+    lens_mid = [l + steps // 2 for l in lens_before]
+    bytes_rank = max_over_ranks(step_bytes(eng, lens_mid, distinct), world)
     peak, peak_kind = measured_peak()
     step_gbs = bytes_rank / (ms_step / 1000.0) / 1e9
-
-    # dominant kernel: grouped MoE GEMMs (gate_up+SwiGLU and down) of all MoE layers,
-    # replayed alone from a graph with the last routing in place
-    moe_ms, moe_bytes, moe_launches = eng.time_moe_gemms(iters=max(3, min(args.steps, 20)))
-    moe_ms = max_over_ranks(moe_ms, world)
-    dk_gbs = moe_bytes / (moe_ms / 1000.0) / 1e9 if moe_ms > 0 else None
+    if clocks_out is not None:
+        clocks_out.update(clocks.summary())
 
     # end to end through the public API: token ids cross host<->device every step
+    B = B_all // world
     pin_in = torch.zeros(B, dtype=torch.int64, pin_memory=True)
     pin_out = torch.zeros(B, dtype=torch.int64, pin_memory=True)
     pin_in.copy_(eng.input_ids.cpu())
@@ -270,7 +272,7 @@ def run_ours(args, cfg_id: int):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_e2e = time.perf_counter()
     e0.record(stream)
-    for _ in range(args.e2e_steps):
+    for _ in range(e2e_steps):
         eng.input_ids.copy_(pin_in, non_blocking=True)
         eng.replay()
         pin_out.copy_(eng.next_ids, non_blocking=True)
@@ -280,19 +282,81 @@ def run_ours(args, cfg_id: int):
     torch.cuda.synchronize()
     t_e2e = time.perf_counter() - t_e2e
     e2e_s = max_over_ranks(max(t_e2e, e0.elapsed_time(e1) / 1000.0), world)
-    e2e_val = B_all * args.e2e_steps / e2e_s
+    res = {
+        "eng": eng, "B_all": B_all, "family": family, "value": value, "ms_step": ms_step,
+        "bytes_rank": bytes_rank, "step_gbs": step_gbs, "peak": peak, "peak_kind": peak_kind,
+        "distinct": distinct, "launches_per_step": launches_per_step, "lens_before": lens_before,
+        "e2e_value": B_all * e2e_steps / e2e_s, "e2e_bytes": 8 * B_all,
+        "t_build": t_build, "t_prefill": t_prefill, "prefill_tokens": sum(len(p) for p in prompts),
+    }
+    return res
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(model, prompts_all, cfg, args)
+
+def summary_of(res: dict, steps: int) -> dict:
+    return {"value": round(res["value"], 2), "unit": "tok/s", "ms_per_step": round(res["ms_step"], 4),
+            "steps": steps, "global_batch": res["B_all"], "kernel_family": res["family"],
+            "step_roofline_frac": round(res["step_gbs"] / res["peak"], 4),
+            "algorithmic_bytes_per_step": res["bytes_rank"],
+            "distinct_experts_mean": round(sum(res["distinct"]) / max(len(res["distinct"]), 1), 2),
+            "launches_per_step": res["launches_per_step"],
+            "e2e_value": round(res["e2e_value"], 2)}
+
+
+def run_ours(args, cfg_id: int):
+    from dsv2.synthetic import add_router_bias, build_model, dsv2_lite_config, router_bias_zipf
+
+    rank, world, local, group = init_dist(args)
+    dev = torch.device("cuda", local)
+    cfg = CONFIGS[cfg_id]
+    t0 = time.time()
+    mcfg = dsv2_lite_config(num_layers=args.layers)
+    model = build_model(mcfg, seed=WEIGHT_SEED, device=dev, dtype=torch.bfloat16)
+    bias = router_bias_zipf(mcfg.n_routed_experts, 1.1, seed=4).to(dev) if cfg["skew"] else None
+    if bias is not None:
+        add_router_bias(model, bias)
+    t_model = time.time() - t0
+    clocks = {}
+    res = measure(model, cfg_id, args, rank, world, group, local, bias, args.steps, args.warmup, args.e2e_steps,
+                  family=args.family, batch=args.batch, clocks_out=clocks)
+    eng = res["eng"]
+    B_all, family, ms_step = res["B_all"], res["family"], res["ms_step"]
+    peak, peak_kind = res["peak"], res["peak_kind"]
+
+    # dominant kernel: grouped MoE GEMMs (gate_up+SwiGLU and down) of all MoE layers,
+    # replayed alone from a graph with the last routing in place
+    moe_ms, moe_bytes, moe_launches = eng.time_moe_gemms(iters=max(3, min(args.steps, 20)))
+    moe_ms = max_over_ranks(moe_ms, world)
+    dk_gbs = moe_bytes / (moe_ms / 1000.0) / 1e9 if moe_ms > 0 else None
+    lens_before = res["lens_before"]
+    split_len = eng.split_len
     eng.release()
     barrier(world)
     eng.close()
+    del eng, res["eng"]
+    torch.cuda.empty_cache()
+
+    # the other single-GPU configurations of the metric (B=32 batch family, B=1 small
+    # family), summarised beside the headline
+    extra = {}
+    if world == 1 and cfg_id == 4 and not args.no_extra_configs and args.batch is None and args.family is None:
+        for cid in (3, 2):
+            n = min(args.steps, 20)
+            r = measure(model, cid, args, rank, world, group, local, None, n, 3, 5)
+            r["eng"].release()
+            r["eng"].close()
+            del r["eng"]
+            torch.cuda.empty_cache()
+            extra[f"config{cid}"] = summary_of(r, n)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_decode_baseline(cfg_id, B_all, args.layers, steps=2)
+        cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
     out = None
     if rank == 0:
         out = {
             "metric": METRIC,
-            "value": round(value, 2),
+            "value": round(res["value"], 2),
             "unit": "tok/s",
             "n_gpus": world,
             "steps": args.steps,
@@ -311,7 +375,7 @@ def run_ours(args, cfg_id: int):
                 "parallelism": f"ep{world}+dp{world}" if world > 1 else "single",
                 "kernel_family": family,
                 "l2": "inputs larger than L2 (31 GB of weights streamed per step)",
-                "split_len": eng.split_len,
+                "split_len": split_len,
             },
             "roofline": {
                 "bound": "hbm",
@@ -324,28 +388,28 @@ def run_ours(args, cfg_id: int):
                 "frac": round(dk_gbs / peak, 4) if dk_gbs else None,
                 "peak_kind": peak_kind,
                 "traffic": round(moe_bytes / max(moe_launches, 1) * MOE_TRAFFIC_RATIO),
-                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one fused MoE launch "
-                                  "(dsv2.microbench moe, B=256, all 64 experts hit), scaled to this launch "
-                                  "by its algorithmic bytes",
+                "traffic_source": MOE_TRAFFIC_SOURCE,
                 "algorithmic_bytes_per_launch": round(moe_bytes / max(moe_launches, 1)),
                 "launch_ms": round(moe_ms / max(moe_launches, 1), 5),
             },
             "step_roofline": {
-                "algorithmic_bytes_per_step": bytes_rank,
-                "achieved": round(step_gbs, 1),
+                "algorithmic_bytes_per_step": res["bytes_rank"],
+                "achieved": round(res["step_gbs"], 1),
                 "peak": peak,
                 "unit": "GB/s",
-                "frac": round(step_gbs / peak, 4),
-                "distinct_experts_mean": round(sum(distinct) / max(len(distinct), 1), 2),
+                "frac": round(res["step_gbs"] / peak, 4),
+                "distinct_experts_mean": round(sum(res["distinct"]) / max(len(res["distinct"]), 1), 2),
             },
-            "e2e": {"value": round(e2e_val, 2), "unit": "tok/s", "h2d_bytes_per_step": 8 * B_all,
-                    "d2h_bytes_per_step": 8 * B_all, "steps": args.e2e_steps},
-            "gpu_launches": launches_per_step * args.steps,
-            "launches_per_step": launches_per_step,
-            "clocks": clocks.summary(),
+            "e2e": {"value": round(res["e2e_value"], 2), "unit": "tok/s", "h2d_bytes_per_step": res["e2e_bytes"],
+                    "d2h_bytes_per_step": res["e2e_bytes"], "steps": args.e2e_steps},
+            "gpu_launches": res["launches_per_step"] * args.steps,
+            "launches_per_step": res["launches_per_step"],
+            "clocks": clocks,
             "cpu_baseline": cpu,
-            "setup_s": {"build": round(t_build, 1), "prefill": round(t_prefill, 1),
-                        "prefill_method": args.prefill, "prefill_tokens": sum(len(p) for p in prompts)},
+            "other_configs": extra or None,
+            "setup_s": {"model": round(t_model, 1), "engine": round(res["t_build"], 1),
+                        "prefill": round(res["t_prefill"], 1), "prefill_method": args.prefill,
+                        "prefill_tokens": res["prefill_tokens"]},
         }
     if world > 1:
         import torch.distributed as dist
@@ -353,87 +417,103 @@ def run_ours(args, cfg_id: int):
     return out
 
 
-def cpu_baseline(model, prompts_all, cfg, args, rows: int = 4, steps: int = 3) -> dict:
-    """HF eager decode (the reference's CPU path) on the host cores for a bounded sample:
-    a 2-layer slice (dense layer 0 + MoE layer 1) of the same weights, `rows` rows of the
-    workload's prompts, `steps` greedy decode steps; per-layer times are extrapolated to
-    the full depth and the tok/s figure is rows / (extrapolated step time)."""
+def cpu_decode_baseline(cfg_id: int, B_all: int, layers: int, steps: int = 2) -> dict:
+    """The reference's CPU path, HF eager bf16 (transformers 5.5) on the host cores, timed on
+    a bounded sample of the workload: every row of the batch decodes together (one batch,
+    prompts left-padded, the KV cache of each row filled to its prompt length with values
+    that do not affect the cost), through a 2-layer slice of the model (the dense layer 0
+    and one MoE layer, with the embedding, final norm and lm_head).  The layers are timed
+    separately with forward hooks; the full-depth step is the measured
+    rest + dense layer + (layers - 1) x MoE layer (the 26 MoE layers have identical shapes).
+    Shared by bench.py's cpu_baseline and its --impl reference arm."""
+    from transformers import StaticCache
+
     from oracle.hf_model import build_model, dsv2_lite_config
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    cfg2 = dsv2_lite_config(num_layers=2)
-    cpu_model = build_model(cfg2, seed=0, device="cpu", dtype=torch.bfloat16, std=0.0)
-    sd = {k: v for k, v in model.state_dict().items()
-          if not k.startswith("model.layers.") or k.split(".")[2] in ("0", "1")}
-    cpu_model.load_state_dict({k: v.cpu() for k, v in sd.items()}, strict=False)
-    from transformers import DynamicCache
-    rows = min(rows, len(prompts_all))
-    times = []
+    cfg = CONFIGS[cfg_id]
+    mcfg = dsv2_lite_config(num_layers=2)
+    t0 = time.perf_counter()
+    model = build_model(mcfg, seed=WEIGHT_SEED, device="cpu", dtype=torch.float32).to(torch.bfloat16)
+    t_build = time.perf_counter() - t0
+    lens = prompt_lengths(cfg, B_all)
+    R, T0 = len(lens), max(lens)
+    g = torch.Generator().manual_seed(7)
+    cache = StaticCache(config=mcfg, max_cache_len=T0 + steps + 1)
+    heads = mcfg.num_attention_heads
+    for li in range(2):
+        k = (0.1 * torch.randn(R, heads, T0, mcfg.qk_nope_head_dim + mcfg.qk_rope_head_dim, generator=g)).to(torch.bfloat16)
+        v = (0.1 * torch.randn(R, heads, T0, mcfg.v_head_dim, generator=g)).to(torch.bfloat16)
+        cache.update(k, v, li, {"cache_position": torch.arange(T0)})
+        del k, v
+    mask = torch.zeros(R, T0 + steps + 1, dtype=torch.long)
+    for r, n in enumerate(lens):
+        mask[r, T0 - n:] = 1
+    mask[:, T0:] = 1
+    times: dict[str, list[float]] = {"layer0": [], "layer1": [], "total": []}
+    marks = {}
+
+    def pre(name):
+        def f(*_a, **_k):
+            marks[name] = time.perf_counter()
+        return f
+
+    def post(name):
+        def f(*_a, **_k):
+            times[name].append(time.perf_counter() - marks[name])
+        return f
+    hooks = []
+    for i, layer in enumerate(model.model.layers):
+        hooks.append(layer.register_forward_pre_hook(pre(f"layer{i}")))
+        hooks.append(layer.register_forward_hook(post(f"layer{i}")))
+    tok = torch.randint(0, mcfg.vocab_size, (R, 1), generator=g)
     with torch.no_grad():
-        for r in range(rows):
-            p = prompts_all[r].view(1, -1)
-            cache = DynamicCache(config=cfg2)
-            out = cpu_model(input_ids=p, past_key_values=cache, use_cache=True)
+        for s in range(steps + 1):          # the first step is an untimed warm-up
+            pos = (torch.tensor(lens) + s).view(R, 1)
+            t = time.perf_counter()
+            out = model(input_ids=tok, attention_mask=mask[:, :T0 + s + 1], position_ids=pos,
+                        past_key_values=cache, cache_position=torch.tensor([T0 + s]), use_cache=True)
             tok = out.logits[:, -1:].argmax(-1)
-            for _ in range(steps):
-                t = time.perf_counter()
-                out = cpu_model(input_ids=tok, past_key_values=cache, use_cache=True)
-                times.append(time.perf_counter() - t)
-                tok = out.logits[:, -1:].argmax(-1)
-    per_row_step_2l = sorted(times)[len(times) // 2]
-    # 2-layer step = embed + dense layer + MoE layer + lm_head; the other 25 layers are MoE
-    # layers at least as costly as layer 1: estimate the MoE layer as half the sampled step.
-    moe_layer = per_row_step_2l / 2
-    step_full = per_row_step_2l + (args.layers - 2) * moe_layer
-    return {"value": round(1.0 / step_full, 4), "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"HF eager bf16 (transformers 5.5) 2-layer slice, {rows} rows x {steps} decode steps "
-                      f"at the workload's prompt lengths, batch 1 per call, extrapolated to "
-                      f"{args.layers} layers ({per_row_step_2l * 1000:.1f} ms per 2-layer row-step)"}
+            times["total"].append(time.perf_counter() - t)
+    for h in hooks:
+        h.remove()
+
+    def med(xs):
+        xs = sorted(xs[1:])
+        return xs[len(xs) // 2]
+    t_l0, t_l1, t_tot = med(times["layer0"]), med(times["layer1"]), med(times["total"])
+    t_rest = max(t_tot - t_l0 - t_l1, 0.0)
+    step_full = t_rest + t_l0 + (layers - 1) * t_l1
+    value = B_all / step_full
+    sample = (f"HF eager bf16 (transformers 5.5) on {threads} host threads: all {R} rows of config {cfg_id} decoding "
+              f"as one batch (left-padded to {T0}, static KV cache at each row's prompt length), {steps} timed "
+              f"steps of a 2-layer slice; per step: dense layer {t_l0 * 1e3:.1f} ms, MoE layer {t_l1 * 1e3:.1f} ms, "
+              f"embedding + final norm + lm_head {t_rest * 1e3:.1f} ms; full depth = rest + dense + "
+              f"{layers - 1} MoE layers = {step_full * 1e3:.1f} ms")
+    return {"value": round(value, 4), "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample,
+            "ms_per_step": step_full * 1000.0, "build_s": round(t_build, 1)}
 
 
 def run_reference(args, cfg_id: int):
-    """Reference arm: the reference's CPU path (HF eager torch) on the host cores."""
+    """Reference arm: the reference's CPU path (HF eager torch) on the host cores, through
+    the same routine as the GPU arm's cpu_baseline; every step of the arm decodes the whole
+    workload batch (steps of the routine = the arm's steps)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
-    from oracle.hf_model import build_model, dsv2_lite_config
     cfg = CONFIGS[cfg_id]
     B_all = args.batch or cfg["batch"]
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    mcfg = dsv2_lite_config(num_layers=2)
-    model = build_model(mcfg, seed=WEIGHT_SEED, device="cpu", dtype=torch.bfloat16)
-    prompts = make_prompts(cfg, B_all, mcfg.vocab_size)
-    rows = min(4, B_all)
-    from transformers import DynamicCache
-    per_step = []
-    with torch.no_grad():
-        for _ in range(max(args.warmup, 0) and 1):
-            pass
-        for r in range(rows):
-            cache = DynamicCache(config=mcfg)
-            out = model(input_ids=prompts[r].view(1, -1), past_key_values=cache, use_cache=True)
-            tok = out.logits[:, -1:].argmax(-1)
-            for s in range(args.steps):
-                t = time.perf_counter()
-                out = model(input_ids=tok, past_key_values=cache, use_cache=True)
-                per_step.append(time.perf_counter() - t)
-                tok = out.logits[:, -1:].argmax(-1)
-    t2 = sorted(per_step)[len(per_step) // 2]
-    step_full = t2 + (args.layers - 2) * (t2 / 2)
-    value = 1.0 / step_full
-    sample = (f"HF eager bf16 (transformers 5.5) 2-layer slice, {rows} rows x {args.steps} decode steps, "
-              f"batch 1 per call, extrapolated to {args.layers} layers")
+    r = cpu_decode_baseline(cfg_id, B_all, args.layers, steps=max(1, min(args.steps, 4)))
+    value = r["value"]
     return {
-        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "tok/s",
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s",
         "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(step_full * 1000, 3), "higher_is_better": True, "scaling": "strong",
+        "ms_per_step": round(r["ms_per_step"], 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"config {cfg_id}: DeepSeek-V2-Lite, batch {B_all}, prompts {cfg['prompt']}",
-                   "global_batch": B_all, "parallelism": "cpu"},
-        "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": sample},
-        "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": {"workload": f"config {cfg_id}: DeepSeek-V2-Lite {args.layers} layers, batch {B_all}, "
+                               f"prompts {cfg['prompt']}", "global_batch": B_all, "parallelism": "cpu"},
+        "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
 
@@ -452,6 +532,8 @@ def main():
     ap.add_argument("--prefill", default="kernels", choices=["kernels", "eager"],
                     help="prompt prefill: the decode kernels over token batches, or the HF forward")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra-configs", action="store_true",
+                    help="skip the config 3 (B=32) and config 2 (B=1) summaries of the default run")
     args = ap.parse_args()
     if args.impl == "reference":
         out = run_reference(args, args.config)
