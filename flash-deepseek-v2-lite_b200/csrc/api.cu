@@ -295,17 +295,19 @@ int dsv2_reset_progress(void* counters, int64_t count, void* stream) {
                       "reset_progress");
 }
 
-int dsv2_rmsnorm(const void* x, int64_t x_row_stride, const void* w, int w_dtype, void* y,
+int dsv2_rmsnorm(const void* x, int64_t x_row_stride, int x_dtype, const void* w, int w_dtype, void* y,
                  int64_t y_row_stride, int rows, int cols, float eps, void* stream) {
   if (!x || !w || !y) return fail(DSV2_ERR_INVALID, "rmsnorm: null pointer");
   if (cols <= 0 || cols % 8 || cols > 4096)
     return fail(DSV2_ERR_UNSUPPORTED, "rmsnorm: cols=%d (need multiple of 8, <= 4096)", cols);
-  if (w_dtype != DSV2_BF16 && w_dtype != DSV2_F32)
+  if (x_dtype != DSV2_BF16 && x_dtype != DSV2_F16)
+    return fail(DSV2_ERR_UNSUPPORTED, "rmsnorm: activation dtype %d", x_dtype);
+  if (w_dtype != DSV2_BF16 && w_dtype != DSV2_F16 && w_dtype != DSV2_F32)
     return fail(DSV2_ERR_UNSUPPORTED, "rmsnorm: weight dtype %d", w_dtype);
   if (!aligned16(x) || !aligned16(y) || (x_row_stride % 8) || (y_row_stride % 8))
     return fail(DSV2_ERR_INVALID, "rmsnorm: rows must be 16-byte aligned");
   if (rows <= 0) return DSV2_OK;
-  return check_launch(launch_rmsnorm(x, x_row_stride, w, w_dtype, y, y_row_stride, rows, cols, eps,
+  return check_launch(launch_rmsnorm(x, x_row_stride, x_dtype, w, w_dtype, y, y_row_stride, rows, cols, eps,
                                      static_cast<cudaStream_t>(stream)),
                       "rmsnorm");
 }
@@ -347,13 +349,15 @@ int dsv2_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, con
       "embed_rmsnorm");
 }
 
-int dsv2_residual_add(const void* a, const void* b, void* out, int64_t n, void* stream) {
+int dsv2_residual_add(const void* a, const void* b, void* out, int64_t n, int dtype, void* stream) {
   if (!a || !b || !out) return fail(DSV2_ERR_INVALID, "residual_add: null pointer");
+  if (dtype != DSV2_BF16 && dtype != DSV2_F16)
+    return fail(DSV2_ERR_UNSUPPORTED, "residual_add: dtype %d", dtype);
   if (n % 8) return fail(DSV2_ERR_UNSUPPORTED, "residual_add: n=%lld not a multiple of 8", (long long)n);
   if (!aligned16(a) || !aligned16(b) || !aligned16(out))
     return fail(DSV2_ERR_INVALID, "residual_add: operands must be 16-byte aligned");
   if (n <= 0) return DSV2_OK;
-  return check_launch(launch_residual_add(a, b, out, n, static_cast<cudaStream_t>(stream)),
+  return check_launch(launch_residual_add(a, b, out, n, dtype, static_cast<cudaStream_t>(stream)),
                       "residual_add");
 }
 

@@ -30,14 +30,49 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 __device__ __forceinline__ float load_w(const void* w, int w_dtype, int i) {
   if (w_dtype == 2) return reinterpret_cast<const float*>(w)[i];
+  if (w_dtype == 1) return __half2float(reinterpret_cast<const __half*>(w)[i]);
   return __bfloat162float(reinterpret_cast<const bf16*>(w)[i]);
 }
 
-// Normalise the 8-element chunks held in v[] (fp32) and store them as bf16.
-template <int MAXCH>
+// Eight consecutive 16-bit activations (bf16 or fp16) <-> fp32, for the kernels that take
+// either (the reference's rmsnorm / residual add accept both, rmsnorm.py:64-65,
+// attention_prepost.py:197-198).
+template <typename T>
+struct Act16;
+template <>
+struct Act16<bf16> {
+  static __device__ __forceinline__ void unpack(const uint4& u, float (&v)[8]) {
+    const uint32_t* p = reinterpret_cast<const uint32_t*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[2 * j] = bf16lo(p[j]);
+      v[2 * j + 1] = bf16hi(p[j]);
+    }
+  }
+  static __device__ __forceinline__ uint32_t pack2(float a, float b) { return pack_bf16x2(a, b); }
+};
+template <>
+struct Act16<__half> {
+  static __device__ __forceinline__ void unpack(const uint4& u, float (&v)[8]) {
+    const __half2* p = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(p[j]);
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  }
+  static __device__ __forceinline__ uint32_t pack2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+
+// Normalise the 8-element chunks held in v[] (fp32) and store them as T (bf16 or fp16).
+template <int MAXCH, typename T = bf16>
 __device__ __forceinline__ void norm_store(const float (&v)[MAXCH][8], int nch_mine, int chunk0,
                                            int chunk_step, float inv, const void* w, int w_dtype,
-                                           bf16* y) {
+                                           T* y) {
 #pragma unroll
   for (int i = 0; i < MAXCH; ++i) {
     if (i >= nch_mine) break;
@@ -48,7 +83,7 @@ __device__ __forceinline__ void norm_store(const float (&v)[MAXCH][8], int nch_m
     for (int j = 0; j < 4; ++j) {
       const float a = v[i][2 * j] * inv * load_w(w, w_dtype, c * 8 + 2 * j);
       const float b = v[i][2 * j + 1] * inv * load_w(w, w_dtype, c * 8 + 2 * j + 1);
-      op[j] = pack_bf16x2(a, b);
+      op[j] = Act16<T>::pack2(a, b);
     }
     *reinterpret_cast<uint4*>(y + c * 8) = o;
   }
@@ -57,16 +92,17 @@ __device__ __forceinline__ void norm_store(const float (&v)[MAXCH][8], int nch_m
 constexpr int kNormThreads = 256;
 constexpr int kNormMaxCh = 2;  // up to 256 * 2 * 8 = 4096 columns
 
-__global__ __launch_bounds__(kNormThreads) void rmsnorm_kernel(const bf16* __restrict__ x,
+template <typename T>
+__global__ __launch_bounds__(kNormThreads) void rmsnorm_kernel(const T* __restrict__ x,
                                                                long long x_stride,
                                                                const void* __restrict__ w,
-                                                               int w_dtype, bf16* __restrict__ y,
+                                                               int w_dtype, T* __restrict__ y,
                                                                long long y_stride, int cols,
                                                                float eps) {
   pdl_enter();
   __shared__ float red[kNormThreads / 32];
   const int row = blockIdx.x;
-  const bf16* xr = x + row * x_stride;
+  const T* xr = x + row * x_stride;
   const int nch = cols / 8;
   float v[kNormMaxCh][8];
   float ss = 0.f;
@@ -76,19 +112,15 @@ __global__ __launch_bounds__(kNormThreads) void rmsnorm_kernel(const bf16* __res
     const int c = threadIdx.x + i * kNormThreads;
     if (c < nch) {
       const uint4 u = *reinterpret_cast<const uint4*>(xr + c * 8);
-      const uint32_t* up = reinterpret_cast<const uint32_t*>(&u);
+      Act16<T>::unpack(u, v[i]);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        v[i][2 * j] = bf16lo(up[j]);
-        v[i][2 * j + 1] = bf16hi(up[j]);
-        ss += v[i][2 * j] * v[i][2 * j] + v[i][2 * j + 1] * v[i][2 * j + 1];
-      }
+      for (int j = 0; j < 4; ++j) ss += v[i][2 * j] * v[i][2 * j] + v[i][2 * j + 1] * v[i][2 * j + 1];
       mine = i + 1;
     }
   }
   ss = block_sum<kNormThreads>(ss, red);
   const float inv = rsqrtf(ss / static_cast<float>(cols) + eps);
-  norm_store<kNormMaxCh>(v, mine, threadIdx.x, kNormThreads, inv, w, w_dtype, y + row * y_stride);
+  norm_store<kNormMaxCh, T>(v, mine, threadIdx.x, kNormThreads, inv, w, w_dtype, y + row * y_stride);
 }
 
 // h[row] = bf16(h[row] + sum_p delta[row, p]); y[row] = rmsnorm(h[row]) * w.
@@ -239,20 +271,19 @@ __global__ __launch_bounds__(kNormThreads) void embed_rmsnorm_kernel(
 }
 
 // out = bf16(a + b), 8 elements per thread
-__global__ void residual_add_kernel(const bf16* __restrict__ a, const bf16* __restrict__ b,
-                                    bf16* __restrict__ out, long long n8) {
+template <typename T>
+__global__ void residual_add_kernel(const T* __restrict__ a, const T* __restrict__ b,
+                                    T* __restrict__ out, long long n8) {
   pdl_enter();
   const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (i >= n8) return;
-  const uint4 x = reinterpret_cast<const uint4*>(a)[i];
-  const uint4 z = reinterpret_cast<const uint4*>(b)[i];
-  const uint32_t* xp = reinterpret_cast<const uint32_t*>(&x);
-  const uint32_t* zp = reinterpret_cast<const uint32_t*>(&z);
+  float x[8], z[8];
+  Act16<T>::unpack(reinterpret_cast<const uint4*>(a)[i], x);
+  Act16<T>::unpack(reinterpret_cast<const uint4*>(b)[i], z);
   uint4 o;
   uint32_t* op = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
-  for (int j = 0; j < 4; ++j)
-    op[j] = pack_bf16x2(bf16lo(xp[j]) + bf16lo(zp[j]), bf16hi(xp[j]) + bf16hi(zp[j]));
+  for (int j = 0; j < 4; ++j) op[j] = Act16<T>::pack2(x[2 * j] + z[2 * j], x[2 * j + 1] + z[2 * j + 1]);
   reinterpret_cast<uint4*>(out)[i] = o;
 }
 
@@ -382,9 +413,14 @@ __global__ void advance_positions_kernel(long long* __restrict__ pos, int n) {
 // ---------------------------------------------------------------------------
 // host launchers (called from api.cu)
 // ---------------------------------------------------------------------------
-cudaError_t launch_rmsnorm(const void* x, long long xs, const void* w, int wd, void* y,
+cudaError_t launch_rmsnorm(const void* x, long long xs, int xd, const void* w, int wd, void* y,
                            long long ys, int rows, int cols, float eps, cudaStream_t st) {
-  launch_kernel(rmsnorm_kernel, rows, kNormThreads, 0, st, reinterpret_cast<const bf16*>(x), xs, w, wd, reinterpret_cast<bf16*>(y), ys, cols, eps);
+  if (xd == 1)
+    launch_kernel(rmsnorm_kernel<__half>, rows, kNormThreads, 0, st, reinterpret_cast<const __half*>(x), xs, w, wd,
+                  reinterpret_cast<__half*>(y), ys, cols, eps);
+  else
+    launch_kernel(rmsnorm_kernel<bf16>, rows, kNormThreads, 0, st, reinterpret_cast<const bf16*>(x), xs, w, wd,
+                  reinterpret_cast<bf16*>(y), ys, cols, eps);
   return cudaGetLastError();
 }
 
@@ -406,11 +442,17 @@ cudaError_t launch_embed_rmsnorm(const long long* ids, const void* table, long l
   return cudaGetLastError();
 }
 
-cudaError_t launch_residual_add(const void* a, const void* b, void* out, long long n,
+cudaError_t launch_residual_add(const void* a, const void* b, void* out, long long n, int dtype,
                                 cudaStream_t st) {
   const long long n8 = n / 8;
   const int thr = 256;
-  launch_kernel(residual_add_kernel, static_cast<unsigned>((n8 + thr - 1) / thr), thr, 0, st, reinterpret_cast<const bf16*>(a), reinterpret_cast<const bf16*>(b), reinterpret_cast<bf16*>(out), n8);
+  const unsigned grid = static_cast<unsigned>((n8 + thr - 1) / thr);
+  if (dtype == 1)
+    launch_kernel(residual_add_kernel<__half>, grid, thr, 0, st, reinterpret_cast<const __half*>(a),
+                  reinterpret_cast<const __half*>(b), reinterpret_cast<__half*>(out), n8);
+  else
+    launch_kernel(residual_add_kernel<bf16>, grid, thr, 0, st, reinterpret_cast<const bf16*>(a),
+                  reinterpret_cast<const bf16*>(b), reinterpret_cast<bf16*>(out), n8);
   return cudaGetLastError();
 }
 

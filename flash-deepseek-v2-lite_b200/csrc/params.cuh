@@ -122,14 +122,14 @@ struct MlaDecodeParams {
 };
 
 // norm.cu
-cudaError_t launch_rmsnorm(const void*, long long, const void*, int, void*, long long, int, int,
+cudaError_t launch_rmsnorm(const void*, long long, int, const void*, int, void*, long long, int, int,
                            float, cudaStream_t);
 cudaError_t launch_add_rmsnorm(void*, void*, const void*, int, int, long long, long long,
                                const void*, int, void*, int, int, float, cudaStream_t,
                                const PeerTable* peers = nullptr, int layer = 0);
 cudaError_t launch_embed_rmsnorm(const long long*, const void*, long long, const void*, int, void*,
                                  void*, int, int, float, cudaStream_t);
-cudaError_t launch_residual_add(const void*, const void*, void*, long long, cudaStream_t);
+cudaError_t launch_residual_add(const void*, const void*, void*, long long, int, cudaStream_t);
 cudaError_t launch_silu_mul(const void*, const void*, void*, long long, cudaStream_t);
 cudaError_t launch_sum_partials(const float* part, int n_parts, long long ps, long long rs, void* out,
                                int out_f32, long long ors, int rows, int cols, cudaStream_t st);

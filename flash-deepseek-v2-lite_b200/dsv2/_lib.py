@@ -21,6 +21,7 @@ DSV2_ERR_DEVICE = 3
 DSV2_ERR_UNSUPPORTED = 4
 
 DSV2_BF16 = 0
+DSV2_F16 = 1
 DSV2_F32 = 2
 
 EPI_STORE_BF16 = 0
@@ -115,7 +116,7 @@ _SIGNATURES = {
     "dsv2_get_device_error": ([ctypes.POINTER(c_i32), c_i32], c_i32),
     "dsv2_stream_check": ([c_vp], c_i32),
     "dsv2_reset_progress": ([c_vp, c_i64, c_vp], c_i32),
-    "dsv2_rmsnorm": ([c_vp, c_i64, c_vp, c_i32, c_vp, c_i64, c_i32, c_i32, c_f32, c_vp], c_i32),
+    "dsv2_rmsnorm": ([c_vp, c_i64, c_i32, c_vp, c_i32, c_vp, c_i64, c_i32, c_i32, c_f32, c_vp], c_i32),
     "dsv2_add_rmsnorm": ([c_vp, c_vp, c_vp, c_i32, c_i32, c_i64, c_i64, c_vp, c_i32, c_vp, c_i32, c_i32,
                           c_f32, ctypes.POINTER(PeerTable), c_i32, c_vp], c_i32),
     "dsv2_peer_alloc": ([ctypes.c_size_t, ctypes.POINTER(c_vp)], c_i32),
@@ -124,7 +125,7 @@ _SIGNATURES = {
     "dsv2_peer_import": ([c_vp, ctypes.POINTER(c_vp)], c_i32),
     "dsv2_peer_close": ([c_vp], c_i32),
     "dsv2_embed_rmsnorm": ([c_vp, c_vp, c_i64, c_vp, c_i32, c_vp, c_vp, c_i32, c_i32, c_f32, c_vp], c_i32),
-    "dsv2_residual_add": ([c_vp, c_vp, c_vp, c_i64, c_vp], c_i32),
+    "dsv2_residual_add": ([c_vp, c_vp, c_vp, c_i64, c_i32, c_vp], c_i32),
     "dsv2_silu_mul": ([c_vp, c_vp, c_vp, c_i64, c_vp], c_i32),
     "dsv2_sum_partials": ([c_vp, c_i32, c_i64, c_i64, c_vp, c_i32, c_i64, c_i32, c_i32, c_vp], c_i32),
     "dsv2_prepare_decode_inputs": ([c_vp, c_i32, c_vp, c_i64, c_vp, c_i64, c_vp, c_i32, c_i32, c_vp], c_i32),

@@ -51,13 +51,14 @@ def prepare_decode_inputs_triton(cache_position: torch.Tensor, attention_mask: t
 
 
 def residual_add_triton(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    """bf16(a + b) with fp32 math into a new tensor (attention_prepost.py:191-223)."""
+    """a + b with fp32 math, rounded to the inputs' dtype (bf16 or fp16), into a new tensor
+    (attention_prepost.py:191-223)."""
     if a.device.type != "cuda" or b.device.type != "cuda":
         raise NotImplementedError("residual_add_triton requires CUDA tensors")
     if a.shape != b.shape:
         raise ValueError("a and b must have the same shape")
-    if a.dtype != torch.bfloat16 or b.dtype != a.dtype:
-        raise NotImplementedError("residual_add_triton supports bf16 with same dtype")
+    if a.dtype not in (torch.bfloat16, torch.float16) or b.dtype != a.dtype:
+        raise NotImplementedError("residual_add_triton supports bf16/fp16 with same dtype")
     if not a.is_contiguous() or not b.is_contiguous():
         raise NotImplementedError("residual_add_triton requires contiguous inputs")
     if a.numel() % 8:

@@ -9,14 +9,14 @@ from .. import ops
 def rmsnorm_triton(hidden_states: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     """y = x * rsqrt(mean(x^2) + eps) * w over the last dimension, fp32 math, output in
     x's dtype and shape.  Same checks and exception types as the reference
-    (rmsnorm.py:62-76); this build covers bf16 activations with a bf16 or fp32 weight and
-    a last dimension that is a multiple of 8 and at most 4096."""
+    (rmsnorm.py:62-76): bf16 or fp16 activations, a bf16, fp16 or fp32 weight; this build
+    also needs a last dimension that is a multiple of 8 and at most 4096."""
     if hidden_states.device.type != "cuda":
         raise NotImplementedError("rmsnorm_triton requires CUDA tensor")
-    if hidden_states.dtype != torch.bfloat16:
-        raise NotImplementedError("rmsnorm_triton only supports bf16 input")
-    if weight.dtype not in (torch.bfloat16, torch.float32):
-        raise NotImplementedError("rmsnorm_triton only supports bf16/fp32 weight")
+    if hidden_states.dtype not in (torch.bfloat16, torch.float16):
+        raise NotImplementedError("rmsnorm_triton only supports bf16/fp16 input")
+    if weight.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        raise NotImplementedError("rmsnorm_triton only supports bf16/fp16/fp32 weight")
     if not weight.is_contiguous():
         raise NotImplementedError("rmsnorm_triton requires contiguous weight")
     x = hidden_states

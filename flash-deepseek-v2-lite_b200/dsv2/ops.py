@@ -14,7 +14,7 @@ import torch
 
 from . import _lib
 from ._lib import (
-    DSV2_BF16, DSV2_F32, EPI_STORE_BF16, EPI_STORE_F32, EPI_SWIGLU, EPI_SCALE_F32,
+    DSV2_BF16, DSV2_F16, DSV2_F32, EPI_STORE_BF16, EPI_STORE_F32, EPI_SWIGLU, EPI_SCALE_F32,
     FAMILY_SMALL, FAMILY_BATCH, LinearArgs, MlaDecodeArgs, MlaPrepArgs, MoeArgs, PeerTable, RouterArgs,
 )
 
@@ -44,19 +44,25 @@ def _wdtype(w: torch.Tensor) -> int:
         return DSV2_BF16
     if w.dtype == torch.float32:
         return DSV2_F32
+    if w.dtype == torch.float16:
+        return DSV2_F16
     raise NotImplementedError(f"unsupported weight dtype {w.dtype}")
 
 
+_ACT16 = {torch.bfloat16: DSV2_BF16, torch.float16: DSV2_F16}
+
+
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor) -> torch.Tensor:
-    """out[r] = bf16(x[r] * rsqrt(mean(x[r]^2) + eps) * w) for 2-D x (rows, cols)."""
+    """out[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * w for 2-D x (rows, cols), fp32 math, one
+    rounding to x's dtype (bf16 or fp16)."""
     _cuda(x, "x")
-    if x.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
-        raise NotImplementedError("rmsnorm supports bf16 activations")
+    if x.dtype not in _ACT16 or out.dtype != x.dtype:
+        raise NotImplementedError("rmsnorm supports bf16 / fp16 activations (out in the same dtype)")
     if x.stride(-1) != 1 or out.stride(-1) != 1 or not w.is_contiguous():
         raise NotImplementedError("rmsnorm requires a contiguous last dimension and weight")
     rows, cols = x.shape
-    _lib.call("dsv2_rmsnorm", x.data_ptr(), x.stride(0), w.data_ptr(), _wdtype(w), out.data_ptr(),
-              out.stride(0), rows, cols, float(eps), stream())
+    _lib.call("dsv2_rmsnorm", x.data_ptr(), x.stride(0), _ACT16[x.dtype], w.data_ptr(), _wdtype(w),
+              out.data_ptr(), out.stride(0), rows, cols, float(eps), stream())
     return out
 
 
@@ -100,7 +106,11 @@ def embed_rmsnorm(ids: torch.Tensor, table: torch.Tensor, w: torch.Tensor, eps: 
 
 
 def residual_add(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
-    _lib.call("dsv2_residual_add", a.data_ptr(), b.data_ptr(), out.data_ptr(), a.numel(), stream())
+    """out = a + b in fp32, rounded once to the inputs' dtype (bf16 or fp16)."""
+    if a.dtype not in _ACT16 or b.dtype != a.dtype or out.dtype != a.dtype:
+        raise NotImplementedError("residual_add supports bf16 / fp16 tensors of one dtype")
+    _lib.call("dsv2_residual_add", a.data_ptr(), b.data_ptr(), out.data_ptr(), a.numel(), _ACT16[a.dtype],
+              stream())
     return out
 
 

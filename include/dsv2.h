@@ -36,6 +36,7 @@ extern "C" {
 
 /* ---- dtype codes ---------------------------------------------------------- */
 #define DSV2_BF16 0
+#define DSV2_F16 1 /* activations of dsv2_rmsnorm / dsv2_residual_add; norm weights */
 #define DSV2_F32 2
 
 /* ---- linear epilogues ----------------------------------------------------- */
@@ -140,11 +141,12 @@ DSV2_API int dsv2_peer_export(const void* ptr, void* handle /* 64 bytes */);
 DSV2_API int dsv2_peer_import(const void* handle, void** ptr);
 DSV2_API int dsv2_peer_close(void* ptr);
 
-/* RMSNorm: y[r] = bf16(x[r] * rsqrt(mean(x[r]^2) + eps) * w), fp32 math, one
- * rounding.  cols % 8 == 0, cols <= 4096.  w_dtype DSV2_BF16 or DSV2_F32.
+/* RMSNorm: y[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * w, fp32 math, one rounding to
+ * x's dtype.  x_dtype DSV2_BF16 or DSV2_F16 (y has the same dtype); w_dtype DSV2_BF16,
+ * DSV2_F16 or DSV2_F32.  cols % 8 == 0, cols <= 4096.
  * Reference: rmsnorm_triton, triton_kernels/rmsnorm.py:60-95 (kernel :8-57). */
-DSV2_API int dsv2_rmsnorm(const void* x, int64_t x_row_stride, const void* w, int w_dtype, void* y,
-                 int64_t y_row_stride, int rows, int cols, float eps, void* stream);
+DSV2_API int dsv2_rmsnorm(const void* x, int64_t x_row_stride, int x_dtype, const void* w, int w_dtype,
+                 void* y, int64_t y_row_stride, int rows, int cols, float eps, void* stream);
 
 /* Fused residual add + RMSNorm (two outputs):
  *   h_out[r] = bf16(h[r] + sum_p delta[r, p]),  y[r] = rmsnorm(h_out[r]) * w.
@@ -168,9 +170,10 @@ DSV2_API int dsv2_embed_rmsnorm(const int64_t* ids, const void* table, int64_t v
                        int w_dtype, void* h, void* y, int rows, int cols, float eps,
                        void* stream);
 
-/* out = bf16(a + b) over n contiguous bf16 elements (n % 8 == 0).
+/* out = a + b in fp32, rounded once to the inputs' dtype (dtype DSV2_BF16 or DSV2_F16),
+ * over n contiguous elements (n % 8 == 0).
  * Reference: residual_add_triton, triton_kernels/attention_prepost.py:191-223. */
-DSV2_API int dsv2_residual_add(const void* a, const void* b, void* out, int64_t n, void* stream);
+DSV2_API int dsv2_residual_add(const void* a, const void* b, void* out, int64_t n, int dtype, void* stream);
 
 /* out = bf16(silu(gate) * up) over n contiguous bf16 elements (n % 8 == 0).
  * Reference: silu_mul_triton, triton_kernels/mlp_elementwise.py:24-45. */

@@ -27,8 +27,8 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 
 
 def residual_add(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    """REF attention_prepost.py:85-110: fp32 add, bf16 result."""
-    return (a.float() + b.float()).to(BF16)
+    """REF attention_prepost.py:85-110: fp32 add, result in the inputs' dtype (bf16 / fp16)."""
+    return (a.float() + b.float()).to(a.dtype)
 
 
 def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:

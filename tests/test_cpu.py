@@ -35,9 +35,9 @@ def test_library_loads_and_exports_every_declared_symbol():
 def test_ops_fail_loudly_without_valid_args():
     from dsv2 import _lib
     with pytest.raises(ValueError):
-        _lib.call("dsv2_rmsnorm", None, 0, None, 0, None, 0, 1, 2048, 1e-6, None)
+        _lib.call("dsv2_rmsnorm", None, 0, 0, None, 0, None, 0, 1, 2048, 1e-6, None)
     with pytest.raises(NotImplementedError):
-        _lib.call("dsv2_rmsnorm", 16, 2048, 16, 0, 16, 2048, 1, 4100, 1e-6, None)
+        _lib.call("dsv2_rmsnorm", 16, 2048, 0, 16, 0, 16, 2048, 1, 4100, 1e-6, None)
 
 
 def trunc_bf16(x: torch.Tensor) -> torch.Tensor:

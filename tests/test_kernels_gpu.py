@@ -43,6 +43,25 @@ def test_rmsnorm_triton_golden(K, golden_ref):
         torch.testing.assert_close(y.reshape(g["y"].shape).cpu().float(), g["y"].float(), rtol=2 ** -7, atol=1e-6)
 
 
+@pytest.mark.parametrize("wdt", [torch.float16, torch.float32, torch.bfloat16])
+def test_rmsnorm_and_residual_add_fp16(K, wdt):
+    """fp16 activations, as the reference's wrappers accept (rmsnorm.py:64-65,
+    attention_prepost.py:197-198): within one fp16 rounding of the oracle's fp32 math."""
+    g = torch.Generator().manual_seed(17)
+    x = torch.randn(6, 1, 2048, generator=g).to(torch.float16)
+    w = (1 + 0.1 * torch.randn(2048, generator=g)).to(wdt)
+    y = K.rmsnorm.rmsnorm_triton(x.to(DEV), w.to(DEV), 1e-6)
+    assert y.dtype == torch.float16 and y.shape == x.shape
+    torch.testing.assert_close(y.cpu().float(), O.rmsnorm(x, w, 1e-6).float(), rtol=2 ** -10, atol=1e-5)
+    a = torch.randn(4, 1, 2048, generator=g).to(torch.float16)
+    b = torch.randn(4, 1, 2048, generator=g).to(torch.float16)
+    out = K.pre.residual_add_triton(a.to(DEV), b.to(DEV))
+    assert out.dtype == torch.float16
+    assert torch.equal(out.cpu(), O.residual_add(a, b))
+    with pytest.raises(NotImplementedError):
+        K.pre.residual_add_triton(a.to(DEV), b.to(DEV).to(torch.bfloat16))
+
+
 def test_elementwise_golden(K, golden_ref):
     g = golden_ref["residual_add"]
     out = K.pre.residual_add_triton(g["a"].to(DEV), g["b"].to(DEV))
