@@ -240,6 +240,8 @@ def measure(model, cfg_id: int, args, rank: int, world: int, group, local: int, 
     for _ in range(warmup):
         eng.replay()
     lens_before = [int(x) for x in eng.positions.cpu()]
+    if getattr(eng, "peer_wait_stats", None) is not None:
+        eng.peer_wait_stats.zero_()
     barrier(world)
     stream = torch.cuda.current_stream()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -252,7 +254,20 @@ def measure(model, cfg_id: int, args, rank: int, world: int, group, local: int, 
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_pop()
     barrier(world)
-    ms = max_over_ranks(start.elapsed_time(end), world)
+    ms_rank = start.elapsed_time(end)
+    per_rank = None
+    if world > 1:
+        # per-rank step time and the cross-GPU waits (mean CTA wait of a launch x MoE layers)
+        import torch.distributed as dist
+        waits = None
+        if getattr(eng, "peer_wait_stats", None) is not None:
+            st = [int(v) for v in eng.peer_wait_stats.cpu()]
+            n_moe = int(eng.peers.n_moe_layers)
+            waits = {"dispatch_wait_us_per_step": round(st[0] / max(st[1], 1) * n_moe / 1e3, 2),
+                     "combine_wait_us_per_step": round(st[2] / max(st[3], 1) * n_moe / 1e3, 2)}
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, {"rank": rank, "ms_per_step": round(ms_rank / steps, 4), **(waits or {})})
+    ms = max_over_ranks(ms_rank, world)
     ms_step = ms / steps
     value = B_all * steps / (ms / 1000.0)
     distinct = distinct_experts(eng)
@@ -288,6 +303,7 @@ def measure(model, cfg_id: int, args, rank: int, world: int, group, local: int, 
         "distinct": distinct, "launches_per_step": launches_per_step, "lens_before": lens_before,
         "e2e_value": B_all * e2e_steps / e2e_s, "e2e_bytes": 8 * B_all,
         "t_build": t_build, "t_prefill": t_prefill, "prefill_tokens": sum(len(p) for p in prompts),
+        "per_rank": per_rank,
     }
     return res
 
@@ -407,6 +423,7 @@ def run_ours(args, cfg_id: int):
             "clocks": clocks,
             "cpu_baseline": cpu,
             "other_configs": extra or None,
+            "per_rank": res["per_rank"],
             "setup_s": {"model": round(t_model, 1), "engine": round(res["t_build"], 1),
                         "prefill": round(res["t_prefill"], 1), "prefill_method": args.prefill,
                         "prefill_tokens": res["prefill_tokens"]},

@@ -200,6 +200,7 @@ int to_peers(const dsv2_peer_table* t, PeerTable* out) {
   out->epoch = reinterpret_cast<const long long*>(t->epoch);
   if (t->wait_polls < 0) return fail(DSV2_ERR_INVALID, "peer table: wait_polls %d", t->wait_polls);
   out->wait_polls = static_cast<unsigned int>(t->wait_polls);
+  out->wait_stats = reinterpret_cast<unsigned long long*>(t->wait_stats);
   return DSV2_OK;
 }
 

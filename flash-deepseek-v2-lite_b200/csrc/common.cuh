@@ -85,16 +85,28 @@ __device__ __forceinline__ void red_release_sys_add_u64(unsigned long long* p, u
 // of any kernel already failed (so that a broken exchange ends quickly instead of timing
 // out at every layer).
 constexpr uint32_t kPeerWaitPolls = 1u << 24;
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// stat (optional): [0] += nanoseconds spent in this wait, [1] += 1
 __device__ __forceinline__ bool wait_counter_sys(const unsigned long long* ctr, unsigned long long target,
-                                                 uint32_t polls) {
+                                                 uint32_t polls, unsigned long long* stat = nullptr) {
   const uint32_t limit = polls ? polls : kPeerWaitPolls;
+  const unsigned long long t0 = stat ? globaltimer_ns() : 0ull;
+  bool ok = false;
   for (uint32_t i = 0; i < limit; ++i) {
-    if (ld_acquire_sys_u64(ctr) >= target) return true;
+    if (ld_acquire_sys_u64(ctr) >= target) { ok = true; break; }
     if ((i & 255) == 0 && *reinterpret_cast<volatile int*>(&g_device_error) != 0) return false;
     __nanosleep(64);
   }
-  set_device_error(kErrMbarTimeout);
-  return false;
+  if (stat) {
+    atomicAdd(&stat[0], globaltimer_ns() - t0);
+    atomicAdd(&stat[1], 1ull);
+  }
+  if (!ok) set_device_error(kErrMbarTimeout);
+  return ok;
 }
 
 // ----------------------------------------------------------------------------

@@ -164,7 +164,8 @@ __global__ __launch_bounds__(kNormThreads) void add_rmsnorm_kernel(
     // expert parallel: every rank has written its MoE slot outputs for these rows
     __shared__ int s_ok;
     if (threadIdx.x == 0)
-      s_ok = wait_counter_sys(peer_ctr(peers, peers.rank, 1), peer_target(peers, layer, 1ull), peers.wait_polls);
+      s_ok = wait_counter_sys(peer_ctr(peers, peers.rank, 1), peer_target(peers, layer, 1ull), peers.wait_polls,
+                              peers.wait_stats ? peers.wait_stats + 2 : nullptr);
     __syncthreads();
     if (!s_ok) return;
   }

@@ -22,6 +22,7 @@ struct PeerTable {
   int n_moe;                  // MoE layers per step
   const long long* epoch;     // completed steps of this rank
   unsigned int wait_polls;    // poll limit of the cross-GPU waits (0 = kPeerWaitPolls)
+  unsigned long long* wait_stats;  // optional [4]: dispatch waits (ns, count), combine waits (ns, count)
 };
 
 __device__ __forceinline__ unsigned long long* peer_ctr(const PeerTable& t, int rank, int which) {

@@ -381,7 +381,7 @@ __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams 
     if (threadIdx.x == 0) {
       const unsigned long long per_rank = (p.peers.rows_per_rank + kRtTok - 1) / kRtTok;
       s_ok = wait_counter_sys(peer_ctr(p.peers, p.peers.rank, 0), peer_target(p.peers, p.layer, per_rank),
-                              p.peers.wait_polls);
+                              p.peers.wait_polls, p.peers.wait_stats);
     }
     __syncthreads();
     if (!s_ok) return;

@@ -56,7 +56,7 @@ class PeerTable(ctypes.Structure):
         ("world", c_i32), ("rank", c_i32), ("base", c_vp * 8),
         ("xg_offset", c_i64), ("ids_offset", c_i64), ("w_offset", c_i64), ("part_offset", c_i64),
         ("ctr_offset", c_i64), ("rows_per_rank", c_i32), ("n_moe_layers", c_i32), ("epoch", c_vp),
-        ("wait_polls", c_i32),
+        ("wait_polls", c_i32), ("wait_stats", c_vp),
     ]
 
 

@@ -227,6 +227,9 @@ class DecodeEngine:
         t.xg_offset, t.ids_offset, t.w_offset, t.part_offset, t.ctr_offset = off_xg, off_ids, off_w, off_part, off_ctr
         t.rows_per_rank, t.n_moe_layers = B, n_moe
         t.epoch = self.step_count.data_ptr()
+        # time the CTAs spend in the cross-GPU waits (dispatch, combine), for the bench
+        self.peer_wait_stats = torch.zeros(4, device=self.dev, dtype=torch.int64)
+        t.wait_stats = self.peer_wait_stats.data_ptr()
         self.peers = t
         self._peer_local, self._peer_remote = local, [b for q, b in enumerate(bases) if q != self.rank]
         self.x_g = _device_view(local + off_xg, (Ball, HIDDEN), torch.int16, self.dev).view(torch.bfloat16)

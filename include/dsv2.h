@@ -133,6 +133,10 @@ typedef struct dsv2_peer_table {
   /* polls before a cross-GPU wait gives up and sets the device error word
    * (DSV2_DEVERR_TIMEOUT); 0 = the default 2^24 (several seconds) */
   int32_t wait_polls;
+  /* optional uint64[4] accumulators (NULL = none): [0] nanoseconds the CTAs of the
+   * bucketing launches spent waiting for every rank's dispatch, [1] their number of
+   * waits, [2] / [3] the same for the combine waits of the add+RMSNorm launches */
+  uint64_t* wait_stats;
 } dsv2_peer_table;
 
 DSV2_API int dsv2_peer_alloc(size_t bytes, void** ptr);

@@ -5,10 +5,11 @@ of the routed experts and half of the rows; the MoE activations are all-gathered
 the expert outputs combined inside the captured decode graph: batch family over NVLink
 peer memory (the router writes every rank's inputs, the fused MoE writes each slot into
 its owner's buffer), small family with NCCL all-gather / reduce-scatter.  Logits
-cosine >= 0.999 and first-step tokens identical: a rank holds half the rows, so the
-latent attention spreads a different tile stream over the SMs (rows are cut between
-CTAs at other places) and the small family's fp32 sums over experts are associated
-differently across ranks.
+cosine >= 0.999 and first-step tokens identical up to a near-tie of the single-GPU logits:
+a rank holds half the rows, so the latent attention spreads a different tile stream over
+the SMs (rows are cut between CTAs at other places), the expert-parallel router sums the
+gate logits in another order, and the small family's fp32 sums over experts are
+associated differently across ranks.
 """
 import os
 import socket
@@ -85,7 +86,14 @@ def test_expert_parallel_matches_single_gpu(family, tmp_path):
     for r in range(2):
         got = torch.load(f"{out}.{r}")
         rows = slice(r * half, (r + 1) * half)
-        assert torch.equal(got["toks"][0], ref_toks[0, rows])
+        # first greedy tokens equal, except a near-tie of the single-GPU logits (the expert-
+        # parallel router and the attention sum in another order): at most one per rank
+        same = got["toks"][0] == ref_toks[0, rows]
+        assert int((~same).sum()) <= 1, (r, got["toks"][0], ref_toks[0, rows])
+        for i in torch.nonzero(~same).flatten().tolist():
+            lg = ref_logits[0, r * half + i].double()
+            gap = float(lg[int(ref_toks[0, r * half + i])] - lg[int(got["toks"][0][i])])
+            assert 0 <= gap <= 2e-2 * float(lg.abs().max()), (r, i, gap)
         # a row is compared while its inputs agree: up to and including the first step
         # whose greedy token differs (a near-tie can flip under the different summation
         # order; from then on the row decodes a different sequence)
