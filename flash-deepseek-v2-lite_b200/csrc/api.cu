@@ -523,6 +523,7 @@ static int linear_impl(const dsv2_linear_args* a, int family, void* stream, bool
   p.k_splits = a->k_splits > 1 ? a->k_splits : 1;
   p.y_split_stride = a->y_split_stride;
   p.offsets_prior = a->offsets_prior != 0;
+  p.active_groups = (a->group_offsets && a->max_routes > 0) ? std::min(a->n_groups, a->max_routes) : a->n_groups;
   if (p.k_splits > 1) {
     if (family != DSV2_FAMILY_BATCH || a->group_offsets || a->epilogue != DSV2_EPI_STORE_F32)
       return fail(DSV2_ERR_UNSUPPORTED, "linear: a K split needs the batch family, dense mode and fp32 output");

@@ -48,6 +48,7 @@ struct LinearParams {
   int k_splits;                 // batch family, dense fp32 output: K split across CTAs
   long long y_split_stride;     // elements between the fp32 partial outputs of the splits
   int offsets_prior;            // group_offsets were written at least two launches earlier
+  int active_groups;            // grouped small family: launch work for this many non-empty groups
 };
 
 __device__ __forceinline__ float silu_ref(float g) { return g / (1.f + expf(-g)); }

@@ -17,6 +17,8 @@
 // read on the device, so the launch grid is fixed by host-side upper bounds and the
 // kernel is CUDA-graph safe.  Unlike the reference's route-GEMV, tokens routed to
 // the same expert share one pass over the expert's weights (up to 8 at a time).
+#include <algorithm>
+
 #include "linear.cuh"
 
 namespace dsv2 {
@@ -24,6 +26,22 @@ namespace dsv2 {
 constexpr int kGemvWarps = 8;
 constexpr int kGemvRows = 16;
 constexpr int kGemvTok = 8;
+
+// Index of the k-th group (in order) that holds at least one route, or -1.  Every warp
+// of the CTA computes it from the device-side offsets (at most a few hundred groups).
+__device__ __forceinline__ int kth_routed_group(const int* go, int G, int k) {
+  const int lane = threadIdx.x & 31;
+  int seen = 0;
+  for (int base = 0; base < G; base += 32) {
+    const int g = base + lane;
+    const bool hit = g < G && go[g + 1] > go[g];
+    const unsigned m = __ballot_sync(0xffffffffu, hit);
+    const int c = __popc(m);
+    if (seen + c > k) return base + static_cast<int>(__fns(m, 0, k - seen + 1));
+    seen += c;
+  }
+  return -1;
+}
 
 template <bool SWIGLU, int U>
 __global__ __launch_bounds__(kGemvWarps * 32) void gemv_mma_kernel(const LinearParams p,
@@ -40,10 +58,15 @@ __global__ __launch_bounds__(kGemvWarps * 32) void gemv_mma_kernel(const LinearP
   const int tc = item % tc_count;
   item /= tc_count;
   const int rb = item % rb_count;
-  const int g = item / rb_count;
+  // grouped launches cover the groups that hold routes, in order (item / rb_count-th of them)
+  const int g = p.group_offsets ? kth_routed_group(p.group_offsets, p.n_groups, item / rb_count) : item / rb_count;
 
   int r0, cnt;
   if (p.group_offsets) {
+    if (g < 0) {
+      if (!waited) pdl_enter();
+      return;
+    }
     r0 = p.group_offsets[g];
     cnt = p.group_offsets[g + 1] - r0;
   } else {
@@ -157,7 +180,8 @@ cudaError_t launch_linear_gemv(const LinearParams& p, cudaStream_t st) {
   const int rb_count = (p.n_rows + kGemvRows - 1) / kGemvRows;
   const int max_tok = p.group_offsets ? p.max_routes_per_group : p.n_tokens;
   const int tc_count = max(1, (max_tok + kGemvTok - 1) / kGemvTok);
-  const long long items = static_cast<long long>(p.n_groups) * rb_count * tc_count;
+  const int groups = p.group_offsets ? std::max(1, std::min(p.n_groups, p.active_groups)) : p.n_groups;
+  const long long items = static_cast<long long>(groups) * rb_count * tc_count;
   if (items <= 0) return cudaSuccess;
   if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
   const dim3 grid(static_cast<unsigned>(items));

@@ -47,7 +47,7 @@ class LinearArgs(ctypes.Structure):
         ("epilogue", c_i32), ("n_groups", c_i32), ("n_tokens", c_i32), ("max_routes_per_group", c_i32),
         ("group_offsets", c_vp), ("route_x_row", c_vp), ("route_y_row", c_vp), ("route_scale", c_vp),
         ("w_group_rows", c_i64), ("x_group_rows", c_i64),
-        ("k_splits", c_i32), ("y_split_stride", c_i64), ("offsets_prior", c_i32),
+        ("k_splits", c_i32), ("y_split_stride", c_i64), ("offsets_prior", c_i32), ("max_routes", c_i32),
     ]
 
 

@@ -374,12 +374,12 @@ class DecodeEngine:
         self._linear(w=m.gate_up, n_rows=m.inter, k=HIDDEN, up_offset=m.inter * HIDDEN,
                      w_group_stride=2 * m.inter * HIDDEN, x=gx, y=self.h_moe, epilogue=ops.EPI_SWIGLU,
                      n_groups=G, group_offsets=go, max_routes_per_group=self.B_all,
-                     route_x_row=rx, w_group_rows=2 * m.inter, x_group_rows=self.r_max)
+                     route_x_row=rx, w_group_rows=2 * m.inter, x_group_rows=self.r_max, max_routes=self.r_max)
         self._linear(w=m.down, n_rows=HIDDEN, k=m.inter, w_group_stride=HIDDEN * m.inter, x=self.h_moe,
                      y=self.partial.view(-1, HIDDEN), epilogue=ops.EPI_SCALE_F32, n_groups=G,
                      group_offsets=go, max_routes_per_group=self.B_all,
                      route_y_row=self.route_slot, route_scale=self.route_weight, w_group_rows=HIDDEN,
-                     x_group_rows=self.r_max, offsets_prior=True)
+                     x_group_rows=self.r_max, offsets_prior=True, max_routes=self.r_max)
 
     def time_moe_gemms(self, iters: int = 10) -> tuple[float, float, int]:
         """Replay only the grouped MoE GEMMs of every MoE layer (routing of the last step's

@@ -172,7 +172,7 @@ def linear(*, w: torch.Tensor, n_rows: int, k: int, x: torch.Tensor, y: torch.Te
            route_scale: torch.Tensor | None = None,
            w_group_rows: int | None = None, x_group_rows: int | None = None,
            x_base: int | None = None, k_splits: int = 1, y_split_stride: int = 0,
-           offsets_prior: bool = False) -> None:
+           offsets_prior: bool = False, max_routes: int = 0) -> None:
     """Generic linear (see dsv2_linear_args in include/dsv2.h).
 
     Strides are in elements; defaults take them from the 2-D views of w / x / y.
@@ -206,6 +206,7 @@ def linear(*, w: torch.Tensor, n_rows: int, k: int, x: torch.Tensor, y: torch.Te
     a.k_splits = k_splits
     a.y_split_stride = y_split_stride
     a.offsets_prior = 1 if offsets_prior else 0
+    a.max_routes = max_routes
     _lib.call("dsv2_linear", ctypes.byref(a), family, stream())
 
 

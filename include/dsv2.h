@@ -265,6 +265,10 @@ typedef struct dsv2_linear_args {
    * GEMM after bucketing -> gate_up.  The kernel then reads them, and starts streaming
    * weights, while the previous kernel is still running.  0 = no such guarantee. */
   int32_t offsets_prior;
+  /* grouped mode, optional: an upper bound on the total routes group_offsets[n_groups]
+   * (0 = none).  The small family then launches work only for as many groups as can hold
+   * a route (at B = 1, 8 of the 66 MoE groups) instead of one CTA set per group. */
+  int32_t max_routes;
 } dsv2_linear_args;
 
 DSV2_API int dsv2_linear(const dsv2_linear_args* args, int family, void* stream);

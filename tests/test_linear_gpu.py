@@ -103,10 +103,11 @@ def _routes(B, n_exp, g):
 
 
 @pytest.mark.parametrize("family", FAMILIES)
-@pytest.mark.parametrize("B", [1, 5, 32, 256])
-def test_grouped_moe(D, family, B):
+@pytest.mark.parametrize("B,bounded", [(1, False), (1, True), (5, True), (32, False), (256, True)])
+def test_grouped_moe(D, family, B, bounded):
     """gate_up + SwiGLU and down + route-weight scaling over experts (8 routed + 2 shared
-    groups; the expert count is reduced to keep the test small)."""
+    groups; the expert count is reduced to keep the test small).  bounded: the launch is
+    told the total route count, so the small family covers only the groups holding routes."""
     g = torch.Generator().manual_seed(100 + B)
     E, I, H = 8, 1408, 2048
     G = E + 2
@@ -129,10 +130,12 @@ def test_grouped_moe(D, family, B):
     gud, dnd = gate_up.to(DEV), down.to(DEV)
     D.linear(w=gud, n_rows=I, k=H, up_offset=I * H, w_group_stride=2 * I * H, x=gx, y=h, epilogue=D.EPI_SWIGLU,
              n_groups=G, group_offsets=god, max_routes_per_group=B, route_x_row=rx, family=f,
+             max_routes=R if bounded else 0,
              w_group_rows=2 * I, x_group_rows=R)
     partial = torch.zeros(B, 8, H, device=DEV)
     D.linear(w=dnd, n_rows=H, k=I, w_group_stride=H * I, x=h, y=partial.view(-1, H), epilogue=D.EPI_SCALE_F32,
              n_groups=G, group_offsets=god, max_routes_per_group=B, route_y_row=rsd, route_scale=rwd, family=f,
+             max_routes=R if bounded else 0,
              w_group_rows=H, x_group_rows=R)
     # oracle, route by route
     h_ref = torch.zeros(R, I, dtype=torch.bfloat16)
