@@ -79,6 +79,8 @@ int ensure_init(int* sms_out) {
       return fail(DSV2_ERR_LAUNCH, "scratch address of the allocation-free entry point: %s", cudaGetErrorString(e));
     if ((e = router_fused_max_clusters(&g_router_clusters[dev])) != cudaSuccess)
       return fail(DSV2_ERR_LAUNCH, "router occupancy: %s", cudaGetErrorString(e));
+    if ((e = linear_splitk_init()) != cudaSuccess)
+      return fail(DSV2_ERR_LAUNCH, "linear_splitk_init: %s", cudaGetErrorString(e));
     g_dev_sms[dev] = sms;
     g_dev_init[dev] = true;
   }
@@ -149,6 +151,44 @@ int tensor_map_3d(const void* base, uint64_t inner, uint64_t rows, uint64_t grou
                 static_cast<int>(r), (unsigned long long)inner, (unsigned long long)rows,
                 (unsigned long long)groups, (unsigned long long)row_stride_b,
                 (unsigned long long)group_stride_b);
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_maps.size() > 4096) g_maps.clear();
+  g_maps[key] = m;
+  *out = m;
+  return DSV2_OK;
+}
+
+// 3-D fp32 tensor map {inner, rows, groups} with a {128, box_rows, 1} box, no swizzle: the
+// partial-tile stores of the split-K linear.
+int tensor_map_f32_store(void* base, uint64_t inner, uint64_t rows, uint64_t groups, uint64_t row_stride_b,
+                         uint64_t group_stride_b, uint32_t box_rows, CUtensorMap* out) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const MapKey key(dev, reinterpret_cast<uintptr_t>(base), inner, rows, groups, row_stride_b, group_stride_b,
+                   box_rows, 1);
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+      *out = it->second;
+      return DSV2_OK;
+    }
+  }
+  int rc = get_encode();
+  if (rc) return rc;
+  if (!aligned16(base) || (row_stride_b & 15) || (group_stride_b & 15))
+    return fail(DSV2_ERR_INVALID, "TMA output not 16-byte aligned (base %p, strides %llu/%llu)", base,
+                (unsigned long long)row_stride_b, (unsigned long long)group_stride_b);
+  cuuint64_t dims[3] = {inner, rows, groups};
+  cuuint64_t strides[2] = {row_stride_b, group_stride_b};
+  cuuint32_t box[3] = {128, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUtensorMap m;
+  CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(DSV2_ERR_INVALID, "cuTensorMapEncodeTiled (fp32 store) failed (%d)", static_cast<int>(r));
   std::lock_guard<std::mutex> lk(g_mu);
   if (g_maps.size() > 4096) g_maps.clear();
   g_maps[key] = m;
@@ -564,6 +604,20 @@ static int linear_impl(const dsv2_linear_args* a, int family, void* stream, bool
                           : xrs * static_cast<uint64_t>(a->x_group_rows);
   rc = tensor_map_3d(a->x, a->k, a->x_group_rows, xg ? a->n_groups : 1, xrs, xgs, 16, &mx);
   if (rc) return rc;
+  if (p.k_splits > 1 && a->n_groups == 1 && a->n_tokens <= 256 && !a->route_y_row) {
+    // decode-sized dense split: one (row tile, split) per CTA, weights requested before the
+    // programmatic-launch wait
+    CUtensorMap mxs, mys;
+    rc = tensor_map_3d(a->x, a->k, a->x_group_rows, 1, xrs, xgs, static_cast<uint32_t>(round_up(a->n_tokens, 16)),
+                       &mxs);
+    if (rc) return rc;
+    // partial tiles leave through TMA stores of 128 rows x 32 tokens
+    rc = tensor_map_f32_store(a->y, static_cast<uint64_t>(a->n_rows), static_cast<uint64_t>(a->n_tokens),
+                              static_cast<uint64_t>(p.k_splits), static_cast<uint64_t>(a->y_row_stride) * 4,
+                              static_cast<uint64_t>(a->y_split_stride) * 4, kSkStoreTokens, &mys);
+    if (rc) return rc;
+    return check_launch(launch_linear_splitk(p, mw, mxs, mys, st), "linear(batch, split K)");
+  }
   TcShape shp;
   int mt_count = 0, nt_count = 0;
   const long long items = tc_launch_shape(p, sms, &shp, &mt_count, &nt_count);

@@ -3,6 +3,7 @@
 #include "norm.cu"
 #include "linear_gemv.cu"
 #include "linear_tc.cu"
+#include "linear_splitk.cu"
 #include "moe_tc.cu"
 #include "router.cu"
 #include "mla.cu"

@@ -8,7 +8,7 @@
 //
 // Phase 1 item (group g, 128-row tile of the intermediate dimension, token tile):
 //   h[route, i] = bf16( silu(bf16(W_gate[g] x)) * bf16(W_up[g] x) )
-// Phase 2 item (group g, 128-row tile of the hidden dimension, token tile):
+// Phase 2 item (group g, 256-row tile of the hidden dimension, token tile):
 //   y[route_slot[route], n] = bf16(W_down[g] h[route]) * route_weight[route]
 // A group is a routed expert or one half of the shared MLP (see the router's bucketing).
 // All phase-1 items followed by all phase-2 items form one list, groups in order of token
@@ -22,9 +22,11 @@
 // (one per SM, grid <= SM count), so every wait is for work that is running.  The
 // last CTA to finish returns the counters to zero for the next launch.
 //
-// Data path per item: TMA (128-byte swizzle) stages of W (gate + up rows, or down
-// rows) and activations (expert-ordered x, or h) through a shared-memory ring;
-// tcgen05.mma with the weights as A (M = 128) and the tokens as B (N = token tile);
+// Data path per item: TMA (128-byte swizzle) stages of W (128 gate rows and the matching
+// 128 up rows, or the two 128-row halves of 256 down rows, so a token tile is read once per
+// 256 weight rows) and activations (expert-ordered x, or h) through a shared-memory ring;
+// tcgen05.mma with the weights as A (M = 128, two MMAs per K step) and the tokens as B
+// (N = token tile);
 // fp32 accumulators in TMEM, double-buffered; epilogue warps read them with
 // tcgen05.ld.  Warp roles as in linear_tc.cu.
 #include "linear.cuh"
@@ -58,6 +60,7 @@ struct MoeShape {
   int tmem_cols;
   int x_box;
   int nt_count;      // token tiles per group (host bound)
+  int down_rows;     // down-projection rows per item: 256 (token tiles of 128) or 128
 };
 
 __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
@@ -135,7 +138,10 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
   const int n_tile = shp.n_tile;
   const int G = p.n_groups;
   const int mt1 = (p.inter + kTcM - 1) / kTcM;    // phase-1 row tiles (intermediate)
-  const int mt2 = (p.hidden + kTcM - 1) / kTcM;   // phase-2 row tiles (hidden)
+  // phase-2 row tiles: 256 hidden rows (two 128-row halves sharing one h tile) when the token
+  // tiles are large, so h is re-read half as often; 128 rows for small token tiles (finer items)
+  const bool wide = shp.down_rows == 2 * kTcM;
+  const int mt2 = (p.hidden + shp.down_rows - 1) / shp.down_rows;
   const int nkb1 = p.hidden / kTcK, nkb2 = p.inter / kTcK;
   for (int g = threadIdx.x; g < G; g += kMoeThreads) {
     const int r0 = p.group_offsets[g];
@@ -269,20 +275,27 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
             tma_load_3d(smem_u32(sb + (nbig * shp.x_box + bx * kTcBoxRows) * 128), mx, bar, kb * kTcK,
                         xrow0 + nbig * shp.x_box + bx * kTcBoxRows, 0);
         };
-        // phase 1: one K block per slot (gate + up tiles); phase 2: up to two K blocks per
-        // slot when their token tiles fit, so the down GEMM keeps as many weight bytes in
-        // flight as the gate/up GEMM
-        const int per_slot = (ph == 2 && 2 * npad <= n_tile) ? 2 : 1;
+        // two 128-row weight tiles per slot: phase 1 gate rows and the matching up rows of one
+        // K block; phase 2 (wide) the two halves of 256 down rows of one K block, or (narrow)
+        // two K blocks of 128 down rows when their token tiles fit, so the down GEMM keeps as
+        // many weight bytes in flight as the gate/up GEMM
+        const int per_slot = (ph == 2 && !wide && 2 * npad <= n_tile) ? 2 : 1;
         const int nkb = ph == 1 ? nkb1 : nkb2;
         for (int kb = 0; kb < nkb; kb += per_slot) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { *abort_flag = 1; break; }
           unsigned char* st = smem + stage * shp.stage_bytes;
           unsigned char* sb = st + 2 * kTcABytes;
-          if (ph == 1) {
+          if (ph == 1 || wide) {
             mbar_arrive_expect_tx(&full_bar[stage], 2 * kTcABytes + npad * 128);
-            tma_load_3d(smem_u32(st), &tm_w1, &full_bar[stage], kb * kTcK, mt * kTcM, g);
-            tma_load_3d(smem_u32(st + kTcABytes), &tm_w1, &full_bar[stage], kb * kTcK,
-                        mt * kTcM + p.inter, g);  // the matching up rows
+            if (ph == 1) {
+              tma_load_3d(smem_u32(st), &tm_w1, &full_bar[stage], kb * kTcK, mt * kTcM, g);
+              tma_load_3d(smem_u32(st + kTcABytes), &tm_w1, &full_bar[stage], kb * kTcK,
+                          mt * kTcM + p.inter, g);  // the matching up rows
+            } else {
+              tma_load_3d(smem_u32(st), &tm_w2, &full_bar[stage], kb * kTcK, mt * 2 * kTcM, g);
+              tma_load_3d(smem_u32(st + kTcABytes), &tm_w2, &full_bar[stage], kb * kTcK,
+                          mt * 2 * kTcM + kTcM, g);
+            }
             load_x(sb, kb, &full_bar[stage]);
           } else {
             const int nb = min(per_slot, nkb - kb);
@@ -319,22 +332,22 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
         tc_fence_after();
         const uint32_t dacc = tmem_base + buf * shp.acc_cols;
         const int nkb = ph == 1 ? nkb1 : nkb2;
-        const int per_slot = (ph == 2 && 2 * npad <= n_tile) ? 2 : 1;
+        const int per_slot = (ph == 2 && !wide && 2 * npad <= n_tile) ? 2 : 1;
         bool ok = true;
         for (int kb = 0; kb < nkb; kb += per_slot) {
           if (!mbar_wait(&full_bar[stage], phase)) { ok = false; break; }
           tc_fence_after();
           unsigned char* st = smem + stage * shp.stage_bytes;
           unsigned char* sb = st + 2 * kTcABytes;
-          if (ph == 1) {
+          if (ph == 1 || wide) {
             const uint64_t da = sw128_kmajor_desc(smem_u32(st));
             const uint64_t du = sw128_kmajor_desc(smem_u32(st + kTcABytes));
             const uint64_t db = sw128_kmajor_desc(smem_u32(sb));
 #pragma unroll
             for (int k = 0; k < kTcK / 16; ++k) {
               const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
-              tc_mma_bf16(dacc, da + 2 * k, db + 2 * k, idesc, acc);
-              tc_mma_bf16(dacc + npad, du + 2 * k, db + 2 * k, idesc, acc);
+              tc_mma_bf16(dacc, da + 2 * k, db + 2 * k, idesc, acc);          // gate / down rows 0-127
+              tc_mma_bf16(dacc + npad, du + 2 * k, db + 2 * k, idesc, acc);   // up / down rows 128-255
             }
           } else {
             const int nb = min(per_slot, nkb - kb);
@@ -407,10 +420,13 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
           red_release_gpu_add(&p.sync[g], 1);
         }
       } else {
-        const bool row_ok = n < p.hidden;
+        // row nd (accumulator columns [0, npad)) and, wide, row nd + 128 ([npad, 2 npad))
+        const int nd = mt * shp.down_rows + row_in_tile;
+        const bool row_ok0 = nd < p.hidden, row_ok1 = wide && nd + kTcM < p.hidden;
         for (int c0 = 0; c0 < npad; c0 += 16) {
-          float acc[16];
+          float acc[16], acc1[16];
           tmem_ld16(tbase + c0, acc);
+          if (wide) tmem_ld16(tbase + npad + c0, acc1);
           int my_row = 0;
           float my_scale = 1.f;
           {
@@ -429,7 +445,7 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
           for (int j = 0; j < 16; ++j) {
             const int yrow = __shfl_sync(0xffffffffu, my_row, j);
             const float sc = __shfl_sync(0xffffffffu, my_scale, j);
-            if (row_ok && c0 + j < ntok) {
+            if (c0 + j < ntok) {
               float* dst;
               if (p.peers.world > 0) {  // slot of a row owned by rank yrow / slots_per_rank
                 const int spr = 8 * p.peers.rows_per_rank;
@@ -439,7 +455,8 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
               } else {
                 dst = p.y + static_cast<long long>(yrow) * p.hidden;
               }
-              dst[n] = bf16_round(acc[j]) * sc;
+              if (row_ok0) dst[nd] = bf16_round(acc[j]) * sc;
+              if (row_ok1) dst[nd + kTcM] = bf16_round(acc1[j]) * sc;
             }
           }
         }
@@ -487,6 +504,7 @@ MoeShape moe_shape(int max_routes_per_group, int tile_tokens) {
   s.tmem_cols = c;
   s.x_box = min(64, s.n_tile);
   s.nt_count = max(1, (max_routes_per_group + s.n_tile - 1) / s.n_tile);
+  s.down_rows = s.n_tile >= 128 ? 2 * kTcM : kTcM;
   return s;
 }
 

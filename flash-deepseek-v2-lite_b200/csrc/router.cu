@@ -418,45 +418,6 @@ constexpr int kRcKParts = 16;                        // warps per CTA, one K par
 constexpr int kRcThreads = 32 * kRcKParts;
 constexpr int kRcKb = kRtMaxHidden / 32 / kRcKParts;  // 32-wide K blocks per warp (4)
 
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t cluster_id_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t n_clusters_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void cluster_arrive_relaxed() {
-  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_arrive_release() {
-  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait_acquire() {
-  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t cluster_addr(const void* local, uint32_t rank) {
-  const uint32_t la = static_cast<uint32_t>(__cvta_generic_to_shared(local));
-  uint32_t ra;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(rank));
-  return ra;
-}
-// store v at the address of `local` in the shared memory of cluster CTA `rank`
-__device__ __forceinline__ void st_cluster_f32(const float* local, uint32_t rank, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr(local, rank)), "f"(v) : "memory");
-}
-__device__ __forceinline__ void st_cluster_v4(const void* local, uint32_t rank, uint4 v) {
-  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr(local, rank)),
-               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-               : "memory");
-}
 __device__ __forceinline__ int ld_acquire_gpu_s32(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

@@ -45,12 +45,17 @@ def choose_split_len(batch: int, max_len: int, num_sms: int, family: int = ops.F
     return int(min(max(s, unit), 4096))
 
 
-def split_count(n_rows: int, k: int, num_sms: int) -> int:
-    """K splits for a dense batch-family linear: about one 128-row tile per two SMs (the
-    token dimension splits too), at least two 64-wide K blocks per split.  Fewer splits
-    also mean fewer fp32 partials for the consumer to read (measured on B200 at B=256:
-    qkva 3 splits 13.4 us vs 5 splits 13.2 us, o_proj 5 splits 11.7 us vs 9 splits 12.1 us)."""
+def split_count(n_rows: int, k: int, num_sms: int, n_tokens: int = 256) -> int:
+    """K splits for a dense batch-family linear with fp32 partial outputs.  Decode batches
+    (<= 256 tokens: one (row tile, split) item per CTA, weights requested before the
+    programmatic-launch wait): as many splits as fill the SMs, so each CTA's weight slice
+    and activation traffic are small.  Larger token batches (kernel prefill, persistent
+    kernel over several token tiles): about one 128-row tile per two SMs, which also keeps
+    the partials the consumer sums few.  At least one 64-wide K block per split, at most 16."""
     m_tiles = (n_rows + 127) // 128
+    if n_tokens <= 256:
+        s = max(1, num_sms // m_tiles)
+        return int(min(s, k // 64, 16))
     s = max(1, round(num_sms / (2 * m_tiles)))
     return int(min(s, max(1, (k // 64) // 2), 16))
 
@@ -143,12 +148,12 @@ class DecodeEngine:
         # batch family: split-K fp32 partials for the dense linears whose consumers sum them
         self.split_k = self.family == ops.FAMILY_BATCH
         if self.split_k:
-            s_q = split_count(QKVA_ROWS, HIDDEN, self.num_sms)
-            s_o = split_count(HIDDEN, N_HEADS * V_DIM, self.num_sms)
+            s_q = split_count(QKVA_ROWS, HIDDEN, self.num_sms, B)
+            s_o = split_count(HIDDEN, N_HEADS * V_DIM, self.num_sms, B)
             self.qkva_part = torch.zeros((s_q, B, QKVA_ROWS), device=dev, dtype=f32)
             self.o_proj_part = torch.zeros((s_o, B, HIDDEN), device=dev, dtype=f32)
             dense_k = max([lp.dense.inter for lp in self.layers if lp.dense is not None], default=0)
-            s_d = split_count(HIDDEN, dense_k, self.num_sms) if dense_k else 1
+            s_d = split_count(HIDDEN, dense_k, self.num_sms, B) if dense_k else 1
             self.dense_part = torch.zeros((s_d, B, HIDDEN), device=dev, dtype=f32)
         self.q_abs = torch.zeros((B, N_HEADS, KV_LORA), device=dev, dtype=bf)
         self.o_lat = torch.zeros((B, N_HEADS, KV_LORA), device=dev, dtype=bf)

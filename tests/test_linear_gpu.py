@@ -68,6 +68,35 @@ def test_dense_fp32_out(D, family):
     assert relerr(y, O.linear(w, x, "f32")) < 1e-4
 
 
+@pytest.mark.parametrize("N,K,T,S", [(3648, 2048, 256, 5), (2048, 2048, 256, 9), (2048, 2048, 1, 9),
+                                     (3648, 2048, 32, 5), (2048, 10944, 77, 9), (300, 512, 100, 3),
+                                     (136, 2048, 255, 2), (2048, 2048, 5, 16), (3648, 2048, 300, 3)])
+def test_dense_split_k(D, N, K, T, S):
+    """fp32 partials of a K split (the batch decode step's attention projections and dense
+    down projection): split s of the K blocks at y[s]; their sum matches the oracle's fp32
+    linear, each split matches the oracle over its own K range, and a second call gives the
+    same bits.  Up to 256 tokens one CTA takes one (row tile, split) item with its weight
+    slice resident (K = 10944: more K blocks than weight slots, streamed); 300 tokens take
+    the persistent kernel."""
+    g = torch.Generator().manual_seed(N + K + T + S)
+    w, x = rnd((N, K), g, 0.02).to(DEV), rnd((T, K), g).to(DEV)
+    y = torch.full((S, T, N), float("nan"), device=DEV)
+    D.linear(w=w, n_rows=N, k=K, x=x, y=y[0], family=D.FAMILY_BATCH, epilogue=D.EPI_STORE_F32, n_tokens=T,
+             x_group_rows=T, k_splits=S, y_split_stride=y.stride(0))
+    torch.cuda.synchronize()
+    assert not torch.isnan(y).any()
+    assert relerr(y.sum(0), O.linear(w.cpu(), x.cpu(), "f32")) < 1e-4
+    nkb = K // 64
+    for sp in (0, S - 1):
+        k0, k1 = sp * nkb // S * 64, (sp + 1) * nkb // S * 64
+        ref = O.linear(w[:, k0:k1].cpu(), x[:, k0:k1].cpu(), "f32")
+        assert relerr(y[sp], ref) < 1e-4
+    y2 = torch.zeros_like(y)
+    D.linear(w=w, n_rows=N, k=K, x=x, y=y2[0], family=D.FAMILY_BATCH, epilogue=D.EPI_STORE_F32, n_tokens=T,
+             x_group_rows=T, k_splits=S, y_split_stride=y.stride(0))
+    assert torch.equal(y, y2)
+
+
 @pytest.mark.parametrize("family", FAMILIES)
 @pytest.mark.parametrize("B", [1, 7, 64])
 def test_heads_absorb_and_unabsorb(D, family, B):
