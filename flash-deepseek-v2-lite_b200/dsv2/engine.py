@@ -48,14 +48,16 @@ def choose_split_len(batch: int, max_len: int, num_sms: int, family: int = ops.F
 def split_count(n_rows: int, k: int, num_sms: int, n_tokens: int = 256) -> int:
     """K splits for a dense batch-family linear with fp32 partial outputs.  Decode batches
     (<= 256 tokens: one (row tile, split) item per CTA, weights requested before the
-    programmatic-launch wait): as many splits as fill the SMs, so each CTA's weight slice
-    and activation traffic are small.  Larger token batches (kernel prefill, persistent
+    programmatic-launch wait): as many splits as fill the SMs (up to 5), so each CTA's
+    weight slice and activation traffic are small.  Larger token batches (kernel prefill, persistent
     kernel over several token tiles): about one 128-row tile per two SMs, which also keeps
     the partials the consumer sums few.  At least one 64-wide K block per split, at most 16."""
     m_tiles = (n_rows + 127) // 128
     if n_tokens <= 256:
+        # at most 5: the consumers (mla_prep, the fused add + RMSNorm) read every partial
+        # (measured on B200, config 4: o_proj 5 splits 8.11 ms/step vs 9 splits 8.14-8.16)
         s = max(1, num_sms // m_tiles)
-        return int(min(s, k // 64, 16))
+        return int(min(s, k // 64, 5))
     s = max(1, round(num_sms / (2 * m_tiles)))
     return int(min(s, max(1, (k // 64) // 2), 16))
 
