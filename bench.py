@@ -57,8 +57,8 @@ EXPERT_BYTES = 2 * 8_650_752
 KV_ROW_BYTES = 576 * 2
 # DRAM traffic / algorithmic bytes of the fused MoE launch, from one ncu capture of the
 # current kernel at B=256 (all 64 experts hit; profiles/moe_tc_b256.md):
-# (1159.34 + 23.19) MB / 1141.90 MB
-MOE_TRAFFIC_RATIO = 1.0356
+# (1159.24 + 21.20) MB / 1141.90 MB
+MOE_TRAFFIC_RATIO = 1.0337
 MOE_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one fused MoE launch "
                       "(dsv2.microbench moe, B=256, all 64 experts hit; profiles/moe_tc_b256.md), "
                       "scaled to this launch by its algorithmic bytes")

@@ -16,8 +16,9 @@ Cases (shapes of the B=256 decode step):
              SwiGLU, grouped down, top-6 reduce; 64 routed experts) vs moe_tc_kernel over the
              same 64 routed experts (bucketing + expert-ordered copy + the fused launch);
   qkva, o    reference _batched_linear_kernel (attention_decode_batch.py:420-468, bf16 out,
-             its own tile choice for B >= 128) vs linear_tc_kernel as the decode step runs it
-             (fp32 split-K partials) and with a bf16 output;
+             its own tile choice for B >= 128) vs linear_splitk_kernel as the decode step runs
+             it (fp32 split-K partials, weights requested before the launch wait) and
+             linear_tc_kernel with a bf16 output;
   attention  reference batched_attention_decode_q1_triton (attention_decode_batch.py:240-400)
              over the expanded K [B,16,S,192] / V [B,16,S,128] cache at one shared length
              (its only mode) vs mla_decode_kernel over the 576-wide latent cache, same
