@@ -54,26 +54,29 @@ __device__ void softmax_topk_warp(const float* lg, int n_experts, float scaling,
   float e0 = lane < n_experts ? expf(v0 - m) : 0.f;
   float e1 = lane + 32 < n_experts ? expf(v1 - m) : 0.f;
   const float s = warp_sum(e0 + e1);
-  float p0 = lane < n_experts ? e0 / s : -INFINITY;
-  float p1 = lane + 32 < n_experts ? e1 / s : -INFINITY;
-  for (int k = 0; k < kTopK; ++k) {
-    // best value, lowest index on ties
-    float bv;
-    int bi;
-    if (p1 > p0) { bv = p1; bi = lane + 32; } else { bv = p0; bi = lane; }
+  const float p0 = lane < n_experts ? e0 / s : -INFINITY;
+  const float p1 = lane + 32 < n_experts ? e1 / s : -INFINITY;
+  // top-6 by rank: expert e's rank is the number of experts with a larger probability, or
+  // an equal one and a lower index (the greedy order: largest first, lowest index on ties);
+  // every lane ranks its two experts against all 64 at once instead of six serial arg-max
+  // rounds
+  int r0 = 0, r1 = 0;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-    }
-    if (lane == 0) {
-      if (ids64) ids64[row * kTopK + k] = bi;
-      ids32[row * kTopK + k] = bi;
-      tw[row * kTopK + k] = bv * scaling;
-    }
-    if (bi == lane) p0 = -INFINITY;
-    if (bi == lane + 32) p1 = -INFINITY;
+  for (int j = 0; j < 32; ++j) {
+    const float a = __shfl_sync(0xffffffffu, p0, j);   // expert j
+    const float b = __shfl_sync(0xffffffffu, p1, j);   // expert j + 32
+    r0 += (a > p0 || (a == p0 && j < lane)) + (b > p0);
+    r1 += (a >= p1) + (b > p1 || (b == p1 && j < lane));
+  }
+  if (r0 < kTopK) {
+    if (ids64) ids64[row * kTopK + r0] = lane;
+    ids32[row * kTopK + r0] = lane;
+    tw[row * kTopK + r0] = p0 * scaling;
+  }
+  if (r1 < kTopK) {
+    if (ids64) ids64[row * kTopK + r1] = lane + 32;
+    ids32[row * kTopK + r1] = lane + 32;
+    tw[row * kTopK + r1] = p1 * scaling;
   }
 }
 
