@@ -411,7 +411,8 @@ __global__ __launch_bounds__(kRouteThreads) void route_kernel(const RouteParams 
 //
 // With bucketing (p.group_offsets) the CTAs then meet at a grid-wide barrier (arrival
 // count + generation in p.grid_sync, bounded wait; the grid never exceeds the clusters
-// that fit on the GPU at once, so every CTA is resident) and each CTA buckets a slice of
+// that fit on the GPU at once, so every CTA is resident; a grid of one cluster uses the
+// cluster barrier instead) and each CTA buckets a slice of
 // the tokens and copies their activation rows into expert order (route_cta).  The
 // kernel triggers its dependents only after that barrier, so the next launch cannot take
 // the SMs that CTAs still waiting to start would need.
@@ -622,7 +623,15 @@ __global__ __cluster_dims__(kRcCtas, 1, 1) __launch_bounds__(kRcThreads) void ro
   }
   cluster_wait_acquire();      // no CTA leaves while another may still store into it
   if (!bucket) return;
-  const bool ok = grid_barrier(p.grid_sync);
+  // a grid of one cluster (up to 8 tokens) meets at a cluster barrier instead of the
+  // global-memory one
+  bool ok = true;
+  if (gridDim.x == kRcCtas) {
+    cluster_arrive_release();
+    cluster_wait_acquire();
+  } else {
+    ok = grid_barrier(p.grid_sync);
+  }
   pdl_launch_dependents();
   if (!ok) return;
   RouteParams q = {};
