@@ -171,16 +171,28 @@ __global__ __launch_bounds__(kMoeThreads, 1) void moe_tc_kernel(
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int a1 = 0, a2 = 0;
-    for (int i = 0; i < G; ++i) {
-      s_first1[i] = a1;
-      s_first2[i] = a2;
-      a1 += s_nts[s_order[i]] * mt1;
-      a2 += s_nts[s_order[i]] * mt2;
+  if (warp == 0) {
+    // item prefix over the list (exclusive scan of token tiles per position, warp-wide)
+    int run = 0;
+    for (int base = 0; base < G; base += 32) {
+      const int i = base + lane;
+      const int v = i < G ? s_nts[s_order[i]] : 0;
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += u;
+      }
+      if (i < G) {
+        s_first1[i] = (run + incl - v) * mt1;
+        s_first2[i] = (run + incl - v) * mt2;
+      }
+      run += __shfl_sync(0xffffffffu, incl, 31);
     }
-    s_first1[G] = a1;
-    s_first2[G] = a2;
+    if (lane == 0) {
+      s_first1[G] = run * mt1;
+      s_first2[G] = run * mt2;
+    }
   }
   __syncthreads();
   const int total1 = s_first1[G];
