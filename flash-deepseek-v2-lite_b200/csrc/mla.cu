@@ -39,6 +39,7 @@ constexpr int kRowBytes = kRow * 2;             // 1152
 constexpr int kChunks = kRow / 64;              // 9 swizzle chunks of 64 dims
 constexpr int kTile = 32;                       // positions per tile
 constexpr int kStages = 5;                      // cache tiles in flight per CTA (one CTA per SM)
+constexpr int kSegUnits = 2;                    // per-row cost in tile units (work balance)
 constexpr int kTileBytes = kTile * kRowBytes;   // 36864
 constexpr int kQBytes = kHeads * kRowBytes;     // 18432
 constexpr int kPStride = kTile + 8;             // bf16 row stride of P
@@ -206,6 +207,10 @@ __device__ __forceinline__ int mla_row_len(const MlaDecodeParams& p, int b) {
   return static_cast<int>(max(0LL, min(static_cast<long long>(p.max_len), pos + 1)));
 }
 __device__ __forceinline__ int mla_tiles_of(int len) { return len > 0 ? (len + kTile - 1) / kTile : 1; }
+// Units of row b in the work stream that is cut between the CTAs: its tiles plus kSegUnits
+// units of fixed per-row cost (query block, softmax finish, output store), which come
+// before the row's first tile, so that a CTA's share of rows counts in its share of work.
+__device__ __forceinline__ int mla_units_of(int len) { return mla_tiles_of(len) + kSegUnits; }
 
 // Bounded mbarrier wait that gives up at once when this CTA (or any kernel) has already
 // recorded a failure, so that one lost wait cannot turn into a long chain of timeouts.
@@ -231,9 +236,10 @@ __device__ __forceinline__ long long mla_owner(long long t, long long T, long lo
   return ((t + 1) * n - 1) / T;
 }
 
-// The whole decode in one launch: the 32-position tiles of all rows form one stream of
-// T = sum_b ceil(len_b / 32) tiles, cut into equal contiguous ranges, one per CTA (one
-// CTA per SM, so ragged batches keep every SM busy to the end).  Each CTA walks its
+// The whole decode in one launch: the rows form one stream of T = sum_b (ceil(len_b / 32)
+// + kSegUnits) units (each row's per-row cost, then its 32-position tiles), cut into equal
+// contiguous ranges, one per CTA (one CTA per SM, so ragged batches keep every SM busy to
+// the end, and a CTA that takes more rows takes fewer tiles).  Each CTA walks its
 // range row by row ("segments"): a row that lies wholly inside the range is normalised
 // and written to o_lat; a row cut by a range boundary leaves (o, m, l) partials in the
 // CTA's slot 0 (first segment) or 1 (last segment), and the last of the row's CTAs to
@@ -310,15 +316,15 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
     fence_mbar_init();
   }
 
-  // --- tile prefix over the rows (every CTA computes the same one): T = all tiles, then
-  // this CTA's range [start, end) and its first row b0 (S_b0 <= start < S_b0 + nt_b0).
+  // --- unit prefix over the rows (every CTA computes the same one): T = all units, then
+  // this CTA's range [start, end) and its first row b0 (S_b0 <= start < S_b0 + units_b0).
   // One pass when the batch fits the block (the usual case), else two.
   long long T = 0, start = 0, end = 0, c = blockIdx.x, n_cta = 0;
   const long long min_tpc = max(1, p.split_len / kTile);
   int nt_mine = 0, incl = 0;
   for (int base = 0; base < B; base += kMlaThreads) {
     const int b = base + tid;
-    const int nt = b < B ? mla_tiles_of(mla_row_len(p, b)) : 0;
+    const int nt = b < B ? mla_units_of(mla_row_len(p, b)) : 0;
     int v = nt;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -357,7 +363,7 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
     long long run = 0;
     for (int base = 0; base < B; base += kMlaThreads) {
       const int b = base + tid;
-      const int nt = b < B ? mla_tiles_of(mla_row_len(p, b)) : 0;
+      const int nt = b < B ? mla_units_of(mla_row_len(p, b)) : 0;
       int v = nt;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -405,9 +411,10 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
         tma_load_3d(smem_u32(dq + (kLatent / 64) * (kHeads * 128)), &tm_qp, &q_full[qb], 0, 0, row);
       };
       long long S = S0;
-      for (int b = b0; S < end && b < B; ++b, ++seg) {
+      for (int b = b0; S + kSegUnits < end && b < B; ++b, ++seg) {
         const int len = mla_row_len(p, b), nt = mla_tiles_of(len);
-        const int j0 = static_cast<int>(max(0LL, start - S)), j1 = static_cast<int>(min(static_cast<long long>(nt), end - S));
+        const long long St = S + kSegUnits;   // stream position of the row's first tile
+        const int j0 = static_cast<int>(max(0LL, start - St)), j1 = static_cast<int>(min(static_cast<long long>(nt), end - St));
         // cache row read by query row b (prefill: many query rows share one sequence)
         int crow_b = p.cache_rows ? p.cache_rows[b] : b;
         if (crow_b < 0 || crow_b >= p.cache_batch) {
@@ -431,7 +438,7 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
             tma_load_3d(smem_u32(s_kv + st * kTileBytes + ch * (kTile * 128)), &tm_kv, &full_bar[st], ch * 64,
                         j * kTile, crow_b);
         }
-        S += nt;
+        S += nt + kSegUnits;
       }
       if (!waited) pdl_enter();
       for (; q_issued < seg; ++q_issued) issue_q(q_issued, early_rows[q_issued]);
@@ -458,12 +465,13 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
     if (lane == 0) {
       int n_pend = 0;
       long long S = S0;
-      for (int b = b0; S < end && b < B; ++b) {
+      for (int b = b0; S + kSegUnits < end && b < B; ++b) {
         const int nt = mla_tiles_of(mla_row_len(p, b));
-        if (!((S >= start) && (S + nt <= end))) {
+        const long long St = S + kSegUnits;
+        if (!((St >= start) && (St + nt <= end))) {
           const int slot = mla_slot(S, start);
           if (mla_wait(&tk_full[slot], 0, s_abort)) {
-            const int n_seg = static_cast<int>(mla_owner(S + nt - 1, T, n_cta) - mla_owner(S, T, n_cta) + 1);
+            const int n_seg = static_cast<int>(mla_owner(St + nt - 1, T, n_cta) - mla_owner(St, T, n_cta) + 1);
             __threadfence();   // the partial (written by other warps, ordered by the mbarrier) first
             const int t = atomicAdd(&p.row_sync[b], 1);
             if (t == n_seg - 1) {
@@ -476,7 +484,7 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
             }
           }
         }
-        S += nt;
+        S += nt + kSegUnits;
       }
       s_misc[15] = n_pend;
       mbar_arrive(tk_done);
@@ -495,10 +503,11 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
   if (warp < 2 * kScoreWarps) {
     // ============ score warps
     const int half = warp / kScoreWarps, sw = warp % kScoreWarps;
-    for (int b = b0; S < end && b < B; ++b, ++seg) {
+    for (int b = b0; S + kSegUnits < end && b < B; ++b, ++seg) {
       const int len = mla_row_len(p, b), nt = mla_tiles_of(len);
-      const int j0 = static_cast<int>(max(0LL, start - S)), j1 = static_cast<int>(min(static_cast<long long>(nt), end - S));
-      const bool complete = (S >= start) && (S + nt <= end);
+      const long long St = S + kSegUnits;
+      const int j0 = static_cast<int>(max(0LL, start - St)), j1 = static_cast<int>(min(static_cast<long long>(nt), end - St));
+      const bool complete = (St >= start) && (St + nt <= end);
       // this half's 16 x 288 query slice as 18 A fragments (k-steps of 16 dims)
       const int qb = seg & 1;
       mla_wait(&q_full[qb], static_cast<uint32_t>((seg >> 1) & 1), s_abort);
@@ -631,15 +640,16 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
         }
         // s_lsum is rewritten at the next segment end, after that segment's tile barriers
       }
-      S += nt;
+      S += nt + kSegUnits;
     }
   } else {
     // ============ P @ V warps
     const int pv = warp - 2 * kScoreWarps;   // latent dims [128 pv, 128 pv + 128)
-    for (int b = b0; S < end && b < B; ++b, ++seg) {
+    for (int b = b0; S + kSegUnits < end && b < B; ++b, ++seg) {
       const int len = mla_row_len(p, b), nt = mla_tiles_of(len);
-      const int j0 = static_cast<int>(max(0LL, start - S)), j1 = static_cast<int>(min(static_cast<long long>(nt), end - S));
-      const bool complete = (S >= start) && (S + nt <= end);
+      const long long St = S + kSegUnits;
+      const int j0 = static_cast<int>(max(0LL, start - St)), j1 = static_cast<int>(min(static_cast<long long>(nt), end - St));
+      const bool complete = (St >= start) && (St + nt <= end);
       float o_acc[16][4];
 #pragma unroll
       for (int i = 0; i < 16; ++i) o_acc[i][0] = o_acc[i][1] = o_acc[i][2] = o_acc[i][3] = 0.f;
@@ -704,7 +714,7 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
         mbar_arrive(&fin_empty[fb]);
         if (!complete) mbar_arrive(&tk_full[mla_slot(S, start)]);
       }
-      S += nt;
+      S += nt + kSegUnits;
     }
   }
 
@@ -714,7 +724,7 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
   for (int pi = 0; pi < n_pend; ++pi) {
     const int b = s_misc[13 + pi], nt = s_misc[5 + pi];
     const long long Sb = s_ll[2 + pi];
-    const long long c_first = mla_owner(Sb, T, n_cta), c_last = mla_owner(Sb + nt - 1, T, n_cta);
+    const long long c_first = mla_owner(Sb + kSegUnits, T, n_cta), c_last = mla_owner(Sb + kSegUnits + nt - 1, T, n_cta);
     const int n_seg = static_cast<int>(c_last - c_first + 1);
     float* s_m = s_mrg;
     float* s_l = s_mrg + kHeads * n_seg;
