@@ -525,7 +525,11 @@ int dsv2_lm_head_argmax(const void* w, int vocab, int hidden, const void* x, int
 }
 
 static int linear_impl(const dsv2_linear_args* a, int family, void* stream, bool argmax) {
-  if (!a || !a->w || !a->x || !a->y) return fail(DSV2_ERR_INVALID, "linear: null pointer");
+  if (!a || !a->w || (!a->x && !a->x_parts) || !a->y) return fail(DSV2_ERR_INVALID, "linear: null pointer");
+  if (a->x_parts && (family != DSV2_FAMILY_SMALL || a->n_tokens != 1 || a->group_offsets || argmax ||
+                     !a->x_parts_ml || !a->x_parts_count))
+    return fail(DSV2_ERR_UNSUPPORTED,
+                "linear: x_parts needs the small family, one token, dense mode, x_parts_ml and x_parts_count");
   if (a->n_rows <= 0 || a->k <= 0 || a->n_groups <= 0)
     return fail(DSV2_ERR_INVALID, "linear: n_rows=%d k=%d n_groups=%d", a->n_rows, a->k, a->n_groups);
   if (a->epilogue < DSV2_EPI_STORE_BF16 || a->epilogue > (argmax ? DSV2_EPI_ARGMAX : DSV2_EPI_SCALE_F32))
@@ -564,6 +568,9 @@ static int linear_impl(const dsv2_linear_args* a, int family, void* stream, bool
   p.y_split_stride = a->y_split_stride;
   p.offsets_prior = a->offsets_prior != 0;
   p.active_groups = (a->group_offsets && a->max_routes > 0) ? std::min(a->n_groups, a->max_routes) : a->n_groups;
+  p.x_parts = a->x_parts;
+  p.x_parts_ml = a->x_parts_ml;
+  p.x_parts_count = a->x_parts_count;
   if (p.k_splits > 1) {
     if (family != DSV2_FAMILY_BATCH || a->group_offsets || a->epilogue != DSV2_EPI_STORE_F32)
       return fail(DSV2_ERR_UNSUPPORTED, "linear: a K split needs the batch family, dense mode and fp32 output");
@@ -889,6 +896,11 @@ int dsv2_mla_decode(const dsv2_mla_decode_args* a, void* stream) {
   p.batch = a->batch;
   p.cache_rows = a->cache_rows;
   p.cache_batch = a->cache_batch > 0 ? a->cache_batch : a->batch;
+  if (a->part_count) {
+    if (tc || a->batch != 1 || a->cache_rows)
+      return fail(DSV2_ERR_UNSUPPORTED, "mla_decode: part_count (unmerged partials) needs the small family and batch 1");
+    p.part_count = a->part_count;
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   CUtensorMap tm_kv;
   if (tc) {

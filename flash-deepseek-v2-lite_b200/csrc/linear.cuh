@@ -49,6 +49,13 @@ struct LinearParams {
   long long y_split_stride;     // elements between the fp32 partial outputs of the splits
   int offsets_prior;            // group_offsets were written at least two launches earlier
   int active_groups;            // grouped small family: launch work for this many non-empty groups
+  // small family, one token, dense: the token's activation row of group g is the merge of a
+  // one-row latent attention's unmerged partials instead of x: partial c holds o at
+  // x_parts + (2c * n_groups + g) * k and (m, l) at x_parts_ml + (2c * n_groups + g) * 2,
+  // for c in [x_parts_count[0], x_parts_count[0] + x_parts_count[1])
+  const float* x_parts;
+  const float* x_parts_ml;
+  const int* x_parts_count;
 };
 
 __device__ __forceinline__ float silu_ref(float g) { return g / (1.f + expf(-g)); }

@@ -26,6 +26,34 @@ namespace dsv2 {
 constexpr int kGemvWarps = 8;
 constexpr int kGemvRows = 16;
 constexpr int kGemvTok = 8;
+constexpr int kGemvMaxParts = 160;   // merged partials (one per attention CTA)
+
+// Merge weights of the unmerged attention partials of head g (warp-wide, into wt[0, n)):
+// a_c = 2^(m_c - M) / sum_c 2^(m_c - M) l_c over the partials with l_c > 0, the latent
+// attention's own merge rule.  ml[i] / ll[i]: (m, l) of partial lane + 32 i, loaded by the
+// caller.
+constexpr int kGemvMlPerLane = (kGemvMaxParts + 31) / 32;
+__device__ __forceinline__ void gemv_part_weights(int n, const float (&ml)[kGemvMlPerLane],
+                                                  const float (&ll)[kGemvMlPerLane], float* wt, int lane) {
+  float M = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kGemvMlPerLane; ++i)
+    if (lane + 32 * i < n && ll[i] > 0.f) M = fmaxf(M, ml[i]);
+  M = warp_max(M);
+  float w[kGemvMlPerLane];
+  float den = 0.f;
+#pragma unroll
+  for (int i = 0; i < kGemvMlPerLane; ++i) {
+    w[i] = (lane + 32 * i < n && ll[i] > 0.f) ? exp2f(ml[i] - M) : 0.f;
+    den += w[i] * ll[i];
+  }
+  den = warp_sum(den);
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+#pragma unroll
+  for (int i = 0; i < kGemvMlPerLane; ++i)
+    if (lane + 32 * i < n) wt[lane + 32 * i] = w[i] * inv;
+  __syncwarp();
+}
 
 // Index of the k-th group (in order) that holds at least one route, or -1.  Every warp
 // of the CTA computes it from the device-side offsets (at most a few hundred groups).
@@ -43,7 +71,9 @@ __device__ __forceinline__ int kth_routed_group(const int* go, int G, int k) {
   return -1;
 }
 
-template <bool SWIGLU, int U>
+// XP: activations merged from unmerged attention partials (p.x_parts; its own instance, so
+// that the registers of that path do not cut the occupancy of the others)
+template <bool SWIGLU, int U, bool XP = false>
 __global__ __launch_bounds__(kGemvWarps * 32) void gemv_mma_kernel(const LinearParams p,
                                                                     int rb_count, int tc_count) {
   // Dense launches, and grouped ones whose routing is older than the previous launch
@@ -54,6 +84,9 @@ __global__ __launch_bounds__(kGemvWarps * 32) void gemv_mma_kernel(const LinearP
   if (!early) pdl_enter();
   __shared__ float red[kGemvWarps][32][SWIGLU ? 8 : 4];
   __shared__ unsigned long long s_key[kGemvRows * kGemvTok];  // arg-max epilogue only
+  __shared__ float s_wt[kGemvWarps][XP ? kGemvMaxParts : 1];  // x_parts merge weights, per warp
+  int n_parts = -1, part_c0 = 0;
+  bool have_wt = false;
   int item = blockIdx.x;
   const int tc = item % tc_count;
   item /= tc_count;
@@ -118,10 +151,73 @@ __global__ __launch_bounds__(kGemvWarps * 32) void gemv_mma_kernel(const LinearP
       pdl_enter();
       waited = true;
     }
+    if (XP) {
+      // lane L merges element 32 kb + L of the row over the partials, then the lanes of token
+      // 0 (gq == 0) gather their 8 consecutive elements as bf16 (the attention's o_lat).  The
+      // first partials' values are requested together with the (m, l) pairs, before the
+      // merge weights are known.
+      constexpr int kPB = 4;   // partials per batch of loads
+      if (n_parts < 0) {
+        part_c0 = __ldcg(p.x_parts_count);
+        n_parts = __ldcg(p.x_parts_count + 1);
+        if (n_parts < 0 || n_parts > kGemvMaxParts || part_c0 < 0) {
+          if (lane == 0) set_device_error(kErrIndex);
+          n_parts = 0;
+          part_c0 = 0;
+        }
+      }
+      const long long ps = 2LL * p.n_groups * p.k;   // floats between consecutive partials
+      const float* ob = p.x_parts + (static_cast<long long>(2 * part_c0) * p.n_groups + g) * p.k;
+      float mv[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int kb = kb0 + u * kGemvWarps;
-      if (kb < nkb && okT) xv[u] = *reinterpret_cast<const uint4*>(xp + kb * 32);
+      for (int u = 0; u < U; ++u) mv[u] = 0.f;
+      for (int s0 = 0; s0 < n_parts; s0 += kPB) {
+        float v[kPB][U];
+#pragma unroll
+        for (int q = 0; q < kPB; ++q)
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int kb = kb0 + u * kGemvWarps;
+            v[q][u] = (kb < nkb && s0 + q < n_parts) ? __ldcg(ob + (s0 + q) * ps + kb * 32 + lane) : 0.f;
+          }
+        if (!have_wt) {
+          float ml[kGemvMlPerLane], ll[kGemvMlPerLane];
+#pragma unroll
+          for (int i = 0; i < kGemvMlPerLane; ++i) {
+            const int s = lane + 32 * i;
+            const float* mp = p.x_parts_ml + (static_cast<long long>(2 * (part_c0 + s)) * p.n_groups + g) * 2;
+            ml[i] = s < n_parts ? __ldcg(mp) : 0.f;
+            ll[i] = s < n_parts ? __ldcg(mp + 1) : 0.f;
+          }
+          gemv_part_weights(n_parts, ml, ll, s_wt[warp], lane);
+          have_wt = true;
+        }
+#pragma unroll
+        for (int q = 0; q < kPB; q += 2) {
+          const float w0 = s0 + q < n_parts ? s_wt[warp][s0 + q] : 0.f;
+          const float w1 = s0 + q + 1 < n_parts ? s_wt[warp][s0 + q + 1] : 0.f;
+#pragma unroll
+          for (int u = 0; u < U; ++u) mv[u] += w0 * v[q][u] + w1 * v[q + 1][u];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        uint32_t qv[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float a = __shfl_sync(0xffffffffu, mv[u], tq * 8 + 2 * j);
+          const float b = __shfl_sync(0xffffffffu, mv[u], tq * 8 + 2 * j + 1);
+          qv[j] = pack_bf16x2(a, b);
+        }
+        const int kb = kb0 + u * kGemvWarps;
+        if (kb < nkb && okT) xv[u] = make_uint4(qv[0], qv[1], qv[2], qv[3]);
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int kb = kb0 + u * kGemvWarps;
+        if (kb < nkb && okT) xv[u] = *reinterpret_cast<const uint4*>(xp + kb * 32);
+      }
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -185,10 +281,14 @@ cudaError_t launch_linear_gemv(const LinearParams& p, cudaStream_t st) {
   if (items <= 0) return cudaSuccess;
   if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
   const dim3 grid(static_cast<unsigned>(items));
-  if (p.epilogue == kEpiSwiglu)
+  if (p.x_parts) {
+    if (p.epilogue == kEpiSwiglu || p.n_tokens != 1) return cudaErrorInvalidValue;
+    launch_kernel(gemv_mma_kernel<false, 2, true>, grid, kGemvWarps * 32, 0, st, p, rb_count, tc_count);
+  } else if (p.epilogue == kEpiSwiglu) {
     launch_kernel(gemv_mma_kernel<true, 4>, grid, kGemvWarps * 32, 0, st, p, rb_count, tc_count);
-  else
+  } else {
     launch_kernel(gemv_mma_kernel<false, 8>, grid, kGemvWarps * 32, 0, st, p, rb_count, tc_count);
+  }
   return cudaGetLastError();
 }
 

@@ -289,6 +289,8 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int B = p.batch;
   const bool early = p.inputs_prior != 0;
+  // one row whose partials are left for the consumer to merge: no tickets, no o_lat
+  const bool defer = p.part_count != nullptr;
 
   if (warp == kProducerWarp && lane == 0) {
     prefetch_tmap(&tm_kv);
@@ -465,7 +467,7 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
     if (lane == 0) {
       int n_pend = 0;
       long long S = S0;
-      for (int b = b0; S + kSegUnits < end && b < B; ++b) {
+      for (int b = b0; !defer && S + kSegUnits < end && b < B; ++b) {
         const int nt = mla_tiles_of(mla_row_len(p, b));
         const long long St = S + kSegUnits;
         if (!((St >= start) && (St + nt <= end))) {
@@ -494,6 +496,13 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
 
   // ================= compute warps
   if (early) pdl_enter();
+  // deferred merge (one row): the consumer merges slot 0 of CTAs [first, first + count),
+  // the CTAs that hold tiles of the row (a first range of per-row units alone holds none)
+  if (defer && c == 0 && tid == 0) {
+    const long long c_first = mla_owner(kSegUnits, T, n_cta), c_last = mla_owner(T - 1, T, n_cta);
+    p.part_count[0] = static_cast<int>(c_first);
+    p.part_count[1] = static_cast<int>(c_last - c_first + 1);
+  }
   const int gq = lane >> 2, tq = lane & 3;
   const int mi = lane >> 3, ri = lane & 7;
   long long g = 0;   // tiles of this CTA so far (ring slot, P buffer)
@@ -507,7 +516,7 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
       const int len = mla_row_len(p, b), nt = mla_tiles_of(len);
       const long long St = S + kSegUnits;
       const int j0 = static_cast<int>(max(0LL, start - St)), j1 = static_cast<int>(min(static_cast<long long>(nt), end - St));
-      const bool complete = (St >= start) && (St + nt <= end);
+      const bool complete = !defer && (St >= start) && (St + nt <= end);
       // this half's 16 x 288 query slice as 18 A fragments (k-steps of 16 dims)
       const int qb = seg & 1;
       mla_wait(&q_full[qb], static_cast<uint32_t>((seg >> 1) & 1), s_abort);
@@ -649,7 +658,7 @@ __global__ __launch_bounds__(kMlaThreads, 1) void mla_decode_kernel(const MlaDec
       const int len = mla_row_len(p, b), nt = mla_tiles_of(len);
       const long long St = S + kSegUnits;
       const int j0 = static_cast<int>(max(0LL, start - St)), j1 = static_cast<int>(min(static_cast<long long>(nt), end - St));
-      const bool complete = (St >= start) && (St + nt <= end);
+      const bool complete = !defer && (St >= start) && (St + nt <= end);
       float o_acc[16][4];
 #pragma unroll
       for (int i = 0; i < 16; ++i) o_acc[i][0] = o_acc[i][1] = o_acc[i][2] = o_acc[i][3] = 0.f;

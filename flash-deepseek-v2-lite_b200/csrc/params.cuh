@@ -120,6 +120,7 @@ struct MlaDecodeParams {
   int batch;
   const int* cache_rows;       // optional [B]: cache row read by query row b (else b)
   int cache_batch;             // rows of the cache
+  int* part_count;             // optional (B = 1): partials left unmerged; [first CTA, count]
 };
 
 // norm.cu

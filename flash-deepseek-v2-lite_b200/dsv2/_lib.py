@@ -48,6 +48,7 @@ class LinearArgs(ctypes.Structure):
         ("group_offsets", c_vp), ("route_x_row", c_vp), ("route_y_row", c_vp), ("route_scale", c_vp),
         ("w_group_rows", c_i64), ("x_group_rows", c_i64),
         ("k_splits", c_i32), ("y_split_stride", c_i64), ("offsets_prior", c_i32), ("max_routes", c_i32),
+        ("x_parts", c_vp), ("x_parts_ml", c_vp), ("x_parts_count", c_vp),
     ]
 
 
@@ -103,7 +104,7 @@ class MlaDecodeArgs(ctypes.Structure):
         ("positions", c_vp), ("pos_numel", c_i32), ("softmax_scale", c_f32),
         ("split_len", c_i32), ("n_splits", c_i32), ("o_part", c_vp), ("ml_part", c_vp),
         ("o_lat", c_vp), ("batch", c_i32), ("inputs_prior", c_i32), ("row_sync", c_vp), ("family", c_i32),
-        ("cache_rows", c_vp), ("cache_batch", c_i32),
+        ("cache_rows", c_vp), ("cache_batch", c_i32), ("part_count", c_vp),
     ]
 
 

@@ -100,6 +100,9 @@ class DecodeEngine:
         self.max_len = int(max_len)
         self.rank, self.world, self.group = rank, world, group
         self.fused_moe = fused_moe
+        # B = 1, small family: the un-absorb GEMV merges the attention's partials (spread over
+        # its CTAs) instead of one attention CTA
+        self.defer_mla_merge = True
         self._gate_bias = gate_bias
         self.keep_logits = keep_logits   # also materialise the bf16 logits every step
         # cache given: rows of this engine are tokens of the cache's sequences (kernel
@@ -164,6 +167,9 @@ class DecodeEngine:
         self.o_part = torch.zeros((B, self.n_splits, N_HEADS, KV_LORA), device=dev, dtype=f32)
         self.ml_part = torch.zeros((B, self.n_splits, N_HEADS, 2), device=dev, dtype=f32)
         self.mla_sync = torch.zeros(B, device=dev, dtype=i32)
+        # one row (small family): {first CTA, count} of the attention partials that the
+        # un-absorb GEMV merges
+        self.mla_parts = torch.zeros(2, device=dev, dtype=i32)
         dense = [lp.dense for lp in self.layers if lp.dense is not None]
         inter_d = max([d.inter for d in dense], default=8)
         self.mlp_h = torch.zeros((B, inter_d), device=dev, dtype=bf)
@@ -288,16 +294,18 @@ class DecodeEngine:
                      x_group_stride=QK_NOPE, y=self.q_abs, y_row_stride=N_HEADS * KV_LORA,
                      y_group_stride=KV_LORA, n_groups=N_HEADS, n_tokens=B, w_group_rows=KV_LORA,
                      x_group_rows=B)
+        defer = (self.defer_mla_merge and self.family == ops.FAMILY_SMALL and B == 1
+                 and self.cache_rows is None)
         ops.mla_decode(q_abs=self.q_abs, q_pe=self.q_pe, cache=self.cache[li], positions=self.positions,
                        softmax_scale=self.scale, split_len=self.split_len, o_part=self.o_part,
                        ml_part=self.ml_part, o_lat=self.o_lat, inputs_prior=True, row_sync=self.mla_sync,
-                       cache_rows=self.cache_rows)
+                       cache_rows=self.cache_rows, part_count=self.mla_parts if defer else None)
         # o[b, h] = o_lat[b, h] @ W_UV[h]^T,  W_UV[h] = kv_b[h*256 + 128 : h*256 + 256]
         self._linear(w=a.kv_b[QK_NOPE:], n_rows=V_DIM, k=KV_LORA, w_row_stride=KV_LORA,
                      w_group_stride=(QK_NOPE + V_DIM) * KV_LORA, x=self.o_lat, x_row_stride=N_HEADS * KV_LORA,
                      x_group_stride=KV_LORA, y=self.attn_o, y_row_stride=N_HEADS * V_DIM,
                      y_group_stride=V_DIM, n_groups=N_HEADS, n_tokens=B, w_group_rows=V_DIM,
-                     x_group_rows=B)
+                     x_group_rows=B, x_parts=(self.o_part, self.ml_part, self.mla_parts) if defer else None)
         if self.split_k:
             return self._split_linear(w=a.o, n_rows=HIDDEN, k=N_HEADS * V_DIM, x=self.attn_o, out=self.o_proj_part)
         self._linear(w=a.o, n_rows=HIDDEN, k=N_HEADS * V_DIM, x=self.attn_o, y=self.attn_out, n_tokens=B,

@@ -161,7 +161,7 @@ def advance_positions(pos: torch.Tensor) -> None:
     _lib.call("dsv2_advance_positions", pos.data_ptr(), pos.numel(), stream())
 
 
-def linear(*, w: torch.Tensor, n_rows: int, k: int, x: torch.Tensor, y: torch.Tensor,
+def linear(*, w: torch.Tensor, n_rows: int, k: int, x: torch.Tensor | None, y: torch.Tensor,
            family: int, epilogue: int = EPI_STORE_BF16,
            w_row_stride: int | None = None, w_group_stride: int = 0, up_offset: int = 0,
            x_row_stride: int | None = None, x_group_stride: int = 0,
@@ -172,8 +172,12 @@ def linear(*, w: torch.Tensor, n_rows: int, k: int, x: torch.Tensor, y: torch.Te
            route_scale: torch.Tensor | None = None,
            w_group_rows: int | None = None, x_group_rows: int | None = None,
            x_base: int | None = None, k_splits: int = 1, y_split_stride: int = 0,
-           offsets_prior: bool = False, max_routes: int = 0) -> None:
+           offsets_prior: bool = False, max_routes: int = 0,
+           x_parts: tuple | None = None) -> None:
     """Generic linear (see dsv2_linear_args in include/dsv2.h).
+
+    x_parts (small family, one token): (o_part, ml_part, part_count) of a mla_decode call
+    that left its partials unmerged; the activation rows are merged from them (x unused).
 
     Strides are in elements; defaults take them from the 2-D views of w / x / y.
     x_base overrides x's data pointer (strided column views such as q_nope).
@@ -187,8 +191,10 @@ def linear(*, w: torch.Tensor, n_rows: int, k: int, x: torch.Tensor, y: torch.Te
     a.up_offset = up_offset
     a.n_rows = n_rows
     a.k = k
-    a.x = x.data_ptr() if x_base is None else x_base
-    a.x_row_stride = x.stride(-2) if x_row_stride is None else x_row_stride
+    if x is None and x_parts is None:
+        raise ValueError("linear: x or x_parts is required")
+    a.x = (x.data_ptr() if x is not None else None) if x_base is None else x_base
+    a.x_row_stride = (x.stride(-2) if x is not None else k) if x_row_stride is None else x_row_stride
     a.x_group_stride = x_group_stride
     a.y = y.data_ptr()
     a.y_row_stride = y.stride(-2) if y_row_stride is None else y_row_stride
@@ -207,6 +213,13 @@ def linear(*, w: torch.Tensor, n_rows: int, k: int, x: torch.Tensor, y: torch.Te
     a.y_split_stride = y_split_stride
     a.offsets_prior = 1 if offsets_prior else 0
     a.max_routes = max_routes
+    if x_parts is not None:
+        o_part, ml_part, part_count = x_parts
+        for name, t in (("o_part", o_part), ("ml_part", ml_part), ("part_count", part_count)):
+            _cuda(t, name)
+        if o_part.dtype != torch.float32 or ml_part.dtype != torch.float32 or part_count.dtype != torch.int32:
+            raise ValueError("linear: x_parts are (fp32 o_part, fp32 ml_part, int32 part_count)")
+        a.x_parts, a.x_parts_ml, a.x_parts_count = o_part.data_ptr(), ml_part.data_ptr(), part_count.data_ptr()
     _lib.call("dsv2_linear", ctypes.byref(a), family, stream())
 
 
@@ -443,8 +456,11 @@ def mla_workspace(batch: int, max_len: int, split_len: int, device, family: int 
 def mla_decode(*, q_abs: torch.Tensor, q_pe: torch.Tensor, cache: torch.Tensor, positions: torch.Tensor,
                softmax_scale: float, split_len: int, o_part: torch.Tensor, ml_part: torch.Tensor,
                o_lat: torch.Tensor, inputs_prior: bool = False, row_sync: torch.Tensor | None = None,
-               family: int = FAMILY_SMALL, cache_rows: torch.Tensor | None = None) -> None:
+               family: int = FAMILY_SMALL, cache_rows: torch.Tensor | None = None,
+               part_count: torch.Tensor | None = None) -> None:
     """Latent attention for every row (see dsv2_mla_decode_args in include/dsv2.h).
+    part_count (FAMILY_SMALL, one row, optional int32 [2]): leave the partials unmerged for
+    a following linear(x_parts=...); o_lat is then not written.
     inputs_prior: q_pe, positions and the cache were written at least two launches earlier
     on this stream (only q_abs by the previous one).
     family FAMILY_SMALL: balanced mma.sync kernel, one launch; split_len = fewest positions
@@ -494,4 +510,9 @@ def mla_decode(*, q_abs: torch.Tensor, q_pe: torch.Tensor, cache: torch.Tensor, 
         if row_sync.dtype != torch.int32 or row_sync.numel() < q_abs.shape[0]:
             raise ValueError("row_sync must be int32 with one entry per row")
         a.row_sync = row_sync.data_ptr()
+    if part_count is not None:
+        _cuda(part_count, "part_count")
+        if part_count.dtype != torch.int32 or part_count.numel() < 2:
+            raise ValueError("part_count must be int32 [2]")
+        a.part_count = part_count.data_ptr()
     _lib.call("dsv2_mla_decode", ctypes.byref(a), stream())

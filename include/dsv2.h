@@ -269,6 +269,17 @@ typedef struct dsv2_linear_args {
    * (0 = none).  The small family then launches work only for as many groups as can hold
    * a route (at B = 1, 8 of the 66 MoE groups) instead of one CTA set per group. */
   int32_t max_routes;
+  /* small family, dense, n_tokens 1, optional (x may then be NULL): the token's row of
+   * group g is not read from x but merged from the partials that dsv2_mla_decode left
+   * unmerged (its part_count): row = bf16(sum_c a_c o_c[g]) with
+   * a_c = 2^(m_c - M) / sum_c 2^(m_c - M) l_c, partial c's o at x_parts + (2c n_groups + g) k
+   * and (m, l) at x_parts_ml + (2c n_groups + g) 2, c over
+   * [x_parts_count[0], x_parts_count[0] + x_parts_count[1]) (at most 160).  For the
+   * un-absorb after a one-row attention: the merge is spread over the GEMV's CTAs instead
+   * of one attention CTA.  No reference counterpart. */
+  const float* x_parts;       /* o_part */
+  const float* x_parts_ml;    /* ml_part */
+  const int32_t* x_parts_count;
 } dsv2_linear_args;
 
 DSV2_API int dsv2_linear(const dsv2_linear_args* args, int family, void* stream);
@@ -506,6 +517,12 @@ typedef struct dsv2_mla_decode_args {
    * cache_batch = rows of the cache (0 = batch). */
   const int32_t* cache_rows;
   int32_t cache_batch;
+  /* optional int32[2] (DSV2_FAMILY_SMALL, batch 1): leave the row's partials unmerged for
+   * the next linear (dsv2_linear_args.x_parts) instead of merging them in one CTA and
+   * writing o_lat: CTA c stores its (o, m, l) in partial slot 2c, and the launch stores
+   * {first CTA, number of CTAs} holding the row's tiles here.  o_lat is not written, the
+   * row tickets are not used.  NULL = merge as usual.  No reference counterpart. */
+  int32_t* part_count;
 } dsv2_mla_decode_args;
 
 DSV2_API int dsv2_mla_decode(const dsv2_mla_decode_args* args, void* stream);

@@ -287,6 +287,46 @@ def test_mla_decode_vs_oracle(D, B, S, lengths, split):
     assert int(ws["row_sync"].abs().sum()) == 0
 
 
+@pytest.mark.parametrize("S,L,split", [(128, 1, 32), (128, 33, 32), (700, 613, 64), (1200, 1100, 64),
+                                        (9000, 8999, 64)])
+def test_mla_deferred_merge_into_unabsorb(D, S, L, split):
+    """One row: the attention leaves its partials unmerged (part_count) and the un-absorb
+    GEMV merges them while loading its activations.  Against the usual pair (in-launch merge
+    into o_lat, then the GEMV over o_lat): same tolerance as the GEMV tests, twice in a row,
+    and the first/count record names CTAs that hold tiles."""
+    cache, q_abs, q_pe, pos = _mla_inputs(1, S, [L], seed=S + L)
+    g = torch.Generator().manual_seed(L)
+    kv_b = (torch.randn(4096, 512, generator=g) * 0.05).to(torch.bfloat16).to(DEV)
+    scale = 192 ** -0.5
+    ws = D.mla_workspace(1, S, split, DEV)
+    args = dict(q_abs=q_abs.to(DEV), q_pe=q_pe.to(DEV), cache=cache.to(DEV), positions=pos.to(DEV),
+                softmax_scale=scale, split_len=split)
+    lin = dict(w=kv_b[128:], n_rows=128, k=512, w_row_stride=512, w_group_stride=256 * 512,
+               x_row_stride=16 * 512, x_group_stride=512, y_row_stride=2048, y_group_stride=128, n_groups=16,
+               n_tokens=1, family=D.FAMILY_SMALL, w_group_rows=128, x_group_rows=1)
+    o_lat = torch.zeros((1, 16, 512), dtype=torch.bfloat16, device=DEV)
+    D.mla_decode(o_lat=o_lat, **args, **ws)
+    o_ref = torch.zeros(1, 2048, dtype=torch.bfloat16, device=DEV)
+    D.linear(x=o_lat, y=o_ref, **lin)
+    parts = torch.full((2,), -1, dtype=torch.int32, device=DEV)
+    outs = []
+    for _ in range(2):
+        o_untouched = torch.full((1, 16, 512), float("nan"), dtype=torch.bfloat16, device=DEV)
+        D.mla_decode(o_lat=o_untouched, part_count=parts, **args, **ws)
+        o = torch.full((1, 2048), float("nan"), dtype=torch.bfloat16, device=DEV)
+        D.linear(x=None, y=o, x_parts=(ws["o_part"], ws["ml_part"], parts), **lin)
+        torch.cuda.synchronize()
+        assert torch.isnan(o_untouched.float()).all()   # o_lat is not written
+        assert not torch.isnan(o.float()).any()
+        assert relerr(o, o_ref) < 1e-2
+        outs.append(o)
+    assert torch.equal(outs[0], outs[1])
+    first, count = (int(v) for v in parts.cpu())
+    tiles = (L + 31) // 32
+    assert first >= 0 and 1 <= count <= tiles
+    assert int(ws["row_sync"].abs().sum()) == 0
+
+
 def test_mla_decode_requires_row_tickets(D):
     B, S = 2, 64
     z = torch.zeros(B, 16, 512, dtype=torch.bfloat16, device=DEV)
