@@ -45,8 +45,14 @@ constexpr int kRouteThreads = 256;
 constexpr int kRouteMaxRows = 4096;
 
 // softmax + top-6 for one token with one warp; logits in shared/global memory.
-__device__ void softmax_topk_warp(const float* lg, int n_experts, float scaling, int row,
-                                  long long* ids64, int* ids32, float* tw) {
+// Per lane: the ranks of its two experts (lane, lane + 32) and their probabilities.
+struct TopkLane {
+  int r0, r1;
+  float p0, p1;
+};
+
+__device__ TopkLane softmax_topk_warp(const float* lg, int n_experts, float scaling, int row,
+                                      long long* ids64, int* ids32, float* tw) {
   const int lane = threadIdx.x & 31;
   float v0 = lane < n_experts ? lg[lane] : -INFINITY;
   float v1 = lane + 32 < n_experts ? lg[lane + 32] : -INFINITY;
@@ -77,6 +83,43 @@ __device__ void softmax_topk_warp(const float* lg, int n_experts, float scaling,
     if (ids64) ids64[row * kTopK + r1] = lane + 32;
     ids32[row * kTopK + r1] = lane + 32;
     tw[row * kTopK + r1] = p1 * scaling;
+  }
+  return TopkLane{r0, r1, p0, p1};
+}
+
+// Bucketing of a single row by the warp that ranked its experts (one rank, every expert
+// local): the same group offsets and route arrays as route_cta gives for one token, without
+// reading the ids back.  Expert e's group holds its route (slot = its rank) when e is among
+// the top 6; the two shared groups follow with slots 6 and 7.
+__device__ void bucket_one_row_warp(const RouterParams& p, const TopkLane& t) {
+  const int lane = threadIdx.x & 31;
+  const bool s0 = t.r0 < kTopK && lane < p.n_experts;
+  const bool s1 = t.r1 < kTopK && lane + 32 < p.n_experts;
+  const unsigned m0 = __ballot_sync(0xffffffffu, s0), m1 = __ballot_sync(0xffffffffu, s1);
+  const unsigned lt = (1u << lane) - 1u;
+  const int off0 = __popc(m0 & lt), off1 = __popc(m0) + __popc(m1 & lt);
+  const int total = __popc(m0) + __popc(m1);
+  if (lane < p.n_local) p.group_offsets[lane] = off0;
+  if (lane + 32 < p.n_local) p.group_offsets[lane + 32] = off1;
+  if (s0) {
+    p.route_token[off0] = 0;
+    p.route_slot[off0] = t.r0;
+    p.route_weight[off0] = t.p0 * p.scaling;
+  }
+  if (s1) {
+    p.route_token[off1] = 0;
+    p.route_slot[off1] = t.r1;
+    p.route_weight[off1] = t.p1 * p.scaling;
+  }
+  if (lane == 0) {
+    p.group_offsets[p.n_local] = total;
+    p.group_offsets[p.n_local + 1] = total + 1;
+    p.group_offsets[p.n_local + 2] = total + 2;
+  }
+  if (lane < 2) {
+    p.route_token[total + lane] = 0;
+    p.route_slot[total + lane] = kTopK + lane;
+    p.route_weight[total + lane] = 1.f;
   }
 }
 
@@ -503,6 +546,10 @@ __global__ __cluster_dims__(kRcCtas, 1, 1) __launch_bounds__(kRcThreads) void ro
   pdl_wait();
   const bool bucket = p.group_offsets != nullptr;
   if (!bucket) pdl_launch_dependents();
+  // one row on one rank with every expert local and no gather: its bucketing is a few
+  // ballots in the warp that ranks it (no grid barrier, no second pass over the ids)
+  const bool one_row = bucket && p.rows == 1 && gridDim.x == kRcCtas && !p.gather_x && p.expert_lo == 0 &&
+                       p.n_local == p.n_experts && p.shared_lo == 0 && p.shared_hi == 1;
   const int nch = p.hidden / 8;
   const int n_groups_tok = (p.rows + kRtTok - 1) / kRtTok;
   for (int grp = static_cast<int>(cluster_id_x()); grp < n_groups_tok; grp += static_cast<int>(n_clusters_x())) {
@@ -616,13 +663,19 @@ __global__ __cluster_dims__(kRcCtas, 1, 1) __launch_bounds__(kRcThreads) void ro
     }
     cluster_arrive_release();  // B2: CTA 0 sees every CTA's logits
     cluster_wait_acquire();
-    if (crank == 0 && warp < nt)
-      softmax_topk_warp(s_logits[warp], p.n_experts, p.scaling, row0 + warp, p.topk_ids, p.topk_ids32,
-                        p.topk_w);
+    if (crank == 0 && warp < nt) {
+      const TopkLane tl = softmax_topk_warp(s_logits[warp], p.n_experts, p.scaling, row0 + warp, p.topk_ids,
+                                            p.topk_ids32, p.topk_w);
+      if (one_row) bucket_one_row_warp(p, tl);
+    }
     cluster_arrive_release();  // B0 of the next group (or of the exit)
   }
   cluster_wait_acquire();      // no CTA leaves while another may still store into it
   if (!bucket) return;
+  if (one_row) {               // bucketed above by the warp that ranked the row
+    pdl_launch_dependents();
+    return;
+  }
   // a grid of one cluster (up to 8 tokens) meets at a cluster barrier instead of the
   // global-memory one
   bool ok = true;
