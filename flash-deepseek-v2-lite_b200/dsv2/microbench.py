@@ -66,13 +66,14 @@ def build_case(kernel: str, B: int, family: int, ctx: int, split_len: int | None
             calls.append(lambda: ops.linear(
                 w=gate_up, n_rows=I, k=H, up_offset=I * H, w_group_stride=2 * I * H, x=xs if batch else x,
                 y=h, epilogue=ops.EPI_SWIGLU, n_groups=G, group_offsets=go, max_routes_per_group=B,
-                route_x_row=None if batch else rt, family=family, w_group_rows=2 * I, x_group_rows=R))
+                route_x_row=None if batch else rt, family=family, w_group_rows=2 * I, x_group_rows=R,
+                max_routes=R))
             nbytes = (distinct + 2) * 2 * I * H * 2
         elif kernel == "moe_down":
             calls.append(lambda: ops.linear(
                 w=down, n_rows=H, k=I, w_group_stride=H * I, x=h, y=part.view(-1, H), epilogue=ops.EPI_SCALE_F32,
                 n_groups=G, group_offsets=go, max_routes_per_group=B, route_y_row=rs, route_scale=rw,
-                family=family, w_group_rows=H, x_group_rows=R))
+                family=family, w_group_rows=H, x_group_rows=R, max_routes=R, offsets_prior=True))
             nbytes = (distinct + 2) * H * I * 2
         elif kernel == "moe_bucket":
             calls.append(lambda: ops.moe_bucket(ids, w, 0, E, 0, B, go, rt, rs, rw))
