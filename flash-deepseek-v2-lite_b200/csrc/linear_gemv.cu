@@ -272,7 +272,79 @@ __global__ __launch_bounds__(kGemvWarps * 32) void gemv_mma_kernel(const LinearP
   }
 }
 
+// Short K (at most 8 blocks of 32, e.g. the absorbed-query GEMV, K = 128): splitting K over
+// eight warps would leave most of them idle and still pay the cross-warp reduction, so here
+// each warp owns 16 weight rows and the whole K (4 warps, 64 rows per CTA): all of its weight
+// chunks are requested before the launch wait, its activations after it, and the mma.sync
+// fragment goes straight to the epilogue.
+constexpr int kShortWarps = 4;
+constexpr int kShortMaxKb = 8;
+
+__global__ __launch_bounds__(kShortWarps * 32) void gemv_short_k_kernel(const LinearParams p, int rb_count,
+                                                                         int tc_count) {
+  int item = blockIdx.x;
+  const int tc = item % tc_count;
+  item /= tc_count;
+  const int rb = item % rb_count;
+  const int g = item / rb_count;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int n0 = (rb * kShortWarps + warp) * kGemvRows;
+  const int rowA = n0 + gq, rowB = n0 + gq + 8;
+  const bool okA = rowA < p.n_rows, okB = rowB < p.n_rows;
+  const bf16* wg = p.w + g * p.w_group_stride;
+  const bf16* wA = wg + static_cast<long long>(okA ? rowA : 0) * p.w_row_stride + tq * 8;
+  const bf16* wB = wg + static_cast<long long>(okB ? rowB : 0) * p.w_row_stride + tq * 8;
+  const int nkb = p.k / 32;
+  uint4 wa[kShortMaxKb], wb[kShortMaxKb], xv[kShortMaxKb];
+#pragma unroll
+  for (int u = 0; u < kShortMaxKb; ++u) {
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    wa[u] = z; wb[u] = z; xv[u] = z;
+    if (u < nkb) {
+      if (okA) wa[u] = ld_stream_v4(wA + u * 32);
+      if (okB) wb[u] = ld_stream_v4(wB + u * 32);
+    }
+  }
+  pdl_enter();
+  const int tbeg = tc * kGemvTok;
+  const int tn = min(kGemvTok, p.n_tokens - tbeg);
+  const bool okT = gq < tn;
+  const bf16* xp = p.x + g * p.x_group_stride + static_cast<long long>(tbeg + (okT ? gq : 0)) * p.x_row_stride + tq * 8;
+#pragma unroll
+  for (int u = 0; u < kShortMaxKb; ++u)
+    if (u < nkb && okT) xv[u] = *reinterpret_cast<const uint4*>(xp + u * 32);
+  float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int u = 0; u < kShortMaxKb; ++u) {
+    if (u < nkb) {
+      const uint32_t a0[4] = {wa[u].x, wb[u].x, wa[u].y, wb[u].y};
+      mma_bf16_16816(c, a0, xv[u].x, xv[u].y);
+      const uint32_t a1[4] = {wa[u].z, wb[u].z, wa[u].w, wb[u].w};
+      mma_bf16_16816(c, a1, xv[u].z, xv[u].w);
+    }
+  }
+  // fragment element i: row gq (+8 for i >= 2), token 2 tq + (i & 1)
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int n = n0 + gq + ((i & 2) ? 8 : 0);
+    const int j = 2 * tq + (i & 1);
+    if (j < tn && n < p.n_rows) linear_store(p, g, tbeg + j, n, c[i], 0.f);
+  }
+}
+
 cudaError_t launch_linear_gemv(const LinearParams& p, cudaStream_t st) {
+  if (!p.group_offsets && !p.x_parts && p.k <= 32 * kShortMaxKb && p.n_tokens > 0 &&
+      (p.epilogue == kEpiStoreBf16 || p.epilogue == kEpiStoreF32)) {
+    const int rb_count = (p.n_rows + kShortWarps * kGemvRows - 1) / (kShortWarps * kGemvRows);
+    const int tc_count = (p.n_tokens + kGemvTok - 1) / kGemvTok;
+    const long long items = static_cast<long long>(p.n_groups) * rb_count * tc_count;
+    if (items <= 0) return cudaSuccess;
+    if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
+    launch_kernel(gemv_short_k_kernel, dim3(static_cast<unsigned>(items)), kShortWarps * 32, 0, st, p, rb_count,
+                  tc_count);
+    return cudaGetLastError();
+  }
   const int rb_count = (p.n_rows + kGemvRows - 1) / kGemvRows;
   const int max_tok = p.group_offsets ? p.max_routes_per_group : p.n_tokens;
   const int tc_count = max(1, (max_tok + kGemvTok - 1) / kGemvTok);
